@@ -1,0 +1,283 @@
+"""CPU oracle for the nelisp-gpu hot path -- TEST INFRASTRUCTURE ONLY.
+
+A numpy-facing ctypes binding of ``oracle/_build/libnl_oracle.so``, the C
+restatement of the reference's DSL kernels (lisp/nelisp-gpu-kernels.el in
+zawatton/nelisp-gpu, cited per function in nl_oracle.c).  It is the parity
+checker for the CUDA path and the timed CPU baseline.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline legs may import
+it; the product library never calls it.
+
+Parity of this restatement is pinned by ``tests/test_oracle_golden.py``
+against the reference's own test generators and known answers (the tk LCG
+fixture of test/ternary-kernel-test.el, host/vkmatmul.c's exact integer
+sums, host/vksoftmax.c's double softmax and test/verify.el's generators).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libnl_oracle.so")
+_lib = None
+
+_F = ctypes.POINTER(ctypes.c_float)
+_U = ctypes.POINTER(ctypes.c_uint32)
+_D = ctypes.POINTER(ctypes.c_double)
+_u32 = ctypes.c_uint32
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, -ffp-contract=off)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+def _declare(L):
+    sigs = {
+        "nlo_ternary_rows": [_F, _U, _F, _F, _F] + [_u32] * 5,
+        "nlo_ternary_rows_t": [_U, _F, _F, _F] + [_u32] * 5,
+        "nlo_ternary_gemv_rows": [_F, _U, _F, _F] + [_u32] * 3,
+        "nlo_bitlinear_packed": [_F, _F, _F, _F, _F] + [_u32] * 5 + [ctypes.c_int],
+        "nlo_pack_act_rows": [_F, _U, _F] + [_u32] * 3,
+        "nlo_dp4a_rows": [_U, _U, _F, _F, _F, _F] + [_u32] * 3 + [ctypes.c_int],
+        "nlo_matmul": [_F, _F, _F] + [_u32] * 3,
+        "nlo_matmul_tiled": [_F, _F, _F] + [_u32] * 3,
+        "nlo_matmul_reg": [_F, _F, _F] + [_u32] * 3,
+        "nlo_linear": [_F, _F, _F, _F] + [_u32] * 3,
+        "nlo_softmax": [_F, _F] + [_u32] * 2,
+        "nlo_silu_mul": [_F, _F, _F, _u32],
+        "nlo_add2": [_F, _F, _F, _u32],
+        "nlo_scale": [_F, _F, _F, _u32],
+        "nlo_rmsnorm_istd": [_F, _F, _u32, _u32],
+        "nlo_rmsnorm_fwd": [_F, _F, _F, _F, _u32, _u32],
+        "nlo_rope_half": [_F, _F] + [_u32] * 5,
+        "nlo_decode_rope_b": [_F] * 6 + [_u32] * 3,
+        "nlo_cache_append_b": [_F, _F, _F] + [_u32] * 3,
+        "nlo_decode_attn_b": [_F] * 5 + [_u32] * 5,
+        "nlo_embed_gather": [_F, _F, _F, _u32, _u32],
+        "nlo_matmul_sample_ref": [_u32] * 4,
+        "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
+        "nlo_set_threads": [ctypes.c_int],
+        "nlo_threads": [],
+    }
+    for name, argt in sigs.items():
+        fn = getattr(L, name)
+        fn.argtypes = argt
+        fn.restype = None
+    L.nlo_matmul_sample_ref.restype = ctypes.c_double
+    L.nlo_threads.restype = ctypes.c_int
+
+
+def _f(a):
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_F)
+
+
+def _u(a):
+    assert a.dtype == np.uint32 and a.flags.c_contiguous
+    return a.ctypes.data_as(_U)
+
+
+def f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def u32(a):
+    return np.ascontiguousarray(a, dtype=np.uint32)
+
+
+def threads() -> int:
+    return lib().nlo_threads()
+
+
+def set_threads(n: int) -> None:
+    lib().nlo_set_threads(int(n))
+
+
+# ---- kernels -------------------------------------------------------------
+
+def ternary_rows(X, WP, BIAS, BETA, seq, out, cols, nblk, wng):
+    X, WP, BIAS, BETA = f32(X), u32(WP), f32(BIAS), f32(BETA)
+    Y = np.zeros(seq * out, np.float32)
+    lib().nlo_ternary_rows(_f(X), _u(WP), _f(BIAS), _f(BETA), _f(Y),
+                           seq, out, cols, nblk, wng)
+    return Y
+
+
+def ternary_rows_t(WP, BETA, G, out, cols, nblk, wng, seq):
+    WP, BETA, G = u32(WP), f32(BETA), f32(G)
+    X = np.zeros(seq * cols, np.float32)
+    lib().nlo_ternary_rows_t(_u(WP), _f(BETA), _f(G), _f(X),
+                             out, cols, nblk, wng, seq)
+    return X
+
+
+def ternary_gemv_rows(X, WP, S, seq, out, cols):
+    X, WP, S = f32(X), u32(WP), f32(S)
+    Y = np.zeros(seq * out, np.float32)
+    lib().nlo_ternary_gemv_rows(_f(X), _u(WP), _f(S), _f(Y), seq, out, cols)
+    return Y
+
+
+def bitlinear_packed(X, WPK, BIAS, BETA, seq, inn, out, pk, fcount, per_row):
+    X, WPK, BIAS, BETA = f32(X), f32(WPK), f32(BIAS), f32(BETA)
+    Y = np.zeros(seq * out, np.float32)
+    lib().nlo_bitlinear_packed(_f(X), _f(WPK), _f(BIAS), _f(BETA), _f(Y),
+                               seq, inn, out, pk, fcount, int(per_row))
+    return Y
+
+
+def pack_act_rows(X, seq, cols, ng):
+    X = f32(X)
+    XQ = np.zeros(seq * ng, np.uint32)
+    G = np.zeros(seq, np.float32)
+    lib().nlo_pack_act_rows(_f(X), _u(XQ), _f(G), seq, cols, ng)
+    return XQ, G
+
+
+def dp4a_rows(AP, WP, BIAS, BETA, GAMMA, seq, out, ng, per_row):
+    AP, WP, BIAS, BETA, GAMMA = u32(AP), u32(WP), f32(BIAS), f32(BETA), f32(GAMMA)
+    Y = np.zeros(seq * out, np.float32)
+    lib().nlo_dp4a_rows(_u(AP), _u(WP), _f(BIAS), _f(BETA), _f(GAMMA), _f(Y),
+                        seq, out, ng, int(per_row))
+    return Y
+
+
+def _mm(fn, A, B, M, K, N):
+    A, B = f32(A), f32(B)
+    C = np.zeros(M * N, np.float32)
+    fn(_f(A), _f(B), _f(C), M, K, N)
+    return C
+
+
+def matmul(A, B, M, K, N):
+    return _mm(lib().nlo_matmul, A, B, M, K, N)
+
+
+def matmul_tiled(A, B, M, K, N):
+    return _mm(lib().nlo_matmul_tiled, A, B, M, K, N)
+
+
+def matmul_reg(A, B, M, K, N):
+    return _mm(lib().nlo_matmul_reg, A, B, M, K, N)
+
+
+def linear(X, W, B, M, IN, OUT):
+    X, W, B = f32(X), f32(W), f32(B)
+    C = np.zeros(M * OUT, np.float32)
+    lib().nlo_linear(_f(X), _f(W), _f(B), _f(C), M, IN, OUT)
+    return C
+
+
+def softmax(A, M, N):
+    A = f32(A)
+    C = np.zeros(M * N, np.float32)
+    lib().nlo_softmax(_f(A), _f(C), M, N)
+    return C
+
+
+def _ew(fn, A, B, n):
+    A, B = f32(A), f32(B)
+    C = np.zeros(n, np.float32)
+    fn(_f(A), _f(B), _f(C), n)
+    return C
+
+
+def silu_mul(A, B, n):
+    return _ew(lib().nlo_silu_mul, A, B, n)
+
+
+def add2(A, B, n):
+    return _ew(lib().nlo_add2, A, B, n)
+
+
+def scale(A, S, n):
+    return _ew(lib().nlo_scale, A, S, n)
+
+
+def rmsnorm_istd(X, M, N):
+    X = f32(X)
+    S = np.zeros(M, np.float32)
+    lib().nlo_rmsnorm_istd(_f(X), _f(S), M, N)
+    return S
+
+
+def rmsnorm_fwd(X, S, G, M, N):
+    X, S, G = f32(X), f32(S), f32(G)
+    C = np.zeros(M * N, np.float32)
+    lib().nlo_rmsnorm_fwd(_f(X), _f(S), _f(G), _f(C), M, N)
+    return C
+
+
+def rope_half(X, seq, nheads, hd, rbase_bits, sgn_bits):
+    X = f32(X)
+    Y = np.zeros(seq * nheads * hd, np.float32)
+    lib().nlo_rope_half(_f(X), _f(Y), seq, nheads, hd, rbase_bits, sgn_bits)
+    return Y
+
+
+def decode_rope_b(X, CO, SI, SG, POS, B, cols, heads):
+    X, CO, SI, SG, POS = f32(X), f32(CO), f32(SI), f32(SG), f32(POS)
+    C = np.zeros(B * cols, np.float32)
+    lib().nlo_decode_rope_b(_f(X), _f(CO), _f(SI), _f(SG), _f(POS), _f(C),
+                            B, cols, heads)
+    return C
+
+
+def cache_append_b(SRC, POS, CACHE, B, kvdim, maxseq):
+    SRC, POS = f32(SRC), f32(POS)
+    CACHE = f32(CACHE).copy()
+    lib().nlo_cache_append_b(_f(SRC), _f(POS), _f(CACHE), B, kvdim, maxseq)
+    return CACHE
+
+
+def decode_attn_b(Q, CK, CV, POS, B, dim, heads, kvheads, maxseq):
+    Q, CK, CV, POS = f32(Q), f32(CK), f32(CV), f32(POS)
+    C = np.zeros(B * dim, np.float32)
+    lib().nlo_decode_attn_b(_f(Q), _f(CK), _f(CV), _f(POS), _f(C),
+                            B, dim, heads, kvheads, maxseq)
+    return C
+
+
+def embed_gather(TOK, WTE, seq, dim):
+    TOK, WTE = f32(TOK), f32(WTE)
+    C = np.zeros(seq * dim, np.float32)
+    lib().nlo_embed_gather(_f(TOK), _f(WTE), _f(C), seq, dim)
+    return C
+
+
+def matmul_sample_ref(r, c, K, N) -> float:
+    return lib().nlo_matmul_sample_ref(r, c, K, N)
+
+
+def softmax_ref_f64(A, M, N):
+    A = np.ascontiguousarray(A, np.float64)
+    C = np.zeros(M * N, np.float64)
+    lib().nlo_softmax_ref_f64(A.ctypes.data_as(_D), C.ctypes.data_as(_D), M, N)
+    return C
+
+
+# ---- metrics -------------------------------------------------------------
+
+def tk_err(got, want) -> float:
+    """max|got - want| / max|want| -- test/ternary-kernel-test.el:23-34."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    if want.size == 0:
+        return 0.0
+    scale = max(float(np.max(np.abs(want))), 1.0e-12)
+    return float(np.max(np.abs(got - want))) / scale

@@ -1,0 +1,484 @@
+/* nl_oracle.c -- CPU restatement of the nelisp-gpu hot-path kernels.
+ *
+ * TEST INFRASTRUCTURE ONLY (parity checker and timed CPU baseline); no
+ * product code path links or calls this file.
+ *
+ * Each function follows one kernel spec in the reference's
+ * lisp/nelisp-gpu-kernels.el (cited per function as file:line) with the
+ * same f32 operation order.  Build with -ffp-contract=off: the reference
+ * lowers `(+ acc (* a b))` to a separate OpFMul and OpFAdd.  exp, sqrt, sin,
+ * cos and pow come from libm in single precision; the reference uses
+ * GLSL.std.450, whose precision Vulkan leaves relaxed, so those ops are
+ * compared with a tolerance rather than bit for bit.
+ */
+#include "nl_oracle.h"
+#include <math.h>
+#include <string.h>
+#include <stdlib.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+int nlo_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+void nlo_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
+static inline float bits_f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline uint32_t f_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+
+/* OpConvertFToU as GPUs execute it (round toward zero, saturating, NaN->0). */
+static inline uint32_t f2u(float f) {
+  if (!(f > 0.0f)) return 0u;
+  if (f >= 4294967296.0f) return 0xffffffffu;
+  return (uint32_t)f;
+}
+
+/* Field f of a packed word, sign-extended: the DSL's
+ * (>>s (bitcast-i (<< wpk sh)) 30) with sh = 30 - 2f.
+ * 00 -> 0, 01 -> +1, 11 -> -1, 10 -> -2. */
+static inline float trit(uint32_t wpk, uint32_t f) {
+  int32_t v = (int32_t)(wpk << (30u - 2u * f));
+  return (float)(v >> 30);
+}
+
+/* lisp/nelisp-gpu-kernels.el:713-746 (ternary-rows) */
+void nlo_ternary_rows(const float *X, const uint32_t *WP, const float *BIAS,
+                      const float *BETA, float *Y, uint32_t seq, uint32_t out,
+                      uint32_t cols, uint32_t nblk, uint32_t wng) {
+  long long total = (long long)seq * out;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t s = (uint32_t)(idx / out), o = (uint32_t)(idx % out);
+    uint32_t xb = s * cols, wb = o * wng;
+    float acc = 0.0f;
+    for (uint32_t b = 0; b < nblk; b++) {
+      float bacc = 0.0f;
+      for (uint32_t w = 0; w < 8; w++) {
+        uint32_t wi = b * 8 + w;
+        if (wi < wng) {
+          uint32_t wpk = WP[wb + wi];
+          for (uint32_t f = 0; f < 16; f++) {
+            uint32_t i = wi * 16 + f;
+            if (i < cols) {
+              float prod = trit(wpk, f) * X[xb + i];
+              bacc = bacc + prod;
+            }
+          }
+        }
+      }
+      float sc = BETA[o * nblk + b] * bacc;
+      acc = acc + sc;
+    }
+    Y[idx] = BIAS[o] + acc;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:750-772 (ternary-rows-t) */
+void nlo_ternary_rows_t(const uint32_t *WP, const float *BETA, const float *G,
+                        float *X, uint32_t out, uint32_t cols, uint32_t nblk,
+                        uint32_t wng, uint32_t seq) {
+  long long total = (long long)seq * cols;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t p = (uint32_t)(idx / cols), i = (uint32_t)(idx % cols);
+    uint32_t b = i / 128, wi = i / 16, fd = i % 16;
+    uint32_t gb = p * out;
+    float acc = 0.0f;
+    for (uint32_t o = 0; o < out; o++) {
+      float sv = trit(WP[o * wng + wi], fd);
+      float bg = BETA[o * nblk + b] * G[gb + o];
+      float prod = sv * bg;
+      acc = acc + prod;
+    }
+    X[idx] = acc;
+  }
+}
+
+void nlo_ternary_gemv_rows(const float *X, const uint32_t *WP, const float *S,
+                           float *Y, uint32_t seq, uint32_t out,
+                           uint32_t cols) {
+  uint32_t wng = (cols + 15) / 16, nblk = (cols + 127) / 128;
+  float *beta = (float *)malloc(sizeof(float) * (size_t)out * nblk);
+  float *bias = (float *)calloc(out, sizeof(float));
+  for (uint32_t o = 0; o < out; o++)
+    for (uint32_t b = 0; b < nblk; b++) beta[(size_t)o * nblk + b] = S[o];
+  nlo_ternary_rows(X, WP, bias, beta, Y, seq, out, cols, nblk, wng);
+  free(beta);
+  free(bias);
+}
+
+/* lisp/nelisp-gpu-kernels.el:998-1016 (bitlinear-packed, BETA[0]) and
+ * :1022-1040 (bitlinear-packed-v, BETA[o]).  Codes are base-4 digits of the
+ * f32 VALUE converted to an unsigned integer, least significant first. */
+void nlo_bitlinear_packed(const float *X, const float *WPK, const float *BIAS,
+                          const float *BETA, float *Y, uint32_t seq,
+                          uint32_t in, uint32_t out, uint32_t pk,
+                          uint32_t fcount, int per_row) {
+  long long total = (long long)seq * out;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t s = (uint32_t)(idx / out), o = (uint32_t)(idx % out);
+    float acc = BIAS[o];
+    float beta = per_row ? BETA[o] : BETA[0];
+    uint32_t xb = s * in, rowf = o * fcount;
+    for (uint32_t f = 0; f < fcount; f++) {
+      uint32_t packed = f2u(WPK[rowf + f]);
+      uint32_t i0 = f * pk;
+      for (uint32_t z = 0; z < pk; z++) {
+        uint32_t i = i0 + z;
+        if (i < in) {
+          uint32_t code = packed % 4u;
+          float tern = (float)code - 1.0f;
+          float w = beta * tern;
+          float prod = X[xb + i] * w;
+          acc = acc + prod;
+        }
+        packed = packed / 4u;
+      }
+    }
+    Y[idx] = acc;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:898-932 (pack-act-rows) */
+void nlo_pack_act_rows(const float *X, uint32_t *XQ, float *GAMMA,
+                       uint32_t seq, uint32_t cols, uint32_t ng) {
+#pragma omp parallel for schedule(static)
+  for (long long row = 0; row < (long long)seq; row++) {
+    uint32_t base = (uint32_t)row * cols;
+    float amax = 0.0f;
+    for (uint32_t c = 0; c < cols; c++) {
+      float v = X[base + c];
+      float av = v;
+      if (v < 0.0f) av = 0.0f - v;
+      if (av > amax) amax = av;
+    }
+    float gamma = amax / 127.0f;
+    GAMMA[row] = gamma;
+    uint32_t wb = (uint32_t)row * ng;
+    for (uint32_t w = 0; w < ng; w++) {
+      uint32_t word = 0, sh = 1;
+      for (uint32_t l = 0; l < 4; l++) {
+        uint32_t c = w * 4 + l;
+        uint32_t lane = 0;
+        if (c < cols) {
+          float v = X[base + c];
+          float q = 0.0f;
+          if (gamma > 0.0f) q = v / gamma;
+          uint32_t neg = 0;
+          float aq = q;
+          if (q < 0.0f) { neg = 1; aq = 0.0f - q; }
+          uint32_t ri = f2u(aq + 0.5f);
+          if (ri > 127u) ri = 127u;
+          lane = ri;
+          if (neg == 1) lane = (256u - ri) % 256u;
+        }
+        word = word + lane * sh;
+        sh = sh * 256u;
+      }
+      XQ[wb + w] = word;
+    }
+  }
+}
+
+/* OpSDot with PackedVectorFormat4x8Bit: signed 8-bit lanes, int32 sum. */
+static inline int32_t sdot4(uint32_t a, uint32_t b) {
+  int32_t acc = 0;
+  for (int l = 0; l < 4; l++)
+    acc += (int32_t)(int8_t)(a >> (8 * l)) * (int32_t)(int8_t)(b >> (8 * l));
+  return acc;
+}
+
+/* lisp/nelisp-gpu-kernels.el:642-653 (bitlinear-dp4a-rows, BETA[o]) and
+ * :623-634 (bitlinear-dp4a-1f, BETA[0]).  The integer sum wraps mod 2^32 like
+ * the reference's 32-bit OpIAdd. */
+void nlo_dp4a_rows(const uint32_t *AP, const uint32_t *WP, const float *BIAS,
+                   const float *BETA, const float *GAMMA, float *Y,
+                   uint32_t seq, uint32_t out, uint32_t ng, int per_row) {
+  long long total = (long long)seq * out;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t s = (uint32_t)(idx / out), o = (uint32_t)(idx % out);
+    uint32_t ab = s * ng, wb = o * ng;
+    uint32_t acc = 0;
+    for (uint32_t g = 0; g < ng; g++)
+      acc += (uint32_t)sdot4(AP[ab + g], WP[wb + g]);
+    float bg = (per_row ? BETA[o] : BETA[0]) * GAMMA[s];
+    float scaled = bg * (float)(int32_t)acc;
+    Y[idx] = BIAS[o] + scaled;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:17-27 (matmul); :129 (matmul-reg) accumulates
+ * each of its sixteen outputs in the same k order, so it is the same sum. */
+void nlo_matmul(const float *A, const float *B, float *C, uint32_t M,
+                uint32_t K, uint32_t N) {
+  long long total = (long long)M * N;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t row = (uint32_t)(idx / N), col = (uint32_t)(idx % N);
+    float acc = 0.0f;
+    for (uint32_t k = 0; k < K; k++) {
+      float prod = A[row * K + k] * B[k * N + col];
+      acc = acc + prod;
+    }
+    C[idx] = acc;
+  }
+}
+
+void nlo_matmul_reg(const float *A, const float *B, float *C, uint32_t M,
+                    uint32_t K, uint32_t N) {
+  nlo_matmul(A, B, C, M, K, N);
+}
+
+/* lisp/nelisp-gpu-kernels.el:82-107 (matmul-tiled): per 16-wide k tile the
+ * sixteen products are summed right-nested, p0 + (p1 + (... + p15)), and
+ * that tile sum is added to the accumulator.  Out-of-range tile elements
+ * are zero. */
+void nlo_matmul_tiled(const float *A, const float *B, float *C, uint32_t M,
+                      uint32_t K, uint32_t N) {
+  long long total = (long long)M * N;
+  uint32_t nt = (K + 15) / 16;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t row = (uint32_t)(idx / N), col = (uint32_t)(idx % N);
+    float acc = 0.0f;
+    for (uint32_t tt = 0; tt < nt; tt++) {
+      float p[16];
+      for (uint32_t j = 0; j < 16; j++) {
+        uint32_t k = tt * 16 + j;
+        float a = (k < K) ? A[row * K + k] : 0.0f;
+        float b = (k < K) ? B[k * N + col] : 0.0f;
+        p[j] = a * b;
+      }
+      float s = p[15];
+      for (int j = 14; j >= 0; j--) s = p[j] + s;
+      acc = acc + s;
+    }
+    C[idx] = acc;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:71-81 (linear): C = X . W^T + B */
+void nlo_linear(const float *X, const float *W, const float *B, float *C,
+                uint32_t M, uint32_t IN, uint32_t OUT) {
+  long long total = (long long)M * OUT;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t row = (uint32_t)(idx / OUT), o = (uint32_t)(idx % OUT);
+    float acc = B[o];
+    for (uint32_t k = 0; k < IN; k++) {
+      float prod = X[row * IN + k] * W[o * IN + k];
+      acc = acc + prod;
+    }
+    C[idx] = acc;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:28-42 (softmax) */
+void nlo_softmax(const float *A, float *C, uint32_t M, uint32_t N) {
+#pragma omp parallel for schedule(static)
+  for (long long r = 0; r < (long long)M; r++) {
+    uint32_t base = (uint32_t)r * N;
+    float m = A[base];
+    for (uint32_t j = 0; j < N; j++) {
+      float v = A[base + j];
+      if (v > m) m = v;
+    }
+    float s = 0.0f;
+    for (uint32_t j = 0; j < N; j++) s = s + expf(A[base + j] - m);
+    for (uint32_t j = 0; j < N; j++) C[base + j] = expf(A[base + j] - m) / s;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:187-193 (silu-mul) */
+void nlo_silu_mul(const float *A, const float *B, float *C, uint32_t n) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; i++) {
+    float a = A[i];
+    float sg = 1.0f / (1.0f + expf(0.0f - a));
+    float as = a * sg;
+    C[i] = as * B[i];
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:816-821 (add2) */
+void nlo_add2(const float *A, const float *B, float *C, uint32_t n) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; i++) C[i] = A[i] + B[i];
+}
+
+/* lisp/nelisp-gpu-kernels.el:141 (scale) */
+void nlo_scale(const float *A, const float *S, float *C, uint32_t n) {
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < (long long)n; i++) C[i] = A[i] * S[0];
+}
+
+/* lisp/nelisp-gpu-kernels.el:1250-1256 (rmsnorm-istd) */
+void nlo_rmsnorm_istd(const float *X, float *S, uint32_t M, uint32_t N) {
+#pragma omp parallel for schedule(static)
+  for (long long r = 0; r < (long long)M; r++) {
+    uint32_t base = (uint32_t)r * N;
+    float ss = 0.0f;
+    for (uint32_t k = 0; k < N; k++) {
+      float v = X[base + k];
+      float sq = v * v;
+      ss = ss + sq;
+    }
+    float mean = ss / (float)N;
+    S[r] = 1.0f / sqrtf(mean + 0.000001f);
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:1259-1265 (rmsnorm-fwd) */
+void nlo_rmsnorm_fwd(const float *X, const float *S, const float *G, float *C,
+                     uint32_t M, uint32_t N) {
+  long long total = (long long)M * N;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t r = (uint32_t)(idx / N), j = (uint32_t)(idx % N);
+    float xs = X[idx] * S[r];
+    C[idx] = xs * G[j];
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:857-882 (rope-half): element m pairs with
+ * m + hd/2 at position p = row index. */
+void nlo_rope_half(const float *X, float *Y, uint32_t seq, uint32_t nheads,
+                   uint32_t hd, uint32_t rbase_bits, uint32_t sgn_bits) {
+  uint32_t half = hd / 2;
+  long long total = (long long)seq * nheads * half;
+  float rbase = bits_f(rbase_bits), sgn = bits_f(sgn_bits);
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t m = (uint32_t)(idx % half), tmp = (uint32_t)(idx / half);
+    uint32_t h = tmp % nheads, p = tmp / nheads;
+    uint32_t b0 = p * (nheads * hd) + h * hd;
+    float ex = (2.0f * (float)m) / (float)hd;
+    float theta = (float)p / powf(rbase, ex);
+    float c = cosf(theta);
+    float s = sgn * sinf(theta);
+    float a0 = X[b0 + m], a1 = X[b0 + m + half];
+    float t0 = a0 * c, t1 = a1 * s, t2 = a1 * c, t3 = a0 * s;
+    Y[b0 + m] = t0 - t1;
+    Y[b0 + m + half] = t2 + t3;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:342-355 (decode-rope-b): adjacent pairs
+ * (2m, 2m+1) rotated by host tables CO/SI at row POS[0]. */
+void nlo_decode_rope_b(const float *X, const float *CO, const float *SI,
+                       const float *SG, const float *POS, float *C,
+                       uint32_t B, uint32_t cols, uint32_t heads) {
+  uint32_t hd = cols / heads, half = hd / 2, rh = heads * half;
+  long long total = (long long)B * rh;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t bb = (uint32_t)(idx / rh), rem = (uint32_t)(idx % rh);
+    uint32_t m = rem % half, h = rem / half;
+    uint32_t pos = f2u(POS[0]);
+    uint32_t ci = pos * half + m;
+    float cc = CO[ci], ss = SI[ci] * SG[0];
+    uint32_t b0 = bb * cols + h * hd, i0 = b0 + 2 * m, i1 = i0 + 1;
+    float a0 = X[i0], a1 = X[i1];
+    float t0 = a0 * cc, t1 = a1 * ss, t2 = a0 * ss, t3 = a1 * cc;
+    C[i0] = t0 - t1;
+    C[i1] = t2 + t3;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:358-365 (cache-append-b) */
+void nlo_cache_append_b(const float *SRC, const float *POS, float *CACHE,
+                        uint32_t B, uint32_t kvdim, uint32_t maxseq) {
+  uint32_t pos = f2u(POS[0]);
+  for (uint32_t idx = 0; idx < B * kvdim; idx++) {
+    uint32_t bb = idx / kvdim, t = idx % kvdim;
+    CACHE[(bb * maxseq + pos) * kvdim + t] = SRC[idx];
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:368-390 (decode-attn-b): two passes over
+ * positions 0..POS[0]; the q.k dot product is recomputed in each. */
+void nlo_decode_attn_b(const float *Q, const float *CK, const float *CV,
+                       const float *POS, float *C, uint32_t B, uint32_t dim,
+                       uint32_t heads, uint32_t kvheads, uint32_t maxseq) {
+  uint32_t hd = dim / heads, grp = heads / kvheads, kvdim = kvheads * hd;
+  long long total = (long long)B * dim;
+  uint32_t pos = f2u(POS[0]), len = pos + 1;
+  float coef = 1.0f / sqrtf((float)hd);
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t bb = (uint32_t)(idx / dim), c = (uint32_t)(idx % dim);
+    uint32_t h = c / hd, t = c % hd, kvh = h / grp;
+    uint32_t cbase = bb * maxseq * kvdim, c0q = bb * dim + h * hd;
+    float mx = -1.0e30f;
+    for (uint32_t j = 0; j < len; j++) {
+      uint32_t kb = cbase + j * kvdim + kvh * hd;
+      float acc = 0.0f;
+      for (uint32_t tt = 0; tt < hd; tt++) {
+        float prod = Q[c0q + tt] * CK[kb + tt];
+        acc = acc + prod;
+      }
+      float s = acc * coef;
+      if (s > mx) mx = s;
+    }
+    float z = 0.0f, ctx = 0.0f;
+    for (uint32_t j = 0; j < len; j++) {
+      uint32_t kb = cbase + j * kvdim + kvh * hd;
+      float acc = 0.0f;
+      for (uint32_t tt = 0; tt < hd; tt++) {
+        float prod = Q[c0q + tt] * CK[kb + tt];
+        acc = acc + prod;
+      }
+      float e = expf(acc * coef - mx);
+      z = z + e;
+      float ev = e * CV[kb + t];
+      ctx = ctx + ev;
+    }
+    C[idx] = ctx / z;
+  }
+}
+
+/* lisp/nelisp-gpu-kernels.el:1385-1392 (embed-gather) */
+void nlo_embed_gather(const float *TOK, const float *WTE, float *C,
+                      uint32_t seq, uint32_t dim) {
+  long long total = (long long)seq * dim;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t i = (uint32_t)(idx / dim), j = (uint32_t)(idx % dim);
+    uint32_t tk = f2u(TOK[i]);
+    C[idx] = WTE[tk * dim + j];
+  }
+}
+
+/* host/vkmatmul.c:172-180: the exact double sum the matmul CLI checks a
+ * sampled C[r,c] against, for A[i] = i%4 and B[i] = i%3. */
+double nlo_matmul_sample_ref(uint32_t r, uint32_t c, uint32_t K, uint32_t N) {
+  double acc = 0.0;
+  for (uint32_t k = 0; k < K; k++)
+    acc += (double)(((size_t)r * K + k) % 4) * (double)(((size_t)k * N + c) % 3);
+  return acc;
+}
+
+/* host/vksoftmax.c:103-114: the double-precision softmax it checks with. */
+void nlo_softmax_ref_f64(const double *A, double *C, uint32_t M, uint32_t N) {
+  for (uint32_t r = 0; r < M; r++) {
+    const double *a = A + (size_t)r * N;
+    double mx = -1e30, s = 0.0;
+    for (uint32_t j = 0; j < N; j++) if (a[j] > mx) mx = a[j];
+    for (uint32_t j = 0; j < N; j++) s += exp(a[j] - mx);
+    for (uint32_t j = 0; j < N; j++) C[(size_t)r * N + j] = exp(a[j] - mx) / s;
+  }
+}

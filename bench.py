@@ -1,0 +1,456 @@
+#!/usr/bin/env python
+"""Benchmark of the ternary GEMV hot path.
+
+Workload (one step): 64 independent ternary GEMVs y = diag(s) (W x) with
+W 4096x4096 (trits -1/0/+1 each p=1/3, two bits per weight, four per byte,
+row-major), s ~ U[0.5, 1.5] per row, x ~ N(0, 1), batch 1 -- 64 distinct
+weight copies (271 MB per step, more than the 126 MB L2) so every step
+streams its weights from HBM.  All inputs are seeded synthetic data.
+
+Metric: GB/s of algorithmic bytes (packed weights + scales + x + y per GEMV,
+4,243,456 B at batch 1), whole job, as a fraction of the measured HBM peak.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's own arithmetic on the host cores: the
+C restatement of `ternary-rows' under oracle/ (the reference's own path is
+Elisp/SPIR-V/Vulkan and cannot run here), all host threads, bounded samples.
+Under torchrun with N>1 each rank runs its own 64 copies (weak scaling; the
+path has no exchange step) and the time is the max over ranks; the reference
+arm runs on rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "nelisp-gpu_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+BASE = json.load(open(os.path.join(ROOT, "BASELINE.json")))
+METRIC = BASE["metric"]
+OUT = COLS = 4096
+COPIES = 64
+FALLBACK_HBM_GBS = 6650.0
+
+
+def gemv_bytes(out, cols, batch):
+    """Algorithmic bytes of one GEMV: packed W, per-row s, x and y."""
+    return out * cols // 4 + out * 4 + cols * 4 * batch + out * 4 * batch
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_summary():
+    """Per-launch DRAM bytes of the main GEMV kernel from the committed ncu
+    summary, if there is one."""
+    p = os.path.join(ROOT, "profiles", "ternary_gemv_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p))
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+# ---- distributed plumbing -----------------------------------------------------------
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def init_dist(ws):
+    if ws <= 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+# ---- clocks -------------------------------------------------------------------------
+
+CLOCK_FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={CLOCK_FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1])); smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def physical_gpu(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        items = [v.strip() for v in vis.split(",") if v.strip()]
+        if local_rank < len(items) and items[local_rank].isdigit():
+            return int(items[local_rank])
+    return local_rank
+
+
+# ---- problem generation (on the device, seeded) ----------------------------------------
+
+def make_weights(torch, copies, out, cols, seed, device):
+    """Packed trits, codes 00 (0), 01 (+1), 11 (-1) each with p = 1/3."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    lut = torch.tensor([0, 1, 3], dtype=torch.int64, device=device)
+    shifts = (2 * torch.arange(16, device=device, dtype=torch.int64))
+    W = torch.empty(copies, out * cols // 16, dtype=torch.int32, device=device)
+    for z in range(copies):
+        r = torch.randint(0, 3, (out, cols // 16, 16), generator=g, device=device)
+        w = (lut[r] << shifts).sum(-1)
+        w = torch.where(w >= 2 ** 31, w - 2 ** 32, w)
+        W[z] = w.reshape(-1).to(torch.int32)
+    S = torch.rand(copies, out, generator=g, device=device) + 0.5
+    return W, S
+
+
+# ---- the GPU arm -------------------------------------------------------------------------
+
+def run_gpu(args):
+    import numpy as np
+    import torch
+
+    from nelisp_cuda import dev, load
+    ws, rank, local = dist_env()
+    dist = init_dist(ws)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    lib = load()
+    from nelisp_cuda import _lib as L0
+    L0.check(lib.nl_init(local))          # the library's context on this rank's GPU
+    batch = args.batch
+    W, S = make_weights(torch, COPIES, OUT, COLS, 1234 + rank, device)
+    g = torch.Generator(device=device)
+    g.manual_seed(99 + rank)
+    X = torch.randn(COPIES, batch, COLS, generator=g, device=device)
+    Y = torch.empty(COPIES, batch, OUT, device=device)
+    wsb = COPIES * dev.ternary_workspace_bytes(batch, COLS)
+    WS = torch.empty(wsb, dtype=torch.uint8, device=device)
+
+    def step():
+        dev.ternary_gemv_batched(COPIES, X, batch * COLS, W, OUT * COLS // 16, S, OUT, Y,
+                                 batch * OUT, batch, OUT, COLS, workspace=WS)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+
+    def load_for(seconds):
+        t_end = time.time() + seconds
+        while time.time() < t_end:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    # the clock record covers load only: 0.5 s before the timed region, the
+    # region itself and 1 s after it, all running this same step
+    sampler = ClockSampler(physical_gpu(local))
+    sampler.start()
+    load_for(0.5)
+    n0 = dev.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    barrier()
+    n1 = dev.launch_count()
+    ms = e0.elapsed_time(e1) / args.steps
+    load_for(1.0)
+    clocks = sampler.stop()
+    if dist:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    per_gemv = gemv_bytes(OUT, COLS, batch)
+    step_bytes = COPIES * per_gemv
+    value = ws * step_bytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9        # this rank's launches, prep included
+
+    # single-GEMV latency (L2 holds the 4 MB weights: reported, not the headline)
+    one = []
+    for _ in range(20):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dev.ternary_gemv(X[0].reshape(-1), W[0], S[0], Y[0].reshape(-1), batch, OUT, COLS,
+                         workspace=WS)
+        b.record()
+        torch.cuda.synchronize()
+        one.append(a.elapsed_time(b))
+    single_us = 1e3 * statistics.median(one[5:])
+
+    # other batch sizes of the config, same 64 copies
+    batches = {}
+    for bb in ([4, 16] if batch == 1 else []):
+        Xb = torch.randn(COPIES, bb, COLS, generator=g, device=device)
+        Yb = torch.empty(COPIES, bb, OUT, device=device)
+        WSb = torch.empty(COPIES * dev.ternary_workspace_bytes(bb, COLS), dtype=torch.uint8,
+                          device=device)
+
+        def stepb():
+            dev.ternary_gemv_batched(COPIES, Xb, bb * COLS, W, OUT * COLS // 16, S, OUT, Yb,
+                                     bb * OUT, bb, OUT, COLS, workspace=WSb)
+        for _ in range(3):
+            stepb()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            stepb()
+        b.record()
+        torch.cuda.synchronize()
+        msb = a.elapsed_time(b) / args.steps
+        gbs = COPIES * gemv_bytes(OUT, COLS, bb) / (msb * 1e-3) / 1e9
+        batches[str(bb)] = {"GB/s": round(gbs, 1), "frac": round(gbs / peak, 4),
+                            "ms_per_step": round(msb, 4)}
+        del Xb, Yb, WSb
+
+    # e2e: through the C ABI with host buffers -- weights resident (uploaded
+    # once, as a client of the server uploads them), every step copies its
+    # activations in from pinned memory and reads its outputs back.
+    import ctypes
+    from nelisp_cuda import _lib as L
+    hw, hs, hx, hy = (ctypes.c_uint32() for _ in range(4))
+    Wh = W.cpu().numpy().view(np.uint32)
+    Sh = S.cpu().numpy()
+    Xp = X.cpu().pin_memory()
+    Yp = torch.empty(COPIES * batch * OUT, dtype=torch.float32).pin_memory()
+    L.check(lib.nl_upload(Wh.ctypes.data, Wh.size, ctypes.byref(hw)))
+    L.check(lib.nl_upload(Sh.ctypes.data, Sh.size, ctypes.byref(hs)))
+    nx, ny = COPIES * batch * COLS, COPIES * batch * OUT
+    L.check(lib.nl_upload(Xp.data_ptr(), nx, ctypes.byref(hx)))
+    L.check(lib.nl_upload(Yp.data_ptr(), ny, ctypes.byref(hy)))
+    ptr = {}
+    for name, h in (("w", hw), ("s", hs), ("x", hx), ("y", hy)):
+        p, n = ctypes.c_void_p(), ctypes.c_uint32()
+        L.check(lib.nl_resident_info(h.value, ctypes.byref(p), ctypes.byref(n)))
+        ptr[name] = p.value
+
+    def e2e_step():
+        L.check(lib.nl_write_resident(hx.value, Xp.data_ptr(), nx))
+        L.check(lib.nl_ternary_gemv_batched_dev(
+            COPIES, ptr["x"], batch * COLS, ptr["w"], OUT * COLS // 16, ptr["s"], OUT,
+            ptr["y"], batch * OUT, batch, OUT, COLS, None, 0, None))
+        L.check(lib.nl_read_resident(hy.value, Yp.data_ptr(), ny))
+
+    for _ in range(args.warmup):
+        e2e_step()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    if dist:
+        t = torch.tensor([e2e_s], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = ws * step_bytes / e2e_s / 1e9
+    y_dev = Y.reshape(-1).cpu().numpy()
+    e2e_ok = bool(np.allclose(Yp.numpy(), y_dev, rtol=0, atol=0))
+    for h in (hw, hs, hx, hy):
+        lib.nl_free(h.value)
+
+    # CPU baseline: the oracle port on this box's host cores (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cpu = cpu_baseline(Wh[:1].ravel(), Sh[0], X[0].reshape(-1).cpu().numpy(), batch,
+                           seconds=args.cpu_seconds)
+
+    tr = traffic_summary()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8xint8->int32 (exact ternary x 3-limb activations) + f32 epilogue",
+            "data": "synthetic (seeded; trits p=1/3, s~U[0.5,1.5], x~N(0,1))",
+            "config": {"workload": "ternary GEMV y=diag(s)(W x), W 4096x4096 2-bit packed, "
+                                   f"batch {batch}, {COPIES} distinct weight copies per step",
+                       "out": OUT, "cols": COLS, "batch": batch, "copies_per_step": COPIES,
+                       "bytes_per_gemv": per_gemv,
+                       "l2": "inputs larger than L2 (271 MB of weights per step per GPU)",
+                       "parallelism": f"weak: {ws} independent replica(s), no collective"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                         if peak_kind == "measured" else "fallback 6650 GB/s",
+                         "traffic": (tr or {}).get("bytes_per_launch"),
+                         "note": "achieved = algorithmic bytes per step / device time of the "
+                                 "step's two launches (prep + tensor-core GEMV)"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
+                    "h2d_bytes_per_step": nx * 4, "d2h_bytes_per_step": ny * 4,
+                    "path": "C ABI: nl_write_resident + nl_ternary_gemv_batched_dev + "
+                            "nl_read_resident, weights resident", "matches_device_run": e2e_ok},
+            "gpu_launches": int(n1 - n0),
+            "clocks": clocks,
+            "single_gemv_us": round(single_us, 2),
+            "batches": batches,
+        }
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(WP, S, X, batch, seconds=10.0):
+    """The oracle's ternary GEMV (restated `ternary-rows' with the row scale
+    in every block) on all host threads, timed over a bounded sample."""
+    import oracle as nlo
+    nlo.lib()
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        nlo.ternary_gemv_rows(X, WP, S, batch, OUT, COLS)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or n >= 10000:
+            break
+    per = el / n
+    return {"value": round(gemv_bytes(OUT, COLS, batch) / per / 1e9, 3), "unit": "GB/s",
+            "cores": nlo.threads(), "kind": "port",
+            "sample": f"{n} GEMVs 4096x4096 batch {batch} in {el:.1f} s "
+                      "(oracle/nl_oracle.c ternary-rows restatement, OpenMP)"}
+
+
+# ---- the reference arm ----------------------------------------------------------------------
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle as nlo
+    nlo.lib()
+    batch = args.batch
+    rng = np.random.default_rng(1234)
+    n_copies = 4                      # a bounded sample of the 64-copy step
+    Ws, Ss, Xs = [], [], []
+    for _ in range(n_copies):
+        t = rng.integers(0, 3, size=(OUT, COLS // 16, 16))
+        codes = np.array([0, 1, 3], np.uint32)[t]
+        Ws.append((codes << (2 * np.arange(16, dtype=np.uint32))).sum(-1).astype(np.uint32).ravel())
+        Ss.append(rng.uniform(0.5, 1.5, OUT).astype(np.float32))
+        Xs.append(rng.standard_normal(batch * COLS).astype(np.float32))
+
+    def step():
+        for z in range(n_copies):
+            nlo.ternary_gemv_rows(Xs[z], Ws[z], Ss[z], batch, OUT, COLS)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    per = (time.perf_counter() - t0) / args.steps
+    value = n_copies * gemv_bytes(OUT, COLS, batch) / per / 1e9
+    sample = (f"{n_copies} of the step's {COPIES} GEMVs per step (4096x4096, batch {batch}); "
+              "oracle/nl_oracle.c restatement of ternary-rows, OpenMP on all host threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "ternary GEMV y=diag(s)(W x), W 4096x4096 2-bit packed, "
+                               f"batch {batch}, {COPIES} distinct weight copies per step",
+                   "out": OUT, "cols": COLS, "batch": batch, "copies_per_step": COPIES,
+                   "parallelism": "host cores (reference arm runs on rank 0 only)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nlo.threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "note": "the reference's own path (Elisp DSL -> SPIR-V -> Vulkan) cannot run: no "
+                "Emacs, no Vulkan loader or ICD (unavailable on this box)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

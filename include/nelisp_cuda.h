@@ -1,0 +1,222 @@
+/* nelisp_cuda.h -- C ABI of libnelisp_cuda, the CUDA (sm_100a) replacement
+ * for the Vulkan compute host of zawatton/nelisp-gpu.
+ *
+ * Two layers:
+ *
+ *  1. The operator surface of the reference's persistent server
+ *     (host/vkserver.c), one entry point per opcode, so a protocol server
+ *     (nelisp-cuserver) or an FFI binding can drive the library exactly as
+ *     lisp/nelisp-gpu-server.el drives vkserver.  Buffers are raw 32-bit
+ *     words (f32 bit patterns or packed integers), kernels are addressed by
+ *     the reference's DSL names (lisp/nelisp-gpu-kernels.el), push constants
+ *     are uint32 and `groups` is the reference's 64-wide workgroup count.
+ *     Host memory belongs to the caller; device memory to the library.
+ *
+ *  2. Typed entry points on device pointers and a CUDA stream, for callers
+ *     that keep their tensors on the GPU (the decoder, the benchmarks, a
+ *     PyTorch/ctypes caller).
+ *
+ * Status codes: NL_OK (0); NL_ERROR (1) for a recoverable error -- the
+ * server's wire status 1 -- with the reason in nl_last_error(); NL_FATAL (2)
+ * for a CUDA error after which the context is unusable (the reference's
+ * VK_CHECK exit(2), host/vkserver.c:47-48).
+ *
+ * Not thread-safe: one context per process, as vkserver has one device,
+ * one queue and one fence.  The device is nl_init's argument, or
+ * NELISP_GPU_DEVICE when that is negative (host/vkserver.c:220).
+ */
+#ifndef NELISP_CUDA_H
+#define NELISP_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NL_OK 0
+#define NL_ERROR 1
+#define NL_FATAL 2
+
+/* OP_RUN buffer kinds (host/vkserver.c:16-19). */
+#define NL_RUN_IN 0        /* inline input: sent, not returned */
+#define NL_RUN_RESIDENT 1  /* resident buffer, by handle */
+#define NL_RUN_OUT 2       /* output: zeroed, returned */
+#define NL_RUN_INOUT 3     /* inline input, returned */
+
+/* OP_BATCH / OP_COMPILE slot kinds (host/vkserver.c:424-426).  The numbering
+ * and the field order differ from OP_RUN's, as in the reference. */
+#define NL_SLOT_IN 0
+#define NL_SLOT_RESIDENT 1
+#define NL_SLOT_TMP 2      /* transient: zeroed (every run, when compiled) */
+#define NL_SLOT_OUT 3      /* zeroed, returned */
+
+/* Table limits of host/vkserver.c (:71-100, :435-436). */
+#define NL_MAX_BUFS 16
+#define NL_MAX_PUSH 16
+#define NL_MAX_NAME 63
+#define NL_MAX_RESIDENT 4096
+#define NL_MAX_COMPILED 16
+#define NL_MAX_SLOTS 8192
+#define NL_MAX_DISPATCH 8192
+
+/* One OP_RUN buffer descriptor (host/vkserver.c:15). `handle` is read only
+ * for NL_RUN_RESIDENT. */
+typedef struct {
+  uint32_t size;   /* 32-bit words */
+  uint32_t kind;
+  uint32_t handle;
+} nl_run_buffer;
+
+/* One OP_BATCH / OP_COMPILE slot (host/vkserver.c:425). */
+typedef struct {
+  uint32_t kind;
+  uint32_t size;   /* 32-bit words */
+  uint32_t handle;
+} nl_slot;
+
+/* One dispatch of a batch (host/vkserver.c:428-429, :433). */
+typedef struct {
+  char name[NL_MAX_NAME + 1];
+  uint32_t nbuf;
+  uint32_t slot[NL_MAX_BUFS];
+  uint32_t npush;
+  uint32_t push[NL_MAX_PUSH];
+  uint32_t groups;
+} nl_dispatch;
+
+/* ---- context -------------------------------------------------------- */
+
+/* Create the context on DEVICE (<0: NELISP_GPU_DEVICE, else 0).  Replaces
+ * init_vulkan (host/vkserver.c:213-245).  Idempotent. */
+int nl_init(int device);
+/* Release every resident buffer, compiled batch and the device context. */
+void nl_shutdown(void);
+const char *nl_last_error(void);
+const char *nl_version(void);
+/* The CUDA device ordinal in use, or -1 before nl_init. */
+int nl_device(void);
+/* Name of the device in use (the reference logs it, host/vkserver.c:225). */
+const char *nl_device_name(void);
+
+/* The kernel registry: names the server accepts, and their arity (number of
+ * buffers and push constants in lisp/nelisp-gpu-kernels.el). */
+int nl_kernel_count(void);
+const char *nl_kernel_name(int index);
+int nl_kernel_arity(const char *name, uint32_t *nbuf, uint32_t *npush);
+
+/* ---- resident buffers ---------------------------------------------- */
+
+/* OP_UPLOAD (host/vkserver.c:336-351): copy NWORDS words to a new resident
+ * device buffer.  Handles are the first free slot of a 4096-entry table, as
+ * in the reference.  Status 1 when the table is full. */
+int nl_upload(const void *words, uint32_t nwords, uint32_t *handle);
+/* OP_UPLOAD_FILE (host/vkserver.c:371-410): read NWORDS words at byte
+ * OFFSET of PATH straight into a new resident buffer.  Status 1 (and no
+ * handle allocated) on open, seek or short-read failure. */
+int nl_upload_file(const char *path, uint64_t offset, uint32_t nwords,
+                   uint32_t *handle);
+/* OP_WRITE_RESIDENT (host/vkserver.c:356-367): overwrite in place.  Status 1
+ * for a bad handle or more words than the buffer holds. */
+int nl_write_resident(uint32_t handle, const void *words, uint32_t nwords);
+/* Read back the first NWORDS words (the reference reads through the `scale`
+ * kernel, lisp/nelisp-gpu-server.el:211-217). */
+int nl_read_resident(uint32_t handle, void *words, uint32_t nwords);
+/* OP_FREE (host/vkserver.c:412-418): an unknown handle is not an error. */
+int nl_free(uint32_t handle);
+/* Device address and size of a resident buffer. */
+int nl_resident_info(uint32_t handle, void **dev_ptr, uint32_t *nwords);
+
+/* ---- dispatch by kernel name ---------------------------------------- */
+
+/* OP_RUN (host/vkserver.c:274-334).  INLINE_WORDS holds the data of the
+ * NL_RUN_IN and NL_RUN_INOUT buffers, concatenated in binding order; OUT_WORDS
+ * receives the NL_RUN_OUT and NL_RUN_INOUT buffers, in binding order. */
+int nl_run(const char *name, uint32_t nbuf, const nl_run_buffer *bufs,
+           uint32_t npush, const uint32_t *push, uint32_t groups,
+           const void *inline_words, void *out_words);
+
+/* OP_BATCH (host/vkserver.c:437-506): the dispatches run in order on one
+ * stream (stream order is the reference's barrier between dispatches).
+ * INLINE_WORDS holds the NL_SLOT_IN slots in slot order; OUT_WORDS receives
+ * the NL_SLOT_OUT slots in slot order. */
+int nl_batch(uint32_t nslot, const nl_slot *slots, uint32_t ndisp,
+             const nl_dispatch *disps, const void *inline_words,
+             void *out_words);
+
+/* OP_COMPILE (host/vkserver.c:511-587): allocate the non-resident slots once,
+ * copy the inline inputs once and capture the dispatches -- with memset
+ * nodes zeroing the tmp and out slots -- into a CUDA graph.  Resident
+ * buffers are bound by address at compile time, as the reference binds
+ * them into its recorded command buffer.  Status 1 when all 16 entries are
+ * in use. */
+int nl_compile(uint32_t nslot, const nl_slot *slots, uint32_t ndisp,
+               const nl_dispatch *disps, const void *inline_words,
+               uint32_t *handle);
+/* OP_RUN_COMPILED (host/vkserver.c:591-604): replay the graph; OUT_WORDS
+ * receives the out slots in slot order.  Status 1 for a bad handle. */
+int nl_run_compiled(uint32_t handle, void *out_words);
+/* OP_FREE_COMPILED (host/vkserver.c:606-615). */
+int nl_free_compiled(uint32_t handle);
+/* Total words OP_RUN_COMPILED returns for HANDLE. */
+int nl_compiled_out_words(uint32_t handle, uint64_t *nwords);
+/* Replay HANDLE's graph REPS times back to back without copying outputs and
+ * report the device time per replay (CUDA events).  This is what
+ * host/vkmatmul.c times: one submit of a recorded command buffer
+ * (:163-169). */
+int nl_time_compiled(uint32_t handle, uint32_t reps, double *ms_per_rep);
+
+/* Any registry kernel on caller-owned device buffers, enqueued on STREAM
+ * (a cudaStream_t, used as given: 0 is the legacy default stream).  NWORDS gives each
+ * buffer's size for the bounds checks.  Does not synchronise. */
+int nl_dispatch_dev(const char *name, uint32_t nbuf, void *const *bufs,
+                    const uint32_t *nwords, uint32_t npush,
+                    const uint32_t *push, uint32_t groups, void *stream);
+
+/* ---- typed entry points (device pointers) --------------------------- */
+
+/* Workspace the ternary kernels need for SEQ activation rows of COLS
+ * columns: the activations re-expressed as three exact int8 limbs per value
+ * for the tensor-core path.  Pass at least this many bytes, or NULL to use
+ * the library's own workspace. */
+size_t nl_ternary_workspace_bytes(uint32_t seq, uint32_t cols);
+
+/* ternary-rows (lisp/nelisp-gpu-kernels.el:713-746) on device pointers:
+ * Y[s,o] = BIAS[o] + sum_b BETA[o*nblk+b] * sum_{i in block b} t(o,i) X[s,i]
+ * with WP holding sixteen two-bit fields per word (field i at bits 2(i%16)
+ * of word i/16; 00 -> 0, 01 -> +1, 11 -> -1, 10 -> -2). */
+int nl_ternary_rows_dev(const float *X, const uint32_t *WP, const float *BIAS,
+                        const float *BETA, float *Y, uint32_t seq,
+                        uint32_t out, uint32_t cols, uint32_t nblk,
+                        uint32_t wng, void *workspace, size_t ws_bytes,
+                        void *stream);
+
+/* The ternary GEMV with one scale per output row -- y = diag(S)(W x) + BIAS
+ * -- i.e. ternary-rows with S[o] in every 128-column block.  WP rows are
+ * cols/16 words (cols a multiple of 16).  BIAS may be NULL. */
+int nl_ternary_gemv_dev(const float *X, const uint32_t *WP, const float *S,
+                        const float *BIAS, float *Y, uint32_t seq,
+                        uint32_t out, uint32_t cols, void *workspace,
+                        size_t ws_bytes, void *stream);
+
+/* COUNT independent GEMVs of the shape above in one launch: problem z uses
+ * X + z*x_stride, WP + z*w_stride, S + z*s_stride and writes Y + z*y_stride
+ * (strides in elements).  The workspace must hold COUNT times
+ * nl_ternary_workspace_bytes(seq, cols). */
+int nl_ternary_gemv_batched_dev(uint32_t count, const float *X,
+                                uint64_t x_stride, const uint32_t *WP,
+                                uint64_t w_stride, const float *S,
+                                uint64_t s_stride, float *Y,
+                                uint64_t y_stride, uint32_t seq, uint32_t out,
+                                uint32_t cols, void *workspace,
+                                size_t ws_bytes, void *stream);
+
+/* Launch counter: how many kernels this library has enqueued since the
+ * context was created (each graph replay counts the kernels it holds). */
+uint64_t nl_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NELISP_CUDA_H */

@@ -1,0 +1,115 @@
+// nl_internal.h -- shared declarations of libnelisp_cuda's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "nelisp_cuda.h"
+
+namespace nl {
+
+// Arguments of one dispatch of a registry kernel: the reference's binding
+// list (buffers in binding order, sizes in 32-bit words), its push constants
+// and its workgroup count, plus the stream and the scratch memory the
+// launcher may use.
+struct OpArgs {
+  void *buf[NL_MAX_BUFS];
+  uint32_t words[NL_MAX_BUFS];
+  uint32_t nbuf;
+  uint32_t push[NL_MAX_PUSH];
+  uint32_t npush;
+  uint32_t groups;
+  cudaStream_t stream;
+  void *scratch;
+  size_t scratch_bytes;
+};
+
+// A registry entry.  `check` validates buffer sizes against the extents the
+// push constants imply and returns NULL or a message; `scratch` reports the
+// scratch bytes `launch` needs; `launch` enqueues the kernels (no host
+// synchronisation, no allocation: it must be safe inside stream capture).
+struct OpSpec {
+  const char *name;
+  uint32_t nbuf;
+  uint32_t npush;
+  const char *(*check)(const OpArgs &);
+  size_t (*scratch)(const OpArgs &);
+  cudaError_t (*launch)(const OpArgs &);
+};
+
+// Registry (nl_registry.cu).
+const OpSpec *find_op(const char *name);
+int op_count();
+const OpSpec *op_at(int index);
+
+// Per-family tables, defined next to their kernels.
+extern const OpSpec kTernaryOps[];
+extern const int kTernaryOpsCount;
+extern const OpSpec kInt8Ops[];
+extern const int kInt8OpsCount;
+extern const OpSpec kDenseOps[];
+extern const int kDenseOpsCount;
+extern const OpSpec kRowOps[];
+extern const int kRowOpsCount;
+extern const OpSpec kAttnOps[];
+extern const int kAttnOpsCount;
+
+// Error reporting (nl_runtime.cu).
+int set_error(int code, const char *fmt, ...);
+int cuda_status(cudaError_t e, const char *what);
+
+// Launch accounting: every kernel the library enqueues is counted.
+void count_launches(uint64_t n);
+
+// Bounds-check helper for `check` functions: buffer B must hold at least
+// NEED words.  Returns NULL when it does.
+const char *need_words(const OpArgs &a, uint32_t b, uint64_t need,
+                       const char *what);
+// Formats a message into a per-thread buffer.
+const char *fmt_msg(const char *fmt, ...);
+
+// The number of reference invocations a dispatch of GROUPS workgroups of
+// LOCAL invocations covers; kernels leave outputs of invocations at or past
+// this index untouched, emulating a short grid.
+static inline uint64_t invocations(uint32_t groups, uint32_t local) {
+  return (uint64_t)groups * local;
+}
+
+// Ternary GEMV entry used by the typed API and the registry.
+cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
+                                uint64_t x_stride, const uint32_t *WP,
+                                uint64_t w_stride, const float *SCALE,
+                                uint64_t s_stride, const float *BIAS,
+                                float *Y, uint64_t y_stride, uint32_t seq,
+                                uint32_t out, uint32_t cols, uint32_t nblk,
+                                uint32_t wng, bool per_block, uint64_t limit,
+                                void *ws, size_t ws_bytes,
+                                cudaStream_t stream);
+size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols);
+bool ternary_fast_shape(uint32_t cols, uint32_t nblk, uint32_t wng,
+                        bool per_block);
+
+// Library workspace for typed calls that pass no workspace (nl_runtime.cu).
+void *library_workspace(size_t bytes, cudaStream_t stream);
+
+static inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+static inline uint64_t ceil_div64(uint64_t a, uint64_t b) {
+  return (a + b - 1) / b;
+}
+static inline bool aligned16(const void *p) {
+  return ((uintptr_t)p & 15u) == 0;
+}
+
+// Grid-size helper: at most `cap` blocks of `threads` covering `n` items.
+static inline unsigned grid_for(uint64_t n, unsigned threads,
+                                unsigned cap = 148u * 32u) {
+  uint64_t g = ceil_div64(n, threads);
+  if (g == 0) g = 1;
+  if (g > cap) g = cap;
+  return (unsigned)g;
+}
+
+}  // namespace nl
+
+#define NL_LAUNCH_CHECK() cudaPeekAtLastError()

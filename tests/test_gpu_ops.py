@@ -1,0 +1,303 @@
+"""Every registry kernel on the GPU against the oracle, through the C ABI
+(nl_run / nl_batch), including the reference test generators, odd sizes,
+short grids and the error statuses.
+
+Bars (BASELINE): bit-exact for the int8 quantizer and integer accumulation;
+tk-err <= 1e-5 for f32 GEMV-like sums; 1e-4 for matmul, softmax and
+attention; elementwise ops within a few f32 ulps of the oracle's libm.
+"""
+import numpy as np
+import pytest
+
+import oracle as nlo
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def host():
+    from nelisp_cuda.host import Host
+    return Host()
+
+
+def g64(n):
+    return (n + 63) // 64
+
+
+# ---- f32 matmul family -----------------------------------------------------------
+
+@pytest.mark.parametrize("mkn", [(256, 256, 256), (128, 128, 128), (20, 24, 12), (1, 300, 7),
+                                 (1024, 64, 512)])
+def test_matmul_random(host, mkn):
+    M, K, N = mkn
+    rng = np.random.default_rng(M + K + N)
+    A = rng.uniform(-1, 1, M * K).astype(np.float32)
+    B = rng.uniform(-1, 1, K * N).astype(np.float32)
+    want = nlo.matmul(A, B, M, K, N)
+    for name, groups in [("matmul", g64(M * N)),
+                         ("matmul-tiled", ((M + 15) // 16) * ((N + 15) // 16))]:
+        C = host.run2(name, [("in", A), ("in", B), ("out", M * N)], [M, K, N], groups)[0]
+        assert nlo.tk_err(C, want) < 1e-4, name
+
+
+def test_matmul_vkmatmul_exact(host):
+    M = K = N = 256
+    A = (np.arange(M * K) % 4).astype(np.float32)
+    B = (np.arange(K * N) % 3).astype(np.float32)
+    for name, groups in [("matmul", g64(M * N)), ("matmul-tiled", 256),
+                         ("matmul-reg", g64((M // 4) * (N // 4)))]:
+        C = host.run2(name, [("in", A), ("in", B), ("out", M * N)], [M, K, N], groups)[0]
+        for r in range(0, M, M // 7):
+            for c in range(0, N, N // 7):
+                assert C[r * N + c] == nlo.matmul_sample_ref(r, c, K, N), (name, r, c)
+
+
+def test_verify_el_matmul_family(host, verify_fixture):
+    d = verify_fixture
+    C = host.run2("matmul", [("in", d["matmul_A"]), ("in", d["matmul_B"]), ("out", 32 * 16)],
+                  [32, 24, 16], g64(32 * 16))[0]
+    assert np.max(np.abs(C - d["matmul_C"])) < 1e-3
+    C = host.run2("matmul-tiled", [("in", d["tiled_A"]), ("in", d["tiled_B"]), ("out", 240)],
+                  [20, 24, 12], 2)[0]
+    assert np.max(np.abs(C - d["tiled_C"])) < 1e-3
+    C = host.run2("matmul-reg", [("in", d["tiled_A"]), ("in", d["tiled_B"]), ("out", 240)],
+                  [20, 24, 12], g64(5 * 3))[0]
+    assert np.max(np.abs(C - d["tiled_C"])) < 1e-3
+    C = host.run2("linear", [("in", d["linear_X"]), ("in", d["linear_W"]), ("in", d["linear_B"]),
+                             ("out", 20 * 16)], [20, 12, 16], g64(320))[0]
+    assert np.max(np.abs(C - d["linear_C"])) < 1e-3
+    C = host.run2("scale", [("in", d["scale_A"]), ("in", d["scale_k"]), ("out", 50)], [50], 1)[0]
+    assert np.max(np.abs(C - d["scale_C"])) < 1e-5
+
+
+def test_matmul_reg_rejects_unaligned(host):
+    from nelisp_cuda import NlError
+    with pytest.raises(NlError) as e:
+        host.run2("matmul-reg", [("in", np.zeros(18)), ("in", np.zeros(18)), ("out", 9)],
+                  [3, 6, 3], 1)
+    assert e.value.code == 1
+
+
+def test_matmul_tiled_short_grid(host):
+    M = K = N = 32
+    rng = np.random.default_rng(1)
+    A, B = rng.standard_normal(M * K).astype(np.float32), rng.standard_normal(K * N).astype(np.float32)
+    C = host.run2("matmul-tiled", [("in", A), ("in", B), ("out", M * N)], [M, K, N], 1)[0]
+    want = nlo.matmul(A, B, M, K, N).reshape(M, N)
+    C = C.reshape(M, N)
+    assert nlo.tk_err(C[:16, :16], want[:16, :16]) < 1e-4
+    assert not C[16:].any() and not C[:, 16:].any()
+
+
+# ---- softmax, silu-mul, elementwise, rmsnorm ---------------------------------------
+
+@pytest.mark.parametrize("mn", [(24, 40), (64, 4096), (3, 10000), (5, 1)])
+def test_softmax(host, mn):
+    M, N = mn
+    rng = np.random.default_rng(N)
+    A = (2.0 * rng.standard_normal(M * N)).astype(np.float32)
+    C = host.run2("softmax", [("in", A), ("out", M * N)], [M, N], g64(M))[0]
+    assert nlo.tk_err(C, nlo.softmax(A, M, N)) < 1e-4
+
+
+def test_softmax_vksoftmax_generator(host, verify_fixture):
+    C = host.run2("softmax", [("in", verify_fixture["softmax_A"]), ("out", 960)], [24, 40], 1)[0]
+    assert np.max(np.abs(C - verify_fixture["softmax_C"])) < 1e-4
+    M, N = 64, 256
+    i = np.arange(M * N)
+    A = (i % 7).astype(np.float32) * np.float32(0.3)
+    C = host.run2("softmax", [("in", A), ("out", M * N)], [M, N], 1)[0]
+    assert np.max(np.abs(C - nlo.softmax_ref_f64((i % 7) * 0.3, M, N))) <= 1e-3
+
+
+@pytest.mark.parametrize("name", ["silu-mul", "add2", "vadd", "mul"])
+def test_elementwise(host, name):
+    rng = np.random.default_rng(len(name))
+    for n in [1, 7, 4096, 16 * 11008 + 3]:
+        A = rng.standard_normal(n).astype(np.float32)
+        B = rng.standard_normal(n).astype(np.float32)
+        C = host.run2(name, [("in", A), ("in", B), ("out", n)], [n], g64(n))[0]
+        if name == "silu-mul":
+            want = nlo.silu_mul(A, B, n)
+            assert np.max(np.abs(C - want) / (np.abs(want) + 1e-30)) < 4e-6
+        elif name == "mul":
+            assert np.array_equal(C.astype(np.float32), A * B)
+        else:
+            assert np.array_equal(C.astype(np.float32), nlo.add2(A, B, n))
+
+
+def test_rmsnorm(host):
+    rng = np.random.default_rng(2)
+    M, N = 8, 2560
+    X = rng.standard_normal(M * N).astype(np.float32)
+    G = rng.uniform(0.5, 1.5, N).astype(np.float32)
+    S = host.run2("rmsnorm-istd", [("in", X), ("out", M)], [M, N], 1)[0]
+    assert nlo.tk_err(S, nlo.rmsnorm_istd(X, M, N)) < 1e-6
+    C = host.run2("rmsnorm-fwd", [("in", X), ("in", S), ("in", G), ("out", M * N)], [M, N],
+                  g64(M * N))[0]
+    assert np.array_equal(C.astype(np.float32), nlo.rmsnorm_fwd(X, S, G, M, N))
+
+
+def test_embed_gather(host):
+    rng = np.random.default_rng(4)
+    V, dim, seq = 300, 64, 9
+    WTE = rng.standard_normal(V * dim).astype(np.float32)
+    TOK = rng.integers(0, V, seq).astype(np.float32)
+    C = host.run2("embed-gather", [("in", TOK), ("in", WTE), ("out", seq * dim)], [seq, dim],
+                  g64(seq * dim))[0]
+    assert np.array_equal(C.astype(np.float32), nlo.embed_gather(TOK, WTE, seq, dim))
+
+
+# ---- rope, cache, attention -----------------------------------------------------------
+
+def test_rope_half(host):
+    rng = np.random.default_rng(6)
+    seq, nh, hd = 7, 4, 128
+    X = rng.standard_normal(seq * nh * hd).astype(np.float32)
+    rb = int(np.float32(10000.0).view(np.uint32))
+    for sg in (1.0, -1.0):
+        sgb = int(np.float32(sg).view(np.uint32))
+        Y = host.run2("rope-half", [("in", X), ("out", X.size)], [seq, nh, hd, rb, sgb],
+                      g64(seq * nh * hd // 2))[0]
+        assert np.max(np.abs(Y - nlo.rope_half(X, seq, nh, hd, rb, sgb))) < 2e-5
+
+
+def test_decode_rope_b_and_cache_append_b(host):
+    rng = np.random.default_rng(8)
+    B, heads, hd, maxseq, pos = 3, 4, 16, 10, 6
+    cols, half = heads * hd, hd // 2
+    X = rng.standard_normal(B * cols).astype(np.float32)
+    th = np.arange(maxseq)[:, None] / (10000.0 ** (2 * np.arange(half) / hd))[None]
+    CO, SI = np.cos(th).astype(np.float32).ravel(), np.sin(th).astype(np.float32).ravel()
+    C = host.run2("decode-rope-b", [("in", X), ("in", CO), ("in", SI), ("in", [1.0]),
+                                    ("in", [float(pos)]), ("out", B * cols)],
+                  [B, cols, heads], g64(B * heads * half))[0]
+    want = nlo.decode_rope_b(X, CO, SI, [1.0], [float(pos)], B, cols, heads)
+    assert np.array_equal(C.astype(np.float32), want)
+    kvdim = cols
+    cache = rng.standard_normal(B * maxseq * kvdim).astype(np.float32)
+    got = host.run2("cache-append-b", [("in", X), ("in", [float(pos)]), ("inout", cache)],
+                    [B, kvdim, maxseq], g64(B * kvdim))[0]
+    assert np.array_equal(got.astype(np.float32),
+                          nlo.cache_append_b(X, [float(pos)], cache, B, kvdim, maxseq))
+
+
+@pytest.mark.parametrize("B,heads,kvheads,hd,maxseq,pos", [
+    (8, 32, 32, 128, 512, 511),    # the benchmark's shape, shorter context
+    (2, 8, 2, 128, 300, 200),      # GQA group 4
+    (1, 20, 20, 128, 96, 0),       # one key
+    (3, 6, 3, 64, 70, 69),
+    (2, 4, 2, 16, 33, 20),         # head size the split kernel does not cover
+])
+def test_decode_attn_b(host, B, heads, kvheads, hd, maxseq, pos):
+    rng = np.random.default_rng(B * 100 + hd + pos)
+    dim, kvdim = heads * hd, kvheads * hd
+    Q = rng.standard_normal(B * dim).astype(np.float32)
+    CK = rng.standard_normal(B * maxseq * kvdim).astype(np.float32)
+    CV = rng.standard_normal(B * maxseq * kvdim).astype(np.float32)
+    C = host.run2("decode-attn-b", [("in", Q), ("in", CK), ("in", CV), ("in", [float(pos)]),
+                                    ("out", B * dim)], [B, dim, heads, kvheads, maxseq],
+                  g64(B * dim))[0]
+    want = nlo.decode_attn_b(Q, CK, CV, [float(pos)], B, dim, heads, kvheads, maxseq)
+    assert nlo.tk_err(C, want) < 1e-4
+
+
+def test_decode_attn_single(host):
+    rng = np.random.default_rng(12)
+    heads, kvheads, hd, rows, pos = 8, 8, 128, 64, 40
+    dim, kvdim = heads * hd, kvheads * hd
+    Q = rng.standard_normal(dim).astype(np.float32)
+    CK = rng.standard_normal(rows * kvdim).astype(np.float32)
+    CV = rng.standard_normal(rows * kvdim).astype(np.float32)
+    C = host.run2("decode-attn", [("in", Q), ("in", CK), ("in", CV), ("in", [float(pos)]),
+                                  ("out", dim)], [dim, heads, kvheads], g64(dim))[0]
+    want = nlo.decode_attn_b(Q, CK, CV, [float(pos)], 1, dim, heads, kvheads, rows)
+    assert nlo.tk_err(C, want) < 1e-4
+
+
+# ---- int8 path: bit-exact --------------------------------------------------------------
+
+def test_pack_act_rows_bit_exact(host):
+    rng = np.random.default_rng(14)
+    seq, cols = 5, 2561
+    ng = (cols + 3) // 4
+    X = (rng.standard_normal(seq * cols) * 3).astype(np.float32)
+    X[:7] = [0.0, -0.0, 126.999, -127.5, 1e-30, -1e-30, 0.5]
+    X[cols:2 * cols] = 0.0                                  # gamma 0 row
+    X[3 * cols + 11] = np.nan                               # NaN never wins the max
+    XQ, G = host.run2("pack-act-rows", [("in", X), ("out", seq * ng), ("out", seq)],
+                      [seq, cols, ng], 1, words=True)
+    wq, wg = nlo.pack_act_rows(X, seq, cols, ng)
+    assert np.array_equal(XQ, wq) and np.array_equal(G, wg.view(np.uint32))
+
+
+@pytest.mark.parametrize("per_row", [0, 1])
+def test_dp4a_bit_exact(host, per_row):
+    rng = np.random.default_rng(15 + per_row)
+    seq, out, ng = 6, 77, 640
+    AP = rng.integers(0, 2 ** 32, seq * ng, dtype=np.uint64).astype(np.uint32)
+    WP = rng.integers(0, 2 ** 32, out * ng, dtype=np.uint64).astype(np.uint32)
+    BIAS = rng.standard_normal(out).astype(np.float32)
+    BETA = rng.uniform(0.1, 2, out if per_row else 1).astype(np.float32)
+    GAM = rng.uniform(0.01, 1, seq).astype(np.float32)
+    name = "bitlinear-dp4a-rows" if per_row else "bitlinear-dp4a-1f"
+    Y = host.run2(name, [("in", AP), ("in", WP), ("in", BIAS), ("in", BETA), ("in", GAM),
+                         ("out", seq * out)], [seq, out, ng], g64(seq * out), words=True)[0]
+    want = nlo.dp4a_rows(AP, WP, BIAS, BETA, GAM, seq, out, ng, per_row)
+    assert np.array_equal(Y, want.view(np.uint32))
+
+
+# ---- executor: batch, compile, errors ---------------------------------------------------
+
+def test_batch_chain_and_tmp_slots(host):
+    rng = np.random.default_rng(16)
+    n = 1000
+    A, B = rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32)
+    out = host.batch([("in", A), ("in", B), ("tmp", n), ("out", n)],
+                     [("add2", [0, 1, 2], [n], g64(n)), ("silu-mul", [2, 1, 3], [n], g64(n))])[0]
+    want = nlo.silu_mul(nlo.add2(A, B, n), B, n)
+    assert np.max(np.abs(out - want) / (np.abs(want) + 1e-30)) < 4e-6
+
+
+def test_compile_replays_and_zeroes_tmp(host):
+    rng = np.random.default_rng(17)
+    n = 513
+    A = rng.standard_normal(n).astype(np.float32)
+    h = host.upload(A)
+    # out = tmp + A, where tmp starts at zero on every run (vkserver.c:554-556)
+    hc, outs = host.compile([("res", h, n), ("tmp", n), ("out", n)],
+                            [("add2", [1, 0, 1], [n], g64(n)), ("add2", [1, 1, 2], [n], g64(n))])
+    for k in range(3):
+        r = host.run_compiled(hc, outs)[0]
+        assert np.array_equal(r.astype(np.float32), 2 * A)
+    host.write_resident(h, 3 * A)
+    r = host.run_compiled(hc, outs)[0]
+    assert np.array_equal(r.astype(np.float32), 6 * A)
+    host.free_compiled(hc)
+    host.free(h)
+
+
+def test_error_statuses(host):
+    from nelisp_cuda import NlError
+    with pytest.raises(NlError) as e:
+        host.run2("no-such-kernel", [("out", 4)], [4], 1)
+    assert e.value.code == 1
+    with pytest.raises(NlError) as e:
+        host.run2("add2", [("res", 4000, 4), ("in", np.zeros(4)), ("out", 4)], [4], 1)
+    assert e.value.code == 1
+    with pytest.raises(NlError) as e:                 # buffers too small for the push constants
+        host.run2("add2", [("in", np.zeros(4)), ("in", np.zeros(4)), ("out", 4)], [8], 1)
+    assert e.value.code == 1
+    with pytest.raises(NlError):
+        host.run_compiled(15, [1])
+    host.free(4000)                                    # unknown handle: not an error
+
+
+def test_resident_table_order_and_readback(host):
+    hs = [host.upload(np.full(8, i, np.float32)) for i in range(3)]
+    host.free(hs[1])
+    h = host.upload(np.arange(8, dtype=np.float32))
+    assert h == hs[1]                                  # first free slot, as vkserver
+    assert np.array_equal(host.read_resident(h, 8), np.arange(8))
+    for x in (hs[0], h, hs[2]):
+        host.free(x)

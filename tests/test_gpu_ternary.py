@@ -1,0 +1,253 @@
+"""Ternary linear kernels on the GPU against the oracle and the reference's
+own ternary test (test/ternary-kernel-test.el).
+
+Bars: unpacking is bit-exact (one-hot activations return the weight times
+its scale exactly); f32 outputs are within tk-err 1e-5 of the oracle, the
+reference's own metric and threshold (ternary-kernel-test.el:23-34, :104).
+"""
+import numpy as np
+import pytest
+
+import oracle as nlo
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def host():
+    from nelisp_cuda.host import Host
+    return Host()
+
+
+@pytest.fixture(scope="module")
+def server():
+    from nelisp_cuda.server import Server
+    s = Server()
+    yield s
+    s.stop()
+
+
+def pack_trits(t):
+    """tk-pack for an (out, cols) trit matrix, codes 00/01/11 (and 10 for -2)."""
+    out, cols = t.shape
+    wng = (cols + 15) // 16
+    codes = np.where(t == 1, 1, np.where(t == -1, 3, np.where(t == -2, 2, 0))).astype(np.uint32)
+    pad = np.zeros((out, wng * 16), np.uint32)
+    pad[:, :cols] = codes
+    w = np.zeros((out, wng), np.uint32)
+    for f in range(16):
+        w |= pad[:, f::16] << np.uint32(2 * f)
+    return w.ravel()
+
+
+def rand_problem(rng, seq, out, cols, nblk=None, wng=None, p10=0.0):
+    nblk = (cols + 127) // 128 if nblk is None else nblk
+    t = rng.integers(-1, 2, size=(out, cols)).astype(np.int64)
+    if p10:
+        t[rng.random((out, cols)) < p10] = -2
+    WP = pack_trits(t)
+    real_wng = (cols + 15) // 16
+    if wng is not None and wng != real_wng:
+        W2 = np.zeros((out, wng), np.uint32)
+        k = min(wng, real_wng)
+        W2[:, :k] = WP.reshape(out, real_wng)[:, :k]
+        WP = W2.ravel()
+    else:
+        wng = real_wng
+    X = rng.standard_normal(seq * cols).astype(np.float32)
+    BETA = rng.uniform(0.5, 1.5, size=out * nblk).astype(np.float32)
+    BIAS = rng.uniform(-0.2, 0.2, size=out).astype(np.float32)
+    return X, WP, BIAS, BETA, nblk, wng
+
+
+def run_rows(host, X, WP, BIAS, BETA, seq, out, cols, nblk, wng, groups=None):
+    g = (seq * out + 63) // 64 if groups is None else groups
+    return host.run2("ternary-rows", [("in", X), ("in", WP), ("in", BIAS), ("in", BETA),
+                                      ("out", seq * out)], [seq, out, cols, nblk, wng], g)[0]
+
+
+# ---- the reference's own test, through the protocol server -------------------
+
+def _tk_batch(server, h, d, x, bias, beta):
+    seq, out, cols, nblk, wng = (int(d[k]) for k in ("seq", "out", "cols", "nblk", "wng"))
+    return server.batch([("in", x), ("res", h, out * wng), ("in", bias), ("in", beta),
+                         ("out", seq * out)],
+                        [("ternary-rows", [0, 1, 2, 3, 4], [seq, out, cols, nblk, wng],
+                          (seq * out + 63) // 64)])[0]
+
+
+def test_tk_forward_transpose_controls_via_server(server, tk_fixture):
+    d = tk_fixture
+    seq, out, cols, nblk, wng = (int(d[k]) for k in ("seq", "out", "cols", "nblk", "wng"))
+    h = server.upload_bytes(d["wp"].astype("<u4").tobytes())
+    y = _tk_batch(server, h, d, d["x"], d["bias"], d["beta"])
+    assert nlo.tk_err(y, d["y_want"]) < TOL
+    assert np.any(y != 0.0)
+    xt = server.batch([("res", h, out * wng), ("in", d["beta"]), ("in", d["g"]),
+                       ("out", seq * cols)],
+                      [("ternary-rows-t", [0, 1, 2, 3], [out, cols, nblk, wng, seq],
+                        (seq * cols + 63) // 64)])[0]
+    assert nlo.tk_err(xt, d["xt_want"]) < TOL
+    y0 = _tk_batch(server, h, d, d["x"], np.zeros(out), d["beta"])
+    l, r = float(np.dot(y0, d["g"])), float(np.dot(d["x"], xt))
+    assert abs(l - r) / max(1e-6, abs(l)) < TOL
+    b2 = d["beta"].copy()
+    b2[1] *= 3.0
+    ya, yb = _tk_batch(server, h, d, d["x"], d["bias"], d["beta"]), _tk_batch(server, h, d, d["x"], d["bias"], b2)
+    moved = sum(ya[s * out] != yb[s * out] for s in range(seq))
+    spilled = sum(ya[s * out + o] != yb[s * out + o] for s in range(seq) for o in range(1, out))
+    assert moved == seq and spilled == 0
+    server.free(h)
+
+
+# ---- shapes, paths and edge cases through the C ABI ---------------------------
+
+@pytest.mark.parametrize("seq,out,cols", [(1, 64, 128), (3, 70, 256), (4, 256, 1024),
+                                          (8, 40, 384), (13, 33, 512), (16, 96, 2560),
+                                          (17, 48, 256), (40, 16, 128)])
+def test_fast_path_matches_oracle(host, seq, out, cols):
+    rng = np.random.default_rng(seq * 1000 + cols)
+    X, WP, BIAS, BETA, nblk, wng = rand_problem(rng, seq, out, cols)
+    y = run_rows(host, X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    want = nlo.ternary_rows(X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    assert nlo.tk_err(y, want) < TOL
+
+
+@pytest.mark.parametrize("seq,out,cols,nblk,wng", [
+    (2, 10, 200, 2, 13),      # cols not a multiple of 16 or 128
+    (3, 9, 256, 1, 16),       # nblk below the row: trailing words ignored
+    (1, 5, 256, 3, 16),       # nblk past the row: an empty block
+    (2, 7, 100, 1, 9),        # wng past the row
+    (1, 1, 16, 1, 1),
+])
+def test_generic_path_edge_shapes(host, seq, out, cols, nblk, wng):
+    rng = np.random.default_rng(7 + cols)
+    X, WP, BIAS, BETA, _, wng = rand_problem(rng, seq, out, cols, nblk=nblk, wng=wng)
+    y = run_rows(host, X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    want = nlo.ternary_rows(X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    assert nlo.tk_err(y, want) < TOL
+
+
+def test_code_10_decodes_to_minus_two(host):
+    rng = np.random.default_rng(11)
+    seq, out, cols = 2, 32, 256
+    X, WP, BIAS, BETA, nblk, wng = rand_problem(rng, seq, out, cols, p10=0.2)
+    y = run_rows(host, X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    want = nlo.ternary_rows(X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    assert nlo.tk_err(y, want) < TOL
+
+
+def test_unpack_is_bit_exact(host):
+    rng = np.random.default_rng(3)
+    out, cols = 48, 512
+    t = rng.integers(-2, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, size=out).astype(np.float32)
+    nblk, wng = cols // 128, cols // 16
+    BETA = np.repeat(S, nblk)
+    for i in [0, 1, 15, 16, 127, 128, 300, 511]:
+        X = np.zeros(cols, np.float32)
+        X[i] = 1.0
+        y = run_rows(host, X, WP, np.zeros(out, np.float32), BETA, 1, out, cols, nblk, wng)
+        assert np.array_equal(y, (t[:, i] * S.astype(np.float64)).astype(np.float32))
+
+
+def test_nonfinite_and_tiny_rows_take_the_exact_path(host):
+    rng = np.random.default_rng(5)
+    seq, out, cols = 4, 40, 256
+    X, WP, BIAS, BETA, nblk, wng = rand_problem(rng, seq, out, cols)
+    X = X.reshape(seq, cols)
+    X[1, 17] = np.inf          # row 1: non-finite
+    X[2] *= 1e-35              # row 2: below the limb range
+    X[3] = 0.0                 # row 3: zero
+    X = X.ravel()
+    y = run_rows(host, X, WP, BIAS, BETA, seq, out, cols, nblk, wng).reshape(seq, out)
+    want = nlo.ternary_rows(X, WP, BIAS, BETA, seq, out, cols, nblk, wng).reshape(seq, out)
+    for s in (0, 2, 3):
+        assert nlo.tk_err(y[s], want[s]) < TOL
+    fin = np.isfinite(want[1])
+    assert np.array_equal(np.isnan(y[1]), np.isnan(want[1]))
+    assert np.array_equal(y[1][~fin & ~np.isnan(want[1])], want[1][~fin & ~np.isnan(want[1])])
+
+
+def test_short_grid_leaves_tail_zero(host):
+    rng = np.random.default_rng(9)
+    seq, out, cols = 2, 100, 256
+    X, WP, BIAS, BETA, nblk, wng = rand_problem(rng, seq, out, cols)
+    y = run_rows(host, X, WP, BIAS, BETA, seq, out, cols, nblk, wng, groups=2)
+    want = nlo.ternary_rows(X, WP, BIAS, BETA, seq, out, cols, nblk, wng)
+    assert nlo.tk_err(y[:128], want[:128]) < TOL and not y[128:].any()
+
+
+def test_transpose_matches_oracle(host):
+    rng = np.random.default_rng(13)
+    out, cols, seq = 50, 384, 3
+    X, WP, BIAS, BETA, nblk, wng = rand_problem(rng, 1, out, cols)
+    G = rng.standard_normal(seq * out).astype(np.float32)
+    xt = host.run2("ternary-rows-t", [("in", WP), ("in", BETA), ("in", G), ("out", seq * cols)],
+                   [out, cols, nblk, wng, seq], (seq * cols + 63) // 64)[0]
+    want = nlo.ternary_rows_t(WP, BETA, G, out, cols, nblk, wng, seq)
+    assert np.array_equal(xt.astype(np.float32), want)     # same order: bit-exact
+
+
+@pytest.mark.parametrize("per_row", [0, 1])
+def test_bitlinear_packed(host, per_row):
+    rng = np.random.default_rng(21 + per_row)
+    seq, inn, out, pk = 3, 100, 17, 12
+    fcount = (inn + pk - 1) // pk
+    codes = rng.integers(0, 3, size=(out, fcount, pk))
+    WPK = (codes * (4 ** np.arange(pk))).sum(-1).astype(np.float32).ravel()
+    X = rng.standard_normal(seq * inn).astype(np.float32)
+    BIAS = rng.uniform(-1, 1, out).astype(np.float32)
+    BETA = rng.uniform(0.1, 1, out if per_row else 1).astype(np.float32)
+    name = "bitlinear-packed-v" if per_row else "bitlinear-packed"
+    y = host.run2(name, [("in", X), ("in", WPK), ("in", BIAS), ("in", BETA), ("out", seq * out)],
+                  [seq, inn, out, pk, fcount], 1)[0]
+    want = nlo.bitlinear_packed(X, WPK, BIAS, BETA, seq, inn, out, pk, fcount, per_row)
+    assert nlo.tk_err(y, want) < TOL
+
+
+# ---- the per-row-scale GEMV of the benchmark config, on device tensors ---------
+
+@pytest.mark.parametrize("batch", [1, 4, 16])
+def test_gemv_4096_per_row_scale(batch):
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(100 + batch)
+    out = cols = 4096
+    t = rng.integers(-1, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, out).astype(np.float32)
+    X = rng.standard_normal(batch * cols).astype(np.float32)
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X, WP.view(np.int32), S))
+    tY = torch.empty(batch * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, batch, out, cols)
+    torch.cuda.synchronize()
+    want = nlo.ternary_gemv_rows(X, WP, S, batch, out, cols)
+    assert nlo.tk_err(tY.cpu().numpy(), want) < TOL
+
+
+def test_gemv_batched_matches_single():
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(77)
+    count, batch, out, cols = 3, 2, 256, 1024
+    d = torch.device("cuda")
+    Ws, Ss, Xs, want = [], [], [], []
+    for z in range(count):
+        t = rng.integers(-1, 2, size=(out, cols))
+        Ws.append(pack_trits(t)); Ss.append(rng.uniform(0.5, 1.5, out).astype(np.float32))
+        Xs.append(rng.standard_normal(batch * cols).astype(np.float32))
+        want.append(nlo.ternary_gemv_rows(Xs[z], Ws[z], Ss[z], batch, out, cols))
+    tW = torch.from_numpy(np.concatenate(Ws).view(np.int32)).to(d)
+    tS = torch.from_numpy(np.concatenate(Ss)).to(d)
+    tX = torch.from_numpy(np.concatenate(Xs)).to(d)
+    tY = torch.zeros(count * batch * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv_batched(count, tX, batch * cols, tW, out * cols // 16, tS, out, tY,
+                             batch * out, batch, out, cols)
+    torch.cuda.synchronize()
+    y = tY.cpu().numpy().reshape(count, -1)
+    for z in range(count):
+        assert nlo.tk_err(y[z], want[z]) < TOL

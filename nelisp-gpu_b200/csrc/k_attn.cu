@@ -99,12 +99,7 @@ __global__ void cache_append_b_kernel(const float *__restrict__ SRC,
 // ---- split-K decode attention -------------------------------------------------
 // Partials per (b, query head h, split): m (running max of the scaled
 // scores), l (sum of exp(score - m)) and o[hd] (sum of exp(score - m) v).
-struct AttnGeom {
-  uint32_t B, heads, kvheads, hd, grp, kvdim, maxseq;  // maxseq: rows per sequence
-  uint32_t nsplit, chunk;                                // key range per split
-  uint64_t cache_words;                                  // CK/CV capacity
-  float coef;                                            // 1/sqrt(hd)
-};
+// The geometry (AttnGeom) is declared in nl_internal.h.
 
 constexpr int kAttnWarps = 4;
 constexpr int kMaxGrp = 8;
@@ -454,6 +449,17 @@ cudaError_t run_attn(const OpArgs &a) {
 }
 
 }  // namespace
+
+AttnGeom attn_geom(uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads,
+                   uint32_t maxseq, uint64_t cache_words) {
+  return make_geom(B, dim, heads, kvheads, maxseq, cache_words);
+}
+size_t attn_scratch_bytes(const AttnGeom &g) { return attn_scratch(g); }
+cudaError_t attn_decode_launch(const float *Q, const float *CK, const float *CV,
+                               const float *POS, float *C, const AttnGeom &g, void *scratch,
+                               cudaStream_t st) {
+  return attn_launch(Q, CK, CV, POS, C, g, UINT64_MAX, scratch, st);
+}
 
 const OpSpec kAttnOps[] = {
     {"rope-half", 2, 5, chk_rope_half, no_scratch, run_rope_half},

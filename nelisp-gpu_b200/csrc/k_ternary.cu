@@ -18,9 +18,10 @@
 //    f32's own accumulation error over a row).  Limbs are written straight
 //    into mma B-fragment order, so the main loop loads one uint2 per MMA.
 //  * main: each warp owns 16 weight rows.  Lanes load the packed words
-//    (8 bytes per row per 128-column block, 4 lanes per row), expand the
-//    two-bit codes to int8 with three-instruction PRMT lookups
-//    (00->0, 01->+1, 10->-2, 11->-1: the reference's sign-extending decode)
+//    (8 bytes per row per 128-column block, 4 lanes per row), turn the
+//    two-bit codes into int8 operands with a shift and a mask per four codes
+//    (a code in the top two bits of a byte is 64 times its trit:
+//    00->0, 01->+1, 10->-2, 11->-1, the reference's sign-extending decode)
 //    and issue mma.m16n8k32.s8 with int32 accumulation: the dot products are
 //    exact.  N carries (sequence, limb) pairs: n = 3s + l.
 //  * epilogue: the three limb sums of (row, s) are combined in int64,
@@ -33,17 +34,19 @@
 // int8 limbs; prep flags them and the epilogue recomputes those outputs on
 // the CUDA cores with the generic kernel's arithmetic.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "nl_internal.h"
+#include "ternary_prep.cuh"
 
 namespace nl {
 namespace {
 
-constexpr int kMaxFastSeq = 16;  // 48 (s, limb) columns = 6 n-tiles of 8
-constexpr int kWarps = 4;        // warps per CTA in the MMA kernel
 constexpr int kDepth = 8;        // 128-column blocks in flight per warp
 
 __device__ __forceinline__ float trit_of(uint32_t w, uint32_t f) {
@@ -147,126 +150,19 @@ ternary_generic_kernel(const float *__restrict__ X, uint64_t x_stride,
 // ---------------------------------------------------------------------------
 // Fast path, step 1: activations -> int8 limbs in mma B-fragment order.
 // ---------------------------------------------------------------------------
-// Fragment layout for one problem: uint2 frag[nt][blk][j][lane], where n-tile
-// nt holds columns n = 8nt .. 8nt+7 (n = 3s + limb), blk is the 128-column
-// block, j the k32 step within it and lane = 4*(n%8) + q.  Lane q of MMA j in
-// block blk covers word w = 2q + (j>>1) of the block and, within it, codes
-// 8*(j&1) + {0,2,4,6} (b0) and 8*(j&1) + {1,3,5,7} (b1).
-struct PrepOut {
-  uint2 *frag;      // NT * cols * 8 bytes
-  float *rowinv;    // [kMaxFastSeq] 2^-e_s
-  int *rowflag;     // [kMaxFastSeq] 1: compute (., s) on the CUDA cores
-};
-
-__host__ __device__ inline int n_tiles(int seq) { return (3 * seq + 7) / 8; }
-__host__ __device__ inline size_t frag_bytes(int seq, uint32_t cols) {
-  return (size_t)n_tiles(seq) * cols * 8u;
-}
-__host__ __device__ inline size_t align256(size_t b) {
-  return (b + 255u) & ~(size_t)255u;
-}
-__host__ __device__ inline size_t prep_bytes(int seq, uint32_t cols) {
-  return align256(frag_bytes(seq, cols)) + 256u;
-}
-__device__ inline PrepOut prep_at(void *ws, int seq, uint32_t cols, uint32_t z) {
-  char *base = (char *)ws + (size_t)z * prep_bytes(seq, cols);
-  PrepOut p;
-  p.frag = (uint2 *)base;
-  p.rowinv = (float *)(base + align256(frag_bytes(seq, cols)));
-  p.rowflag = (int *)(p.rowinv + kMaxFastSeq);
-  return p;
-}
-
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
-         ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
-}
+// The fragment format and the activation prep live in ternary_prep.cuh, shared
+// with the decoder's fused normalisation kernels.
 
 // grid (ceil(8*NT/3), count), 256 threads.  CTA s handles sequence row s
 // (rows s >= seq write the zero padding of the last n-tile).
 __global__ void __launch_bounds__(256)
 ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
                     uint32_t seq, uint32_t cols, void *ws) {
+  __shared__ float red[34];
   const uint32_t s = blockIdx.x, z = blockIdx.y;
-  const int NT = n_tiles((int)seq);
   PrepOut P = prep_at(ws, (int)seq, cols, z);
-  const uint32_t nblk = cols / 128u;
-  const float *xr = X + z * x_stride + (size_t)s * cols;
-  __shared__ float red[8];
-  __shared__ float s_mul;
-  __shared__ int s_ok;
-  bool live = s < seq;
-  if (live) {
-    float m = 0.0f;
-    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x)
-      m = fmaxf(m, fabsf(__ldg(xr + i)));
-    // NaN is dropped by fmaxf; catch it (and inf) separately.
-    int bad = 0;
-    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x)
-      bad |= !isfinite(__ldg(xr + i));
-    bad = __syncthreads_or(bad);
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float mm = 0.0f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); w++) mm = fmaxf(mm, red[w]);
-      int ok = !bad;
-      float mul = 0.0f, inv = 0.0f;
-      if (ok && mm > 0.0f) {
-        int E;
-        frexpf(mm, &E);              // mm in [2^(E-1), 2^E)
-        int e = 22 - E;              // mm * 2^e in [2^21, 2^22)
-        if (e > 126 || e < -126) {
-          ok = 0;                    // 2^e or 2^-e would leave the normals
-        } else {
-          mul = ldexpf(1.0f, e);
-          inv = ldexpf(1.0f, -e);
-        }
-      }
-      s_mul = mul;
-      s_ok = ok;
-      P.rowinv[s] = inv;
-      P.rowflag[s] = !ok;
-    }
-    __syncthreads();
-  }
-  const float mul = live ? s_mul : 0.0f;
-  const bool ok = live && s_ok;
-  // One thread per 8-column group.
-  const uint32_t ngroups = cols / 8u;
-  for (uint32_t c8 = threadIdx.x; c8 < ngroups; c8 += blockDim.x) {
-    int l[3][8];
-    if (ok) {
-      float4 v0 = *reinterpret_cast<const float4 *>(xr + 8u * c8);
-      float4 v1 = *reinterpret_cast<const float4 *>(xr + 8u * c8 + 4u);
-      float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-      for (int k = 0; k < 8; k++) {
-        int q = __float2int_rn(v[k] * mul);   // exact scaling, one rounding
-        int l0 = (int)(int8_t)(q & 0xff);
-        int r = (q - l0) >> 8;
-        int l1 = (int)(int8_t)(r & 0xff);
-        int l2 = (r - l1) >> 8;               // |q| <= 2^22 -> |l2| <= 64
-        l[0][k] = l0; l[1][k] = l1; l[2][k] = l2;
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 8; k++) l[0][k] = l[1][k] = l[2][k] = 0;
-    }
-    const uint32_t blk = c8 / 16u, wq = (c8 % 16u) / 2u, half = c8 & 1u;
-    const uint32_t q = wq >> 1, j = ((wq & 1u) << 1) | half;
-#pragma unroll
-    for (int li = 0; li < 3; li++) {
-      int n = 3 * (int)s + li;
-      if (n >= 8 * NT) continue;
-      uint2 fr;
-      fr.x = pack4(l[li][0], l[li][2], l[li][4], l[li][6]);
-      fr.y = pack4(l[li][1], l[li][3], l[li][5], l[li][7]);
-      size_t idx = (((size_t)(n / 8) * nblk + blk) * 4u + j) * 32u + (uint32_t)(n % 8) * 4u + q;
-      P.frag[idx] = fr;
-    }
-  }
+  const float *xr = s < seq ? X + z * x_stride + (size_t)s * cols : nullptr;
+  prep_row(xr, cols, s, seq, P, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -281,115 +177,192 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
 }
 
-// Two-bit code -> int8 lookup: bytes {0, +1, -2, -1} for codes 00,01,10,11.
-constexpr uint32_t kTritLut = 0xFFFE0100u;
-
-__device__ __forceinline__ uint32_t expand4(uint32_t sel) {
-  return __byte_perm(kTritLut, 0u, sel);
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::);
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Blocks per shared-memory chunk of activation fragments; also the depth of
+// the per-warp weight prefetch (one chunk ahead).
+constexpr int kChunk = kDepth;
+
+__host__ __device__ inline size_t mma_smem_bytes(int NT) {
+  return (size_t)2 * kChunk * NT * 128 * sizeof(uint2);   // double-buffered chunk
+}
+
+// Two-bit codes -> int8 operands of four m16n8k32 steps, with no lookup: a
+// code moved to bits 6..7 of a byte, the bits below cleared, IS the int8
+// value 64*t of its trit (00 -> 0, 01 -> 64, 10 -> -128 = 64*(-2),
+// 11 -> -64), the reference's sign-extending decode scaled by 64.  Byte j of
+// word w holds codes 4j..4j+3; (w << 2(3-k)) & 0xC0C0C0C0 is the operand
+// register of codes {k, 4+k, 8+k, 12+k}.  The dot products come out
+// multiplied by 64, which the epilogue removes exactly.
+//   MMA j = 0: codes {0,4,8,12} | {1,5,9,13} of the lane's first word
+//   MMA j = 1: codes {2,6,10,14} | {3,7,11,15} of the first word
+//   MMA j = 2, 3: the same of the second word
+// (a0/a2 = rows g, a1/a3 = rows g+8; the activation fragments follow the
+// same column order, see ternary_prep.cuh).
+constexpr uint32_t kTop2 = 0xC0C0C0C0u;
+__device__ __forceinline__ void unpack_block(uint2 a, uint2 c, uint32_t (&A)[4][4]) {
+  A[0][0] = (a.x << 6) & kTop2; A[0][1] = (c.x << 6) & kTop2;
+  A[0][2] = (a.x << 4) & kTop2; A[0][3] = (c.x << 4) & kTop2;
+  A[1][0] = (a.x << 2) & kTop2; A[1][1] = (c.x << 2) & kTop2;
+  A[1][2] = a.x & kTop2;        A[1][3] = c.x & kTop2;
+  A[2][0] = (a.y << 6) & kTop2; A[2][1] = (c.y << 6) & kTop2;
+  A[2][2] = (a.y << 4) & kTop2; A[2][3] = (c.y << 4) & kTop2;
+  A[3][0] = (a.y << 2) & kTop2; A[3][1] = (c.y << 2) & kTop2;
+  A[3][2] = a.y & kTop2;        A[3][3] = c.y & kTop2;
+}
+
+// One chunk of kChunk blocks for one warp: consume the weight registers,
+// refill them with the blocks kChunk further on, run the MMAs against the
+// staged fragments.  PRED guards a partial chunk and the last refill; whole
+// chunks run without any per-block test.
+template <int NT, bool PER_BLOCK, bool PRED>
+__device__ __forceinline__ void mma_chunk(int (&acc)[NT][2][4], float (&yf)[NT][4],
+                                          uint2 (&wa)[kChunk], uint2 (&wb)[kChunk],
+                                          const uint2 *fb, const uint2 *pa, const uint2 *pb,
+                                          uint32_t blk0, uint32_t nblk, const float *Sz,
+                                          uint32_t rA, uint32_t rB) {
+#pragma unroll
+  for (int u = 0; u < kChunk; u++) {
+    if (PRED && blk0 + u >= nblk) break;
+    const uint2 a = wa[u], c = wb[u];
+    if (!PRED || blk0 + u + kChunk < nblk) {
+      wa[u] = __ldcs(pa + 4 * (u + kChunk));
+      wb[u] = __ldcs(pb + 4 * (u + kChunk));
+    }
+    uint32_t A[4][4];
+    unpack_block(a, c, A);
+    const uint2 *fu = fb + u * NT * 128;
+    // Two accumulator chains per n-tile, so consecutive MMAs do not wait on
+    // each other's results.
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        mma_s8(acc[t][j & 1], A[j][0], A[j][1], A[j][2], A[j][3], fu[(t * 4 + j) * 32]);
+    }
+    if (PER_BLOCK) {
+      // BETA is per (row, 128-column block): flush the exact block sums.
+      const uint32_t blk = blk0 + u;
+      const float bA = __ldg(Sz + (uint64_t)rA * nblk + blk);
+      const float bB = __ldg(Sz + (uint64_t)rB * nblk + blk);
+#pragma unroll
+      for (int t = 0; t < NT; t++) {
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          yf[t][r] = fmaf((float)(acc[t][0][r] + acc[t][1][r]), r < 2 ? bA : bB, yf[t][r]);
+          acc[t][0][r] = acc[t][1][r] = 0;
+        }
+      }
+    }
+  }
+}
+
+// One CTA = `blockDim.x / 32` warps over consecutive 16-row groups of one
+// problem z.  The warps share the problem's activation fragments: chunks of
+// kChunk blocks are copied into shared memory with cp.async (double
+// buffered), while each warp streams its own weight rows kChunk blocks ahead
+// through registers.
 template <int NT, bool PER_BLOCK>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(256)
 ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
                    const uint32_t *__restrict__ WP, uint64_t w_stride,
                    const float *__restrict__ SCALE, uint64_t s_stride,
                    const float *__restrict__ BIAS, float *__restrict__ Y,
                    uint64_t y_stride, uint32_t seq, uint32_t out,
                    uint32_t cols, uint64_t limit, void *ws) {
+  extern __shared__ __align__(16) uint2 smem[];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
   const int g = lane >> 2, q = lane & 3;
   const uint32_t z = blockIdx.y;
-  const uint32_t rg = blockIdx.x * kWarps + warp;          // 16-row group
+  const uint32_t rg = blockIdx.x * nwarps + warp;          // 16-row group
+  const bool active = rg * 16u < out;
   const uint32_t nblk = cols / 128u, wng = cols / 16u;
-  __shared__ int s_acc[kWarps][16][8 * NT + 1];
-  if (rg * 16u >= out) return;
+  const uint32_t nchunk = (nblk + kChunk - 1) / kChunk;
   PrepOut P = prep_at(ws, (int)seq, cols, z);
-  const uint32_t rA = min(rg * 16u + (uint32_t)g, out - 1u);
-  const uint32_t rB = min(rg * 16u + (uint32_t)g + 8u, out - 1u);
+  const uint32_t rA = active ? min(rg * 16u + (uint32_t)g, out - 1u) : 0u;
+  const uint32_t rB = active ? min(rg * 16u + (uint32_t)g + 8u, out - 1u) : 0u;
   const uint32_t *Wz = WP + z * w_stride;
   const uint2 *pA = reinterpret_cast<const uint2 *>(Wz + (uint64_t)rA * wng) + q;
   const uint2 *pB = reinterpret_cast<const uint2 *>(Wz + (uint64_t)rB * wng) + q;
-  const uint2 *frag = P.frag + lane;
   const float *Sz = SCALE + z * s_stride;
+  constexpr int kChunkU2 = kChunk * NT * 128;              // uint2 per chunk
 
-  int acc[NT][4];
+  // Stage chunk c of the fragments into buffer b.
+  auto stage = [&](uint32_t c, int b) {
+    const uint32_t nb = min((uint32_t)kChunk, nblk - c * kChunk);
+    const uint32_t n16 = nb * NT * 64;                       // 16-byte pieces
+    const char *src = reinterpret_cast<const char *>(P.frag + (size_t)c * kChunkU2);
+    char *dst = reinterpret_cast<char *>(smem + b * kChunkU2);
+    for (uint32_t i = threadIdx.x; i < n16; i += blockDim.x) cp_async16(dst + 16 * i, src + 16 * i);
+    cp_async_commit();
+  };
+
+  int acc[NT][2][4];
   float yf[NT][4];
 #pragma unroll
   for (int t = 0; t < NT; t++)
 #pragma unroll
-    for (int r = 0; r < 4; r++) { acc[t][r] = 0; yf[t][r] = 0.0f; }
+    for (int r = 0; r < 4; r++) { acc[t][0][r] = acc[t][1][r] = 0; yf[t][r] = 0.0f; }
 
-  uint2 wa[kDepth], wb[kDepth];
+  uint2 wa[kChunk], wb[kChunk];
+  if (active) {
 #pragma unroll
-  for (int u = 0; u < kDepth; u++) {
-    if ((uint32_t)u < nblk) {
-      wa[u] = __ldcs(pA + 4u * u);
-      wb[u] = __ldcs(pB + 4u * u);
-    }
-  }
-  for (uint32_t b0 = 0; b0 < nblk; b0 += kDepth) {
-#pragma unroll
-    for (int u = 0; u < kDepth; u++) {
-      const uint32_t blk = b0 + u;
-      if (blk < nblk) {
-        const uint2 a = wa[u], c = wb[u];
-        if (blk + kDepth < nblk) {
-          wa[u] = __ldcs(pA + 4u * (blk + kDepth));
-          wb[u] = __ldcs(pB + 4u * (blk + kDepth));
-        }
-        const uint32_t loA0 = a.x & 0x33333333u, hiA0 = (a.x >> 2) & 0x33333333u;
-        const uint32_t loA1 = a.y & 0x33333333u, hiA1 = (a.y >> 2) & 0x33333333u;
-        const uint32_t loB0 = c.x & 0x33333333u, hiB0 = (c.x >> 2) & 0x33333333u;
-        const uint32_t loB1 = c.y & 0x33333333u, hiB1 = (c.y >> 2) & 0x33333333u;
-        uint32_t A[4][4];
-        A[0][0] = expand4(loA0);       A[0][1] = expand4(loB0);
-        A[0][2] = expand4(hiA0);       A[0][3] = expand4(hiB0);
-        A[1][0] = expand4(loA0 >> 16); A[1][1] = expand4(loB0 >> 16);
-        A[1][2] = expand4(hiA0 >> 16); A[1][3] = expand4(hiB0 >> 16);
-        A[2][0] = expand4(loA1);       A[2][1] = expand4(loB1);
-        A[2][2] = expand4(hiA1);       A[2][3] = expand4(hiB1);
-        A[3][0] = expand4(loA1 >> 16); A[3][1] = expand4(loB1 >> 16);
-        A[3][2] = expand4(hiA1 >> 16); A[3][3] = expand4(hiB1 >> 16);
-#pragma unroll
-        for (int t = 0; t < NT; t++) {
-          const uint2 *ft = frag + (((size_t)t * nblk + blk) * 4u) * 32u;
-#pragma unroll
-          for (int j = 0; j < 4; j++) {
-            uint2 bf = __ldg(ft + j * 32);
-            mma_s8(acc[t], A[j][0], A[j][1], A[j][2], A[j][3], bf);
-          }
-        }
-        if (PER_BLOCK) {
-          // BETA is per (row, 128-column block): flush the exact block sums.
-          const float bA = __ldg(Sz + (uint64_t)rA * nblk + blk);
-          const float bB = __ldg(Sz + (uint64_t)rB * nblk + blk);
-#pragma unroll
-          for (int t = 0; t < NT; t++) {
-            yf[t][0] = fmaf((float)acc[t][0], bA, yf[t][0]);
-            yf[t][1] = fmaf((float)acc[t][1], bA, yf[t][1]);
-            yf[t][2] = fmaf((float)acc[t][2], bB, yf[t][2]);
-            yf[t][3] = fmaf((float)acc[t][3], bB, yf[t][3]);
-            acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0;
-          }
-        }
+    for (int u = 0; u < kChunk; u++) {
+      if ((uint32_t)u < nblk) {
+        wa[u] = __ldcs(pA + 4u * u);
+        wb[u] = __ldcs(pB + 4u * u);
       }
     }
   }
+  stage(0, 0);
+  for (uint32_t c = 0; c < nchunk; c++) {
+    if (c + 1 < nchunk) {
+      stage(c + 1, (c + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (active) {
+      const uint2 *fb = smem + (c & 1) * kChunkU2 + lane;
+      const uint32_t blk0 = c * kChunk;
+      if (blk0 + 2 * kChunk <= nblk)   // this chunk and the next are whole
+        mma_chunk<NT, PER_BLOCK, false>(acc, yf, wa, wb, fb, pA + 4u * blk0, pB + 4u * blk0,
+                                        blk0, nblk, Sz, rA, rB);
+      else
+        mma_chunk<NT, PER_BLOCK, true>(acc, yf, wa, wb, fb, pA + 4u * blk0, pB + 4u * blk0,
+                                       blk0, nblk, Sz, rA, rB);
+    }
+    __syncthreads();   // the buffer is restaged two chunks later
+  }
+  if (!active) return;
 
-  // Epilogue: stage per-(row, n) results in shared memory, then combine the
-  // three limbs of each (row, s).
-  // Per-block results are float sums; they travel through the int array as
-  // bit patterns.
+  // Epilogue: stage per-(row, n) results in shared memory (reusing the
+  // fragment buffers), then combine the three limbs of each (row, s).
+  // Per-block results are float sums; they travel as bit patterns.
+  int(*s_acc)[8 * NT + 1] =
+      reinterpret_cast<int(*)[8 * NT + 1]>(reinterpret_cast<int *>(smem) + warp * 16 * (8 * NT + 1));
 #pragma unroll
   for (int t = 0; t < NT; t++) {
-    const int v0 = PER_BLOCK ? __float_as_int(yf[t][0]) : acc[t][0];
-    const int v1 = PER_BLOCK ? __float_as_int(yf[t][1]) : acc[t][1];
-    const int v2 = PER_BLOCK ? __float_as_int(yf[t][2]) : acc[t][2];
-    const int v3 = PER_BLOCK ? __float_as_int(yf[t][3]) : acc[t][3];
-    s_acc[warp][g][8 * t + 2 * q] = v0;
-    s_acc[warp][g][8 * t + 2 * q + 1] = v1;
-    s_acc[warp][g + 8][8 * t + 2 * q] = v2;
-    s_acc[warp][g + 8][8 * t + 2 * q + 1] = v3;
+    const int v0 = PER_BLOCK ? __float_as_int(yf[t][0]) : acc[t][0][0] + acc[t][1][0];
+    const int v1 = PER_BLOCK ? __float_as_int(yf[t][1]) : acc[t][0][1] + acc[t][1][1];
+    const int v2 = PER_BLOCK ? __float_as_int(yf[t][2]) : acc[t][0][2] + acc[t][1][2];
+    const int v3 = PER_BLOCK ? __float_as_int(yf[t][3]) : acc[t][0][3] + acc[t][1][3];
+    s_acc[g][8 * t + 2 * q] = v0;
+    s_acc[g][8 * t + 2 * q + 1] = v1;
+    s_acc[g + 8][8 * t + 2 * q] = v2;
+    s_acc[g + 8][8 * t + 2 * q + 1] = v3;
   }
   __syncwarp();
   float *Yz = Y + z * y_stride;
@@ -401,14 +374,14 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
     if (o >= out) continue;
     float y;
     if (PER_BLOCK) {
-      const int *sr = s_acc[warp][r];
+      const int *sr = s_acc[r];
       float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
-      v = v + __int_as_float(sr[3 * s + 2]) * 65536.0f;
+      v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
       y = v * P.rowinv[s];
     } else {
-      long long tot = (long long)s_acc[warp][r][3 * s] +
-                      256ll * s_acc[warp][r][3 * s + 1] +
-                      65536ll * s_acc[warp][r][3 * s + 2];
+      long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
+                      65536ll * s_acc[r][3 * s + 2];
+      tot >>= 6;                               // the operands carried 64 * t: exact
       y = ((float)tot * P.rowinv[s]) * __ldg(Sz + o);
     }
     if (BIAS) y = __ldg(BIAS + o) + y;
@@ -441,24 +414,384 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fast path, step 2 (TMA): the same GEMV with the weight tiles streamed by the
+// Tensor Memory Accelerator.  One producer warp issues, per chunk of four
+// 128-column blocks, a 2-D tensor copy of the CTA's rows (128 bytes per row,
+// 128B-swizzled so the consumers' 8-byte reads are bank-conflict free) and a
+// 1-D bulk copy of the matching activation fragments, both completing on
+// the stage's mbarrier.  Consumer warps wait on it, unpack and issue the
+// MMAs, and release the stage.  Every wait is bounded: on timeout the warp
+// records an error and returns.
+// ---------------------------------------------------------------------------
+constexpr int kTmaBlocks = 4;                 // 128-column blocks per stage
+constexpr uint32_t kSpinLimit = 1u << 24;     // try_wait rounds before giving up
+
+__device__ int g_tma_error;                   // set by a wait that gave up
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+               "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait for the phase of parity PARITY to complete.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t i = 0; i < kSpinLimit; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(a), "r"(parity) : "memory");
+    if (done) return true;
+  }
+  atomicExch(&g_tma_error, 1);
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+__host__ __device__ inline int tma_stages(int NT, int nw) {
+  int per = 2048 * nw + NT * kTmaBlocks * 1024;
+  int st = (112 * 1024) / per;
+  return st < 2 ? 2 : (st > 6 ? 6 : st);
+}
+__host__ __device__ inline size_t tma_smem_bytes(int NT, int nw) {
+  int S = tma_stages(NT, nw);
+  return 1024 /* alignment slack */ + (size_t)S * (2048 * nw + NT * kTmaBlocks * 1024) +
+         (size_t)2 * S * 8 + (size_t)nw * 16 * (8 * NT + 1) * 4;
+}
+
+template <int NT, bool PER_BLOCK>
+__global__ void __launch_bounds__(288)
+ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
+                   uint64_t x_stride, const uint32_t *__restrict__ WP, uint64_t w_stride,
+                   const float *__restrict__ SCALE, uint64_t s_stride,
+                   const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
+                   uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws) {
+  extern __shared__ uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = (blockDim.x >> 5) - 1;            // consumer warps; warp nw produces
+  const int S = tma_stages(NT, nw);
+  const uint32_t wbytes = 2048u * nw;              // weight tile per stage
+  const uint32_t fstage = NT * kTmaBlocks * 128;   // fragment uint2 per stage
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t *wbuf = base;                                                // S x wbytes
+  uint2 *fbuf = reinterpret_cast<uint2 *>(base + (size_t)S * wbytes);  // S x fstage
+  uint64_t *full = reinterpret_cast<uint64_t *>(fbuf + (size_t)S * fstage);
+  uint64_t *empty = full + S;
+  int *epi = reinterpret_cast<int *>(empty + S);
+
+  const uint32_t z = blockIdx.y;
+  const uint32_t nblk = cols / 128u, wng = cols / 16u;
+  const uint32_t nchunk = (nblk + kTmaBlocks - 1) / kTmaBlocks;
+  const uint32_t row0 = blockIdx.x * 16u * nw;     // first row of the CTA in problem z
+  PrepOut P = prep_at(ws, (int)seq, cols, z);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], (uint32_t)nw);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == nw) {
+    // ---- producer ----
+    if (lane == 0) {
+      const int y = (int)(z * out + row0);
+      for (uint32_t c = 0; c < nchunk; c++) {
+        const int st = (int)(c % (uint32_t)S);
+        if (c >= (uint32_t)S && !mbar_wait(&empty[st], ((c / S) - 1) & 1)) break;
+        const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
+        const uint32_t fbytes = nb * NT * 1024u;
+        mbar_expect_tx(&full[st], wbytes + fbytes);
+        tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u), y, &full[st]);
+        bulk_load(fbuf + (size_t)st * fstage, P.frag + (size_t)c * fstage, fbytes, &full[st]);
+      }
+      // Leave only when the last copies have landed (bounded).
+      for (uint32_t c = nchunk > (uint32_t)S ? nchunk - S : 0; c < nchunk; c++)
+        mbar_wait(&full[c % S], (c / S) & 1);
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  const int g = lane >> 2, q = lane & 3;
+  const uint32_t rg = blockIdx.x * nw + warp;      // 16-row group
+  const bool active = rg * 16u < out;
+  const uint32_t rA = active ? min(rg * 16u + (uint32_t)g, out - 1u) : 0u;
+  const uint32_t rB = active ? min(rg * 16u + (uint32_t)g + 8u, out - 1u) : 0u;
+  const float *Sz = SCALE + z * s_stride;
+  // Byte offsets of this lane's 8-byte words in a stage's weight tile: row r
+  // of the tile holds 128 bytes; the 16-byte chunk k of row r sits at chunk
+  // k ^ (r % 8) (128B swizzle).  Block b, words 2q..2q+1 -> chunk 2b + q/2.
+  const uint32_t rowA = (uint32_t)warp * 16u + g, rowB = rowA + 8u;
+  uint32_t offA[kTmaBlocks], offB[kTmaBlocks];
+#pragma unroll
+  for (int b = 0; b < kTmaBlocks; b++) {
+    const uint32_t k = 2u * b + (q >> 1), in = (q & 1) * 8u;
+    offA[b] = rowA * 128u + ((k ^ (rowA & 7u)) << 4) + in;
+    offB[b] = rowB * 128u + ((k ^ (rowB & 7u)) << 4) + in;
+  }
+
+  int acc[NT][4][4];                      // [n-tile][k-step][reg]: independent chains
+  float yf[NT][4];
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+      yf[t][r] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; j++) acc[t][j][r] = 0;
+    }
+
+  bool ok = true;
+  for (uint32_t c = 0; c < nchunk && ok; c++) {
+    const int st = (int)(c % (uint32_t)S);
+    ok = mbar_wait(&full[st], (c / S) & 1);
+    if (!ok) break;
+    const uint8_t *wt = wbuf + (size_t)st * wbytes;
+    const uint2 *fb = fbuf + (size_t)st * fstage + lane;
+    const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
+#pragma unroll
+    for (int b = 0; b < kTmaBlocks; b++) {
+      if ((uint32_t)b >= nb) break;
+      const uint2 a = *reinterpret_cast<const uint2 *>(wt + offA[b]);
+      const uint2 cw = *reinterpret_cast<const uint2 *>(wt + offB[b]);
+      uint32_t A[4][4];
+      unpack_block(a, cw, A);
+      const uint2 *fu = fb + b * NT * 128;
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          mma_s8(acc[t][j], A[j][0], A[j][1], A[j][2], A[j][3], fu[(t * 4 + j) * 32]);
+      if (PER_BLOCK) {
+        const uint32_t blk = c * kTmaBlocks + b;
+        const float bA = __ldg(Sz + (uint64_t)rA * nblk + blk);
+        const float bB = __ldg(Sz + (uint64_t)rB * nblk + blk);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+#pragma unroll
+          for (int r = 0; r < 4; r++) {
+            const int v = acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
+            yf[t][r] = fmaf((float)v, r < 2 ? bA : bB, yf[t][r]);
+            acc[t][0][r] = acc[t][1][r] = acc[t][2][r] = acc[t][3][r] = 0;
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+  if (!active || !ok) return;
+
+  int(*s_acc)[8 * NT + 1] = reinterpret_cast<int(*)[8 * NT + 1]>(epi + warp * 16 * (8 * NT + 1));
+#pragma unroll
+  for (int t = 0; t < NT; t++) {
+    int v[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+      v[r] = PER_BLOCK ? __float_as_int(yf[t][r])
+                       : acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
+    s_acc[g][8 * t + 2 * q] = v[0];
+    s_acc[g][8 * t + 2 * q + 1] = v[1];
+    s_acc[g + 8][8 * t + 2 * q] = v[2];
+    s_acc[g + 8][8 * t + 2 * q + 1] = v[3];
+  }
+  __syncwarp();
+  const uint32_t *Wz = WP + z * w_stride;
+  float *Yz = Y + z * y_stride;
+  bool any_flag = false;
+  for (uint32_t s = 0; s < seq; s++) any_flag |= (P.rowflag[s] != 0);
+  for (uint32_t idx = lane; idx < 16u * seq; idx += 32u) {
+    const uint32_t r = idx & 15u, s = idx >> 4;
+    const uint32_t o = rg * 16u + r;
+    if (o >= out) continue;
+    float yv;
+    if (PER_BLOCK) {
+      const int *sr = s_acc[r];
+      float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
+      v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
+      yv = v * P.rowinv[s];
+    } else {
+      long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
+                      65536ll * s_acc[r][3 * s + 2];
+      tot >>= 6;                               // the operands carried 64 * t: exact
+      yv = ((float)tot * P.rowinv[s]) * __ldg(Sz + o);
+    }
+    if (BIAS) yv = __ldg(BIAS + o) + yv;
+    uint64_t oi = (uint64_t)s * out + o;
+    if (oi < limit && !P.rowflag[s]) Yz[oi] = yv;
+  }
+  if (any_flag) {
+    const float *Xz = X + z * x_stride;
+    for (uint32_t r = 0; r < 16u; r++) {
+      const uint32_t o = rg * 16u + r;
+      if (o >= out) break;
+      float acc8[8];
+      const uint32_t *Wrow = Wz + (uint64_t)o * wng;
+      for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
+        int ns = (int)min(8u, seq - s0);
+        ternary_row_generic<8>(Xz, Wrow, PER_BLOCK ? Sz + (uint64_t)o * nblk : nullptr,
+                               PER_BLOCK, PER_BLOCK ? 1.0f : __ldg(Sz + o),
+                               (int)s0, ns, cols, nblk, wng, acc8);
+        if (lane == 0) {
+          for (int k = 0; k < ns; k++) {
+            uint32_t s = s0 + k;
+            uint64_t oi = (uint64_t)s * out + o;
+            if (P.rowflag[s] && oi < limit)
+              Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
+          }
+        }
+      }
+    }
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+// The weight rows of all problems as one [rows x wng] u32 tensor, box
+// [16*nw rows x 32 words], 128B swizzle.  False when TMA cannot describe it.
+bool make_weight_map(CUtensorMap *map, const uint32_t *WP, uint64_t rows, uint32_t wng, int nw) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn || ((uintptr_t)WP & 15u) || (wng * 4u) % 16u || rows == 0) return false;
+  cuuint64_t dims[2] = {wng, rows};
+  cuuint64_t strides[1] = {(cuuint64_t)wng * 4u};
+  cuuint32_t box[2] = {32u, 16u * (uint32_t)nw};
+  cuuint32_t estr[2] = {1u, 1u};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t *>(WP), dims, strides,
+            box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NT, bool PB>
+cudaError_t launch_tma_nt(const CUtensorMap &map, dim3 grid, int nw, cudaStream_t st,
+                          const float *X, uint64_t xs, const uint32_t *WP, uint64_t wst,
+                          const float *S, uint64_t ss, const float *B, float *Y, uint64_t ys,
+                          uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws) {
+  static int configured = 0;
+  size_t smem = tma_smem_bytes(NT, 2);         // the largest CTA this instance runs
+  if (tma_smem_bytes(NT, 4) > smem) smem = tma_smem_bytes(NT, 4);
+  if (tma_smem_bytes(NT, 8) > smem) smem = tma_smem_bytes(NT, 8);
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(ternary_tma_kernel<NT, PB>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = 1;
+  }
+  ternary_tma_kernel<NT, PB><<<grid, 32 * (nw + 1), tma_smem_bytes(NT, nw), st>>>(
+      map, X, xs, WP, wst, S, ss, B, Y, ys, seq, out, cols, limit, ws);
+  return cudaPeekAtLastError();
+}
+
+// Launch the TMA variant when the weights of all COUNT problems form one
+// row-major [count*out x wng] tensor; returns false when it does not apply.
+bool try_launch_tma(uint32_t count, const float *X, uint64_t xs, const uint32_t *WP, uint64_t wst,
+                    const float *S, uint64_t ss, const float *B, float *Y, uint64_t ys,
+                    uint32_t seq, uint32_t out, uint32_t cols, bool per_block, uint64_t limit,
+                    void *ws, cudaStream_t st, cudaError_t *err) {
+  // NELISP_TERNARY_PATH=ring selects the register-ring kernel instead.
+  static const int use_tma = [] {
+    const char *v = getenv("NELISP_TERNARY_PATH");
+    return (v && strcmp(v, "ring") == 0) ? 0 : 1;
+  }();
+  const uint32_t wng = cols / 16u;
+  if (!use_tma || (count > 1 && wst != (uint64_t)out * wng)) return false;
+  const int groups16 = ceil_div((int)out, 16);
+  int nw = 8;
+  while (nw > 2 && (uint64_t)ceil_div(groups16, nw) * count < 2u * 148u) nw >>= 1;
+  CUtensorMap map;
+  if (!make_weight_map(&map, WP, (uint64_t)count * out, wng, nw)) return false;
+  dim3 grid(ceil_div(groups16, nw), count);
+  const int NT = n_tiles((int)seq);
+#define NL_CASE(N)                                                                        \
+  case N:                                                                                 \
+    *err = per_block ? launch_tma_nt<N, true>(map, grid, nw, st, X, xs, WP, wst, S, ss, B, \
+                                              Y, ys, seq, out, cols, limit, ws)           \
+                     : launch_tma_nt<N, false>(map, grid, nw, st, X, xs, WP, wst, S, ss,  \
+                                               B, Y, ys, seq, out, cols, limit, ws);      \
+    return true;
+  switch (NT) {
+    NL_CASE(1) NL_CASE(2) NL_CASE(3) NL_CASE(4) NL_CASE(5) NL_CASE(6)
+    default: return false;
+  }
+#undef NL_CASE
+}
+
+template <int NT, bool PB>
+cudaError_t launch_mma_nt(dim3 grid, int threads, cudaStream_t st, const float *X,
+                          uint64_t xs, const uint32_t *WP, uint64_t wst, const float *S,
+                          uint64_t ss, const float *B, float *Y, uint64_t ys, uint32_t seq,
+                          uint32_t out, uint32_t cols, uint64_t limit, void *ws) {
+  static bool configured = false;
+  const size_t smem = mma_smem_bytes(NT);
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(ternary_mma_kernel<NT, PB>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  ternary_mma_kernel<NT, PB><<<grid, threads, smem, st>>>(X, xs, WP, wst, S, ss, B, Y, ys, seq,
+                                                          out, cols, limit, ws);
+  return cudaPeekAtLastError();
+}
+
 template <bool PB>
-cudaError_t launch_mma(int NT, dim3 grid, cudaStream_t st, const float *X,
-                       uint64_t xs, const uint32_t *WP, uint64_t ws_,
-                       const float *S, uint64_t ss, const float *B, float *Y,
-                       uint64_t ys, uint32_t seq, uint32_t out, uint32_t cols,
-                       uint64_t limit, void *ws) {
-  dim3 block(kWarps * 32);
-#define NL_CASE(N)                                                          \
-  case N:                                                                   \
-    ternary_mma_kernel<N, PB><<<grid, block, 0, st>>>(                      \
-        X, xs, WP, ws_, S, ss, B, Y, ys, seq, out, cols, limit, ws);        \
-    break;
+cudaError_t launch_mma(int NT, dim3 grid, int threads, cudaStream_t st, const float *X,
+                       uint64_t xs, const uint32_t *WP, uint64_t wst, const float *S,
+                       uint64_t ss, const float *B, float *Y, uint64_t ys, uint32_t seq,
+                       uint32_t out, uint32_t cols, uint64_t limit, void *ws) {
+#define NL_CASE(N)                                                                  \
+  case N:                                                                           \
+    return launch_mma_nt<N, PB>(grid, threads, st, X, xs, WP, wst, S, ss, B, Y, ys, \
+                                seq, out, cols, limit, ws);
   switch (NT) {
     NL_CASE(1) NL_CASE(2) NL_CASE(3) NL_CASE(4) NL_CASE(5) NL_CASE(6)
     default: return cudaErrorInvalidValue;
   }
 #undef NL_CASE
-  return cudaPeekAtLastError();
 }
 
 }  // namespace
@@ -509,24 +842,82 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
                                                     x_stride, ns, cols, ws);
     cudaError_t e = cudaPeekAtLastError();
     if (e != cudaSuccess) return e;
-    dim3 grid(ceil_div(ceil_div((int)out, 16), kWarps), count);
+    {
+      // The short-grid limit is an index into the whole Y; shift it per chunk.
+      uint64_t b0 = (uint64_t)s0 * out;
+      uint64_t l0 = limit > b0 ? limit - b0 : 0;
+      if (try_launch_tma(count, X + (uint64_t)s0 * cols, x_stride, WP, w_stride, SCALE,
+                         s_stride, BIAS, Y + (uint64_t)s0 * out, y_stride, ns, out, cols,
+                         per_block, l0, ws, stream, &e)) {
+        count_launches(2);
+        if (e != cudaSuccess) return e;
+        continue;
+      }
+    }
+    // Warps per CTA: as many as keep the grid at two or more CTAs per SM.
+    const int groups16 = ceil_div((int)out, 16);
+    int nw = 8;
+    while (nw > 2 && (uint64_t)ceil_div(groups16, nw) * count < 2u * 148u) nw >>= 1;
+    dim3 grid(ceil_div(groups16, nw), count);
     // The short-grid limit is an index into the whole Y; shift it per chunk.
     uint64_t base = (uint64_t)s0 * out;
     uint64_t lim = limit > base ? limit - base : 0;
     if (per_block)
-      e = launch_mma<true>(NT, grid, stream, X + (uint64_t)s0 * cols, x_stride,
+      e = launch_mma<true>(NT, grid, nw * 32, stream, X + (uint64_t)s0 * cols, x_stride,
                            WP, w_stride, SCALE, s_stride, BIAS,
-                           Y + (uint64_t)s0 * out, y_stride, ns, out, cols,
-                           lim, ws);
+                           Y + (uint64_t)s0 * out, y_stride, ns, out, cols, lim, ws);
     else
-      e = launch_mma<false>(NT, grid, stream, X + (uint64_t)s0 * cols,
-                            x_stride, WP, w_stride, SCALE, s_stride, BIAS,
-                            Y + (uint64_t)s0 * out, y_stride, ns, out, cols,
-                            lim, ws);
+      e = launch_mma<false>(NT, grid, nw * 32, stream, X + (uint64_t)s0 * cols, x_stride,
+                            WP, w_stride, SCALE, s_stride, BIAS,
+                            Y + (uint64_t)s0 * out, y_stride, ns, out, cols, lim, ws);
     count_launches(2);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
+                                uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream) {
+  if (count == 0 || seq == 0) return cudaSuccess;
+  dim3 pgrid((8 * n_tiles((int)seq) + 2) / 3, count);
+  ternary_prep_kernel<<<pgrid, 256, 0, stream>>>(X, x_stride, seq, cols, ws);
+  count_launches(1);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_stride,
+                                const uint32_t *WP, uint64_t w_stride, const float *SCALE,
+                                uint64_t s_stride, const float *BIAS, float *Y,
+                                uint64_t y_stride, uint32_t seq, uint32_t out, uint32_t cols,
+                                bool per_block, void *ws, cudaStream_t stream) {
+  if (count == 0 || seq == 0 || out == 0) return cudaSuccess;
+  const uint32_t nblk = (cols + 127) / 128, wng = (cols + 15) / 16;
+  if (!ws || seq > (uint32_t)kMaxFastSeq || !ternary_fast_shape(cols, nblk, wng, per_block)) {
+    dim3 grid(ceil_div((int)out, 8), count);
+    ternary_generic_kernel<<<grid, 256, 0, stream>>>(X, x_stride, WP, w_stride, SCALE, s_stride,
+                                                     BIAS, Y, y_stride, seq, out, cols, nblk,
+                                                     wng, per_block ? 1 : 0, UINT64_MAX);
+    count_launches(1);
+    return cudaPeekAtLastError();
+  }
+  cudaError_t e;
+  if (try_launch_tma(count, X, x_stride, WP, w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq,
+                     out, cols, per_block, UINT64_MAX, ws, stream, &e)) {
+    count_launches(1);
+    return e;
+  }
+  const int groups16 = ceil_div((int)out, 16);
+  int nw = 8;
+  while (nw > 2 && (uint64_t)ceil_div(groups16, nw) * count < 2u * 148u) nw >>= 1;
+  dim3 grid(ceil_div(groups16, nw), count);
+  e = per_block ? launch_mma<true>(n_tiles((int)seq), grid, nw * 32, stream, X, x_stride, WP,
+                                   w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq, out, cols,
+                                   UINT64_MAX, ws)
+                : launch_mma<false>(n_tiles((int)seq), grid, nw * 32, stream, X, x_stride, WP,
+                                    w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq, out, cols,
+                                    UINT64_MAX, ws);
+  count_launches(1);
+  return e;
 }
 
 // ---------------------------------------------------------------------------

@@ -87,8 +87,34 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
                                 void *ws, size_t ws_bytes,
                                 cudaStream_t stream);
 size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols);
+// The two halves of the fast path, for callers that fuse the prep into the
+// kernel producing the activations: the prep alone, and the GEMV alone on a
+// workspace the prep has filled (seq <= 16; shapes the fast path does not
+// cover, or a NULL workspace, take the generic kernel, which reads X).
+cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
+                                uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream);
+cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_stride,
+                                const uint32_t *WP, uint64_t w_stride, const float *SCALE,
+                                uint64_t s_stride, const float *BIAS, float *Y,
+                                uint64_t y_stride, uint32_t seq, uint32_t out, uint32_t cols,
+                                bool per_block, void *ws, cudaStream_t stream);
 bool ternary_fast_shape(uint32_t cols, uint32_t nblk, uint32_t wng,
                         bool per_block);
+
+// Split-K single-query attention over a [B x maxseq x kvheads*hd] cache,
+// positions 0..POS[0] (POS a float, as the reference's buffer).
+struct AttnGeom {
+  uint32_t B, heads, kvheads, hd, grp, kvdim, maxseq;  // maxseq: rows per sequence
+  uint32_t nsplit, chunk;                                // key range per split
+  uint64_t cache_words;                                  // CK/CV capacity
+  float coef;                                            // 1/sqrt(hd)
+};
+AttnGeom attn_geom(uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads,
+                   uint32_t maxseq, uint64_t cache_words);
+size_t attn_scratch_bytes(const AttnGeom &g);
+cudaError_t attn_decode_launch(const float *Q, const float *CK, const float *CV,
+                               const float *POS, float *C, const AttnGeom &g, void *scratch,
+                               cudaStream_t st);
 
 // Library workspace for typed calls that pass no workspace (nl_runtime.cu).
 void *library_workspace(size_t bytes, cudaStream_t stream);

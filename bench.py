@@ -346,6 +346,15 @@ def run_gpu(args):
         cpu = cpu_baseline(Wh[:1].ravel(), Sh[0], X[0].reshape(-1).cpu().numpy(), batch,
                            seconds=args.cpu_seconds)
 
+    decode = None
+    if not args.no_decode:
+        decode = run_decoder(dist, ws, rank, local, peak)
+        decode = {"metric": "ternary-LM decode tok/s (BitNet-b1.58-2B shape, greedy)",
+                  "tp": ws, "prompt": PROMPT_LEN, "generated": GEN_STEPS,
+                  "data": "synthetic seeded weights and prompt ids", **decode}
+        if rank == 0 and ws == 1 and not args.no_cpu:
+            decode["cpu_baseline"] = cpu_decode_baseline()
+
     tr = traffic_summary()
     if rank == 0:
         line = {
@@ -378,10 +387,68 @@ def run_gpu(args):
         }
         if cpu:
             line["cpu_baseline"] = cpu
+        if decode:
+            line["decode"] = decode
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+PROMPT_LEN, GEN_STEPS = 512, 256
+
+
+def decode_step_bytes(info, cfg, batch, prompt_len, steps):
+    """Bytes one rank streams per decode step, averaged over the STEPS steps:
+    its ternary weights and scales, its LM-head rows, and the KV cache read
+    by attention (positions 0..p for the step at position p)."""
+    H, L, hd = cfg["hidden"], cfg["layers"], cfg["head_dim"]
+    avg_ctx = prompt_len + (steps - 1) / 2.0
+    kv = 2 * L * batch * avg_ctx * info["kv_heads"] * hd * 4
+    return info["weight_bytes"] + kv + batch * H * 4 * 2
+
+
+def run_decoder(dist, ws, rank, local, peak):
+    """ternary-LM decode tok/s at tensor parallelism = ws."""
+    import numpy as np
+    import torch
+
+    from nelisp_cuda.decoder import BITNET_2B, Decoder, nccl_unique_id
+    nid = None
+    if ws > 1:
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    dec = Decoder(BITNET_2B, max_batch=8, max_seq=PROMPT_LEN + GEN_STEPS, tp_rank=rank,
+                  tp_size=ws, nccl_id=nid)
+    info = dec.info()
+    res = {}
+    rng = np.random.default_rng(512)
+    for batch in (1, 8):
+        prompt = rng.integers(0, BITNET_2B["vocab"], size=(batch, PROMPT_LEN))
+        dec.generate(prompt[:, :8], 4)                  # warm-up: capture, attributes, NCCL
+        toks, pf, dc = dec.generate(prompt, GEN_STEPS)
+        t = torch.tensor([pf, dc], device=torch.device("cuda", local))
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pf, dc = float(t[0]), float(t[1])
+        step_ms = dc / GEN_STEPS
+        nbytes = decode_step_bytes(info, BITNET_2B, batch, PROMPT_LEN, GEN_STEPS)
+        gbs = nbytes / (step_ms * 1e-3) / 1e9
+        res[f"batch{batch}"] = {
+            "tok_s": round(batch * GEN_STEPS / (dc * 1e-3), 1),
+            "ms_per_step": round(step_ms, 4),
+            "prefill_ms": round(pf, 1),
+            "prefill_tok_s": round(batch * (PROMPT_LEN - 1) / (pf * 1e-3), 1),
+            "bytes_per_step_per_gpu": int(nbytes),
+            "achieved_GBs_per_gpu": round(gbs, 1),
+            "frac_of_hbm": round(gbs / peak, 4),
+            "tokens_head": [int(v) for v in toks[0, :8]],
+        }
+    res["kernels_per_step"] = dec.info()["kernels_per_step"]
+    res["shard_rank0"] = {k: info[k] for k in ("kv_heads", "ffn", "vocab")}
+    dec.close()
+    return res
 
 
 def cpu_baseline(WP, S, X, batch, seconds=10.0):
@@ -402,6 +469,41 @@ def cpu_baseline(WP, S, X, batch, seconds=10.0):
             "cores": nlo.threads(), "kind": "port",
             "sample": f"{n} GEMVs 4096x4096 batch {batch} in {el:.1f} s "
                       "(oracle/nl_oracle.c ternary-rows restatement, OpenMP)"}
+
+
+def run_decode_profile(args):
+    import numpy as np
+    import torch
+
+    from nelisp_cuda.decoder import BITNET_2B, Decoder
+    torch.cuda.set_device(0)
+    dec = Decoder(BITNET_2B, max_batch=8, max_seq=64, device=0)
+    prompt = np.random.default_rng(5).integers(0, BITNET_2B["vocab"], size=(args.batch, 4))
+    toks, pf, dc = dec.generate(prompt, 4)
+    print(json.dumps({"decode_profile": True, "batch": args.batch, "ms_per_step": dc / 4,
+                      "kernels_per_step": dec.info()["kernels_per_step"]}), flush=True)
+    dec.close()
+
+
+def cpu_decode_baseline():
+    """The CPU model of the decoder (oracle/nl_oracle_decoder.c) on the full
+    configuration, batch 1, over a bounded sample: a 2-token prompt and 2
+    generated tokens (3 positions, all host threads)."""
+    import numpy as np
+
+    import oracle as nlo
+    from nelisp_cuda.decoder import BITNET_2B
+    cfg = dict(BITNET_2B, max_batch=1, max_seq=4)
+    t0 = time.perf_counter()
+    nlo.decoder_generate(cfg, np.array([[11, 12]]), 1)
+    setup = time.perf_counter() - t0                    # weight generation + 2 positions
+    t0 = time.perf_counter()
+    nlo.decoder_generate(cfg, np.array([[11, 12]]), 2)
+    full = time.perf_counter() - t0                     # weight generation + 3 positions
+    per_tok = max(full - setup, 1e-9)
+    return {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": nlo.threads(),
+            "kind": "port", "sample": "batch 1, one decode position at context 3 "
+            "(difference of two runs, so weight generation is excluded)"}
 
 
 # ---- the reference arm ----------------------------------------------------------------------
@@ -466,12 +568,17 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-decode", action="store_true", help="skip the decoder section")
+    ap.add_argument("--decode-profile", action="store_true",
+                    help="only a short decoder run, batch --batch (the case ncu lists)")
     ap.add_argument("--profile-run", action="store_true",
                     help="only warm-up and timed steps (the case ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
+    elif args.decode_profile:
+        run_decode_profile(args)
     else:
         run_gpu(args)
 

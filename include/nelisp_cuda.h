@@ -212,6 +212,53 @@ int nl_ternary_gemv_batched_dev(uint32_t count, const float *X,
                                 uint32_t cols, void *workspace,
                                 size_t ws_bytes, void *stream);
 
+/* ---- the ternary decoder (tensor-parallel) --------------------------- */
+
+/* A LLaMA-style decoder with ternary linears (BitNet-b1.58-2B shaped): RMSNorm,
+ * fused Q|K|V and gate|up ternary linears with per-row f32 scales, half-split
+ * RoPE, a per-sequence f32 KV cache, SwiGLU, a tied f32 embedding / LM head
+ * and greedy argmax.  Weights are synthetic: generated on the device from
+ * SEED by a counter-based hash of (seed, tensor, element), trits -1/0/+1
+ * with p = 1/3, row scales (0.5 + u) / sqrt(2K/3), norm gains 0.75 + u/2,
+ * embeddings 2u - 1 (u uniform in [0, 1)).  The reference has no decoder of
+ * its own in its repository; this composition of its kernels is this
+ * library's (no reference interface is replaced). */
+typedef struct {
+  uint32_t hidden, layers, heads, kv_heads, head_dim, ffn, vocab;
+  uint32_t max_batch;   /* <= 16 */
+  uint32_t max_seq;     /* KV-cache rows per sequence */
+  float rms_eps, rope_base;
+  uint64_t seed;
+} nl_decoder_config;
+
+typedef struct nl_decoder nl_decoder;
+
+/* NCCL unique id (128 bytes) for a tensor-parallel group; rank 0 makes it
+ * and the caller broadcasts it. */
+int nl_nccl_unique_id(void *id_out);
+/* One rank of a TP_SIZE-way tensor-parallel decoder on the current device
+ * (NCCL_ID ignored when TP_SIZE is 1).  KEEP_LOGITS stores every step's
+ * logits for nl_decoder_logits. */
+int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int tp_size,
+                      const void *nccl_id, int keep_logits, nl_decoder **out);
+/* Greedy generation for BATCH sequences: PROMPT is [batch x prompt_len]
+ * int32 (host); OUT_TOKENS receives [batch x steps].  Each step is one CUDA
+ * graph replay; PREFILL_MS times the prompt_len - 1 replays that fill the
+ * cache with the prompt, DECODE_MS the STEPS replays that generate (device
+ * time, CUDA events).  All ranks must call it together. */
+int nl_decoder_generate(nl_decoder *dec, uint32_t batch, uint32_t prompt_len,
+                        const int32_t *prompt, uint32_t steps,
+                        int32_t *out_tokens, double *prefill_ms,
+                        double *decode_ms);
+/* The stored logits: [max_seq][max_batch][vocab rows of this rank]. */
+int nl_decoder_logits(nl_decoder *dec, float *out, uint64_t nfloats);
+/* SHARD[6] = kv-head begin, kv-head count, ffn begin, ffn count, vocab
+ * begin, vocab count of this rank; bytes of weights this rank streams per
+ * step; kernels per decode step. */
+int nl_decoder_info(nl_decoder *dec, uint32_t *shard, uint64_t *weight_bytes,
+                    uint64_t *kernels_per_step);
+void nl_decoder_destroy(nl_decoder *dec);
+
 /* Launch counter: how many kernels this library has enqueued since the
  * context was created (each graph replay counts the kernels it holds). */
 uint64_t nl_launch_count(void);

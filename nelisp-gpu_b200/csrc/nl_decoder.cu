@@ -1,0 +1,793 @@
+// nl_decoder.cu -- the ternary LLaMA-style decoder (BitNet-b1.58-2B shaped)
+// assembled from the hot-path kernels, tensor-parallel over NCCL.
+//
+// The reference holds the kernels of this model but not the model
+// (lisp/nelisp-gpu-kernels.el; its decoder lives outside the repository), so
+// the composition follows the conventions its kernels document: RMSNorm
+// before attention and FFN (rmsnorm-istd/-fwd, :1250-1265, with the eps a
+// parameter), a fused Q|K|V and a fused gate|up ternary linear with per-row
+// scales (bitlinear-packed-v, :1022-1040, on the two-bit format of
+// ternary-rows, :713-746), half-split RoPE at the absolute position
+// (rope-half, :857-882), a per-sequence KV cache (cache-append-b, :358-365),
+// single-query attention with scale 1/sqrt(hd) (decode-attn-b, :368-390),
+// SwiGLU (silu-mul, :187-193), residual adds (add2, :816-821), a tied f32
+// LM head and greedy argmax (lowest index on ties).
+//
+// One decode step is one CUDA graph replay.  The position, the tokens and
+// the argmax keys live on the device, so consecutive replays advance the
+// sequence without the host: while the prompt is consumed the next token
+// comes from it (teacher forcing), afterwards from the argmax.
+//
+// Tensor parallelism (one process per GPU): KV heads (with their query
+// heads) and 128-column FFN blocks are split across ranks, unevenly where
+// they do not divide; Q|K|V and gate|up are column-parallel, O and down
+// row-parallel, followed by an NCCL all-reduce (sum); the LM head is split
+// by vocabulary rows and the (logit, index) argmax keys are all-reduced with
+// max.  Every rank generates its own shard of the synthetic weights from
+// global element indices (nl_rng.h), so no weights cross the links.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <map>
+#include <vector>
+
+#include "nl_internal.h"
+#include "nl_rng.h"
+#include "ternary_prep.cuh"
+
+namespace nl {
+namespace {
+
+// ---- NCCL, loaded on demand (single-GPU use needs no NCCL) -----------------
+typedef struct ncclComm *ncclComm_t;
+typedef struct { char internal[128]; } ncclUniqueId;
+typedef int ncclResult_t;
+constexpr int kNcclSum = 0, kNcclMax = 2, kNcclUint64 = 5, kNcclFloat32 = 7;
+
+struct Nccl {
+  void *h = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, int, int, ncclComm_t, cudaStream_t) =
+      nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  const char *(*GetErrorString)(ncclResult_t) = nullptr;
+};
+
+Nccl *nccl() {
+  static Nccl n;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    n.h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!n.h) n.h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (n.h) {
+      n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(n.h, "ncclGetUniqueId");
+      n.CommInitRank = (decltype(n.CommInitRank))dlsym(n.h, "ncclCommInitRank");
+      n.AllReduce = (decltype(n.AllReduce))dlsym(n.h, "ncclAllReduce");
+      n.CommDestroy = (decltype(n.CommDestroy))dlsym(n.h, "ncclCommDestroy");
+      n.GetErrorString = (decltype(n.GetErrorString))dlsym(n.h, "ncclGetErrorString");
+    }
+  }
+  if (!n.h || !n.GetUniqueId || !n.CommInitRank || !n.AllReduce || !n.CommDestroy) return nullptr;
+  return &n;
+}
+
+struct Split {
+  uint32_t begin, count;
+};
+Split split(uint32_t n, uint32_t parts, uint32_t r) {
+  uint32_t base = n / parts, rem = n % parts;
+  return {r * base + (r < rem ? r : rem), base + (r < rem ? 1u : 0u)};
+}
+
+// ---- weight generation -------------------------------------------------------------
+__global__ void gen_ternary_kernel(uint32_t *W, uint32_t rows, uint32_t k_local, uint64_t key,
+                                   uint64_t grow0, uint64_t k_full, uint64_t c0) {
+  const uint32_t wng = (k_local + 15) / 16;
+  const uint64_t n = (uint64_t)rows * wng;
+  for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t r = (uint32_t)(idx / wng), w = (uint32_t)(idx % wng);
+    uint32_t word = 0;
+    for (uint32_t f = 0; f < 16; f++) {
+      const uint32_t c = 16 * w + f;
+      if (c >= k_local) break;
+      const int t = nl_trit(key, (grow0 + r) * k_full + c0 + c);
+      const uint32_t code = t == 1 ? 1u : (t == -1 ? 3u : 0u);
+      word |= code << (2 * f);
+    }
+    W[idx] = word;
+  }
+}
+
+__global__ void gen_scale_kernel(float *S, uint32_t n, uint64_t key, uint64_t g0, float rs) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    S[i] = __fmul_rn(__fadd_rn(0.5f, nl_unit(key, g0 + i)), rs);
+}
+
+__global__ void gen_norm_kernel(float *G, uint32_t n, uint64_t key) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    G[i] = __fadd_rn(0.75f, __fmul_rn(0.5f, nl_unit(key, i)));
+}
+
+__global__ void gen_embed_kernel(float *E, uint64_t n, uint64_t key) {
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (uint64_t)gridDim.x * blockDim.x)
+    E[i] = __fsub_rn(__fmul_rn(2.0f, nl_unit(key, i)), 1.0f);
+}
+
+// ---- step kernels ---------------------------------------------------------------------
+__device__ float block_reduce_sum(float v, float *red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = 0.0f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) r += red[i];
+  return r;
+}
+
+enum { kNormGather = 0, kNormAdd = 1 };
+
+// One CTA per sequence row b: h = E[tok] (gather) or h = h + delta (add);
+// x = (h * rsqrt(mean h^2 + eps)) * g; then x is converted into the next
+// GEMV's activation fragments.  CTAs b >= B write the fragment padding.
+template <int MODE>
+__global__ void __launch_bounds__(256)
+k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restrict__ h,
+       const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
+       void *ws, uint32_t B, uint32_t H, float eps) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[34];
+  const uint32_t b = blockIdx.x;
+  PrepOut P = prep_at(ws, (int)B, H, 0);
+  if (b < B) {
+    float *hb = h + (size_t)b * H;
+    const float *src = MODE == kNormGather ? E + (size_t)__ldg(tok + b) * H : nullptr;
+    float ss = 0.0f;
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
+      float v = MODE == kNormGather ? __ldg(src + i) : __fadd_rn(hb[i], delta[(size_t)b * H + i]);
+      hb[i] = v;
+      xs[i] = v;
+      ss = fmaf(v, v, ss);
+    }
+    ss = block_reduce_sum(ss, red);
+    const float rinv = 1.0f / sqrtf(ss / (float)H + eps);
+    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
+      float xv = __fmul_rn(__fmul_rn(xs[i], rinv), __ldg(g + i));
+      xs[i] = xv;
+      x[(size_t)b * H + i] = xv;
+    }
+    if (ws) prep_row(xs, H, b, B, P, red);
+  } else if (ws) {
+    prep_row(nullptr, H, b, B, P, red);
+  }
+}
+
+// q/k rotation (half-split, position *pos), k and v appended to the cache.
+__global__ void k_rope_append(const float *__restrict__ qkv, float *__restrict__ q,
+                              float *__restrict__ ck, float *__restrict__ cv,
+                              const int *__restrict__ pos, uint32_t B, uint32_t hr, uint32_t kvr,
+                              uint32_t hd, uint32_t maxseq, float base) {
+  const uint32_t half = hd / 2, nh = hr + 2 * kvr;
+  const uint32_t p = (uint32_t)*pos;
+  const uint64_t n = (uint64_t)B * nh * half;
+  const uint32_t rows = nh * hd, kvdim = kvr * hd;
+  for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t m = (uint32_t)(idx % half);
+    const uint32_t head = (uint32_t)((idx / half) % nh);
+    const uint32_t b = (uint32_t)(idx / ((uint64_t)half * nh));
+    const float *src = qkv + (size_t)b * rows + (size_t)head * hd;
+    const float a0 = src[m], a1 = src[m + half];
+    if (head < hr + kvr) {
+      const float ex = __fdiv_rn(2.0f * (float)m, (float)hd);
+      const float theta = __fdiv_rn((float)p, powf(base, ex));
+      const float c = cosf(theta), s = sinf(theta);
+      const float y0 = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s));
+      const float y1 = __fadd_rn(__fmul_rn(a1, c), __fmul_rn(a0, s));
+      float *dst = head < hr ? q + (size_t)b * hr * hd + (size_t)head * hd
+                             : ck + ((size_t)b * maxseq + p) * kvdim + (size_t)(head - hr) * hd;
+      dst[m] = y0;
+      dst[m + half] = y1;
+    } else {
+      float *dst = cv + ((size_t)b * maxseq + p) * kvdim + (size_t)(head - hr - kvr) * hd;
+      dst[m] = a0;
+      dst[m + half] = a1;
+    }
+  }
+}
+
+// a = silu(gate) * up for one sequence row per CTA, then the down GEMV's prep.
+__global__ void __launch_bounds__(256)
+k_silu_prep(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint32_t B,
+            uint32_t fr) {
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[34];
+  const uint32_t b = blockIdx.x;
+  PrepOut P = prep_at(ws, (int)B, fr, 0);
+  if (b < B) {
+    const float *gr = gu + (size_t)b * 2 * fr;
+    for (uint32_t j = threadIdx.x; j < fr; j += blockDim.x) {
+      const float gv = gr[j], uv = gr[fr + j];
+      const float sg = 1.0f / (1.0f + expf(-gv));
+      const float v = __fmul_rn(__fmul_rn(gv, sg), uv);
+      xs[j] = v;
+      a[(size_t)b * fr + j] = v;
+    }
+    if (ws) prep_row(xs, fr, b, B, P, red);
+  } else if (ws) {
+    prep_row(nullptr, fr, b, B, P, red);
+  }
+}
+
+// Order-preserving 64-bit argmax key: larger logit first, then lower index.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  if (v != v) u = 0;   // NaN never wins
+  return ((unsigned long long)u << 32) | (0xFFFFFFFFu - idx);
+}
+
+// LM head over this rank's vocabulary rows with the argmax fused: each warp
+// takes RPW consecutive rows at a time, lanes stride the hidden dimension in
+// float4 steps against x held in shared memory.
+template <int NB>
+__global__ void __launch_bounds__(256)
+k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
+         unsigned long long *__restrict__ keys, float *__restrict__ logits,
+         const int *__restrict__ pos, uint32_t B, uint32_t vr, uint32_t v0, uint32_t H,
+         uint32_t logit_stride) {
+  constexpr int RPW = 4;
+  extern __shared__ __align__(16) float xs[];   // [NB][H]
+  for (uint32_t i = threadIdx.x; i < NB * H; i += blockDim.x)
+    xs[i] = (i / H) < B ? x[i] : 0.0f;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const uint32_t gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const uint32_t nw = gridDim.x * (blockDim.x >> 5);
+  const uint32_t h4 = H / 4;
+  unsigned long long best[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) best[b] = 0ull;
+  float *lg = logits ? logits + (size_t)(*pos) * logit_stride : nullptr;
+  for (uint32_t r0 = gw * RPW; r0 < vr; r0 += nw * RPW) {
+    float acc[RPW][NB];
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+#pragma unroll
+      for (int b = 0; b < NB; b++) acc[r][b] = 0.0f;
+    const float4 *er[RPW];
+#pragma unroll
+    for (int r = 0; r < RPW; r++)
+      er[r] = reinterpret_cast<const float4 *>(E + (size_t)min(r0 + r, vr - 1) * H);
+    for (uint32_t c = lane; c < h4; c += 32) {
+      float4 ev[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; r++) ev[r] = __ldcs(er[r] + c);
+#pragma unroll
+      for (int b = 0; b < NB; b++) {
+        const float4 xv = reinterpret_cast<const float4 *>(xs + (size_t)b * H)[c];
+#pragma unroll
+        for (int r = 0; r < RPW; r++) {
+          acc[r][b] = fmaf(ev[r].x, xv.x, acc[r][b]);
+          acc[r][b] = fmaf(ev[r].y, xv.y, acc[r][b]);
+          acc[r][b] = fmaf(ev[r].z, xv.z, acc[r][b]);
+          acc[r][b] = fmaf(ev[r].w, xv.w, acc[r][b]);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < RPW; r++) {
+#pragma unroll
+      for (int b = 0; b < NB; b++) {
+        float v = acc[r][b];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t row = r0 + r;
+        if (row < vr && (uint32_t)b < B) {
+          const unsigned long long k = argmax_key(v, v0 + row);
+          if (k > best[b]) best[b] = k;
+          if (lg && lane == 0) lg[(size_t)b * vr + row] = v;
+        }
+      }
+    }
+  }
+  if (lane == 0)
+    for (int b = 0; b < NB; b++)
+      if ((uint32_t)b < B && best[b]) atomicMax(keys + b, best[b]);
+}
+
+// Next token: from the prompt while it lasts, else the argmax; reset the
+// keys and advance the position.  One CTA.
+__global__ void k_next(unsigned long long *keys, const int *prompt, uint32_t P, int *tok,
+                       int *out_tok, int *pos, float *posf, uint32_t B) {
+  const int p = *pos;
+  const uint32_t b = threadIdx.x;
+  if (b < B) {
+    const uint32_t idx = 0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull);
+    int nt;
+    if ((uint32_t)p + 1 < P) {
+      nt = prompt[(size_t)b * P + p + 1];
+    } else {
+      nt = (int)idx;
+      out_tok[(size_t)(p + 1 - P) * B + b] = nt;
+    }
+    tok[b] = nt;
+    keys[b] = 0ull;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *pos = p + 1;
+    *posf = (float)(p + 1);
+  }
+}
+
+__global__ void k_init(const int *prompt, uint32_t P, int *tok, unsigned long long *keys, int *pos,
+                       float *posf, uint32_t B) {
+  const uint32_t b = threadIdx.x;
+  if (b < B) {
+    tok[b] = prompt[(size_t)b * P];
+    keys[b] = 0ull;
+  }
+  if (threadIdx.x == 0) {
+    *pos = 0;
+    *posf = 0.0f;
+  }
+}
+
+}  // namespace
+
+// ---- the decoder object -------------------------------------------------------------------
+struct Layer {
+  uint32_t *wqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr;
+  float *sqkv = nullptr, *so = nullptr, *sgu = nullptr, *sd = nullptr;
+  float *gattn = nullptr, *gffn = nullptr;
+  float *ck = nullptr, *cv = nullptr;
+};
+
+}  // namespace nl
+
+struct nl_decoder {
+  nl_decoder_config cfg;
+  int rank = 0, size = 1;
+  nl::ncclComm_t comm = nullptr;
+  cudaStream_t stream = nullptr;
+  nl::Split kvh, ffb, voc;
+  uint32_t hr = 0, kvr = 0, fr = 0, vr = 0, v0 = 0, qkv_rows = 0;
+  std::vector<nl::Layer> layers;
+  float *embed = nullptr, *gfinal = nullptr;
+  // activations
+  float *h = nullptr, *x = nullptr, *qkv = nullptr, *q = nullptr, *ctx = nullptr, *o = nullptr,
+        *gu = nullptr, *a = nullptr, *d = nullptr, *posf = nullptr, *logits = nullptr;
+  int *tok = nullptr, *prompt = nullptr, *out_tok = nullptr, *pos = nullptr;
+  unsigned long long *keys = nullptr;
+  void *ws_qkv = nullptr, *ws_o = nullptr, *ws_gu = nullptr, *ws_d = nullptr, *attn_scr = nullptr;
+  bool keep_logits = false;
+  std::map<uint32_t, cudaGraphExec_t> graphs;   // by batch
+  uint64_t kernels_per_step = 0;
+  uint64_t weight_bytes = 0;
+  std::vector<void *> allocs;
+  uint32_t last_batch = 0, last_positions = 0;
+};
+
+namespace nl {
+namespace {
+
+int dalloc(nl_decoder *D, void **p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes ? bytes : 16);
+  if (e != cudaSuccess) return cuda_status(e, "decoder: cudaMalloc");
+  D->allocs.push_back(*p);
+  return NL_OK;
+}
+#define DALLOC(ptr, bytes)                                            \
+  do {                                                                \
+    int rc_ = dalloc(D, reinterpret_cast<void **>(&(ptr)), (bytes));  \
+    if (rc_) return rc_;                                              \
+  } while (0)
+
+float inv_sqrt_fan(uint64_t k) { return (float)(1.0 / sqrt(2.0 * (double)k / 3.0)); }
+
+int gen_ternary(nl_decoder *D, uint32_t *W, uint32_t rows, uint32_t k_local, uint64_t tensor,
+                uint64_t grow0, uint64_t k_full, uint64_t c0) {
+  uint64_t key = nl_tensor_key(D->cfg.seed, tensor);
+  uint64_t n = (uint64_t)rows * ((k_local + 15) / 16);
+  gen_ternary_kernel<<<grid_for(n, 256), 256, 0, D->stream>>>(W, rows, k_local, key, grow0,
+                                                             k_full, c0);
+  return cuda_status(cudaPeekAtLastError(), "decoder: weights");
+}
+int gen_scale(nl_decoder *D, float *S, uint32_t n, uint64_t tensor, uint64_t g0, uint64_t k_full) {
+  gen_scale_kernel<<<grid_for(n, 256), 256, 0, D->stream>>>(
+      S, n, nl_tensor_key(D->cfg.seed, tensor), g0, inv_sqrt_fan(k_full));
+  return cuda_status(cudaPeekAtLastError(), "decoder: scales");
+}
+int gen_norm(nl_decoder *D, float *G, uint32_t n, uint64_t tensor) {
+  gen_norm_kernel<<<grid_for(n, 256), 256, 0, D->stream>>>(G, n,
+                                                            nl_tensor_key(D->cfg.seed, tensor));
+  return cuda_status(cudaPeekAtLastError(), "decoder: norms");
+}
+
+int allreduce(nl_decoder *D, void *buf, size_t count, int dtype, int op) {
+  if (D->size <= 1) return NL_OK;
+  Nccl *n = nccl();
+  ncclResult_t r = n->AllReduce(buf, buf, count, dtype, op, D->comm, D->stream);
+  if (r != 0)
+    return set_error(NL_ERROR, "ncclAllReduce: %s", n->GetErrorString ? n->GetErrorString(r) : "?");
+  return NL_OK;
+}
+
+// Enqueue one decode step for batch B on D->stream.
+int enqueue_step(nl_decoder *D, uint32_t B) {
+  const nl_decoder_config &c = D->cfg;
+  const uint32_t H = c.hidden, hd = c.head_dim;
+  const float eps = c.rms_eps;
+  cudaStream_t st = D->stream;
+  const uint32_t npad = (uint32_t)(8 * n_tiles((int)B) + 2) / 3;
+  const uint32_t gnorm = B > npad ? B : npad;
+  const size_t smem_h = (size_t)H * sizeof(float);
+  const bool fast_o = ternary_fast_shape(D->hr * hd, D->hr * hd / 128, D->hr * hd / 16, false);
+  const bool fast_d = ternary_fast_shape(D->fr, D->fr / 128, D->fr / 16, false);
+  const bool fast_h = ternary_fast_shape(H, H / 128, H / 16, false);
+  int rc;
+  cudaError_t e;
+  k_norm<kNormGather><<<gnorm, 256, smem_h, st>>>(D->tok, D->embed, D->h, nullptr,
+                                                  D->layers[0].gattn, D->x,
+                                                  fast_h ? D->ws_qkv : nullptr, B, H, eps);
+  count_launches(1);
+  if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: embed");
+  const AttnGeom geom = attn_geom(B, D->hr * hd, D->hr, D->kvr, c.max_seq,
+                                  (uint64_t)c.max_batch * c.max_seq * D->kvr * hd);
+  for (uint32_t l = 0; l < c.layers; l++) {
+    Layer &L = D->layers[l];
+    e = ternary_main_launch(1, D->x, 0, L.wqkv, 0, L.sqkv, 0, nullptr, D->qkv, 0, B, D->qkv_rows,
+                            H, false, fast_h ? D->ws_qkv : nullptr, st);
+    if (e != cudaSuccess) return cuda_status(e, "step: qkv");
+    const uint64_t nrope = (uint64_t)B * (D->hr + 2 * D->kvr) * (hd / 2);
+    k_rope_append<<<grid_for(nrope, 256), 256, 0, st>>>(D->qkv, D->q, L.ck, L.cv, D->pos, B,
+                                                        D->hr, D->kvr, hd, c.max_seq,
+                                                        c.rope_base);
+    count_launches(1);
+    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: rope");
+    e = attn_decode_launch(D->q, L.ck, L.cv, D->posf, D->ctx, geom, D->attn_scr, st);
+    if (e != cudaSuccess) return cuda_status(e, "step: attention");
+    if (fast_o) {
+      e = ternary_prep_launch(D->ctx, 0, 1, B, D->hr * hd, D->ws_o, st);
+      if (e != cudaSuccess) return cuda_status(e, "step: o prep");
+    }
+    e = ternary_main_launch(1, D->ctx, 0, L.wo, 0, L.so, 0, nullptr, D->o, 0, B, H, D->hr * hd,
+                            false, fast_o ? D->ws_o : nullptr, st);
+    if (e != cudaSuccess) return cuda_status(e, "step: o");
+    if ((rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+    k_norm<kNormAdd><<<gnorm, 256, smem_h, st>>>(nullptr, nullptr, D->h, D->o, L.gffn, D->x,
+                                                 fast_h ? D->ws_gu : nullptr, B, H, eps);
+    count_launches(1);
+    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: ffn norm");
+    e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
+                            false, fast_h ? D->ws_gu : nullptr, st);
+    if (e != cudaSuccess) return cuda_status(e, "step: gate/up");
+    k_silu_prep<<<gnorm, 256, (size_t)D->fr * sizeof(float), st>>>(
+        D->gu, D->a, fast_d ? D->ws_d : nullptr, B, D->fr);
+    count_launches(1);
+    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: swiglu");
+    e = ternary_main_launch(1, D->a, 0, L.wd, 0, L.sd, 0, nullptr, D->d, 0, B, H, D->fr, false,
+                            fast_d ? D->ws_d : nullptr, st);
+    if (e != cudaSuccess) return cuda_status(e, "step: down");
+    if ((rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+    const bool last = l + 1 == c.layers;
+    k_norm<kNormAdd><<<gnorm, 256, smem_h, st>>>(
+        nullptr, nullptr, D->h, D->d, last ? D->gfinal : D->layers[l + 1].gattn, D->x,
+        (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps);
+    count_launches(1);
+    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: attn norm");
+  }
+  const size_t smem_lm = (size_t)(B <= 1 ? 1 : (B <= 2 ? 2 : (B <= 4 ? 4 : (B <= 8 ? 8 : 16)))) *
+                         H * sizeof(float);
+  const unsigned lmgrid = 148 * 4;
+  const float *E = D->embed + (size_t)D->v0 * H;
+  float *lg = D->keep_logits ? D->logits : nullptr;
+  const uint32_t lstride = c.max_batch * D->vr;
+#define NL_LM(NB)                                                                          \
+  k_lmhead<NB><<<lmgrid, 256, smem_lm, st>>>(E, D->x, D->keys, lg, D->pos, B, D->vr, D->v0, \
+                                              H, lstride)
+  if (B <= 1) NL_LM(1);
+  else if (B <= 2) NL_LM(2);
+  else if (B <= 4) NL_LM(4);
+  else if (B <= 8) NL_LM(8);
+  else NL_LM(16);
+#undef NL_LM
+  count_launches(1);
+  if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: lm head");
+  if ((rc = allreduce(D, D->keys, B, kNcclUint64, kNcclMax))) return rc;
+  k_next<<<1, 32, 0, st>>>(D->keys, D->prompt, D->last_positions, D->tok, D->out_tok, D->pos,
+                           D->posf, B);
+  count_launches(1);
+  return cuda_status(cudaPeekAtLastError(), "step: next");
+}
+
+int set_smem_limits(nl_decoder *D) {
+  const size_t lm = (size_t)16 * D->cfg.hidden * sizeof(float);
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(k_lmhead<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)lm)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_lmhead<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(lm / 2))) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_lmhead<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)(lm / 4))) != cudaSuccess)
+    return cuda_status(e, "decoder: lm head smem");
+  const size_t hs = (size_t)D->cfg.hidden * sizeof(float), fs = (size_t)D->fr * sizeof(float);
+  if ((e = cudaFuncSetAttribute(k_norm<kNormGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)hs)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_norm<kNormAdd>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)hs)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_silu_prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)fs)) != cudaSuccess)
+    return cuda_status(e, "decoder: smem");
+  return NL_OK;
+}
+
+}  // namespace
+}  // namespace nl
+
+using namespace nl;
+
+extern "C" int nl_nccl_unique_id(void *id_out) {
+  Nccl *n = nccl();
+  if (!n) return set_error(NL_ERROR, "libnccl.so.2 not available");
+  ncclUniqueId id;
+  ncclResult_t r = n->GetUniqueId(&id);
+  if (r != 0) return set_error(NL_ERROR, "ncclGetUniqueId failed (%d)", r);
+  memcpy(id_out, &id, sizeof(id));
+  return NL_OK;
+}
+
+extern "C" void nl_decoder_destroy(nl_decoder *D) {
+  if (!D) return;
+  if (D->stream) cudaStreamSynchronize(D->stream);
+  for (auto &kv : D->graphs) cudaGraphExecDestroy(kv.second);
+  D->graphs.clear();
+  if (D->comm && nccl()) nccl()->CommDestroy(D->comm);
+  for (void *p : D->allocs) cudaFree(p);
+  if (D->stream) cudaStreamDestroy(D->stream);
+  delete D;
+}
+
+static int decoder_build(nl_decoder *D) {
+  const nl_decoder_config &c = D->cfg;
+  const uint32_t H = c.hidden, hd = c.head_dim;
+  const uint32_t grp = c.heads / c.kv_heads;
+  D->kvh = split(c.kv_heads, D->size, D->rank);
+  D->ffb = split(c.ffn / 128, D->size, D->rank);
+  D->voc = split(c.vocab, D->size, D->rank);
+  D->kvr = D->kvh.count;
+  D->hr = D->kvr * grp;
+  D->fr = D->ffb.count * 128;
+  D->vr = D->voc.count;
+  D->v0 = D->voc.begin;
+  D->qkv_rows = (D->hr + 2 * D->kvr) * hd;
+  if (D->kvr == 0 || D->fr == 0 || D->vr == 0)
+    return set_error(NL_ERROR, "decoder: %d ranks leave rank %d without heads, FFN blocks or vocab",
+                     D->size, D->rank);
+  cudaError_t e = cudaStreamCreateWithFlags(&D->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return cuda_status(e, "decoder: stream");
+  const uint32_t h0 = D->kvh.begin * grp, kv0 = D->kvh.begin, f0 = D->ffb.begin * 128;
+  const uint32_t qd = c.heads * hd, kvd = c.kv_heads * hd;
+  uint64_t wb = 0;
+  D->layers.resize(c.layers);
+  for (uint32_t l = 0; l < c.layers; l++) {
+    Layer &L = D->layers[l];
+    const uint64_t T = (uint64_t)l * 16;
+    const size_t wq = (size_t)D->qkv_rows * (H / 16), wo = (size_t)H * (D->hr * hd / 16);
+    const size_t wgu = (size_t)2 * D->fr * (H / 16), wdn = (size_t)H * (D->fr / 16);
+    DALLOC(L.wqkv, wq * 4);
+    DALLOC(L.wo, wo * 4);
+    DALLOC(L.wgu, wgu * 4);
+    DALLOC(L.wd, wdn * 4);
+    DALLOC(L.sqkv, (size_t)D->qkv_rows * 4);
+    DALLOC(L.so, (size_t)H * 4);
+    DALLOC(L.sgu, (size_t)2 * D->fr * 4);
+    DALLOC(L.sd, (size_t)H * 4);
+    DALLOC(L.gattn, (size_t)H * 4);
+    DALLOC(L.gffn, (size_t)H * 4);
+    const size_t cache = (size_t)c.max_batch * c.max_seq * D->kvr * hd * 4;
+    DALLOC(L.ck, cache);
+    DALLOC(L.cv, cache);
+    wb += (wq + wo + wgu + wdn) * 4 + ((size_t)D->qkv_rows + 2 * H + 2 * D->fr) * 4 + 2 * H * 4;
+    const uint32_t rq = D->hr * hd, rk = D->kvr * hd;
+    int rc;
+    if ((rc = gen_ternary(D, L.wqkv, rq, H, T + NL_T_WQ, (uint64_t)h0 * hd, H, 0)) ||
+        (rc = gen_ternary(D, L.wqkv + (size_t)rq * (H / 16), rk, H, T + NL_T_WK,
+                          (uint64_t)kv0 * hd, H, 0)) ||
+        (rc = gen_ternary(D, L.wqkv + (size_t)(rq + rk) * (H / 16), rk, H, T + NL_T_WV,
+                          (uint64_t)kv0 * hd, H, 0)) ||
+        (rc = gen_scale(D, L.sqkv, rq, T + NL_T_SQ, (uint64_t)h0 * hd, H)) ||
+        (rc = gen_scale(D, L.sqkv + rq, rk, T + NL_T_SK, (uint64_t)kv0 * hd, H)) ||
+        (rc = gen_scale(D, L.sqkv + rq + rk, rk, T + NL_T_SV, (uint64_t)kv0 * hd, H)) ||
+        (rc = gen_ternary(D, L.wo, H, rq, T + NL_T_WO, 0, qd, (uint64_t)h0 * hd)) ||
+        (rc = gen_scale(D, L.so, H, T + NL_T_SO, 0, qd)) ||
+        (rc = gen_ternary(D, L.wgu, D->fr, H, T + NL_T_WGATE, f0, H, 0)) ||
+        (rc = gen_ternary(D, L.wgu + (size_t)D->fr * (H / 16), D->fr, H, T + NL_T_WUP, f0, H, 0)) ||
+        (rc = gen_scale(D, L.sgu, D->fr, T + NL_T_SGATE, f0, H)) ||
+        (rc = gen_scale(D, L.sgu + D->fr, D->fr, T + NL_T_SUP, f0, H)) ||
+        (rc = gen_ternary(D, L.wd, H, D->fr, T + NL_T_WDOWN, 0, c.ffn, f0)) ||
+        (rc = gen_scale(D, L.sd, H, T + NL_T_SDOWN, 0, c.ffn)) ||
+        (rc = gen_norm(D, L.gattn, H, T + NL_T_ATTN_NORM)) ||
+        (rc = gen_norm(D, L.gffn, H, T + NL_T_FFN_NORM)))
+      return rc;
+    (void)kvd;
+  }
+  const size_t en = (size_t)c.vocab * H;
+  DALLOC(D->embed, en * 4);
+  DALLOC(D->gfinal, (size_t)H * 4);
+  gen_embed_kernel<<<grid_for(en, 256), 256, 0, D->stream>>>(
+      D->embed, en, nl_tensor_key(c.seed, NL_T_EMBED));
+  int rc;
+  if ((rc = cuda_status(cudaPeekAtLastError(), "decoder: embedding"))) return rc;
+  if ((rc = gen_norm(D, D->gfinal, H, NL_T_FINAL_NORM))) return rc;
+  wb += (size_t)D->vr * H * 4 + (size_t)H * 4;
+  D->weight_bytes = wb;
+  const uint32_t B = c.max_batch;
+  DALLOC(D->h, (size_t)B * H * 4);
+  DALLOC(D->x, (size_t)B * H * 4);
+  DALLOC(D->qkv, (size_t)B * D->qkv_rows * 4);
+  DALLOC(D->q, (size_t)B * D->hr * hd * 4);
+  DALLOC(D->ctx, (size_t)B * D->hr * hd * 4);
+  DALLOC(D->o, (size_t)B * H * 4);
+  DALLOC(D->gu, (size_t)B * 2 * D->fr * 4);
+  DALLOC(D->a, (size_t)B * D->fr * 4);
+  DALLOC(D->d, (size_t)B * H * 4);
+  DALLOC(D->posf, 16);
+  DALLOC(D->pos, 16);
+  DALLOC(D->tok, (size_t)B * 4);
+  DALLOC(D->keys, (size_t)B * 8);
+  DALLOC(D->prompt, (size_t)B * c.max_seq * 4);
+  DALLOC(D->out_tok, (size_t)B * c.max_seq * 4);
+  DALLOC(D->ws_qkv, ternary_ws_bytes(1, B, H));
+  DALLOC(D->ws_gu, ternary_ws_bytes(1, B, H));
+  DALLOC(D->ws_o, ternary_ws_bytes(1, B, D->hr * hd));
+  DALLOC(D->ws_d, ternary_ws_bytes(1, B, D->fr));
+  size_t scr = 0;   // the split count grows as the batch shrinks: size for every batch
+  for (uint32_t bb = 1; bb <= B; bb++) {
+    const AttnGeom g = attn_geom(bb, D->hr * hd, D->hr, D->kvr, c.max_seq,
+                                 (uint64_t)B * c.max_seq * D->kvr * hd);
+    if (attn_scratch_bytes(g) > scr) scr = attn_scratch_bytes(g);
+  }
+  DALLOC(D->attn_scr, scr + 256);
+  if (D->keep_logits) DALLOC(D->logits, (size_t)c.max_seq * B * D->vr * 4);
+  if ((rc = set_smem_limits(D))) return rc;
+  return cuda_status(cudaStreamSynchronize(D->stream), "decoder: build");
+}
+
+extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int tp_size,
+                                 const void *nccl_id, int keep_logits, nl_decoder **out) {
+  *out = nullptr;
+  int rc = nl_init(-1);
+  if (rc) return rc;
+  const nl_decoder_config &c = *cfg;
+  if (c.hidden == 0 || c.hidden % 128 || c.ffn == 0 || c.ffn % 128 || c.head_dim % 16 ||
+      c.head_dim == 0 || c.heads == 0 || c.kv_heads == 0 || c.heads % c.kv_heads ||
+      c.max_batch == 0 || c.max_batch > 16 || c.max_seq == 0 || c.vocab == 0 || c.layers == 0)
+    return set_error(NL_ERROR,
+                     "decoder config: hidden and ffn multiples of 128, head_dim of 16, heads a "
+                     "multiple of kv_heads, 1 <= max_batch <= 16");
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size)
+    return set_error(NL_ERROR, "decoder: rank %d of %d", tp_rank, tp_size);
+  nl_decoder *D = new nl_decoder();
+  D->cfg = c;
+  D->rank = tp_rank;
+  D->size = tp_size;
+  D->keep_logits = keep_logits != 0;
+  if (tp_size > 1) {
+    Nccl *n = nccl();
+    if (!n) { delete D; return set_error(NL_ERROR, "libnccl.so.2 not available"); }
+    ncclUniqueId id;
+    memcpy(&id, nccl_id, sizeof(id));
+    ncclResult_t r = n->CommInitRank(&D->comm, tp_size, id, tp_rank);
+    if (r != 0) {
+      delete D;
+      return set_error(NL_ERROR, "ncclCommInitRank: %s", n->GetErrorString ? n->GetErrorString(r) : "?");
+    }
+  }
+  if ((rc = decoder_build(D))) {
+    nl_decoder_destroy(D);
+    return rc;
+  }
+  *out = D;
+  return NL_OK;
+}
+
+extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t prompt_len,
+                                   const int32_t *prompt, uint32_t steps, int32_t *out_tokens,
+                                   double *prefill_ms, double *decode_ms) {
+  const nl_decoder_config &c = D->cfg;
+  if (batch == 0 || batch > c.max_batch || prompt_len == 0 || steps == 0 ||
+      prompt_len + steps - 1 > c.max_seq)
+    return set_error(NL_ERROR, "generate: batch %u (max %u), prompt %u + steps %u - 1 > max_seq %u",
+                     batch, c.max_batch, prompt_len, steps, c.max_seq);
+  for (uint64_t i = 0; i < (uint64_t)batch * prompt_len; i++)
+    if (prompt[i] < 0 || (uint32_t)prompt[i] >= c.vocab)
+      return set_error(NL_ERROR, "generate: token %d out of range", prompt[i]);
+  cudaStream_t st = D->stream;
+  cudaError_t e =
+      cudaMemcpyAsync(D->prompt, prompt, (size_t)batch * prompt_len * 4, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return cuda_status(e, "generate: prompt");
+  D->last_positions = prompt_len;
+  int rc;
+  auto it = D->graphs.find(batch * 100000u + prompt_len);
+  if (it == D->graphs.end()) {
+    // One eager step first (kernel attributes, NCCL connections), then capture.
+    k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->keys, D->pos, D->posf, batch);
+    if ((rc = enqueue_step(D, batch))) return rc;
+    if ((rc = cuda_status(cudaStreamSynchronize(st), "generate: warm-up"))) return rc;
+    uint64_t before = nl_launch_count();
+    cudaGraph_t graph;
+    if ((e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+      return cuda_status(e, "generate: capture");
+    rc = enqueue_step(D, batch);
+    e = cudaStreamEndCapture(st, &graph);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_status(e, "generate: end capture");
+    D->kernels_per_step = nl_launch_count() - before;
+    cudaGraphExec_t exec;
+    e = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return cuda_status(e, "generate: instantiate");
+    it = D->graphs.emplace(batch * 100000u + prompt_len, exec).first;
+  }
+  cudaGraphExec_t exec = it->second;
+  k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->keys, D->pos, D->posf, batch);
+  cudaEvent_t e0, e1, e2;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventCreate(&e2);
+  cudaEventRecord(e0, st);
+  for (uint32_t i = 0; i + 1 < prompt_len; i++) cudaGraphLaunch(exec, st);
+  cudaEventRecord(e1, st);
+  for (uint32_t i = 0; i < steps; i++) cudaGraphLaunch(exec, st);
+  cudaEventRecord(e2, st);
+  rc = cuda_status(cudaStreamSynchronize(st), "generate");
+  float a = 0.0f, b = 0.0f;
+  cudaEventElapsedTime(&a, e0, e1);
+  cudaEventElapsedTime(&b, e1, e2);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  cudaEventDestroy(e2);
+  if (rc) return rc;
+  count_launches(D->kernels_per_step * (prompt_len - 1 + steps));
+  if (prefill_ms) *prefill_ms = a;
+  if (decode_ms) *decode_ms = b;
+  D->last_batch = batch;
+  std::vector<int32_t> tmp((size_t)steps * batch);
+  e = cudaMemcpy(tmp.data(), D->out_tok, tmp.size() * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_status(e, "generate: tokens");
+  for (uint32_t i = 0; i < steps; i++)
+    for (uint32_t bb = 0; bb < batch; bb++) out_tokens[(size_t)bb * steps + i] = tmp[(size_t)i * batch + bb];
+  return NL_OK;
+}
+
+extern "C" int nl_decoder_logits(nl_decoder *D, float *out, uint64_t nfloats) {
+  if (!D->keep_logits) return set_error(NL_ERROR, "decoder created without keep_logits");
+  uint64_t have = (uint64_t)D->cfg.max_seq * D->cfg.max_batch * D->vr;
+  if (nfloats > have) nfloats = have;
+  return cuda_status(cudaMemcpy(out, D->logits, nfloats * 4, cudaMemcpyDeviceToHost), "logits");
+}
+
+extern "C" int nl_decoder_info(nl_decoder *D, uint32_t *shard, uint64_t *weight_bytes,
+                               uint64_t *kernels_per_step) {
+  if (shard) {
+    shard[0] = D->kvh.begin;
+    shard[1] = D->kvh.count;
+    shard[2] = D->ffb.begin * 128;
+    shard[3] = D->fr;
+    shard[4] = D->v0;
+    shard[5] = D->vr;
+  }
+  if (weight_bytes) *weight_bytes = D->weight_bytes;
+  if (kernels_per_step) *kernels_per_step = D->kernels_per_step;
+  return NL_OK;
+}

@@ -81,6 +81,13 @@ SIGNATURES = {
     "nl_ternary_gemv_batched_dev": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
                                          _u32, _u32, _u32, _vp, _sz, _vp]),
     "nl_launch_count": (_u64, []),
+    # decoder (nelisp_cuda.decoder rebinds these with the config struct)
+    "nl_nccl_unique_id": (_i, [_vp]),
+    "nl_decoder_create": (_i, [_vp, _i, _i, _vp, _i, ctypes.POINTER(_vp)]),
+    "nl_decoder_generate": (_i, [_vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp]),
+    "nl_decoder_logits": (_i, [_vp, _vp, _u64]),
+    "nl_decoder_info": (_i, [_vp, _vp, _vp, _vp]),
+    "nl_decoder_destroy": (None, [_vp]),
 }
 
 _lib = None

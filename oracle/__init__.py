@@ -72,6 +72,8 @@ def _declare(L):
         "nlo_matmul_sample_ref": [_u32] * 4,
         "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
         "nlo_set_threads": [ctypes.c_int],
+        "nlo_decoder_generate": [ctypes.c_void_p, _u32, _u32, ctypes.POINTER(ctypes.c_int32), _u32,
+                                 ctypes.POINTER(ctypes.c_int32), _F],
         "nlo_threads": [],
     }
     for name, argt in sigs.items():
@@ -80,6 +82,7 @@ def _declare(L):
         fn.restype = None
     L.nlo_matmul_sample_ref.restype = ctypes.c_double
     L.nlo_threads.restype = ctypes.c_int
+    L.nlo_decoder_generate.restype = ctypes.c_int
 
 
 def _f(a):
@@ -269,6 +272,35 @@ def softmax_ref_f64(A, M, N):
     C = np.zeros(M * N, np.float64)
     lib().nlo_softmax_ref_f64(A.ctypes.data_as(_D), C.ctypes.data_as(_D), M, N)
     return C
+
+
+# ---- decoder --------------------------------------------------------------
+
+class DecoderConfig(ctypes.Structure):
+    """Field layout of nl_decoder_config (include/nelisp_cuda.h)."""
+    _fields_ = [("hidden", _u32), ("layers", _u32), ("heads", _u32), ("kv_heads", _u32),
+                ("head_dim", _u32), ("ffn", _u32), ("vocab", _u32), ("max_batch", _u32),
+                ("max_seq", _u32), ("rms_eps", ctypes.c_float), ("rope_base", ctypes.c_float),
+                ("seed", ctypes.c_uint64)]
+
+
+def decoder_generate(cfg: dict, prompt, steps: int, keep_logits: bool = False):
+    """Greedy generation by the CPU model (nl_oracle_decoder.c).  PROMPT is
+    [batch x prompt_len] int; returns (tokens [batch x steps], logits
+    [positions x batch x vocab] or None)."""
+    prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+    B, P = prompt.shape
+    c = DecoderConfig(**cfg)
+    out = np.zeros((B, steps), np.int32)
+    npos = P + steps - 1
+    lg = np.zeros((npos, B, cfg["vocab"]), np.float32) if keep_logits else None
+    rc = lib().nlo_decoder_generate(ctypes.byref(c), B, P,
+                                    prompt.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), steps,
+                                    out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                                    lg.ctypes.data_as(_F) if lg is not None else None)
+    if rc != 0:
+        raise RuntimeError(f"nlo_decoder_generate: {rc}")
+    return out, lg
 
 
 # ---- metrics -------------------------------------------------------------

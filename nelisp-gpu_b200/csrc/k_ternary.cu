@@ -35,6 +35,7 @@
 // the CUDA cores with the generic kernel's arithmetic.
 
 #include <cuda.h>
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -45,6 +46,7 @@
 #include "ternary_prep.cuh"
 
 namespace nl {
+namespace cg = cooperative_groups;
 namespace {
 
 constexpr int kDepth = 8;        // 128-column blocks in flight per warp
@@ -153,16 +155,54 @@ ternary_generic_kernel(const float *__restrict__ X, uint64_t x_stride,
 // The fragment format and the activation prep live in ternary_prep.cuh, shared
 // with the decoder's fused normalisation kernels.
 
-// grid (ceil(8*NT/3), count), 256 threads.  CTA s handles sequence row s
-// (rows s >= seq write the zero padding of the last n-tile).
-__global__ void __launch_bounds__(256)
+// grid (kRowCluster * ceil(8*NT/3), count), kPrepThreads threads, clusters of
+// kRowCluster CTAs.  Cluster s handles sequence row s of problem z (rows
+// s >= seq write the zero padding of the last n-tile); each CTA takes a
+// column slice, and the row maximum is combined through distributed shared
+// memory in rank order, so every CTA scales the row by the same power of two.
+constexpr int kPrepThreads = 128;
+__global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kPrepThreads)
 ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
                     uint32_t seq, uint32_t cols, void *ws) {
-  __shared__ float red[34];
-  const uint32_t s = blockIdx.x, z = blockIdx.y;
-  PrepOut P = prep_at(ws, (int)seq, cols, z);
-  const float *xr = s < seq ? X + z * x_stride + (size_t)s * cols : nullptr;
-  prep_row(xr, cols, s, seq, P, red);
+  __shared__ float red[32];
+  __shared__ float s_max;
+  __shared__ int s_bad;
+  cg::cluster_group cl = cg::this_cluster();
+  const uint32_t rank = cl.block_rank();
+  const uint32_t s = blockIdx.x / kRowCluster, z = blockIdx.y;
+  const RowSlice sl = row_slice(cols, rank);
+  const bool live = s < seq;
+  const float *xr = X + z * x_stride + (size_t)s * cols;
+  float m = 0.0f;
+  int bad = 0;
+  if (live) {
+    for (uint32_t i = sl.c0 + threadIdx.x; i < sl.c1; i += blockDim.x) {
+      const float v = xr[i];
+      m = fmaxf(m, fabsf(v));
+      bad |= !isfinite(v);        // NaN is dropped by fmaxf; catch it here
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  bad = __syncthreads_or(bad);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) r = fmaxf(r, red[i]);
+    s_max = r;
+    s_bad = bad;
+  }
+  cl.sync();
+  float mm = 0.0f;
+  int anybad = 0;
+#pragma unroll
+  for (int k = 0; k < kRowCluster; k++) {
+    mm = fmaxf(mm, *cl.map_shared_rank(&s_max, k));
+    anybad |= *cl.map_shared_rank(&s_bad, k);
+  }
+  quantize_slice(xr + sl.c0, sl, mm, anybad != 0, live, rank == 0, s, seq,
+                 prep_at(ws, (int)seq, cols, z));
+  cl.sync();                      // no CTA leaves while its maximum is read
 }
 
 // ---------------------------------------------------------------------------
@@ -837,8 +877,8 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
   for (uint32_t s0 = 0; s0 < seq; s0 += kMaxFastSeq) {
     uint32_t ns = min((uint32_t)kMaxFastSeq, seq - s0);
     int NT = n_tiles((int)ns);
-    dim3 pgrid((8 * NT + 2) / 3, count);
-    ternary_prep_kernel<<<pgrid, 256, 0, stream>>>(X + (uint64_t)s0 * cols,
+    dim3 pgrid(kRowCluster * ((8 * NT + 2) / 3), count);
+    ternary_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(X + (uint64_t)s0 * cols,
                                                     x_stride, ns, cols, ws);
     cudaError_t e = cudaPeekAtLastError();
     if (e != cudaSuccess) return e;
@@ -879,8 +919,8 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
 cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
                                 uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream) {
   if (count == 0 || seq == 0) return cudaSuccess;
-  dim3 pgrid((8 * n_tiles((int)seq) + 2) / 3, count);
-  ternary_prep_kernel<<<pgrid, 256, 0, stream>>>(X, x_stride, seq, cols, ws);
+  dim3 pgrid(kRowCluster * ((8 * n_tiles((int)seq) + 2) / 3), count);
+  ternary_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(X, x_stride, seq, cols, ws);
   count_launches(1);
   return cudaPeekAtLastError();
 }

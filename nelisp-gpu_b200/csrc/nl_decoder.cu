@@ -26,6 +26,7 @@
 // max.  Every rank generates its own shard of the synthetic weights from
 // global element indices (nl_rng.h), so no weights cross the links.
 
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
@@ -124,51 +125,101 @@ __global__ void gen_embed_kernel(float *E, uint64_t n, uint64_t key) {
 }
 
 // ---- step kernels ---------------------------------------------------------------------
-__device__ float block_reduce_sum(float v, float *red) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float r = 0.0f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); i++) r += red[i];
+namespace cg = cooperative_groups;
+
+enum { kNormGather = 0, kNormAdd = 1 };
+constexpr int kNormThreads = 128;   // per CTA of a row cluster
+
+// Row statistics exchanged between the CTAs of a row cluster.
+struct RowStats {
+  float v;     // partial sum of squares, then partial max |x|
+  int bad;     // a non-finite value in this CTA's slice
+};
+
+// Sum (MAX = false) or maximum of the cluster's RowStats, read from every
+// CTA's shared memory in rank order so that all CTAs get the same bits.
+template <bool MAX>
+__device__ __forceinline__ RowStats cluster_combine(cg::cluster_group &cl, RowStats *mine) {
+  cl.sync();
+  RowStats r{0.0f, 0};
+#pragma unroll
+  for (int k = 0; k < kRowCluster; k++) {
+    const RowStats *o = cl.map_shared_rank(mine, k);
+    r.v = MAX ? fmaxf(r.v, o->v) : r.v + o->v;
+    r.bad |= o->bad;
+  }
   return r;
 }
 
-enum { kNormGather = 0, kNormAdd = 1 };
+// CTA-wide reduction of one value per thread into *OUT (thread 0 writes).
+template <bool MAX>
+__device__ __forceinline__ void cta_reduce(float v, int bad, float *red, RowStats *out) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, w) : v + w;
+  }
+  bad = __syncthreads_or(bad);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) r = MAX ? fmaxf(r, red[i]) : r + red[i];
+    out->v = r;
+    out->bad = bad;
+  }
+}
 
-// One CTA per sequence row b: h = E[tok] (gather) or h = h + delta (add);
-// x = (h * rsqrt(mean h^2 + eps)) * g; then x is converted into the next
-// GEMV's activation fragments.  CTAs b >= B write the fragment padding.
+// One cluster of kRowCluster CTAs per sequence row b: h = E[tok] (gather) or
+// h = h + delta (add); x = (h * rsqrt(mean h^2 + eps)) * g; then x is
+// converted into the next GEMV's activation fragments (when WS is set).
+// Clusters b >= B write the fragment padding.  Each CTA owns a column slice;
+// the sum of squares and the maximum of x are combined across the cluster.
 template <int MODE>
-__global__ void __launch_bounds__(256)
+__global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kNormThreads)
 k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restrict__ h,
        const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
        void *ws, uint32_t B, uint32_t H, float eps) {
   extern __shared__ __align__(16) float xs[];
-  __shared__ float red[34];
-  const uint32_t b = blockIdx.x;
-  PrepOut P = prep_at(ws, (int)B, H, 0);
-  if (b < B) {
+  __shared__ float red[32];
+  __shared__ RowStats st[2];
+  cg::cluster_group cl = cg::this_cluster();
+  const uint32_t rank = cl.block_rank();
+  const uint32_t b = blockIdx.x / kRowCluster;
+  const RowSlice sl = row_slice(H, rank);
+  const bool live = b < B;
+  float mm = 0.0f;
+  int bad = 0;
+  if (live) {
     float *hb = h + (size_t)b * H;
     const float *src = MODE == kNormGather ? E + (size_t)__ldg(tok + b) * H : nullptr;
     float ss = 0.0f;
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
+    for (uint32_t i = sl.c0 + threadIdx.x; i < sl.c1; i += blockDim.x) {
       float v = MODE == kNormGather ? __ldg(src + i) : __fadd_rn(hb[i], delta[(size_t)b * H + i]);
       hb[i] = v;
-      xs[i] = v;
+      xs[i - sl.c0] = v;
       ss = fmaf(v, v, ss);
     }
-    ss = block_reduce_sum(ss, red);
-    const float rinv = 1.0f / sqrtf(ss / (float)H + eps);
-    for (uint32_t i = threadIdx.x; i < H; i += blockDim.x) {
-      float xv = __fmul_rn(__fmul_rn(xs[i], rinv), __ldg(g + i));
-      xs[i] = xv;
+    cta_reduce<false>(ss, 0, red, &st[0]);
+    const RowStats tot = cluster_combine<false>(cl, &st[0]);
+    const float rinv = 1.0f / sqrtf(tot.v / (float)H + eps);
+    for (uint32_t i = sl.c0 + threadIdx.x; i < sl.c1; i += blockDim.x) {
+      const float xv = __fmul_rn(__fmul_rn(xs[i - sl.c0], rinv), __ldg(g + i));
+      xs[i - sl.c0] = xv;
       x[(size_t)b * H + i] = xv;
+      mm = fmaxf(mm, fabsf(xv));
+      bad |= !isfinite(xv);      // NaN is dropped by fmaxf; catch it here
     }
-    if (ws) prep_row(xs, H, b, B, P, red);
-  } else if (ws) {
-    prep_row(nullptr, H, b, B, P, red);
+  } else {
+    cl.sync();                   // keep the cluster's barrier count uniform
   }
+  cta_reduce<true>(mm, bad, red, &st[1]);
+  const RowStats mx = cluster_combine<true>(cl, &st[1]);
+  if (ws) {
+    __syncthreads();
+    quantize_slice(xs, sl, mx.v, mx.bad != 0, live, rank == 0, b, B,
+                   prep_at(ws, (int)B, H, 0));
+  }
+  cl.sync();                     // no CTA leaves while its statistics are read
 }
 
 // q/k rotation (half-split, position *pos), k and v appended to the cache.
@@ -205,27 +256,42 @@ __global__ void k_rope_append(const float *__restrict__ qkv, float *__restrict__
   }
 }
 
-// a = silu(gate) * up for one sequence row per CTA, then the down GEMV's prep.
-__global__ void __launch_bounds__(256)
+// a = silu(gate) * up, then the down GEMV's prep: one cluster per sequence
+// row, each CTA on its column slice, the row maximum combined across the
+// cluster.
+__global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kNormThreads)
 k_silu_prep(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint32_t B,
             uint32_t fr) {
   extern __shared__ __align__(16) float xs[];
-  __shared__ float red[34];
-  const uint32_t b = blockIdx.x;
-  PrepOut P = prep_at(ws, (int)B, fr, 0);
-  if (b < B) {
+  __shared__ float red[32];
+  __shared__ RowStats st;
+  cg::cluster_group cl = cg::this_cluster();
+  const uint32_t rank = cl.block_rank();
+  const uint32_t b = blockIdx.x / kRowCluster;
+  const RowSlice sl = row_slice(fr, rank);
+  const bool live = b < B;
+  float mm = 0.0f;
+  int bad = 0;
+  if (live) {
     const float *gr = gu + (size_t)b * 2 * fr;
-    for (uint32_t j = threadIdx.x; j < fr; j += blockDim.x) {
+    for (uint32_t j = sl.c0 + threadIdx.x; j < sl.c1; j += blockDim.x) {
       const float gv = gr[j], uv = gr[fr + j];
       const float sg = 1.0f / (1.0f + expf(-gv));
       const float v = __fmul_rn(__fmul_rn(gv, sg), uv);
-      xs[j] = v;
+      xs[j - sl.c0] = v;
       a[(size_t)b * fr + j] = v;
+      mm = fmaxf(mm, fabsf(v));
+      bad |= !isfinite(v);
     }
-    if (ws) prep_row(xs, fr, b, B, P, red);
-  } else if (ws) {
-    prep_row(nullptr, fr, b, B, P, red);
   }
+  cta_reduce<true>(mm, bad, red, &st);
+  const RowStats mx = cluster_combine<true>(cl, &st);
+  if (ws) {
+    __syncthreads();
+    quantize_slice(xs, sl, mx.v, mx.bad != 0, live, rank == 0, b, B,
+                   prep_at(ws, (int)B, fr, 0));
+  }
+  cl.sync();
 }
 
 // Order-preserving 64-bit argmax key: larger logit first, then lower index.
@@ -429,14 +495,14 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   const float eps = c.rms_eps;
   cudaStream_t st = D->stream;
   const uint32_t npad = (uint32_t)(8 * n_tiles((int)B) + 2) / 3;
-  const uint32_t gnorm = B > npad ? B : npad;
-  const size_t smem_h = (size_t)H * sizeof(float);
+  const uint32_t gnorm = (B > npad ? B : npad) * kRowCluster;
+  const size_t smem_h = (size_t)row_slice_cols(H) * sizeof(float);
   const bool fast_o = ternary_fast_shape(D->hr * hd, D->hr * hd / 128, D->hr * hd / 16, false);
   const bool fast_d = ternary_fast_shape(D->fr, D->fr / 128, D->fr / 16, false);
   const bool fast_h = ternary_fast_shape(H, H / 128, H / 16, false);
   int rc;
   cudaError_t e;
-  k_norm<kNormGather><<<gnorm, 256, smem_h, st>>>(D->tok, D->embed, D->h, nullptr,
+  k_norm<kNormGather><<<gnorm, kNormThreads, smem_h, st>>>(D->tok, D->embed, D->h, nullptr,
                                                   D->layers[0].gattn, D->x,
                                                   fast_h ? D->ws_qkv : nullptr, B, H, eps);
   count_launches(1);
@@ -464,14 +530,14 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
                             false, fast_o ? D->ws_o : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: o");
     if ((rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
-    k_norm<kNormAdd><<<gnorm, 256, smem_h, st>>>(nullptr, nullptr, D->h, D->o, L.gffn, D->x,
+    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->h, D->o, L.gffn, D->x,
                                                  fast_h ? D->ws_gu : nullptr, B, H, eps);
     count_launches(1);
     if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: ffn norm");
     e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
                             false, fast_h ? D->ws_gu : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: gate/up");
-    k_silu_prep<<<gnorm, 256, (size_t)D->fr * sizeof(float), st>>>(
+    k_silu_prep<<<gnorm, kNormThreads, (size_t)row_slice_cols(D->fr) * sizeof(float), st>>>(
         D->gu, D->a, fast_d ? D->ws_d : nullptr, B, D->fr);
     count_launches(1);
     if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: swiglu");
@@ -480,7 +546,7 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
     if (e != cudaSuccess) return cuda_status(e, "step: down");
     if ((rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
     const bool last = l + 1 == c.layers;
-    k_norm<kNormAdd><<<gnorm, 256, smem_h, st>>>(
+    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(
         nullptr, nullptr, D->h, D->d, last ? D->gfinal : D->layers[l + 1].gattn, D->x,
         (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps);
     count_launches(1);
@@ -520,7 +586,8 @@ int set_smem_limits(nl_decoder *D) {
       (e = cudaFuncSetAttribute(k_lmhead<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)(lm / 4))) != cudaSuccess)
     return cuda_status(e, "decoder: lm head smem");
-  const size_t hs = (size_t)D->cfg.hidden * sizeof(float), fs = (size_t)D->fr * sizeof(float);
+  const size_t hs = (size_t)row_slice_cols(D->cfg.hidden) * sizeof(float),
+               fs = (size_t)row_slice_cols(D->fr) * sizeof(float);
   if ((e = cudaFuncSetAttribute(k_norm<kNormGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)hs)) != cudaSuccess ||
       (e = cudaFuncSetAttribute(k_norm<kNormAdd>, cudaFuncAttributeMaxDynamicSharedMemorySize,

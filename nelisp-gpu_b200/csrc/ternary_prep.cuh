@@ -1,7 +1,7 @@
 // ternary_prep.cuh -- activation prep of the tensor-core ternary GEMV:
-// the fragment format and a CTA-level routine that converts one activation
-// row into exact int8 limbs in mma B-fragment order.  Shared by the GEMV's
-// own prep kernel and the decoder's fused normalisation epilogues.
+// the fragment format and the cluster-level routines that convert one
+// activation row into exact int8 limbs in mma B-fragment order.  Shared by
+// the GEMV's own prep kernel and the decoder's fused normalisation epilogues.
 //
 // Each row s is scaled by a power of two 2^e_s that puts max|x| in
 // [2^21, 2^22), rounded to an integer xq (the only inexact step: half a unit
@@ -58,99 +58,112 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
          ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
 }
 
-// CTA-level: convert row s (X_ROW, global or shared memory; NULL for the
-// padding rows s >= seq of the last n-tile, which are written as zeros) into
-// P's fragments, scale and flag.  RED is 34 floats of shared scratch.  Every
-// thread of the CTA must call it; it synchronises the CTA.
-__device__ __forceinline__ void prep_row(const float *x_row, uint32_t cols,
-                                         uint32_t s, uint32_t seq, PrepOut P,
-                                         float *red) {
-  const int NT = n_tiles((int)seq);
-  const float *xr = x_row;
-  float &s_mul = red[32];
-  int &s_ok = reinterpret_cast<int &>(red[33]);
-  const bool live = s < seq && xr != nullptr;
-  __syncthreads();
-  if (live) {
-    float m = 0.0f;
-    int bad = 0;
-    for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
-      float v = xr[i];
-      m = fmaxf(m, fabsf(v));
-      bad |= !isfinite(v);          // NaN is dropped by fmaxf; catch it here
-    }
-    bad = __syncthreads_or(bad);
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float mm = 0.0f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); w++) mm = fmaxf(mm, red[w]);
-      int ok = !bad;
-      float mul = 0.0f, inv = 0.0f;
-      if (ok && mm > 0.0f) {
-        int E;
-        frexpf(mm, &E);              // mm in [2^(E-1), 2^E)
-        int e = 22 - E;              // mm * 2^e in [2^21, 2^22)
-        if (e > 126 || e < -126) {
-          ok = 0;                    // 2^e or 2^-e would leave the normals
-        } else {
-          mul = ldexpf(1.0f, e);
-          inv = ldexpf(1.0f, -e);
-        }
-      }
-      s_mul = mul;
-      s_ok = ok;
-      P.rowinv[s] = inv;
-      P.rowflag[s] = !ok;
-    }
-    __syncthreads();
-  }
-  const float mul = live ? s_mul : 0.0f;
-  const bool ok = live && s_ok;
-  __syncthreads();
-  // One thread per packed word (16 columns).
-  const uint32_t nwords = cols / 16u;
-  for (uint32_t W = threadIdx.x; W < nwords; W += blockDim.x) {
-    int l[3][16];
+// Exponent of a row: 2^e puts the row maximum MM in [2^21, 2^22).  False
+// when the row cannot be represented (non-finite, or 2^e / 2^-e outside the
+// f32 normals); a zero row is representable with mul = inv = 0.
+__device__ __forceinline__ bool row_scale(float mm, bool bad, float *mul, float *inv) {
+  *mul = 0.0f;
+  *inv = 0.0f;
+  if (bad) return false;
+  if (!(mm > 0.0f)) return true;
+  int E;
+  frexpf(mm, &E);                      // mm in [2^(E-1), 2^E)
+  const int e = 22 - E;
+  if (e > 126 || e < -126) return false;
+  *mul = ldexpf(1.0f, e);
+  *inv = ldexpf(1.0f, -e);
+  return true;
+}
+
+// Quantize the 16 values V of packed word W of sequence row S into the
+// fragments of P (zeros when !OK): three balanced int8 limbs per value,
+// written in the column order of the weight operands (see the layout note).
+__device__ __forceinline__ void quantize_word(const float (&v)[16], float mul, bool ok,
+                                              uint32_t W, uint32_t s, int NT, PrepOut P) {
+  int l[3][16];
+#pragma unroll
+  for (int k = 0; k < 16; k++) {
     if (ok) {
-      const float4 *src = reinterpret_cast<const float4 *>(xr + 16u * W);
+      int qv = __float2int_rn(v[k] * mul);   // exact scaling, one rounding
+      int l0 = (int)(int8_t)(qv & 0xff);
+      int r = (qv - l0) >> 8;
+      int l1 = (int)(int8_t)(r & 0xff);
+      int l2 = (r - l1) >> 8;                // |qv| <= 2^22 -> |l2| <= 64
+      l[0][k] = l0; l[1][k] = l1; l[2][k] = l2;
+    } else {
+      l[0][k] = l[1][k] = l[2][k] = 0;
+    }
+  }
+  const uint32_t blk = W / 8u, wq = W % 8u;
+  const uint32_t q = wq >> 1;
+#pragma unroll
+  for (int li = 0; li < 3; li++) {
+    int n = 3 * (int)s + li;
+    if (n >= 8 * NT) continue;
+#pragma unroll
+    for (int jlo = 0; jlo < 2; jlo++) {
+      const int k = 2 * jlo;
+      const uint32_t j = ((wq & 1u) << 1) | (uint32_t)jlo;
+      uint2 fr;
+      fr.x = pack4(l[li][k], l[li][4 + k], l[li][8 + k], l[li][12 + k]);
+      fr.y = pack4(l[li][k + 1], l[li][5 + k], l[li][9 + k], l[li][13 + k]);
+      size_t idx = (((size_t)blk * NT + (uint32_t)(n / 8)) * 4u + j) * 32u +
+                   (uint32_t)(n % 8) * 4u + q;
+      P.frag[idx] = fr;
+    }
+  }
+}
+
+// ---- one row over a thread-block cluster ------------------------------------
+// A row of a few thousand columns is too little work to keep a whole GPU busy
+// and too much for one CTA to finish quickly, and the prep needs the row's
+// maximum before any value can be quantized.  kRowCluster CTAs of a cluster
+// share one row: each owns a run of columns starting on a packed-word
+// boundary, the row statistics are combined through distributed shared
+// memory, and each CTA quantizes its own words.
+constexpr int kRowCluster = 8;
+
+struct RowSlice {
+  uint32_t c0, c1;   // columns [c0, c1) owned by this CTA; c0 % 16 == 0
+};
+__host__ __device__ inline uint32_t row_slice_cols(uint32_t cols) {
+  const uint32_t per = (cols + kRowCluster - 1) / kRowCluster;
+  return (per + 15u) & ~15u;
+}
+__device__ __forceinline__ RowSlice row_slice(uint32_t cols, uint32_t rank) {
+  const uint32_t per = row_slice_cols(cols);
+  RowSlice r;
+  r.c0 = min(cols, rank * per);
+  r.c1 = min(cols, r.c0 + per);
+  return r;
+}
+
+// Quantize this CTA's slice XS (columns [c0, c1) of row s, staged in shared
+// memory) into P once the row's maximum MM and non-finite flag BAD are known
+// cluster-wide.  LIVE is false for the padding rows s >= seq of the last
+// n-tile, whose fragments are written as zeros.  WRITER (one CTA of the
+// cluster) stores the row's scale and flag.  Needs cols % 16 == 0.
+__device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, float mm, bool bad,
+                                               bool live, bool writer, uint32_t s, uint32_t seq,
+                                               PrepOut P) {
+  const int NT = n_tiles((int)seq);
+  float mul = 0.0f, inv = 0.0f;
+  const bool ok = live && row_scale(mm, bad, &mul, &inv);
+  if (live && writer && threadIdx.x == 0) {
+    P.rowinv[s] = inv;
+    P.rowflag[s] = !ok;
+  }
+  for (uint32_t W = sl.c0 / 16u + threadIdx.x; W < sl.c1 / 16u; W += blockDim.x) {
+    float v[16];
+    if (ok) {
+      const float4 *src = reinterpret_cast<const float4 *>(xs + (16u * W - sl.c0));
 #pragma unroll
       for (int v4 = 0; v4 < 4; v4++) {
         float4 f = src[v4];
-        float v[4] = {f.x, f.y, f.z, f.w};
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-          int qv = __float2int_rn(v[e] * mul);   // exact scaling, one rounding
-          int l0 = (int)(int8_t)(qv & 0xff);
-          int r = (qv - l0) >> 8;
-          int l1 = (int)(int8_t)(r & 0xff);
-          int l2 = (r - l1) >> 8;                // |qv| <= 2^22 -> |l2| <= 64
-          l[0][4 * v4 + e] = l0; l[1][4 * v4 + e] = l1; l[2][4 * v4 + e] = l2;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < 16; k++) l[0][k] = l[1][k] = l[2][k] = 0;
-    }
-    const uint32_t blk = W / 8u, wq = W % 8u;
-    const uint32_t q = wq >> 1;
-#pragma unroll
-    for (int li = 0; li < 3; li++) {
-      int n = 3 * (int)s + li;
-      if (n >= 8 * NT) continue;
-#pragma unroll
-      for (int jlo = 0; jlo < 2; jlo++) {
-        const int k = 2 * jlo;
-        const uint32_t j = ((wq & 1u) << 1) | (uint32_t)jlo;
-        uint2 fr;
-        fr.x = pack4(l[li][k], l[li][4 + k], l[li][8 + k], l[li][12 + k]);
-        fr.y = pack4(l[li][k + 1], l[li][5 + k], l[li][9 + k], l[li][13 + k]);
-        size_t idx = (((size_t)blk * NT + (uint32_t)(n / 8)) * 4u + j) * 32u +
-                     (uint32_t)(n % 8) * 4u + q;
-        P.frag[idx] = fr;
+        v[4 * v4] = f.x; v[4 * v4 + 1] = f.y; v[4 * v4 + 2] = f.z; v[4 * v4 + 3] = f.w;
       }
     }
+    quantize_word(v, mul, ok, W, s, NT, P);
   }
 }
 

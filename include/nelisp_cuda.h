@@ -212,6 +212,24 @@ int nl_ternary_gemv_batched_dev(uint32_t count, const float *X,
                                 uint32_t cols, void *workspace,
                                 size_t ws_bytes, void *stream);
 
+/* Size of the file-scope device workspace of nl_ternary_gemv_static_dev. */
+#define NL_TERNARY_STATIC_WS_BYTES (2u << 20)
+
+/* nl_ternary_gemv_dev with no workspace argument and no allocation: the
+ * scratch is a file-scope device array of NL_TERNARY_STATIC_WS_BYTES
+ * (2 MiB).  No reference counterpart: an addition of this library for
+ * callers that must not let it allocate (the reference's ternary-rows always
+ * takes its buffers from the caller).  Returns NL_ERROR with a message when
+ * nl_ternary_workspace_bytes(seq, cols) exceeds the maximum (e.g. seq 16 with
+ * cols above 43680, seq 1 above 262112).  The first call on a device looks
+ * the array's address up with that device current; make it before any
+ * stream capture.  Calls that overlap in time share the array and race: the
+ * caller serialises them.  Does not synchronise. */
+int nl_ternary_gemv_static_dev(const float *X, const uint32_t *WP,
+                               const float *S, const float *BIAS, float *Y,
+                               uint32_t seq, uint32_t out, uint32_t cols,
+                               void *stream);
+
 /* ---- the ternary decoder (tensor-parallel) --------------------------- */
 
 /* A LLaMA-style decoder with ternary linears (BitNet-b1.58-2B shaped): RMSNorm,

@@ -1,0 +1,96 @@
+"""nl_ternary_gemv_static_dev: the ternary GEMV on the library's file-scope
+device workspace, called through the C ABI, against nl_ternary_gemv_dev with
+a caller-provided workspace on the same inputs (tk-err 1e-5, the bar of the
+ternary tests), two calls in a row; and its size limit.
+
+Collected last (file name) so that it also runs after every other GPU test in
+the same process; it needs nothing from them and passes alone as well.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle as nlo
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+STATIC_MAX = 2 << 20   # NL_TERNARY_STATIC_WS_BYTES
+
+
+def _pack(t):
+    out, cols = t.shape
+    codes = np.where(t == 1, 1, np.where(t == -1, 3, 0)).astype(np.uint32)
+    w = np.zeros((out, cols // 16), np.uint32)
+    for f in range(16):
+        w |= codes[:, f::16] << np.uint32(2 * f)
+    return w.ravel()
+
+
+def _problem(rng, seq, out, cols):
+    import torch
+    t = rng.integers(-1, 2, size=(out, cols))
+    X = rng.standard_normal((seq, cols)).astype(np.float32)
+    S = rng.uniform(0.5, 1.5, size=out).astype(np.float32)
+    B = rng.uniform(-0.2, 0.2, size=out).astype(np.float32)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    WP = torch.from_numpy(_pack(t).view(np.int32)).to(dev)
+    return (torch.from_numpy(X).to(dev), WP, torch.from_numpy(S).to(dev),
+            torch.from_numpy(B).to(dev))
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from nelisp_cuda import dev
+    return dev._lib()   # the library, initialised on the current torch device
+
+
+def test_static_workspace_matches_caller_workspace(lib):
+    import torch
+    from nelisp_cuda import _lib as L
+    rng = np.random.default_rng(20261201)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    cases = [(1, 4096, 4096), (5, 2560, 6912), (16, 1024, 2560), (3, 700, 4096)]
+    probs = [_problem(rng, *c) for c in cases]
+    ws = torch.empty(max(int(lib.nl_ternary_workspace_bytes(s, c)) for s, _, c in cases),
+                     dtype=torch.uint8, device=probs[0][0].device)
+    outs = [(torch.empty(s, o, device=ws.device), torch.empty(s, o, device=ws.device))
+            for s, o, _ in cases]
+    free0 = None
+    for rep in range(2):                     # two calls in a row per shape
+        if rep == 1:
+            # Every kernel involved has run once (and been loaded); the second
+            # round of calls must leave the device's free memory where it was.
+            torch.cuda.synchronize()
+            free0, _ = torch.cuda.mem_get_info()
+        for (seq, out, cols), (X, WP, S, B), (ys, yr) in zip(cases, probs, outs):
+            ys.fill_(float("nan"))
+            yr.fill_(float("nan"))
+            L.check(lib.nl_ternary_gemv_static_dev(_p(X), _p(WP), _p(S), _p(B), _p(ys), seq,
+                                                   out, cols, stream))
+            L.check(lib.nl_ternary_gemv_dev(_p(X), _p(WP), _p(S), _p(B), _p(yr), seq, out,
+                                            cols, _p(ws), ws.numel(), stream))
+            torch.cuda.synchronize()
+            a, r = ys.cpu().numpy(), yr.cpu().numpy()
+            assert np.isfinite(a).all()
+            err = nlo.tk_err(a.ravel(), r.ravel())
+            assert err < TOL, (rep, seq, out, cols, err)
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 >= free0
+
+
+def test_static_workspace_rejects_oversize(lib):
+    import torch
+    from nelisp_cuda import _lib as L
+    cols = 43680 + 16                      # seq 16 needs 48 bytes per column
+    assert lib.nl_ternary_workspace_bytes(16, cols) > STATIC_MAX
+    assert lib.nl_ternary_workspace_bytes(16, 43680) <= STATIC_MAX
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    rc = lib.nl_ternary_gemv_static_dev(None, None, None, None, None, 16, 8, cols, stream)
+    assert rc == L.NL_ERROR
+    msg = lib.nl_last_error().decode()
+    assert "static maximum" in msg and str(STATIC_MAX) in msg

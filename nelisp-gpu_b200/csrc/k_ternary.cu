@@ -496,6 +496,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   atomicExch(&g_tma_error, 1);
   return false;
 }
+// The producer's wait for a free stage: the same bound, with a short sleep
+// between polls so that a full ring does not take issue slots from the
+// consumer warps.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity) {
+  const uint32_t a = smem_u32(bar);
+  for (uint32_t i = 0; i < kSpinLimit; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(a), "r"(parity) : "memory");
+    if (done) return true;
+    __nanosleep(64);
+  }
+  atomicExch(&g_tma_error, 1);
+  return false;
+}
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
   asm volatile(
@@ -511,6 +528,12 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
 __host__ __device__ inline int tma_stages(int NT, int nw) {
   int per = 2048 * nw + NT * kTmaBlocks * 1024;
   int st = (112 * 1024) / per;
@@ -522,13 +545,19 @@ __host__ __device__ inline size_t tma_smem_bytes(int NT, int nw) {
          (size_t)2 * S * 8 + (size_t)nw * 16 * (8 * NT + 1) * 4;
 }
 
+// Persistent: a grid of at most (resident CTAs per SM) x 148 CTAs walks the
+// work items -- (problem z, tile of 16*nw rows) -- round-robin.  The producer
+// warp streams the (item, chunk) sequence through the S-stage ring without a
+// break between items, so the copies of a CTA's next item are in flight while
+// the consumers finish the current one and run its epilogue.
 template <int NT, bool PER_BLOCK>
-__global__ void __launch_bounds__(288)
+__global__ void __launch_bounds__(288, NT <= 3 ? 2 : 1)
 ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
                    uint64_t x_stride, const uint32_t *__restrict__ WP, uint64_t w_stride,
                    const float *__restrict__ SCALE, uint64_t s_stride,
                    const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
-                   uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws) {
+                   uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
+                   uint32_t count) {
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = (blockDim.x >> 5) - 1;            // consumer warps; warp nw produces
@@ -543,11 +572,10 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   uint64_t *empty = full + S;
   int *epi = reinterpret_cast<int *>(empty + S);
 
-  const uint32_t z = blockIdx.y;
   const uint32_t nblk = cols / 128u, wng = cols / 16u;
   const uint32_t nchunk = (nblk + kTmaBlocks - 1) / kTmaBlocks;
-  const uint32_t row0 = blockIdx.x * 16u * nw;     // first row of the CTA in problem z
-  PrepOut P = prep_at(ws, (int)seq, cols, z);
+  const uint32_t tpp = (out + 16u * nw - 1) / (16u * nw);   // tiles per problem
+  const uint32_t items = tpp * count;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; i++) {
@@ -561,34 +589,43 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   if (warp == nw) {
     // ---- producer ----
     if (lane == 0) {
-      const int y = (int)(z * out + row0);
-      for (uint32_t c = 0; c < nchunk; c++) {
-        const int st = (int)(c % (uint32_t)S);
-        if (c >= (uint32_t)S && !mbar_wait(&empty[st], ((c / S) - 1) & 1)) break;
-        const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
-        const uint32_t fbytes = nb * NT * 1024u;
-        mbar_expect_tx(&full[st], wbytes + fbytes);
-        tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u), y, &full[st]);
-        bulk_load(fbuf + (size_t)st * fstage, P.frag + (size_t)c * fstage, fbytes, &full[st]);
+      uint32_t g = 0;                              // chunks issued by this CTA
+      int st = 0;
+      uint32_t ph = 0;                             // parity of the current lap
+      bool ok = true;
+      for (uint32_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
+        const uint32_t z = it / tpp, tile = it % tpp;
+        const int y = (int)(z * out + tile * 16u * nw);
+        const uint2 *fsrc = prep_at(ws, (int)seq, cols, z).frag;
+        for (uint32_t c = 0; c < nchunk; c++, g++) {
+          if (g >= (uint32_t)S && !mbar_wait_backoff(&empty[st], ph ^ 1u)) {
+            ok = false;
+            break;
+          }
+          const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
+          const uint32_t fbytes = nb * NT * 1024u;
+          mbar_expect_tx(&full[st], wbytes + fbytes);
+          tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u), y, &full[st]);
+          bulk_load(fbuf + (size_t)st * fstage, fsrc + (size_t)c * fstage, fbytes, &full[st]);
+          if (++st == S) {
+            st = 0;
+            ph ^= 1u;
+          }
+        }
       }
       // Leave only when the last copies have landed (bounded).
-      for (uint32_t c = nchunk > (uint32_t)S ? nchunk - S : 0; c < nchunk; c++)
-        mbar_wait(&full[c % S], (c / S) & 1);
+      for (uint32_t k = g > (uint32_t)S ? g - S : 0; k < g; k++)
+        mbar_wait(&full[k % S], (k / S) & 1);
     }
     return;
   }
 
   // ---- consumers ----
-  const int g = lane >> 2, q = lane & 3;
-  const uint32_t rg = blockIdx.x * nw + warp;      // 16-row group
-  const bool active = rg * 16u < out;
-  const uint32_t rA = active ? min(rg * 16u + (uint32_t)g, out - 1u) : 0u;
-  const uint32_t rB = active ? min(rg * 16u + (uint32_t)g + 8u, out - 1u) : 0u;
-  const float *Sz = SCALE + z * s_stride;
+  const int gq = lane >> 2, q = lane & 3;
   // Byte offsets of this lane's 8-byte words in a stage's weight tile: row r
   // of the tile holds 128 bytes; the 16-byte chunk k of row r sits at chunk
   // k ^ (r % 8) (128B swizzle).  Block b, words 2q..2q+1 -> chunk 2b + q/2.
-  const uint32_t rowA = (uint32_t)warp * 16u + g, rowB = rowA + 8u;
+  const uint32_t rowA = (uint32_t)warp * 16u + gq, rowB = rowA + 8u;
   uint32_t offA[kTmaBlocks], offB[kTmaBlocks];
 #pragma unroll
   for (int b = 0; b < kTmaBlocks; b++) {
@@ -596,119 +633,137 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     offA[b] = rowA * 128u + ((k ^ (rowA & 7u)) << 4) + in;
     offB[b] = rowB * 128u + ((k ^ (rowB & 7u)) << 4) + in;
   }
+  int(*s_acc)[8 * NT + 1] = reinterpret_cast<int(*)[8 * NT + 1]>(epi + warp * 16 * (8 * NT + 1));
 
-  int acc[NT][4][4];                      // [n-tile][k-step][reg]: independent chains
-  float yf[NT][4];
-#pragma unroll
-  for (int t = 0; t < NT; t++)
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-      yf[t][r] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 4; j++) acc[t][j][r] = 0;
-    }
+  const uint32_t wsm = smem_u32(wbuf), fsm = smem_u32(fbuf);
+  int cst = 0;                                     // ring stage and lap parity
+  uint32_t cph = 0;
+  for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
+    const uint32_t z = it / tpp, tile = it % tpp;
+    const uint32_t rg = tile * nw + warp;          // 16-row group within problem z
+    const bool active = rg * 16u < out;
+    const uint32_t rA = active ? min(rg * 16u + (uint32_t)gq, out - 1u) : 0u;
+    const uint32_t rB = active ? min(rg * 16u + (uint32_t)gq + 8u, out - 1u) : 0u;
+    const float *Sz = SCALE + z * s_stride;
+    PrepOut P = prep_at(ws, (int)seq, cols, z);
 
-  bool ok = true;
-  for (uint32_t c = 0; c < nchunk && ok; c++) {
-    const int st = (int)(c % (uint32_t)S);
-    ok = mbar_wait(&full[st], (c / S) & 1);
-    if (!ok) break;
-    const uint8_t *wt = wbuf + (size_t)st * wbytes;
-    const uint2 *fb = fbuf + (size_t)st * fstage + lane;
-    const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
+    int acc[NT][4][4];                    // [n-tile][k-step][reg]: independent chains
+    float yf[NT][4];
 #pragma unroll
-    for (int b = 0; b < kTmaBlocks; b++) {
-      if ((uint32_t)b >= nb) break;
-      const uint2 a = *reinterpret_cast<const uint2 *>(wt + offA[b]);
-      const uint2 cw = *reinterpret_cast<const uint2 *>(wt + offB[b]);
-      uint32_t A[4][4];
-      unpack_block(a, cw, A);
-      const uint2 *fu = fb + b * NT * 128;
+    for (int t = 0; t < NT; t++)
 #pragma unroll
-      for (int t = 0; t < NT; t++)
+      for (int r = 0; r < 4; r++) {
+        yf[t][r] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 4; j++)
-          mma_s8(acc[t][j], A[j][0], A[j][1], A[j][2], A[j][3], fu[(t * 4 + j) * 32]);
-      if (PER_BLOCK) {
-        const uint32_t blk = c * kTmaBlocks + b;
-        const float bA = __ldg(Sz + (uint64_t)rA * nblk + blk);
-        const float bB = __ldg(Sz + (uint64_t)rB * nblk + blk);
+        for (int j = 0; j < 4; j++) acc[t][j][r] = 0;
+      }
+
+    // Whole chunks without a per-block test: blocks past the row end of a
+    // partial chunk hold TMA's zero fill, and a zero weight operand adds an
+    // exact 0 whatever the stale fragments beside it.
+    for (uint32_t c = 0; c < nchunk; c++) {
+      if (!mbar_wait(&full[cst], cph)) return;
+      const uint32_t wt = wsm + (uint32_t)cst * wbytes;
+      const uint32_t fb = fsm + (uint32_t)cst * (fstage * 8u) + (uint32_t)lane * 8u;
 #pragma unroll
-        for (int t = 0; t < NT; t++) {
+      for (int b = 0; b < kTmaBlocks; b++) {
+        const uint2 a = lds64(wt + offA[b]);
+        const uint2 cw = lds64(wt + offB[b]);
+        uint32_t A[4][4];
+        unpack_block(a, cw, A);
 #pragma unroll
-          for (int r = 0; r < 4; r++) {
-            const int v = acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
-            yf[t][r] = fmaf((float)v, r < 2 ? bA : bB, yf[t][r]);
-            acc[t][0][r] = acc[t][1][r] = acc[t][2][r] = acc[t][3][r] = 0;
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+            mma_s8(acc[t][j], A[j][0], A[j][1], A[j][2], A[j][3],
+                   lds64(fb + (uint32_t)((b * NT + t) * 4 + j) * 256u));
+        if (PER_BLOCK) {
+          const uint32_t blk = c * kTmaBlocks + b;
+          if (blk < nblk) {
+            const float bA = __ldg(Sz + (uint64_t)rA * nblk + blk);
+            const float bB = __ldg(Sz + (uint64_t)rB * nblk + blk);
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+#pragma unroll
+              for (int r = 0; r < 4; r++) {
+                const int v = acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
+                yf[t][r] = fmaf((float)v, r < 2 ? bA : bB, yf[t][r]);
+                acc[t][0][r] = acc[t][1][r] = acc[t][2][r] = acc[t][3][r] = 0;
+              }
+            }
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[cst]);
+      if (++cst == S) {
+        cst = 0;
+        cph ^= 1u;
+      }
+    }
+    if (!active) continue;
+
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+      int v[4];
+#pragma unroll
+      for (int r = 0; r < 4; r++)
+        v[r] = PER_BLOCK ? __float_as_int(yf[t][r])
+                         : acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
+      s_acc[gq][8 * t + 2 * q] = v[0];
+      s_acc[gq][8 * t + 2 * q + 1] = v[1];
+      s_acc[gq + 8][8 * t + 2 * q] = v[2];
+      s_acc[gq + 8][8 * t + 2 * q + 1] = v[3];
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-  }
-  if (!active || !ok) return;
-
-  int(*s_acc)[8 * NT + 1] = reinterpret_cast<int(*)[8 * NT + 1]>(epi + warp * 16 * (8 * NT + 1));
-#pragma unroll
-  for (int t = 0; t < NT; t++) {
-    int v[4];
-#pragma unroll
-    for (int r = 0; r < 4; r++)
-      v[r] = PER_BLOCK ? __float_as_int(yf[t][r])
-                       : acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
-    s_acc[g][8 * t + 2 * q] = v[0];
-    s_acc[g][8 * t + 2 * q + 1] = v[1];
-    s_acc[g + 8][8 * t + 2 * q] = v[2];
-    s_acc[g + 8][8 * t + 2 * q + 1] = v[3];
-  }
-  __syncwarp();
-  const uint32_t *Wz = WP + z * w_stride;
-  float *Yz = Y + z * y_stride;
-  bool any_flag = false;
-  for (uint32_t s = 0; s < seq; s++) any_flag |= (P.rowflag[s] != 0);
-  for (uint32_t idx = lane; idx < 16u * seq; idx += 32u) {
-    const uint32_t r = idx & 15u, s = idx >> 4;
-    const uint32_t o = rg * 16u + r;
-    if (o >= out) continue;
-    float yv;
-    if (PER_BLOCK) {
-      const int *sr = s_acc[r];
-      float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
-      v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
-      yv = v * P.rowinv[s];
-    } else {
-      long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
-                      65536ll * s_acc[r][3 * s + 2];
-      tot >>= 6;                               // the operands carried 64 * t: exact
-      yv = ((float)tot * P.rowinv[s]) * __ldg(Sz + o);
-    }
-    if (BIAS) yv = __ldg(BIAS + o) + yv;
-    uint64_t oi = (uint64_t)s * out + o;
-    if (oi < limit && !P.rowflag[s]) Yz[oi] = yv;
-  }
-  if (any_flag) {
-    const float *Xz = X + z * x_stride;
-    for (uint32_t r = 0; r < 16u; r++) {
+    const uint32_t *Wz = WP + z * w_stride;
+    float *Yz = Y + z * y_stride;
+    bool any_flag = false;
+    for (uint32_t s = 0; s < seq; s++) any_flag |= (P.rowflag[s] != 0);
+    for (uint32_t idx = lane; idx < 16u * seq; idx += 32u) {
+      const uint32_t r = idx & 15u, s = idx >> 4;
       const uint32_t o = rg * 16u + r;
-      if (o >= out) break;
-      float acc8[8];
-      const uint32_t *Wrow = Wz + (uint64_t)o * wng;
-      for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
-        int ns = (int)min(8u, seq - s0);
-        ternary_row_generic<8>(Xz, Wrow, PER_BLOCK ? Sz + (uint64_t)o * nblk : nullptr,
-                               PER_BLOCK, PER_BLOCK ? 1.0f : __ldg(Sz + o),
-                               (int)s0, ns, cols, nblk, wng, acc8);
-        if (lane == 0) {
-          for (int k = 0; k < ns; k++) {
-            uint32_t s = s0 + k;
-            uint64_t oi = (uint64_t)s * out + o;
-            if (P.rowflag[s] && oi < limit)
-              Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
+      if (o >= out) continue;
+      float yv;
+      if (PER_BLOCK) {
+        const int *sr = s_acc[r];
+        float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
+        v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
+        yv = v * P.rowinv[s];
+      } else {
+        long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
+                        65536ll * s_acc[r][3 * s + 2];
+        tot >>= 6;                               // the operands carried 64 * t: exact
+        yv = ((float)tot * P.rowinv[s]) * __ldg(Sz + o);
+      }
+      if (BIAS) yv = __ldg(BIAS + o) + yv;
+      uint64_t oi = (uint64_t)s * out + o;
+      if (oi < limit && !P.rowflag[s]) Yz[oi] = yv;
+    }
+    if (any_flag) {
+      const float *Xz = X + z * x_stride;
+      for (uint32_t r = 0; r < 16u; r++) {
+        const uint32_t o = rg * 16u + r;
+        if (o >= out) break;
+        float acc8[8];
+        const uint32_t *Wrow = Wz + (uint64_t)o * wng;
+        for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
+          int ns = (int)min(8u, seq - s0);
+          ternary_row_generic<8>(Xz, Wrow, PER_BLOCK ? Sz + (uint64_t)o * nblk : nullptr,
+                                 PER_BLOCK, PER_BLOCK ? 1.0f : __ldg(Sz + o),
+                                 (int)s0, ns, cols, nblk, wng, acc8);
+          if (lane == 0) {
+            for (int k = 0; k < ns; k++) {
+              uint32_t s = s0 + k;
+              uint64_t oi = (uint64_t)s * out + o;
+              if (P.rowflag[s] && oi < limit)
+                Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
+            }
           }
         }
       }
     }
+    __syncwarp();                 // s_acc is rewritten by the next item
   }
 }
 
@@ -747,11 +802,13 @@ bool make_weight_map(CUtensorMap *map, const uint32_t *WP, uint64_t rows, uint32
 }
 
 template <int NT, bool PB>
-cudaError_t launch_tma_nt(const CUtensorMap &map, dim3 grid, int nw, cudaStream_t st,
+cudaError_t launch_tma_nt(const CUtensorMap &map, uint32_t items, int nw, cudaStream_t st,
                           const float *X, uint64_t xs, const uint32_t *WP, uint64_t wst,
                           const float *S, uint64_t ss, const float *B, float *Y, uint64_t ys,
-                          uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws) {
+                          uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
+                          uint32_t count) {
   static int configured = 0;
+  static int per_sm[9] = {0};                  // resident CTAs per SM, by nw
   size_t smem = tma_smem_bytes(NT, 2);         // the largest CTA this instance runs
   if (tma_smem_bytes(NT, 4) > smem) smem = tma_smem_bytes(NT, 4);
   if (tma_smem_bytes(NT, 8) > smem) smem = tma_smem_bytes(NT, 8);
@@ -761,8 +818,24 @@ cudaError_t launch_tma_nt(const CUtensorMap &map, dim3 grid, int nw, cudaStream_
     if (e != cudaSuccess) return e;
     configured = 1;
   }
+  if (!per_sm[nw]) {
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+        &n, ternary_tma_kernel<NT, PB>, 32 * (nw + 1), tma_smem_bytes(NT, nw));
+    if (e != cudaSuccess) return e;
+    per_sm[nw] = n > 0 ? n : 1;
+  }
+  int sms = 148;
+  {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaGetLastError();
+  }
+  const uint32_t cap = (uint32_t)(per_sm[nw] * sms);
+  const uint32_t grid = items < cap ? items : cap;
   ternary_tma_kernel<NT, PB><<<grid, 32 * (nw + 1), tma_smem_bytes(NT, nw), st>>>(
-      map, X, xs, WP, wst, S, ss, B, Y, ys, seq, out, cols, limit, ws);
+      map, X, xs, WP, wst, S, ss, B, Y, ys, seq, out, cols, limit, ws, count);
   return cudaPeekAtLastError();
 }
 
@@ -784,14 +857,14 @@ bool try_launch_tma(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   while (nw > 2 && (uint64_t)ceil_div(groups16, nw) * count < 2u * 148u) nw >>= 1;
   CUtensorMap map;
   if (!make_weight_map(&map, WP, (uint64_t)count * out, wng, nw)) return false;
-  dim3 grid(ceil_div(groups16, nw), count);
+  const uint32_t items = (uint32_t)ceil_div(groups16, nw) * count;
   const int NT = n_tiles((int)seq);
-#define NL_CASE(N)                                                                        \
-  case N:                                                                                 \
-    *err = per_block ? launch_tma_nt<N, true>(map, grid, nw, st, X, xs, WP, wst, S, ss, B, \
-                                              Y, ys, seq, out, cols, limit, ws)           \
-                     : launch_tma_nt<N, false>(map, grid, nw, st, X, xs, WP, wst, S, ss,  \
-                                               B, Y, ys, seq, out, cols, limit, ws);      \
+#define NL_CASE(N)                                                                         \
+  case N:                                                                                  \
+    *err = per_block ? launch_tma_nt<N, true>(map, items, nw, st, X, xs, WP, wst, S, ss, B, \
+                                              Y, ys, seq, out, cols, limit, ws, count)     \
+                     : launch_tma_nt<N, false>(map, items, nw, st, X, xs, WP, wst, S, ss,  \
+                                               B, Y, ys, seq, out, cols, limit, ws, count); \
     return true;
   switch (NT) {
     NL_CASE(1) NL_CASE(2) NL_CASE(3) NL_CASE(4) NL_CASE(5) NL_CASE(6)

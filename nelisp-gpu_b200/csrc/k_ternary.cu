@@ -155,15 +155,18 @@ ternary_generic_kernel(const float *__restrict__ X, uint64_t x_stride,
 // The fragment format and the activation prep live in ternary_prep.cuh, shared
 // with the decoder's fused normalisation kernels.
 
-// grid (kRowCluster * ceil(8*NT/3), count), kPrepThreads threads, clusters of
-// kRowCluster CTAs.  Cluster s handles sequence row s of problem z (rows
-// s >= seq write the zero padding of the last n-tile); each CTA takes a
-// column slice, and the row maximum is combined through distributed shared
-// memory in rank order, so every CTA scales the row by the same power of two.
+// grid (kRowCluster * seq, count), kPrepThreads threads, clusters of
+// kRowCluster CTAs.  Cluster s handles sequence row s of problem z; each CTA
+// takes a column slice, and the row maximum is combined through distributed
+// shared memory in rank order, so every CTA scales the row by the same power
+// of two.  The padding columns n >= 3*seq of the last n-tile are not written:
+// an MMA output column depends only on its own B column, and the GEMV's
+// epilogue never reads the padding columns' outputs.
 constexpr int kPrepThreads = 128;
 __global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kPrepThreads)
 ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
                     uint32_t seq, uint32_t cols, void *ws) {
+  pdl_trigger();                  // the GEMV may start streaming its weights
   __shared__ float red[32];
   __shared__ float s_max;
   __shared__ int s_bad;
@@ -589,28 +592,41 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   if (warp == nw) {
     // ---- producer ----
     if (lane == 0) {
-      uint32_t g = 0;                              // chunks issued by this CTA
+      // This CTA's chunks k = 0 .. total-1 are chunk k % nchunk of item
+      // blockIdx.x + (k / nchunk) * gridDim.x.  The weights of the first
+      // `pre` chunks are requested before waiting for the kernel that wrote
+      // the fragments (launch_pdl); the weights are not written by it.
+      const uint32_t mine = items > blockIdx.x ? (items - blockIdx.x + gridDim.x - 1) / gridDim.x
+                                               : 0u;
+      const uint32_t total = mine * nchunk;
+      const uint32_t pre = total < (uint32_t)S ? total : (uint32_t)S;
       int st = 0;
       uint32_t ph = 0;                             // parity of the current lap
-      bool ok = true;
-      for (uint32_t it = blockIdx.x; it < items && ok; it += gridDim.x) {
+      uint32_t g = 0;
+      for (; g < total; g++) {
+        if (g >= (uint32_t)S && !mbar_wait_backoff(&empty[st], ph ^ 1u)) break;
+        const uint32_t it = blockIdx.x + (g / nchunk) * gridDim.x, c = g % nchunk;
         const uint32_t z = it / tpp, tile = it % tpp;
-        const int y = (int)(z * out + tile * 16u * nw);
-        const uint2 *fsrc = prep_at(ws, (int)seq, cols, z).frag;
-        for (uint32_t c = 0; c < nchunk; c++, g++) {
-          if (g >= (uint32_t)S && !mbar_wait_backoff(&empty[st], ph ^ 1u)) {
-            ok = false;
-            break;
+        const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
+        mbar_expect_tx(&full[st], wbytes + nb * NT * 1024u);
+        tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u),
+                    (int)(z * out + tile * 16u * nw), &full[st]);
+        if (g >= pre) {
+          bulk_load(fbuf + (size_t)st * fstage, prep_at(ws, (int)seq, cols, z).frag +
+                    (size_t)c * fstage, nb * NT * 1024u, &full[st]);
+        } else if (g + 1 == pre) {
+          pdl_wait();
+          for (uint32_t k = 0; k < pre; k++) {
+            const uint32_t itk = blockIdx.x + (k / nchunk) * gridDim.x, ck = k % nchunk;
+            const uint32_t nbk = min((uint32_t)kTmaBlocks, nblk - ck * kTmaBlocks);
+            bulk_load(fbuf + (size_t)k * fstage,
+                      prep_at(ws, (int)seq, cols, itk / tpp).frag + (size_t)ck * fstage,
+                      nbk * NT * 1024u, &full[k]);
           }
-          const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
-          const uint32_t fbytes = nb * NT * 1024u;
-          mbar_expect_tx(&full[st], wbytes + fbytes);
-          tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u), y, &full[st]);
-          bulk_load(fbuf + (size_t)st * fstage, fsrc + (size_t)c * fstage, fbytes, &full[st]);
-          if (++st == S) {
-            st = 0;
-            ph ^= 1u;
-          }
+        }
+        if (++st == S) {
+          st = 0;
+          ph ^= 1u;
         }
       }
       // Leave only when the last copies have landed (bounded).
@@ -621,6 +637,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   }
 
   // ---- consumers ----
+  pdl_wait();                                      // the epilogue reads the prep's flags
   const int gq = lane >> 2, q = lane & 3;
   // Byte offsets of this lane's 8-byte words in a stage's weight tile: row r
   // of the tile holds 128 bytes; the 16-byte chunk k of row r sits at chunk
@@ -834,9 +851,11 @@ cudaError_t launch_tma_nt(const CUtensorMap &map, uint32_t items, int nw, cudaSt
   }
   const uint32_t cap = (uint32_t)(per_sm[nw] * sms);
   const uint32_t grid = items < cap ? items : cap;
-  ternary_tma_kernel<NT, PB><<<grid, 32 * (nw + 1), tma_smem_bytes(NT, nw), st>>>(
-      map, X, xs, WP, wst, S, ss, B, Y, ys, seq, out, cols, limit, ws, count);
-  return cudaPeekAtLastError();
+  // The preceding kernel in the stream is always this GEMV's own prep (or a
+  // kernel with the prep fused in), launched without the attribute.
+  return launch_pdl(ternary_tma_kernel<NT, PB>, dim3(grid), dim3(32 * (nw + 1)),
+                    tma_smem_bytes(NT, nw), st, map, X, xs, WP, wst, S, ss, B, Y, ys, seq,
+                    out, cols, limit, ws, count);
 }
 
 // Launch the TMA variant when the weights of all COUNT problems form one
@@ -950,7 +969,7 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
   for (uint32_t s0 = 0; s0 < seq; s0 += kMaxFastSeq) {
     uint32_t ns = min((uint32_t)kMaxFastSeq, seq - s0);
     int NT = n_tiles((int)ns);
-    dim3 pgrid(kRowCluster * ((8 * NT + 2) / 3), count);
+    dim3 pgrid(kRowCluster * ns, count);
     ternary_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(X + (uint64_t)s0 * cols,
                                                     x_stride, ns, cols, ws);
     cudaError_t e = cudaPeekAtLastError();
@@ -992,7 +1011,7 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
 cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
                                 uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream) {
   if (count == 0 || seq == 0) return cudaSuccess;
-  dim3 pgrid(kRowCluster * ((8 * n_tiles((int)seq) + 2) / 3), count);
+  dim3 pgrid(kRowCluster * seq, count);
   ternary_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(X, x_stride, seq, cols, ws);
   count_launches(1);
   return cudaPeekAtLastError();

@@ -172,13 +172,14 @@ __device__ __forceinline__ void cta_reduce(float v, int bad, float *red, RowStat
 // One cluster of kRowCluster CTAs per sequence row b: h = E[tok] (gather) or
 // h = h + delta (add); x = (h * rsqrt(mean h^2 + eps)) * g; then x is
 // converted into the next GEMV's activation fragments (when WS is set).
-// Clusters b >= B write the fragment padding.  Each CTA owns a column slice;
-// the sum of squares and the maximum of x are combined across the cluster.
+// Each CTA owns a column slice; the sum of squares and the maximum of x are
+// combined across the cluster.
 template <int MODE>
 __global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kNormThreads)
 k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restrict__ h,
        const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
        void *ws, uint32_t B, uint32_t H, float eps) {
+  pdl_trigger();                 // the next GEMV may start streaming its weights
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[32];
   __shared__ RowStats st[2];
@@ -262,6 +263,7 @@ __global__ void k_rope_append(const float *__restrict__ qkv, float *__restrict__
 __global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kNormThreads)
 k_silu_prep(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint32_t B,
             uint32_t fr) {
+  pdl_trigger();
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[32];
   __shared__ RowStats st;
@@ -494,8 +496,7 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   const uint32_t H = c.hidden, hd = c.head_dim;
   const float eps = c.rms_eps;
   cudaStream_t st = D->stream;
-  const uint32_t npad = (uint32_t)(8 * n_tiles((int)B) + 2) / 3;
-  const uint32_t gnorm = (B > npad ? B : npad) * kRowCluster;
+  const uint32_t gnorm = B * kRowCluster;
   const size_t smem_h = (size_t)row_slice_cols(H) * sizeof(float);
   const bool fast_o = ternary_fast_shape(D->hr * hd, D->hr * hd / 128, D->hr * hd / 16, false);
   const bool fast_d = ternary_fast_shape(D->fr, D->fr / 128, D->fr / 16, false);

@@ -116,6 +116,35 @@ cudaError_t attn_decode_launch(const float *Q, const float *CK, const float *CV,
                                const float *POS, float *C, const AttnGeom &g, void *scratch,
                                cudaStream_t st);
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may
+// start while the kernel before it in the stream is still running; it must
+// touch nothing that kernel (or anything earlier) writes before pdl_wait(),
+// which returns once the preceding grid has completed and its writes are
+// visible.  A kernel calls pdl_trigger() to let its dependent start early.
+#if defined(__CUDACC__)
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+#endif
+
 // Library workspace for typed calls that pass no workspace (nl_runtime.cu).
 void *library_workspace(size_t bytes, cudaStream_t stream);
 

@@ -8,8 +8,9 @@
 // allocating library routine.
 //
 // Nothing in the workspace must start at zero: the prep launch writes every
-// fragment word (padding included) and the scale and flag of every live row
-// before the GEMV launch reads them, in stream order, on every call.
+// fragment word of the live rows and their scales and flags before the GEMV
+// launch reads them, in stream order, on every call; the padding columns of
+// the last n-tile only reach MMA output columns the epilogue discards.
 //
 // Calls that overlap in time (different streams, or host threads) share the
 // one array and race; the caller serialises them.

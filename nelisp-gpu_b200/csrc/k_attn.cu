@@ -111,6 +111,8 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 attn_partial_kernel(const float *__restrict__ Q, const float *__restrict__ CK,
                     const float *__restrict__ CV, const float *__restrict__ POS,
                     AttnGeom g, float *__restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int DPL = HD / 32;  // dims per lane
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const uint32_t split = blockIdx.x;
@@ -213,6 +215,8 @@ attn_partial_kernel(const float *__restrict__ Q, const float *__restrict__ CK,
 template <int HD>
 __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
                                     float *__restrict__ C, uint64_t limit) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t bh = blockIdx.x;
   const uint32_t bb = bh / g.heads, h = bh % g.heads;
   const float *pp = part + (uint64_t)bh * g.nsplit * (HD + 2);
@@ -301,7 +305,7 @@ size_t attn_scratch(const AttnGeom &g) {
 
 cudaError_t attn_launch(const float *Q, const float *CK, const float *CV,
                         const float *POS, float *C, const AttnGeom &g,
-                        uint64_t limit, void *scratch, cudaStream_t st) {
+                        uint64_t limit, void *scratch, cudaStream_t st, bool pdl = false) {
   if (g.B == 0 || g.heads == 0) return cudaSuccess;
   if (!split_ok(g) || scratch == nullptr || !aligned16(CK) || !aligned16(CV)) {
     uint64_t n = (uint64_t)g.B * g.heads * g.hd;
@@ -311,10 +315,11 @@ cudaError_t attn_launch(const float *Q, const float *CK, const float *CV,
   }
   dim3 grid(g.nsplit, g.B * g.kvheads);
   float *part = (float *)scratch;
+  cudaError_t e = cudaSuccess;
 #define NL_ATTN(HD, G)                                                       \
   case G:                                                                    \
-    attn_partial_kernel<HD, G><<<grid, kAttnWarps * 32, 0, st>>>(Q, CK, CV,  \
-                                                                 POS, g, part); \
+    e = launch_k(attn_partial_kernel<HD, G>, grid, dim3(kAttnWarps * 32), 0, st, pdl, \
+                 Q, CK, CV, POS, g, part);                                       \
     break;
   if (g.hd == 128) {
     switch (g.grp) {
@@ -322,18 +327,22 @@ cudaError_t attn_launch(const float *Q, const float *CK, const float *CV,
       NL_ATTN(128, 5) NL_ATTN(128, 6) NL_ATTN(128, 7) NL_ATTN(128, 8)
       default: return cudaErrorInvalidValue;
     }
-    attn_combine_kernel<128><<<g.B * g.heads, 128, 0, st>>>(part, g, C, limit);
+    if (e == cudaSuccess)
+      e = launch_k(attn_combine_kernel<128>, dim3(g.B * g.heads), dim3(128), 0, st, pdl, part, g,
+                   C, limit);
   } else {
     switch (g.grp) {
       NL_ATTN(64, 1) NL_ATTN(64, 2) NL_ATTN(64, 3) NL_ATTN(64, 4)
       NL_ATTN(64, 5) NL_ATTN(64, 6) NL_ATTN(64, 7) NL_ATTN(64, 8)
       default: return cudaErrorInvalidValue;
     }
-    attn_combine_kernel<64><<<g.B * g.heads, 64, 0, st>>>(part, g, C, limit);
+    if (e == cudaSuccess)
+      e = launch_k(attn_combine_kernel<64>, dim3(g.B * g.heads), dim3(64), 0, st, pdl, part, g, C,
+                   limit);
   }
 #undef NL_ATTN
   count_launches(2);
-  return cudaPeekAtLastError();
+  return e != cudaSuccess ? e : cudaPeekAtLastError();
 }
 
 // ---- registry glue -------------------------------------------------------------
@@ -457,8 +466,8 @@ AttnGeom attn_geom(uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads,
 size_t attn_scratch_bytes(const AttnGeom &g) { return attn_scratch(g); }
 cudaError_t attn_decode_launch(const float *Q, const float *CK, const float *CV,
                                const float *POS, float *C, const AttnGeom &g, void *scratch,
-                               cudaStream_t st) {
-  return attn_launch(Q, CK, CV, POS, C, g, UINT64_MAX, scratch, st);
+                               cudaStream_t st, bool pdl) {
+  return attn_launch(Q, CK, CV, POS, C, g, UINT64_MAX, scratch, st, pdl);
 }
 
 const OpSpec kAttnOps[] = {

@@ -167,6 +167,7 @@ __global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kPrepThrea
 ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
                     uint32_t seq, uint32_t cols, void *ws) {
   pdl_trigger();                  // the GEMV may start streaming its weights
+  pdl_wait();                     // X may come from the preceding kernel
   __shared__ float red[32];
   __shared__ float s_max;
   __shared__ int s_bad;
@@ -1009,12 +1010,14 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
 }
 
 cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
-                                uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream) {
+                                uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream,
+                                bool pdl) {
   if (count == 0 || seq == 0) return cudaSuccess;
   dim3 pgrid(kRowCluster * seq, count);
-  ternary_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(X, x_stride, seq, cols, ws);
+  cudaError_t e = launch_k(ternary_prep_kernel, pgrid, dim3(kPrepThreads), 0, stream, pdl, X,
+                           x_stride, seq, cols, ws);
   count_launches(1);
-  return cudaPeekAtLastError();
+  return e != cudaSuccess ? e : cudaPeekAtLastError();
 }
 
 cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_stride,

@@ -180,6 +180,7 @@ k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restri
        const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
        void *ws, uint32_t B, uint32_t H, float eps) {
   pdl_trigger();                 // the next GEMV may start streaming its weights
+  pdl_wait();
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[32];
   __shared__ RowStats st[2];
@@ -228,6 +229,8 @@ __global__ void k_rope_append(const float *__restrict__ qkv, float *__restrict__
                               float *__restrict__ ck, float *__restrict__ cv,
                               const int *__restrict__ pos, uint32_t B, uint32_t hr, uint32_t kvr,
                               uint32_t hd, uint32_t maxseq, float base) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t half = hd / 2, nh = hr + 2 * kvr;
   const uint32_t p = (uint32_t)*pos;
   const uint64_t n = (uint64_t)B * nh * half;
@@ -264,6 +267,7 @@ __global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kNormThrea
 k_silu_prep(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint32_t B,
             uint32_t fr) {
   pdl_trigger();
+  pdl_wait();
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[32];
   __shared__ RowStats st;
@@ -313,6 +317,8 @@ k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
          unsigned long long *__restrict__ keys, float *__restrict__ logits,
          const int *__restrict__ pos, uint32_t B, uint32_t vr, uint32_t v0, uint32_t H,
          uint32_t logit_stride) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int RPW = 4;
   extern __shared__ __align__(16) float xs[];   // [NB][H]
   for (uint32_t i = threadIdx.x; i < NB * H; i += blockDim.x)
@@ -376,6 +382,8 @@ k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
 // keys and advance the position.  One CTA.
 __global__ void k_next(unsigned long long *keys, const int *prompt, uint32_t P, int *tok,
                        int *out_tok, int *pos, float *posf, uint32_t B) {
+  pdl_trigger();
+  pdl_wait();
   const int p = *pos;
   const uint32_t b = threadIdx.x;
   if (b < B) {
@@ -503,11 +511,15 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   const bool fast_h = ternary_fast_shape(H, H / 128, H / 16, false);
   int rc;
   cudaError_t e;
-  k_norm<kNormGather><<<gnorm, kNormThreads, smem_h, st>>>(D->tok, D->embed, D->h, nullptr,
-                                                  D->layers[0].gattn, D->x,
-                                                  fast_h ? D->ws_qkv : nullptr, B, H, eps);
+  // Every kernel of the step is launched with programmatic stream
+  // serialization and waits for its predecessor before reading anything, so
+  // each one's launch overlaps the tail of the one before.
+  e = launch_pdl(k_norm<kNormGather>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                 (const int *)D->tok, (const float *)D->embed, D->h, (const float *)nullptr,
+                 (const float *)D->layers[0].gattn, D->x, fast_h ? D->ws_qkv : nullptr, B, H,
+                 eps);
   count_launches(1);
-  if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: embed");
+  if (e != cudaSuccess) return cuda_status(e, "step: embed");
   const AttnGeom geom = attn_geom(B, D->hr * hd, D->hr, D->kvr, c.max_seq,
                                   (uint64_t)c.max_batch * c.max_seq * D->kvr * hd);
   for (uint32_t l = 0; l < c.layers; l++) {
@@ -516,42 +528,45 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
                             H, false, fast_h ? D->ws_qkv : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: qkv");
     const uint64_t nrope = (uint64_t)B * (D->hr + 2 * D->kvr) * (hd / 2);
-    k_rope_append<<<grid_for(nrope, 256), 256, 0, st>>>(D->qkv, D->q, L.ck, L.cv, D->pos, B,
-                                                        D->hr, D->kvr, hd, c.max_seq,
-                                                        c.rope_base);
+    e = launch_pdl(k_rope_append, dim3(grid_for(nrope, 256)), dim3(256), 0, st,
+                   (const float *)D->qkv, D->q, L.ck, L.cv, (const int *)D->pos, B, D->hr, D->kvr,
+                   hd, c.max_seq, c.rope_base);
     count_launches(1);
-    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: rope");
-    e = attn_decode_launch(D->q, L.ck, L.cv, D->posf, D->ctx, geom, D->attn_scr, st);
+    if (e != cudaSuccess) return cuda_status(e, "step: rope");
+    e = attn_decode_launch(D->q, L.ck, L.cv, D->posf, D->ctx, geom, D->attn_scr, st, true);
     if (e != cudaSuccess) return cuda_status(e, "step: attention");
     if (fast_o) {
-      e = ternary_prep_launch(D->ctx, 0, 1, B, D->hr * hd, D->ws_o, st);
+      e = ternary_prep_launch(D->ctx, 0, 1, B, D->hr * hd, D->ws_o, st, true);
       if (e != cudaSuccess) return cuda_status(e, "step: o prep");
     }
     e = ternary_main_launch(1, D->ctx, 0, L.wo, 0, L.so, 0, nullptr, D->o, 0, B, H, D->hr * hd,
                             false, fast_o ? D->ws_o : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: o");
     if ((rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
-    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->h, D->o, L.gffn, D->x,
-                                                 fast_h ? D->ws_gu : nullptr, B, H, eps);
+    e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                   (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
+                   (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps);
     count_launches(1);
-    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: ffn norm");
+    if (e != cudaSuccess) return cuda_status(e, "step: ffn norm");
     e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
                             false, fast_h ? D->ws_gu : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: gate/up");
-    k_silu_prep<<<gnorm, kNormThreads, (size_t)row_slice_cols(D->fr) * sizeof(float), st>>>(
-        D->gu, D->a, fast_d ? D->ws_d : nullptr, B, D->fr);
+    e = launch_pdl(k_silu_prep, dim3(gnorm), dim3(kNormThreads),
+                   (size_t)row_slice_cols(D->fr) * sizeof(float), st, (const float *)D->gu, D->a,
+                   fast_d ? D->ws_d : nullptr, B, D->fr);
     count_launches(1);
-    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: swiglu");
+    if (e != cudaSuccess) return cuda_status(e, "step: swiglu");
     e = ternary_main_launch(1, D->a, 0, L.wd, 0, L.sd, 0, nullptr, D->d, 0, B, H, D->fr, false,
                             fast_d ? D->ws_d : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: down");
     if ((rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
     const bool last = l + 1 == c.layers;
-    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(
-        nullptr, nullptr, D->h, D->d, last ? D->gfinal : D->layers[l + 1].gattn, D->x,
-        (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps);
+    e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                   (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
+                   (const float *)(last ? D->gfinal : D->layers[l + 1].gattn), D->x,
+                   (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps);
     count_launches(1);
-    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: attn norm");
+    if (e != cudaSuccess) return cuda_status(e, "step: attn norm");
   }
   const size_t smem_lm = (size_t)(B <= 1 ? 1 : (B <= 2 ? 2 : (B <= 4 ? 4 : (B <= 8 ? 8 : 16)))) *
                          H * sizeof(float);
@@ -559,9 +574,9 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   const float *E = D->embed + (size_t)D->v0 * H;
   float *lg = D->keep_logits ? D->logits : nullptr;
   const uint32_t lstride = c.max_batch * D->vr;
-#define NL_LM(NB)                                                                          \
-  k_lmhead<NB><<<lmgrid, 256, smem_lm, st>>>(E, D->x, D->keys, lg, D->pos, B, D->vr, D->v0, \
-                                              H, lstride)
+#define NL_LM(NB)                                                                         \
+  e = launch_pdl(k_lmhead<NB>, dim3(lmgrid), dim3(256), smem_lm, st, E, (const float *)D->x, \
+                 D->keys, lg, (const int *)D->pos, B, D->vr, D->v0, H, lstride)
   if (B <= 1) NL_LM(1);
   else if (B <= 2) NL_LM(2);
   else if (B <= 4) NL_LM(4);
@@ -569,12 +584,12 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   else NL_LM(16);
 #undef NL_LM
   count_launches(1);
-  if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "step: lm head");
+  if (e != cudaSuccess) return cuda_status(e, "step: lm head");
   if ((rc = allreduce(D, D->keys, B, kNcclUint64, kNcclMax))) return rc;
-  k_next<<<1, 32, 0, st>>>(D->keys, D->prompt, D->last_positions, D->tok, D->out_tok, D->pos,
-                           D->posf, B);
+  e = launch_pdl(k_next, dim3(1), dim3(32), 0, st, D->keys, (const int *)D->prompt,
+                 D->last_positions, D->tok, D->out_tok, D->pos, D->posf, B);
   count_launches(1);
-  return cuda_status(cudaPeekAtLastError(), "step: next");
+  return cuda_status(e, "step: next");
 }
 
 int set_smem_limits(nl_decoder *D) {

@@ -92,7 +92,8 @@ size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols);
 // workspace the prep has filled (seq <= 16; shapes the fast path does not
 // cover, or a NULL workspace, take the generic kernel, which reads X).
 cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
-                                uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream);
+                                uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream,
+                                bool pdl = false);
 cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_stride,
                                 const uint32_t *WP, uint64_t w_stride, const float *SCALE,
                                 uint64_t s_stride, const float *BIAS, float *Y,
@@ -112,9 +113,11 @@ struct AttnGeom {
 AttnGeom attn_geom(uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads,
                    uint32_t maxseq, uint64_t cache_words);
 size_t attn_scratch_bytes(const AttnGeom &g);
+// PDL: launched with programmatic stream serialization (both kernels wait
+// for the preceding grid before reading anything).
 cudaError_t attn_decode_launch(const float *Q, const float *CK, const float *CV,
                                const float *POS, float *C, const AttnGeom &g, void *scratch,
-                               cudaStream_t st);
+                               cudaStream_t st, bool pdl = false);
 
 // Programmatic dependent launch.  A kernel launched with launch_pdl may
 // start while the kernel before it in the stream is still running; it must
@@ -128,9 +131,11 @@ __device__ __forceinline__ void pdl_wait() {
 __device__ __forceinline__ void pdl_trigger() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
+// A launch with the programmatic-serialization attribute when PDL is set,
+// an ordinary launch otherwise.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                       cudaStream_t st, Args... args) {
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t st, bool pdl, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -140,8 +145,13 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  return launch_k(kernel, grid, block, smem, st, true, args...);
 }
 #endif
 

@@ -785,6 +785,188 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fast path, step 2 for few rows: the latency-bound decode GEMV.
+// ---------------------------------------------------------------------------
+// One CTA per 16-row tile of one problem; its kDecWarps warps split the
+// 128-column blocks (warp w takes blocks w, w + kDecWarps, ...), each with
+// the same exact int8 MMAs as the streaming kernels, and the int32 partial
+// sums are added across warps in shared memory -- exact, so the result does
+// not depend on the split.  Weights go straight to registers (the first
+// batch is requested before the programmatic-launch wait: weights are not
+// written by the preceding kernel); fragments come from L2.  For a GEMV of
+// a few MB the streaming kernels leave most SMs idle, this one puts every
+// row tile on its own CTA.
+constexpr int kDecWarps = 8;
+constexpr uint32_t kDecMaxTiles = 2048;   // above this, the persistent TMA kernel
+
+template <int NT>
+__global__ void __launch_bounds__(kDecWarps * 32, 2)
+ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
+                   const uint32_t *__restrict__ WP, uint64_t w_stride,
+                   const float *__restrict__ SCALE, uint64_t s_stride,
+                   const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
+                   uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
+                   uint32_t tiles) {
+  constexpr int KB = NT == 1 ? 4 : (NT <= 4 ? 2 : 1);   // blocks per warp in flight
+  constexpr int CH = NT <= 2 ? 4 : 1;   // accumulator chains per n-tile
+  __shared__ int red[kDecWarps][NT * 4][32];
+  __shared__ int s_acc[16][8 * NT + 1];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gq = lane >> 2, q = lane & 3;
+  const uint32_t z = blockIdx.x / tiles, rt = blockIdx.x % tiles;
+  const uint32_t nblk = cols / 128u, wng = cols / 16u;
+  const uint32_t rA = min(rt * 16u + (uint32_t)gq, out - 1u);
+  const uint32_t rB = min(rt * 16u + (uint32_t)gq + 8u, out - 1u);
+  const uint32_t *Wz = WP + z * w_stride;
+  // words 2q, 2q+1 of block b of a row: uint2 index 4b + q
+  const uint2 *pa = reinterpret_cast<const uint2 *>(Wz + (uint64_t)rA * wng) + q;
+  const uint2 *pb = reinterpret_cast<const uint2 *>(Wz + (uint64_t)rB * wng) + q;
+  constexpr uint32_t step = (uint32_t)KB * kDecWarps;
+
+  uint2 wa[KB], wb[KB];
+#pragma unroll
+  for (int u = 0; u < KB; u++) {
+    const uint32_t b = (uint32_t)warp + (uint32_t)u * kDecWarps;
+    wa[u] = b < nblk ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
+    wb[u] = b < nblk ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
+  }
+  pdl_wait();                                  // fragments, flags and X come after this
+  const PrepOut P = prep_at(ws, (int)seq, cols, z);
+  const uint2 *fr = P.frag + lane;
+
+  int acc[NT][CH][4];
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int j = 0; j < CH; j++)
+#pragma unroll
+      for (int r = 0; r < 4; r++) acc[t][j][r] = 0;
+
+  for (uint32_t b0 = (uint32_t)warp; b0 < nblk; b0 += step) {
+    uint2 f[KB][NT][4];
+#pragma unroll
+    for (int u = 0; u < KB; u++) {
+      const uint32_t b = b0 + (uint32_t)u * kDecWarps;
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          f[u][t][j] = b < nblk ? __ldcg(fr + ((b * NT + t) * 4u + j) * 32u) : make_uint2(0u, 0u);
+    }
+    uint2 na[KB], nb2[KB];
+#pragma unroll
+    for (int u = 0; u < KB; u++) {
+      const uint32_t b = b0 + step + (uint32_t)u * kDecWarps;
+      na[u] = b < nblk ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
+      nb2[u] = b < nblk ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < KB; u++) {
+      uint32_t A[4][4];
+      unpack_block(wa[u], wb[u], A);       // zero weights past nblk add 0
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          mma_s8(acc[t][j % CH], A[j][0], A[j][1], A[j][2], A[j][3], f[u][t][j]);
+    }
+#pragma unroll
+    for (int u = 0; u < KB; u++) {
+      wa[u] = na[u];
+      wb[u] = nb2[u];
+    }
+  }
+
+  // Exact cross-warp sum into the [row][column] layout of the epilogue.
+#pragma unroll
+  for (int t = 0; t < NT; t++)
+#pragma unroll
+    for (int r = 0; r < 4; r++)
+    {
+      int v = 0;
+#pragma unroll
+      for (int j = 0; j < CH; j++) v += acc[t][j][r];
+      red[warp][t * 4 + r][lane] = v;
+    }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NT * 4 * 32; i += blockDim.x) {
+    const int tr = i >> 5, ln = i & 31, t = tr >> 2, r = tr & 3;
+    int v = 0;
+#pragma unroll
+    for (int w = 0; w < kDecWarps; w++) v += red[w][tr][ln];
+    s_acc[(ln >> 2) + (r >= 2 ? 8 : 0)][8 * t + 2 * (ln & 3) + (r & 1)] = v;
+  }
+  __syncthreads();
+
+  const float *Sz = SCALE + z * s_stride;
+  float *Yz = Y + z * y_stride;
+  for (uint32_t idx = threadIdx.x; idx < 16u * seq; idx += blockDim.x) {
+    const uint32_t r = idx & 15u, s = idx >> 4;
+    const uint32_t o = rt * 16u + r;
+    if (o >= out || __ldcg(P.rowflag + s)) continue;
+    long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
+                    65536ll * s_acc[r][3 * s + 2];
+    tot >>= 6;                                   // the operands carried 64 * t: exact
+    float yv = ((float)tot * __ldcg(P.rowinv + s)) * __ldg(Sz + o);
+    if (BIAS) yv = __ldg(BIAS + o) + yv;
+    const uint64_t oi = (uint64_t)s * out + o;
+    if (oi < limit) Yz[oi] = yv;
+  }
+  // Rows the prep flagged (non-finite or unrepresentable) on the CUDA cores.
+  if (warp == 0) {
+    bool any_flag = false;
+    for (uint32_t s = 0; s < seq; s++) any_flag |= (__ldcg(P.rowflag + s) != 0);
+    if (any_flag) {
+      const float *Xz = X + z * x_stride;
+      for (uint32_t r = 0; r < 16u; r++) {
+        const uint32_t o = rt * 16u + r;
+        if (o >= out) break;
+        float acc8[8];
+        const uint32_t *Wrow = Wz + (uint64_t)o * wng;
+        for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
+          const int ns = (int)min(8u, seq - s0);
+          ternary_row_generic<8>(Xz, Wrow, nullptr, false, __ldg(Sz + o), (int)s0, ns, cols,
+                                 nblk, wng, acc8);
+          if (lane == 0) {
+            for (int k = 0; k < ns; k++) {
+              const uint32_t s = s0 + k;
+              const uint64_t oi = (uint64_t)s * out + o;
+              if (__ldcg(P.rowflag + s) && oi < limit)
+                Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// Launch the decode GEMV when the problem has few row tiles; false when the
+// streaming kernels should run instead.
+bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t *WP,
+                    uint64_t wst, const float *S, uint64_t ss, const float *B, float *Y,
+                    uint64_t ys, uint32_t seq, uint32_t out, uint32_t cols, bool per_block,
+                    uint64_t limit, void *ws, cudaStream_t st, cudaError_t *err) {
+  static const int mode = [] {
+    const char *v = getenv("NELISP_TERNARY_PATH");
+    return v && (strcmp(v, "ring") == 0 || strcmp(v, "tma") == 0) ? 0 : 1;
+  }();
+  const uint32_t tiles = (out + 15u) / 16u;
+  if (!mode || per_block || (uint64_t)tiles * count > kDecMaxTiles) return false;
+  const dim3 grid(tiles * count), block(kDecWarps * 32);
+  switch (n_tiles((int)seq)) {
+#define NL_DEC(N)                                                                            \
+  case N:                                                                                    \
+    *err = launch_pdl(ternary_dec_kernel<N>, grid, block, 0, st, X, xs, WP, wst, S, ss, B, Y, \
+                      ys, seq, out, cols, limit, ws, tiles);                                 \
+    return true;
+    NL_DEC(1) NL_DEC(2) NL_DEC(3) NL_DEC(4) NL_DEC(5) NL_DEC(6)
+#undef NL_DEC
+    default: return false;
+  }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
@@ -865,7 +1047,8 @@ bool try_launch_tma(uint32_t count, const float *X, uint64_t xs, const uint32_t 
                     const float *S, uint64_t ss, const float *B, float *Y, uint64_t ys,
                     uint32_t seq, uint32_t out, uint32_t cols, bool per_block, uint64_t limit,
                     void *ws, cudaStream_t st, cudaError_t *err) {
-  // NELISP_TERNARY_PATH=ring selects the register-ring kernel instead.
+  // NELISP_TERNARY_PATH=ring selects the register-ring kernel instead (and
+  // =tma this kernel even where the decode kernel would run).
   static const int use_tma = [] {
     const char *v = getenv("NELISP_TERNARY_PATH");
     return (v && strcmp(v, "ring") == 0) ? 0 : 1;
@@ -979,7 +1162,10 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
       // The short-grid limit is an index into the whole Y; shift it per chunk.
       uint64_t b0 = (uint64_t)s0 * out;
       uint64_t l0 = limit > b0 ? limit - b0 : 0;
-      if (try_launch_tma(count, X + (uint64_t)s0 * cols, x_stride, WP, w_stride, SCALE,
+      if (try_launch_dec(count, X + (uint64_t)s0 * cols, x_stride, WP, w_stride, SCALE,
+                         s_stride, BIAS, Y + (uint64_t)s0 * out, y_stride, ns, out, cols,
+                         per_block, l0, ws, stream, &e) ||
+          try_launch_tma(count, X + (uint64_t)s0 * cols, x_stride, WP, w_stride, SCALE,
                          s_stride, BIAS, Y + (uint64_t)s0 * out, y_stride, ns, out, cols,
                          per_block, l0, ws, stream, &e)) {
         count_launches(2);
@@ -1036,7 +1222,9 @@ cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_strid
     return cudaPeekAtLastError();
   }
   cudaError_t e;
-  if (try_launch_tma(count, X, x_stride, WP, w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq,
+  if (try_launch_dec(count, X, x_stride, WP, w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq,
+                     out, cols, per_block, UINT64_MAX, ws, stream, &e) ||
+      try_launch_tma(count, X, x_stride, WP, w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq,
                      out, cols, per_block, UINT64_MAX, ws, stream, &e)) {
     count_launches(1);
     return e;

@@ -251,3 +251,75 @@ def test_gemv_batched_matches_single():
     y = tY.cpu().numpy().reshape(count, -1)
     for z in range(count):
         assert nlo.tk_err(y[z], want[z]) < TOL
+
+
+# ---- the three fast-path kernels agree bit for bit ----------------------------
+# The decode kernel (row tiles split over warps), the persistent TMA kernel and
+# the register-ring kernel sum the same exact int32 products and share the
+# epilogue, so they must give identical bits.  NELISP_TERNARY_PATH is read once
+# per process, hence one subprocess per path.
+
+_PATH_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path[:0] = [{root!r}, {pkg!r}]
+from nelisp_cuda import dev
+
+
+def pack_trits(t):
+    out, cols = t.shape
+    codes = np.where(t == 1, 1, np.where(t == -1, 3, 0)).astype(np.uint32)
+    w = np.zeros((out, cols // 16), np.uint32)
+    for f in range(16):
+        w |= codes[:, f::16] << np.uint32(2 * f)
+    return w.ravel()
+
+
+out_path = sys.argv[1]
+rng = np.random.default_rng(4242)
+res = {{}}
+for (seq, out, cols) in [(1, 4096, 4096), (4, 2560, 6912), (16, 1000, 2560), (7, 3840, 2560)]:
+    t = rng.integers(-1, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, out).astype(np.float32)
+    X = rng.standard_normal(seq * cols).astype(np.float32)
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X, WP.view(np.int32), S))
+    tY = torch.empty(seq * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols)
+    torch.cuda.synchronize()
+    res[f"{{seq}}_{{out}}_{{cols}}"] = tY.cpu().numpy()
+    res[f"x_{{seq}}_{{out}}_{{cols}}"] = X
+    res[f"w_{{seq}}_{{out}}_{{cols}}"] = WP
+    res[f"s_{{seq}}_{{out}}_{{cols}}"] = S
+np.savez(out_path, **res)
+"""
+
+
+def test_fast_path_kernels_agree_bitwise(tmp_path):
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG, ROOT
+    script = tmp_path / "paths.py"
+    script.write_text(_PATH_SCRIPT.format(root=ROOT, pkg=PKG))
+    results = {}
+    for path in ("auto", "tma", "ring"):
+        env = dict(os.environ)
+        env.pop("NELISP_TERNARY_PATH", None)
+        if path != "auto":
+            env["NELISP_TERNARY_PATH"] = path
+        outp = tmp_path / f"{path}.npz"
+        subprocess.run([sys.executable, str(script), str(outp)], env=env, check=True,
+                       cwd=ROOT, timeout=300)
+        results[path] = np.load(outp)
+    ref = results["auto"]
+    for key in ref.files:
+        if key[0] in "xws":
+            continue
+        for path in ("tma", "ring"):
+            assert np.array_equal(ref[key].view(np.uint32), results[path][key].view(np.uint32)), \
+                (path, key)
+        seq, out, cols = (int(v) for v in key.split("_"))
+        want = nlo.ternary_gemv_rows(ref["x_" + key], ref["w_" + key], ref["s_" + key], seq,
+                                     out, cols)
+        assert nlo.tk_err(ref[key], want) < TOL, key

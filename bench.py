@@ -346,6 +346,10 @@ def run_gpu(args):
         cpu = cpu_baseline(Wh[:1].ravel(), Sh[0], X[0].reshape(-1).cpu().numpy(), batch,
                            seconds=args.cpu_seconds)
 
+    kernels = None
+    if not args.no_kernels:
+        kernels = run_kernel_rows(device, peak, rank == 0 and ws == 1 and not args.no_cpu)
+
     decode = None
     if not args.no_decode:
         decode = run_decoder(dist, ws, rank, local, peak)
@@ -387,6 +391,8 @@ def run_gpu(args):
         }
         if cpu:
             line["cpu_baseline"] = cpu
+        if kernels:
+            line["kernels"] = kernels
         if decode:
             line["decode"] = decode
         print(json.dumps(line), flush=True)
@@ -449,6 +455,120 @@ def run_decoder(dist, ws, rank, local, peak):
     res["shard_rank0"] = {k: info[k] for k in ("kv_heads", "ffn", "vocab")}
     dec.close()
     return res
+
+
+def run_kernel_rows(device, peak, with_cpu):
+    """The other hot-path kernels at BASELINE.json's configs (0, 2, 3):
+    f32 matmul 256^3, row softmax 4096x4096 ~ N(0, 4), SwiGLU 16x11008 and
+    decode attention (B 8, 32 heads x 128, context 4096), each through the
+    registry (nl_dispatch_dev, the reference's kernel names and push
+    constants) on device tensors.  Every timed launch is bracketed by its own
+    CUDA events after a 256 MB L2 flush, so each reads its inputs from HBM
+    (SwiGLU's 2 MB stay L2-sized: reported as such)."""
+    import numpy as np
+    import torch
+
+    from nelisp_cuda import dev
+    g = torch.Generator(device=device)
+    g.manual_seed(2026)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
+
+    def timed(fn, iters=20):
+        for _ in range(3):
+            fn()
+        tot = 0.0
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / iters * 1e-3          # seconds per launch
+
+    def g64(n):
+        return (n + 63) // 64
+
+    def cpu_time(fn, reps=1):
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - t0) / reps
+
+    rows = {}
+    if with_cpu:
+        import oracle as nlo
+        nlo.lib()
+    # f32 matmul 256^3 (configs[0]); FFMA-bound, latency-bound at this size
+    M = K = N = 256
+    A = torch.rand(M * K, generator=g, device=device) * 2 - 1
+    B = torch.rand(K * N, generator=g, device=device) * 2 - 1
+    C = torch.empty(M * N, device=device)
+    for name, groups in (("matmul", g64(M * N)), ("matmul-tiled", (M // 16) * (N // 16)),
+                         ("matmul-reg", g64(M * N // 16))):
+        t = timed(lambda: dev.dispatch(name, [A, B, C], [M, K, N], groups))
+        flops = 2.0 * M * N * K
+        rows[name + " 256^3"] = {"us": round(t * 1e6, 2), "GFLOP/s": round(flops / t / 1e9, 1),
+                                 "bound": "ffma (latency at this size)"}
+    ffma_peak = 148 * 128 * 2 * 1.965e9 / 1e9
+    rows["matmul 256^3"]["peak_GFLOP/s_nominal"] = round(ffma_peak, 1)
+    if with_cpu:
+        Ah, Bh = A.cpu().numpy(), B.cpu().numpy()
+        tc = cpu_time(lambda: nlo.matmul(Ah, Bh, M, K, N), 3)
+        rows["matmul 256^3"]["cpu_GFLOP/s"] = round(2.0 * M * N * K / tc / 1e9, 2)
+    del A, B, C
+    # row softmax 4096 x 4096, x ~ N(0, 4) (configs[2])
+    M = N = 4096
+    X = torch.randn(M * N, generator=g, device=device) * 2.0
+    Y = torch.empty(M * N, device=device)
+    t = timed(lambda: dev.dispatch("softmax", [X, Y], [M, N], g64(M)))
+    nbytes = 8 * M * N
+    rows["softmax 4096x4096"] = {"us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
+                                 "frac_of_hbm": round(nbytes / t / 1e9 / peak, 4),
+                                 "bytes": nbytes, "bound": "hbm"}
+    if with_cpu:
+        Xh = X.cpu().numpy()
+        tc = cpu_time(lambda: nlo.softmax(Xh, M, N))
+        rows["softmax 4096x4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
+    del X, Y
+    # SwiGLU silu(g) * u on 16 x 11008 (configs[2])
+    n = 16 * 11008
+    Gt, U, O = (torch.randn(n, generator=g, device=device), torch.randn(n, generator=g,
+                device=device), torch.empty(n, device=device))
+    t = timed(lambda: dev.dispatch("silu-mul", [Gt, U, O], [n], g64(n)))
+    nbytes = 12 * n
+    rows["silu-mul 16x11008"] = {"us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
+                                 "bytes": nbytes,
+                                 "bound": "latency (2.1 MB: one wave, L2-sized)"}
+    if with_cpu:
+        gh, uh = Gt.cpu().numpy(), U.cpu().numpy()
+        tc = cpu_time(lambda: nlo.silu_mul(gh, uh, n), 5)
+        rows["silu-mul 16x11008"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
+    del Gt, U, O
+    # decode attention: B 8, 32 heads x 128, context 4096 (configs[3]); the
+    # cache holds keys already rotated (RoPE is applied when a key is appended)
+    Bn, H, hd, ctx = 8, 32, 128, 4096
+    dim = H * hd
+    Q = torch.randn(Bn * dim, generator=g, device=device)
+    CK = torch.randn(Bn * ctx * dim, generator=g, device=device)
+    CV = torch.randn(Bn * ctx * dim, generator=g, device=device)
+    POS = torch.tensor([float(ctx - 1)], device=device)
+    Cq = torch.empty(Bn * dim, device=device)
+    t = timed(lambda: dev.dispatch("decode-attn-b", [Q, CK, CV, POS, Cq], [Bn, dim, H, H, ctx],
+                                   g64(Bn * dim)))
+    nbytes = 2 * Bn * ctx * dim * 4 + 2 * Bn * dim * 4
+    rows["decode-attn-b B8 H32 ctx4096"] = {
+        "us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
+        "frac_of_hbm": round(nbytes / t / 1e9 / peak, 4), "bytes": nbytes, "bound": "hbm"}
+    if with_cpu:
+        Qh, Kh, Vh = Q.cpu().numpy(), CK.cpu().numpy(), CV.cpu().numpy()
+        tc = cpu_time(lambda: nlo.decode_attn_b(Qh, Kh, Vh, [float(ctx - 1)], Bn, dim, H, H,
+                                                ctx))
+        rows["decode-attn-b B8 H32 ctx4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
+    del Q, CK, CV, Cq, flush
+    torch.cuda.empty_cache()
+    return rows
 
 
 def cpu_baseline(WP, S, X, batch, seconds=10.0):
@@ -569,6 +689,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-decode", action="store_true", help="skip the decoder section")
+    ap.add_argument("--no-kernels", action="store_true",
+                    help="skip the matmul / softmax / SwiGLU / attention rows")
     ap.add_argument("--decode-profile", action="store_true",
                     help="only a short decoder run, batch --batch (the case ncu lists)")
     ap.add_argument("--profile-run", action="store_true",

@@ -254,6 +254,8 @@ __host__ __device__ inline size_t mma_smem_bytes(int NT) {
 // (a0/a2 = rows g, a1/a3 = rows g+8; the activation fragments follow the
 // same column order, see ternary_prep.cuh).
 constexpr uint32_t kTop2 = 0xC0C0C0C0u;
+__device__ __forceinline__ uint2 lo2(uint4 v) { return make_uint2(v.x, v.y); }
+__device__ __forceinline__ uint2 hi2(uint4 v) { return make_uint2(v.z, v.w); }
 __device__ __forceinline__ void unpack_block(uint2 a, uint2 c, uint32_t (&A)[4][4]) {
   A[0][0] = (a.x << 6) & kTop2; A[0][1] = (c.x << 6) & kTop2;
   A[0][2] = (a.x << 4) & kTop2; A[0][3] = (c.x << 4) & kTop2;
@@ -290,9 +292,12 @@ __device__ __forceinline__ void mma_chunk(int (&acc)[NT][2][4], float (&yf)[NT][
     // each other's results.
 #pragma unroll
     for (int t = 0; t < NT; t++) {
-#pragma unroll
-      for (int j = 0; j < 4; j++)
-        mma_s8(acc[t][j & 1], A[j][0], A[j][1], A[j][2], A[j][3], fu[(t * 4 + j) * 32]);
+      const uint4 f01 = *reinterpret_cast<const uint4 *>(fu + t * 128);
+      const uint4 f23 = *reinterpret_cast<const uint4 *>(fu + t * 128 + 64);
+      mma_s8(acc[t][0], A[0][0], A[0][1], A[0][2], A[0][3], lo2(f01));
+      mma_s8(acc[t][1], A[1][0], A[1][1], A[1][2], A[1][3], hi2(f01));
+      mma_s8(acc[t][0], A[2][0], A[2][1], A[2][2], A[2][3], lo2(f23));
+      mma_s8(acc[t][1], A[3][0], A[3][1], A[3][2], A[3][3], hi2(f23));
     }
     if (PER_BLOCK) {
       // BETA is per (row, 128-column block): flush the exact block sums.
@@ -379,7 +384,7 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
     }
     __syncthreads();
     if (active) {
-      const uint2 *fb = smem + (c & 1) * kChunkU2 + lane;
+      const uint2 *fb = smem + (c & 1) * kChunkU2 + 2 * lane;
       const uint32_t blk0 = c * kChunk;
       if (blk0 + 2 * kChunk <= nblk)   // this chunk and the next are whole
         mma_chunk<NT, PER_BLOCK, false>(acc, yf, wa, wb, fb, pA + 4u * blk0, pB + 4u * blk0,
@@ -469,7 +474,6 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
 // records an error and returns.
 // ---------------------------------------------------------------------------
 constexpr int kTmaBlocks = 4;                 // 128-column blocks per stage
-constexpr uint32_t kSpinLimit = 1u << 24;     // try_wait rounds before giving up
 
 __device__ int g_tma_error;                   // set by a wait that gave up
 
@@ -486,36 +490,28 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
 }
-// Bounded wait for the phase of parity PARITY to complete.
+// Bounded wait for the phase of parity PARITY to complete.  Each try_wait
+// suspends the thread in hardware until the phase completes or kSuspendNs
+// pass, so a waiting warp takes no issue slots; after kWaitRounds rounds
+// (seconds) the wait gives up and flags the error.
+constexpr uint32_t kSuspendNs = 1000000;
+constexpr uint32_t kWaitRounds = 4096;
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
-  for (uint32_t i = 0; i < kSpinLimit; i++) {
+  for (uint32_t i = 0; i < kWaitRounds; i++) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        : "=r"(done) : "r"(a), "r"(parity), "r"(kSuspendNs) : "memory");
     if (done) return true;
   }
   atomicExch(&g_tma_error, 1);
   return false;
 }
-// The producer's wait for a free stage: the same bound, with a short sleep
-// between polls so that a full ring does not take issue slots from the
-// consumer warps.
+// The producer's wait for a free stage (the same bounded, suspending wait).
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity) {
-  const uint32_t a = smem_u32(bar);
-  for (uint32_t i = 0; i < kSpinLimit; i++) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done) : "r"(a), "r"(parity) : "memory");
-    if (done) return true;
-    __nanosleep(64);
-  }
-  atomicExch(&g_tma_error, 1);
-  return false;
+  return mbar_wait(bar, parity);
 }
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
@@ -532,6 +528,12 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
       ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
 __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   uint2 v;
   asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "r"(addr));
@@ -664,6 +666,14 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     const uint32_t rB = active ? min(rg * 16u + (uint32_t)gq + 8u, out - 1u) : 0u;
     const float *Sz = SCALE + z * s_stride;
     PrepOut P = prep_at(ws, (int)seq, cols, z);
+    // The epilogue's operands, requested now so their latency hides behind
+    // the chunk loop: lane l holds the scale and bias of row l % 16 of the
+    // group and the inverse scale and flag of sequence row l.
+    const uint32_t erow = active ? min(rg * 16u + (uint32_t)(lane & 15), out - 1u) : 0u;
+    const float e_scale = PER_BLOCK ? 0.0f : __ldg(Sz + erow);
+    const float e_bias = BIAS ? __ldg(BIAS + erow) : 0.0f;
+    const float e_rinv = (uint32_t)lane < seq ? P.rowinv[lane] : 0.0f;
+    const int e_flag = (uint32_t)lane < seq ? P.rowflag[lane] : 0;
 
     int acc[NT][4][4];                    // [n-tile][k-step][reg]: independent chains
     float yf[NT][4];
@@ -682,7 +692,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     for (uint32_t c = 0; c < nchunk; c++) {
       if (!mbar_wait(&full[cst], cph)) return;
       const uint32_t wt = wsm + (uint32_t)cst * wbytes;
-      const uint32_t fb = fsm + (uint32_t)cst * (fstage * 8u) + (uint32_t)lane * 8u;
+      const uint32_t fb = fsm + (uint32_t)cst * (fstage * 8u) + (uint32_t)lane * 16u;
 #pragma unroll
       for (int b = 0; b < kTmaBlocks; b++) {
         const uint2 a = lds64(wt + offA[b]);
@@ -690,11 +700,14 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
         uint32_t A[4][4];
         unpack_block(a, cw, A);
 #pragma unroll
-        for (int t = 0; t < NT; t++)
-#pragma unroll
-          for (int j = 0; j < 4; j++)
-            mma_s8(acc[t][j], A[j][0], A[j][1], A[j][2], A[j][3],
-                   lds64(fb + (uint32_t)((b * NT + t) * 4 + j) * 256u));
+        for (int t = 0; t < NT; t++) {
+          const uint32_t ft = fb + (uint32_t)(b * NT + t) * 1024u;
+          const uint4 f01 = lds128(ft), f23 = lds128(ft + 512u);
+          mma_s8(acc[t][0], A[0][0], A[0][1], A[0][2], A[0][3], lo2(f01));
+          mma_s8(acc[t][1], A[1][0], A[1][1], A[1][2], A[1][3], hi2(f01));
+          mma_s8(acc[t][2], A[2][0], A[2][1], A[2][2], A[2][3], lo2(f23));
+          mma_s8(acc[t][3], A[3][0], A[3][1], A[3][2], A[3][3], hi2(f23));
+        }
         if (PER_BLOCK) {
           const uint32_t blk = c * kTmaBlocks + b;
           if (blk < nblk) {
@@ -736,27 +749,31 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     __syncwarp();
     const uint32_t *Wz = WP + z * w_stride;
     float *Yz = Y + z * y_stride;
-    bool any_flag = false;
-    for (uint32_t s = 0; s < seq; s++) any_flag |= (P.rowflag[s] != 0);
-    for (uint32_t idx = lane; idx < 16u * seq; idx += 32u) {
-      const uint32_t r = idx & 15u, s = idx >> 4;
+    const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
+    for (uint32_t k = 0; k * 32u < 16u * seq; k++) {     // uniform trip count: shuffles
+      const uint32_t idx = (uint32_t)lane + 32u * k;
+      const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
+      const float sc = __shfl_sync(0xffffffffu, e_scale, (int)r);
+      const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
+      const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
+      const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
       const uint32_t o = rg * 16u + r;
-      if (o >= out) continue;
+      if (idx >= 16u * seq || o >= out || fl) continue;
       float yv;
       if (PER_BLOCK) {
         const int *sr = s_acc[r];
         float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
         v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
-        yv = v * P.rowinv[s];
+        yv = v * ri;
       } else {
         long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
                         65536ll * s_acc[r][3 * s + 2];
         tot >>= 6;                               // the operands carried 64 * t: exact
-        yv = ((float)tot * P.rowinv[s]) * __ldg(Sz + o);
+        yv = ((float)tot * ri) * sc;
       }
-      if (BIAS) yv = __ldg(BIAS + o) + yv;
-      uint64_t oi = (uint64_t)s * out + o;
-      if (oi < limit && !P.rowflag[s]) Yz[oi] = yv;
+      if (BIAS) yv = bi + yv;
+      const uint64_t oi = (uint64_t)s * out + o;
+      if (oi < limit) Yz[oi] = yv;
     }
     if (any_flag) {
       const float *Xz = X + z * x_stride;
@@ -833,7 +850,7 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   }
   pdl_wait();                                  // fragments, flags and X come after this
   const PrepOut P = prep_at(ws, (int)seq, cols, z);
-  const uint2 *fr = P.frag + lane;
+  const uint2 *fr = P.frag + 2 * lane;
 
   int acc[NT][CH][4];
 #pragma unroll
@@ -849,10 +866,17 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
     for (int u = 0; u < KB; u++) {
       const uint32_t b = b0 + (uint32_t)u * kDecWarps;
 #pragma unroll
-      for (int t = 0; t < NT; t++)
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          f[u][t][j] = b < nblk ? __ldcg(fr + ((b * NT + t) * 4u + j) * 32u) : make_uint2(0u, 0u);
+      for (int t = 0; t < NT; t++) {
+        uint4 f01 = make_uint4(0u, 0u, 0u, 0u), f23 = f01;
+        if (b < nblk) {
+          f01 = __ldcg(reinterpret_cast<const uint4 *>(fr + (b * NT + t) * 128u));
+          f23 = __ldcg(reinterpret_cast<const uint4 *>(fr + (b * NT + t) * 128u + 64u));
+        }
+        f[u][t][0] = lo2(f01);
+        f[u][t][1] = hi2(f01);
+        f[u][t][2] = lo2(f23);
+        f[u][t][3] = hi2(f23);
+      }
     }
     uint2 na[KB], nb2[KB];
 #pragma unroll

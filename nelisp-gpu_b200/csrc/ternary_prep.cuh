@@ -19,11 +19,13 @@ namespace nl {
 
 constexpr int kMaxFastSeq = 16;  // 48 (s, limb) columns = 6 n-tiles of 8
 
-// Fragment layout for one problem: uint2 frag[blk][nt][j][lane], where blk is
-// the 128-column block, n-tile nt holds columns n = 8nt .. 8nt+7
-// (n = 3s + limb), j the k32 step within the block and lane = 4*(n%8) + q.
-// Lane q of MMA j in block blk covers word w = 2q + (j>>1) of the block and,
-// within it, with k = 2*(j&1): codes {k, 4+k, 8+k, 12+k} (b0) and
+// Fragment layout for one problem: uint2 frag[blk][nt][h][lane][e], where
+// blk is the 128-column block, n-tile nt holds columns n = 8nt .. 8nt+7
+// (n = 3s + limb), the k32 step within the block is j = 2h + e and
+// lane = 4*(n%8) + q.  A lane's fragments for steps (0,1) and for (2,3) are
+// each one 16-byte load, and the 32 lanes of a warp read 512 contiguous
+// bytes.  Lane q of MMA j in block blk covers word w = 2q + (j>>1) of the
+// block and, within it, with k = 2*(j&1): codes {k, 4+k, 8+k, 12+k} (b0) and
 // {k+1, 5+k, 9+k, 13+k} (b1) -- the order in which the weight operand
 // registers carry them (k_ternary.cu, unpack_block).
 // Blocks are outermost so that a run of blocks is one contiguous chunk the
@@ -35,6 +37,11 @@ struct PrepOut {
 };
 
 __host__ __device__ inline int n_tiles(int seq) { return (3 * seq + 7) / 8; }
+// Offset (in uint2) of the fragment pair (j = 2h, 2h+1) of LANE for n-tile T of
+// block BLK.
+__host__ __device__ inline size_t frag_pair(uint32_t blk, int NT, int t, int h, int lane) {
+  return ((((size_t)blk * NT + t) * 2u + h) * 32u + lane) * 2u;
+}
 __host__ __device__ inline size_t frag_bytes(int seq, uint32_t cols) {
   return (size_t)n_tiles(seq) * cols * 8u;
 }
@@ -107,8 +114,8 @@ __device__ __forceinline__ void quantize_word(const float (&v)[16], float mul, b
       uint2 fr;
       fr.x = pack4(l[li][k], l[li][4 + k], l[li][8 + k], l[li][12 + k]);
       fr.y = pack4(l[li][k + 1], l[li][5 + k], l[li][9 + k], l[li][13 + k]);
-      size_t idx = (((size_t)blk * NT + (uint32_t)(n / 8)) * 4u + j) * 32u +
-                   (uint32_t)(n % 8) * 4u + q;
+      size_t idx = ((((size_t)blk * NT + (uint32_t)(n / 8)) * 2u + (j >> 1)) * 32u +
+                    (uint32_t)(n % 8) * 4u + q) * 2u + (j & 1u);
       P.frag[idx] = fr;
     }
   }

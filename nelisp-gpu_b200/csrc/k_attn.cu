@@ -211,6 +211,158 @@ attn_partial_kernel(const float *__restrict__ Q, const float *__restrict__ CK,
   }
 }
 
+// The decoder's attention step with the RoPE and the cache append fused in
+// (the decoder's own composition; the registry ops above keep the reference's
+// separate decode-rope / cache-append / decode-attn).  QKV holds, per
+// sequence row, the query heads, then the key heads, then the value heads of
+// the current position p = POS[0], unrotated.  Each CTA rotates its query
+// heads in registers -- the same operation order as a separate half-split
+// RoPE pass, hence the same bits -- and the CTA whose split holds p rotates
+// the new key, writes key and value to the cache row p and folds them in from
+// registers (the cache loop stops before p).
+template <int HD, int GRP>
+__global__ void __launch_bounds__(kAttnWarps * 32)
+attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
+                         float *__restrict__ CV, const int *__restrict__ POS, AttnGeom g,
+                         const float2 *__restrict__ rope, float *__restrict__ part) {
+  pdl_trigger();
+  pdl_wait();
+  constexpr int DPL = HD / 32;   // dims per lane; lanes 0-15 hold the first half
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t split = blockIdx.x;
+  const uint32_t bkv = blockIdx.y, bb = bkv / g.kvheads, kvh = bkv % g.kvheads;
+  __shared__ float s_m[kAttnWarps][GRP], s_l[kAttnWarps][GRP];
+  __shared__ float s_o[kAttnWarps][GRP][HD];
+
+  const uint32_t p = (uint32_t)__ldg(POS);
+  const uint32_t len = min(p + 1u, g.maxseq);
+  const uint32_t p0 = split * g.chunk;
+  const uint32_t p1 = min(p0 + g.chunk, len);
+  const bool has_p = p < g.maxseq && p >= p0 && p < p1;
+  const float *row = QKV + (uint64_t)bb * (g.heads + 2u * g.kvheads) * HD;
+
+  // Rotation of this lane's dims at position p: dim m and m + HD/2 pair up;
+  // ROPE[p][m] = (cos, sin) of the angle (rope_table_launch).
+  float cs[DPL], sn[DPL];
+#pragma unroll
+  for (int d = 0; d < DPL; d++) {
+    const uint32_t m = (uint32_t)(lane * DPL + d) % (HD / 2);
+    const float2 r = __ldg(rope + (uint64_t)min(p, g.maxseq - 1u) * (HD / 2) + m);
+    cs[d] = r.x;
+    sn[d] = r.y;
+  }
+  const bool first_half = lane < 16;
+  auto rotate = [&](const float *src, float (&out)[DPL]) {
+#pragma unroll
+    for (int d = 0; d < DPL; d++) {
+      const float own = __ldg(src + lane * DPL + d);
+      const float other = __shfl_xor_sync(0xffffffffu, own, 16);
+      const float a0 = first_half ? own : other, a1 = first_half ? other : own;
+      out[d] = first_half ? __fsub_rn(__fmul_rn(a0, cs[d]), __fmul_rn(a1, sn[d]))
+                          : __fadd_rn(__fmul_rn(a1, cs[d]), __fmul_rn(a0, sn[d]));
+    }
+  };
+  float q[GRP][DPL];
+#pragma unroll
+  for (int hh = 0; hh < GRP; hh++) rotate(row + (uint64_t)(kvh * GRP + hh) * HD, q[hh]);
+  // The new key (rotated) and value of this kv head, cached by the split holding p.
+  float kn[DPL], vn[DPL];
+  const uint64_t cbase = (uint64_t)bb * g.maxseq * g.kvdim + (uint64_t)kvh * HD + lane * DPL;
+  if (has_p) {
+    rotate(row + (uint64_t)(g.heads + kvh) * HD, kn);
+    const float *vs = row + (uint64_t)(g.heads + g.kvheads + kvh) * HD + lane * DPL;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) vn[d] = __ldg(vs + d);
+    const uint64_t off = cbase + (uint64_t)p * g.kvdim;
+    if (warp == 0 && off + DPL <= g.cache_words) {
+#pragma unroll
+      for (int d = 0; d < DPL; d++) {
+        CK[off + d] = kn[d];
+        CV[off + d] = vn[d];
+      }
+    }
+  }
+
+  float m[GRP], l[GRP], o[GRP][DPL];
+#pragma unroll
+  for (int hh = 0; hh < GRP; hh++) {
+    m[hh] = -INFINITY; l[hh] = 0.0f;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) o[hh][d] = 0.0f;
+  }
+  auto fold = [&](const float (&kr)[DPL], const float (&vr)[DPL]) {
+#pragma unroll
+    for (int hh = 0; hh < GRP; hh++) {
+      float dot = 0.0f;
+#pragma unroll
+      for (int d = 0; d < DPL; d++) dot = fmaf(q[hh][d], kr[d], dot);
+      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      const float sc = dot * g.coef;
+      const float mn = fmaxf(m[hh], sc);
+      const float corr = expf(m[hh] - mn);   // exp(-inf) = 0 on the first key
+      const float pr = expf(sc - mn);
+      l[hh] = l[hh] * corr + pr;
+#pragma unroll
+      for (int d = 0; d < DPL; d++) o[hh][d] = fmaf(pr, vr[d], o[hh][d] * corr);
+      m[hh] = mn;
+    }
+  };
+  const uint32_t pc = has_p ? p : p1;             // cached keys: [p0, pc)
+  constexpr int U = 4;                            // key rows in flight per warp
+  for (uint32_t j0 = p0 + warp * U; j0 < pc; j0 += kAttnWarps * U) {
+    float kr[U][DPL], vr[U][DPL];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      const uint32_t j = j0 + u;
+      const uint64_t off = cbase + (uint64_t)j * g.kvdim;
+      const bool ok = j < pc && off + DPL <= g.cache_words;
+      if (DPL == 4) {
+        float4 k4 = ok ? __ldcs(reinterpret_cast<const float4 *>(CK + off)) : make_float4(0, 0, 0, 0);
+        float4 v4 = ok ? __ldcs(reinterpret_cast<const float4 *>(CV + off)) : make_float4(0, 0, 0, 0);
+        kr[u][0] = k4.x; kr[u][1] = k4.y; kr[u][2] = k4.z; kr[u][3] = k4.w;
+        vr[u][0] = v4.x; vr[u][1] = v4.y; vr[u][2] = v4.z; vr[u][3] = v4.w;
+      } else {
+#pragma unroll
+        for (int d = 0; d < DPL; d++) {
+          kr[u][d] = ok ? __ldcs(CK + off + d) : 0.0f;
+          vr[u][d] = ok ? __ldcs(CV + off + d) : 0.0f;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+      if (j0 + u >= pc) break;
+      fold(kr[u], vr[u]);
+    }
+  }
+  if (has_p && warp == (int)(((pc - p0) / U) % kAttnWarps)) fold(kn, vn);
+  // Merge the four warps of the CTA.
+#pragma unroll
+  for (int hh = 0; hh < GRP; hh++) {
+    if (lane == 0) { s_m[warp][hh] = m[hh]; s_l[warp][hh] = l[hh]; }
+#pragma unroll
+    for (int d = 0; d < DPL; d++) s_o[warp][hh][lane * DPL + d] = o[hh][d];
+  }
+  __syncthreads();
+  for (uint32_t e = threadIdx.x; e < (uint32_t)GRP * HD; e += blockDim.x) {
+    const uint32_t hh = e / HD, d = e % HD;
+    float mm = -INFINITY;
+    for (int w = 0; w < kAttnWarps; w++) mm = fmaxf(mm, s_m[w][hh]);
+    float ll = 0.0f, oo = 0.0f;
+    if (mm > -INFINITY) {
+      for (int w = 0; w < kAttnWarps; w++) {
+        const float c = expf(s_m[w][hh] - mm);
+        ll += s_l[w][hh] * c;
+        oo += s_o[w][hh][d] * c;
+      }
+    }
+    const uint32_t h = kvh * GRP + hh;
+    float *pp = part + (((uint64_t)bb * g.heads + h) * g.nsplit + split) * (HD + 2);
+    pp[2 + d] = oo;
+    if (d == 0) { pp[0] = mm; pp[1] = ll; }
+  }
+}
+
 // One CTA per (b, h): merge the splits and write C.
 template <int HD>
 __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
@@ -468,6 +620,71 @@ cudaError_t attn_decode_launch(const float *Q, const float *CK, const float *CV,
                                const float *POS, float *C, const AttnGeom &g, void *scratch,
                                cudaStream_t st, bool pdl) {
   return attn_launch(Q, CK, CV, POS, C, g, UINT64_MAX, scratch, st, pdl);
+}
+
+bool rope_split_ok(const AttnGeom &g) {
+  return (g.hd == 32 || g.hd == 64 || g.hd == 128 || g.hd == 256) && g.grp >= 1 &&
+         g.grp <= (uint32_t)kMaxGrp && g.heads == g.kvheads * g.grp;
+}
+
+// ROPE[p][m] = (cos theta, sin theta), theta = p / base^(2m/hd), for
+// p < maxseq and m < hd/2: the half-split rotation's operand order.
+__global__ void rope_table_kernel(float2 *rope, uint32_t maxseq, uint32_t hd, float base) {
+  const uint32_t half = hd / 2;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (uint64_t)maxseq * half;
+       i += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t p = (uint32_t)(i / half), m = (uint32_t)(i % half);
+    const float ex = __fdiv_rn(2.0f * (float)m, (float)hd);
+    const float theta = __fdiv_rn((float)p, powf(base, ex));
+    rope[i] = make_float2(cosf(theta), sinf(theta));
+  }
+}
+
+cudaError_t rope_table_launch(float2 *rope, uint32_t maxseq, uint32_t hd, float base,
+                              cudaStream_t st) {
+  rope_table_kernel<<<grid_for((uint64_t)maxseq * (hd / 2), 256), 256, 0, st>>>(rope, maxseq, hd,
+                                                                                base);
+  count_launches(1);
+  return cudaPeekAtLastError();
+}
+
+cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, const int *POS,
+                                    float *C, const AttnGeom &g, const float2 *rope,
+                                    void *scratch, cudaStream_t st) {
+  if (g.B == 0 || g.heads == 0) return cudaSuccess;
+  if (!rope_split_ok(g) || !scratch || !aligned16(CK) || !aligned16(CV))
+    return cudaErrorInvalidValue;
+  const dim3 grid(g.nsplit, g.B * g.kvheads);
+  float *part = (float *)scratch;
+  cudaError_t e = cudaErrorInvalidValue;
+#define NL_ATTN(HD, G)                                                                    \
+  case G:                                                                                 \
+    e = launch_pdl(attn_rope_partial_kernel<HD, G>, grid, dim3(kAttnWarps * 32), 0, st, QKV, \
+                   CK, CV, POS, g, rope, part);                                           \
+    break;
+#define NL_HD(HD)                                                                         \
+  case HD:                                                                                \
+    switch (g.grp) {                                                                      \
+      NL_ATTN(HD, 1) NL_ATTN(HD, 2) NL_ATTN(HD, 3) NL_ATTN(HD, 4)                         \
+      NL_ATTN(HD, 5) NL_ATTN(HD, 6) NL_ATTN(HD, 7) NL_ATTN(HD, 8)                         \
+      default: break;                                                                     \
+    }                                                                                     \
+    if (e == cudaSuccess)                                                                 \
+      e = launch_pdl(attn_combine_kernel<HD>, dim3(g.B * g.heads), dim3(HD < 128 ? HD : 128), \
+                     0, st, (const float *)part, g, C, (uint64_t)UINT64_MAX);             \
+    break;
+  switch (g.hd) {
+    NL_HD(32) NL_HD(64) NL_HD(128) NL_HD(256)
+    default: break;
+  }
+#undef NL_HD
+#undef NL_ATTN
+  count_launches(2);
+  return e;
+}
+size_t attn_rope_scratch_bytes(const AttnGeom &g) {
+  if (!rope_split_ok(g)) return 0;
+  return (size_t)g.B * g.heads * g.nsplit * (g.hd + 2) * sizeof(float);
 }
 
 const OpSpec kAttnOps[] = {

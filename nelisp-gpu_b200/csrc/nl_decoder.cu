@@ -224,42 +224,6 @@ k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restri
   cl.sync();                     // no CTA leaves while its statistics are read
 }
 
-// q/k rotation (half-split, position *pos), k and v appended to the cache.
-__global__ void k_rope_append(const float *__restrict__ qkv, float *__restrict__ q,
-                              float *__restrict__ ck, float *__restrict__ cv,
-                              const int *__restrict__ pos, uint32_t B, uint32_t hr, uint32_t kvr,
-                              uint32_t hd, uint32_t maxseq, float base) {
-  pdl_trigger();
-  pdl_wait();
-  const uint32_t half = hd / 2, nh = hr + 2 * kvr;
-  const uint32_t p = (uint32_t)*pos;
-  const uint64_t n = (uint64_t)B * nh * half;
-  const uint32_t rows = nh * hd, kvdim = kvr * hd;
-  for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
-       idx += (uint64_t)gridDim.x * blockDim.x) {
-    const uint32_t m = (uint32_t)(idx % half);
-    const uint32_t head = (uint32_t)((idx / half) % nh);
-    const uint32_t b = (uint32_t)(idx / ((uint64_t)half * nh));
-    const float *src = qkv + (size_t)b * rows + (size_t)head * hd;
-    const float a0 = src[m], a1 = src[m + half];
-    if (head < hr + kvr) {
-      const float ex = __fdiv_rn(2.0f * (float)m, (float)hd);
-      const float theta = __fdiv_rn((float)p, powf(base, ex));
-      const float c = cosf(theta), s = sinf(theta);
-      const float y0 = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s));
-      const float y1 = __fadd_rn(__fmul_rn(a1, c), __fmul_rn(a0, s));
-      float *dst = head < hr ? q + (size_t)b * hr * hd + (size_t)head * hd
-                             : ck + ((size_t)b * maxseq + p) * kvdim + (size_t)(head - hr) * hd;
-      dst[m] = y0;
-      dst[m + half] = y1;
-    } else {
-      float *dst = cv + ((size_t)b * maxseq + p) * kvdim + (size_t)(head - hr - kvr) * hd;
-      dst[m] = a0;
-      dst[m + half] = a1;
-    }
-  }
-}
-
 // a = silu(gate) * up, then the down GEMV's prep: one cluster per sequence
 // row, each CTA on its column slice, the row maximum combined across the
 // cluster.
@@ -440,11 +404,12 @@ struct nl_decoder {
   std::vector<nl::Layer> layers;
   float *embed = nullptr, *gfinal = nullptr;
   // activations
-  float *h = nullptr, *x = nullptr, *qkv = nullptr, *q = nullptr, *ctx = nullptr, *o = nullptr,
+  float *h = nullptr, *x = nullptr, *qkv = nullptr, *ctx = nullptr, *o = nullptr,
         *gu = nullptr, *a = nullptr, *d = nullptr, *posf = nullptr, *logits = nullptr;
   int *tok = nullptr, *prompt = nullptr, *out_tok = nullptr, *pos = nullptr;
   unsigned long long *keys = nullptr;
   void *ws_qkv = nullptr, *ws_o = nullptr, *ws_gu = nullptr, *ws_d = nullptr, *attn_scr = nullptr;
+  float2 *rope = nullptr;   // [max_seq][head_dim / 2] (cos, sin)
   bool keep_logits = false;
   std::map<uint32_t, cudaGraphExec_t> graphs;   // by batch
   uint64_t kernels_per_step = 0;
@@ -527,13 +492,10 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
     e = ternary_main_launch(1, D->x, 0, L.wqkv, 0, L.sqkv, 0, nullptr, D->qkv, 0, B, D->qkv_rows,
                             H, false, fast_h ? D->ws_qkv : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: qkv");
-    const uint64_t nrope = (uint64_t)B * (D->hr + 2 * D->kvr) * (hd / 2);
-    e = launch_pdl(k_rope_append, dim3(grid_for(nrope, 256)), dim3(256), 0, st,
-                   (const float *)D->qkv, D->q, L.ck, L.cv, (const int *)D->pos, B, D->hr, D->kvr,
-                   hd, c.max_seq, c.rope_base);
-    count_launches(1);
-    if (e != cudaSuccess) return cuda_status(e, "step: rope");
-    e = attn_decode_launch(D->q, L.ck, L.cv, D->posf, D->ctx, geom, D->attn_scr, st, true);
+    // RoPE of q and k, the cache append of k and v, and the split-K
+    // attention over positions 0..pos in one kernel (plus the split merge).
+    e = attn_rope_decode_launch(D->qkv, L.ck, L.cv, D->pos, D->ctx, geom, D->rope,
+                                D->attn_scr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: attention");
     if (fast_o) {
       e = ternary_prep_launch(D->ctx, 0, 1, B, D->hr * hd, D->ws_o, st, true);
@@ -718,13 +680,15 @@ static int decoder_build(nl_decoder *D) {
   DALLOC(D->h, (size_t)B * H * 4);
   DALLOC(D->x, (size_t)B * H * 4);
   DALLOC(D->qkv, (size_t)B * D->qkv_rows * 4);
-  DALLOC(D->q, (size_t)B * D->hr * hd * 4);
   DALLOC(D->ctx, (size_t)B * D->hr * hd * 4);
   DALLOC(D->o, (size_t)B * H * 4);
   DALLOC(D->gu, (size_t)B * 2 * D->fr * 4);
   DALLOC(D->a, (size_t)B * D->fr * 4);
   DALLOC(D->d, (size_t)B * H * 4);
   DALLOC(D->posf, 16);
+  DALLOC(D->rope, (size_t)c.max_seq * (hd / 2) * sizeof(float2));
+  if ((e = rope_table_launch(D->rope, c.max_seq, hd, c.rope_base, D->stream)) != cudaSuccess)
+    return cuda_status(e, "decoder: rope table");
   DALLOC(D->pos, 16);
   DALLOC(D->tok, (size_t)B * 4);
   DALLOC(D->keys, (size_t)B * 8);
@@ -738,7 +702,7 @@ static int decoder_build(nl_decoder *D) {
   for (uint32_t bb = 1; bb <= B; bb++) {
     const AttnGeom g = attn_geom(bb, D->hr * hd, D->hr, D->kvr, c.max_seq,
                                  (uint64_t)B * c.max_seq * D->kvr * hd);
-    if (attn_scratch_bytes(g) > scr) scr = attn_scratch_bytes(g);
+    if (attn_rope_scratch_bytes(g) > scr) scr = attn_rope_scratch_bytes(g);
   }
   DALLOC(D->attn_scr, scr + 256);
   if (D->keep_logits) DALLOC(D->logits, (size_t)c.max_seq * B * D->vr * 4);
@@ -752,12 +716,15 @@ extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int 
   int rc = nl_init(-1);
   if (rc) return rc;
   const nl_decoder_config &c = *cfg;
-  if (c.hidden == 0 || c.hidden % 128 || c.ffn == 0 || c.ffn % 128 || c.head_dim % 16 ||
-      c.head_dim == 0 || c.heads == 0 || c.kv_heads == 0 || c.heads % c.kv_heads ||
+  const bool hd_ok = c.head_dim == 32 || c.head_dim == 64 || c.head_dim == 128 ||
+                     c.head_dim == 256;
+  if (c.hidden == 0 || c.hidden % 128 || c.ffn == 0 || c.ffn % 128 || !hd_ok || c.heads == 0 ||
+      c.kv_heads == 0 || c.heads % c.kv_heads || c.heads / c.kv_heads > 8 ||
       c.max_batch == 0 || c.max_batch > 16 || c.max_seq == 0 || c.vocab == 0 || c.layers == 0)
     return set_error(NL_ERROR,
-                     "decoder config: hidden and ffn multiples of 128, head_dim of 16, heads a "
-                     "multiple of kv_heads, 1 <= max_batch <= 16");
+                     "decoder config: hidden and ffn multiples of 128, head_dim 32, 64, 128 or "
+                     "256, heads a multiple of kv_heads (at most 8 per kv head), "
+                     "1 <= max_batch <= 16");
   if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size)
     return set_error(NL_ERROR, "decoder: rank %d of %d", tp_rank, tp_size);
   nl_decoder *D = new nl_decoder();

@@ -155,6 +155,16 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 #endif
 
+// The decoder's attention step with the half-split RoPE of q and k and the
+// cache append of k and v at position POS[0] fused in (k_attn.cu).  ROPE is
+// the [maxseq][hd/2] (cos, sin) table rope_table_launch fills.
+cudaError_t rope_table_launch(float2 *rope, uint32_t maxseq, uint32_t hd, float base,
+                              cudaStream_t st);
+cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, const int *POS,
+                                    float *C, const AttnGeom &g, const float2 *rope,
+                                    void *scratch, cudaStream_t st);
+size_t attn_rope_scratch_bytes(const AttnGeom &g);   // 0: shape not covered
+
 // Library workspace for typed calls that pass no workspace (nl_runtime.cu).
 void *library_workspace(size_t bytes, cudaStream_t stream);
 

@@ -805,15 +805,15 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
 // ---------------------------------------------------------------------------
 // Fast path, step 2 for few rows: the latency-bound decode GEMV.
 // ---------------------------------------------------------------------------
-// One CTA per 16-row tile of one problem; its kDecWarps warps split the
-// 128-column blocks (warp w takes blocks w, w + kDecWarps, ...), each with
-// the same exact int8 MMAs as the streaming kernels, and the int32 partial
-// sums are added across warps in shared memory -- exact, so the result does
-// not depend on the split.  Weights go straight to registers (the first
-// batch is requested before the programmatic-launch wait: weights are not
-// written by the preceding kernel); fragments come from L2.  For a GEMV of
-// a few MB the streaming kernels leave most SMs idle, this one puts every
-// row tile on its own CTA.
+// A CTA takes RT 16-row tiles (RT = 1, 2, 4 or 8, chosen by the launcher so
+// the grid is one wave); the kDecWarps / RT warps of a tile split its
+// 128-column blocks (warp k of a tile takes blocks k, k + kDecWarps/RT, ...),
+// each with the same exact int8 MMAs as the streaming kernels, and the int32
+// partial sums are added across the tile's warps in shared memory -- exact,
+// so the result does not depend on the split.  Weights go straight to
+// registers (the first batch is requested before the programmatic-launch
+// wait: weights are not written by the preceding kernel); fragments come
+// from L2.
 constexpr int kDecWarps = 8;
 constexpr uint32_t kDecMaxTiles = 2048;   // above this, the persistent TMA kernel
 
@@ -824,14 +824,19 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
                    const float *__restrict__ SCALE, uint64_t s_stride,
                    const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
                    uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
-                   uint32_t tiles) {
+                   uint32_t tiles, uint32_t count, int rt_log2) {
   constexpr int KB = NT == 1 ? 4 : (NT <= 4 ? 2 : 1);   // blocks per warp in flight
-  constexpr int CH = NT <= 2 ? 4 : 1;   // accumulator chains per n-tile
+  constexpr int CH = NT <= 2 ? 4 : 1;                   // accumulator chains per n-tile
+  constexpr int kMaxRT = NT >= 5 ? 4 : 8;
   __shared__ int red[kDecWarps][NT * 4][32];
-  __shared__ int s_acc[16][8 * NT + 1];
+  __shared__ int s_acc[kMaxRT][16][8 * NT + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gq = lane >> 2, q = lane & 3;
-  const uint32_t z = blockIdx.x / tiles, rt = blockIdx.x % tiles;
+  const int RT = 1 << rt_log2, wpt = kDecWarps >> rt_log2;   // tiles per CTA, warps per tile
+  const int tl = warp / wpt, kw = warp % wpt;
+  const uint32_t ct = blockIdx.x * (uint32_t)RT + (uint32_t)tl;   // tile over all problems
+  const bool live = ct < tiles * count;
+  const uint32_t z = live ? ct / tiles : 0u, rt = live ? ct % tiles : 0u;
   const uint32_t nblk = cols / 128u, wng = cols / 16u;
   const uint32_t rA = min(rt * 16u + (uint32_t)gq, out - 1u);
   const uint32_t rB = min(rt * 16u + (uint32_t)gq + 8u, out - 1u);
@@ -839,18 +844,25 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   // words 2q, 2q+1 of block b of a row: uint2 index 4b + q
   const uint2 *pa = reinterpret_cast<const uint2 *>(Wz + (uint64_t)rA * wng) + q;
   const uint2 *pb = reinterpret_cast<const uint2 *>(Wz + (uint64_t)rB * wng) + q;
-  constexpr uint32_t step = (uint32_t)KB * kDecWarps;
+  const uint32_t bstep = (uint32_t)wpt, step = (uint32_t)KB * bstep;
+  const uint32_t nb = live ? nblk : 0u;
 
   uint2 wa[KB], wb[KB];
 #pragma unroll
   for (int u = 0; u < KB; u++) {
-    const uint32_t b = (uint32_t)warp + (uint32_t)u * kDecWarps;
-    wa[u] = b < nblk ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
-    wb[u] = b < nblk ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
+    const uint32_t b = (uint32_t)kw + (uint32_t)u * bstep;
+    wa[u] = b < nb ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
+    wb[u] = b < nb ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
   }
+  // The epilogue's immutable operands, also before the wait.
+  const uint32_t erow = min(rt * 16u + (uint32_t)(lane & 15), out - 1u);
+  const float e_scale = __ldg(SCALE + z * s_stride + erow);
+  const float e_bias = BIAS ? __ldg(BIAS + erow) : 0.0f;
   pdl_wait();                                  // fragments, flags and X come after this
   const PrepOut P = prep_at(ws, (int)seq, cols, z);
   const uint2 *fr = P.frag + 2 * lane;
+  const float e_rinv = (uint32_t)lane < seq ? __ldcg(P.rowinv + lane) : 0.0f;
+  const int e_flag = (uint32_t)lane < seq ? __ldcg(P.rowflag + lane) : 0;
 
   int acc[NT][CH][4];
 #pragma unroll
@@ -860,15 +872,15 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
 #pragma unroll
       for (int r = 0; r < 4; r++) acc[t][j][r] = 0;
 
-  for (uint32_t b0 = (uint32_t)warp; b0 < nblk; b0 += step) {
+  for (uint32_t b0 = (uint32_t)kw; b0 < nb; b0 += step) {
     uint2 f[KB][NT][4];
 #pragma unroll
     for (int u = 0; u < KB; u++) {
-      const uint32_t b = b0 + (uint32_t)u * kDecWarps;
+      const uint32_t b = b0 + (uint32_t)u * bstep;
 #pragma unroll
       for (int t = 0; t < NT; t++) {
         uint4 f01 = make_uint4(0u, 0u, 0u, 0u), f23 = f01;
-        if (b < nblk) {
+        if (b < nb) {
           f01 = __ldcg(reinterpret_cast<const uint4 *>(fr + (b * NT + t) * 128u));
           f23 = __ldcg(reinterpret_cast<const uint4 *>(fr + (b * NT + t) * 128u + 64u));
         }
@@ -881,9 +893,9 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
     uint2 na[KB], nb2[KB];
 #pragma unroll
     for (int u = 0; u < KB; u++) {
-      const uint32_t b = b0 + step + (uint32_t)u * kDecWarps;
-      na[u] = b < nblk ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
-      nb2[u] = b < nblk ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
+      const uint32_t b = b0 + step + (uint32_t)u * bstep;
+      na[u] = b < nb ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
+      nb2[u] = b < nb ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
     }
 #pragma unroll
     for (int u = 0; u < KB; u++) {
@@ -902,63 +914,66 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
     }
   }
 
-  // Exact cross-warp sum into the [row][column] layout of the epilogue.
+  // Exact sum over each tile's warps into the [row][column] layout.
 #pragma unroll
   for (int t = 0; t < NT; t++)
 #pragma unroll
-    for (int r = 0; r < 4; r++)
-    {
+    for (int r = 0; r < 4; r++) {
       int v = 0;
 #pragma unroll
       for (int j = 0; j < CH; j++) v += acc[t][j][r];
       red[warp][t * 4 + r][lane] = v;
     }
   __syncthreads();
-  for (int i = threadIdx.x; i < NT * 4 * 32; i += blockDim.x) {
-    const int tr = i >> 5, ln = i & 31, t = tr >> 2, r = tr & 3;
+  for (int i = threadIdx.x; i < RT * NT * 4 * 32; i += blockDim.x) {
+    const int ti = i / (NT * 4 * 32), rem = i % (NT * 4 * 32);
+    const int tr = rem >> 5, ln = rem & 31, t = tr >> 2, r = tr & 3;
     int v = 0;
-#pragma unroll
-    for (int w = 0; w < kDecWarps; w++) v += red[w][tr][ln];
-    s_acc[(ln >> 2) + (r >= 2 ? 8 : 0)][8 * t + 2 * (ln & 3) + (r & 1)] = v;
+    for (int w = 0; w < wpt; w++) v += red[ti * wpt + w][tr][ln];
+    s_acc[ti][(ln >> 2) + (r >= 2 ? 8 : 0)][8 * t + 2 * (ln & 3) + (r & 1)] = v;
   }
   __syncthreads();
 
-  const float *Sz = SCALE + z * s_stride;
+  // Epilogue: warp kw of tile tl covers outputs kw*32 + lane, step wpt*32.
+  if (!live) return;
   float *Yz = Y + z * y_stride;
-  for (uint32_t idx = threadIdx.x; idx < 16u * seq; idx += blockDim.x) {
-    const uint32_t r = idx & 15u, s = idx >> 4;
+  const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
+  for (uint32_t k = (uint32_t)kw; k * 32u < 16u * seq; k += (uint32_t)wpt) {   // warp-uniform
+    const uint32_t idx = (uint32_t)lane + 32u * k;
+    const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
+    const float sc = __shfl_sync(0xffffffffu, e_scale, (int)r);
+    const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
+    const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
+    const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
     const uint32_t o = rt * 16u + r;
-    if (o >= out || __ldcg(P.rowflag + s)) continue;
-    long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
-                    65536ll * s_acc[r][3 * s + 2];
+    if (idx >= 16u * seq || o >= out || fl) continue;
+    long long tot = (long long)s_acc[tl][r][3 * s] + 256ll * s_acc[tl][r][3 * s + 1] +
+                    65536ll * s_acc[tl][r][3 * s + 2];
     tot >>= 6;                                   // the operands carried 64 * t: exact
-    float yv = ((float)tot * __ldcg(P.rowinv + s)) * __ldg(Sz + o);
-    if (BIAS) yv = __ldg(BIAS + o) + yv;
+    float yv = ((float)tot * ri) * sc;
+    if (BIAS) yv = bi + yv;
     const uint64_t oi = (uint64_t)s * out + o;
     if (oi < limit) Yz[oi] = yv;
   }
   // Rows the prep flagged (non-finite or unrepresentable) on the CUDA cores.
-  if (warp == 0) {
-    bool any_flag = false;
-    for (uint32_t s = 0; s < seq; s++) any_flag |= (__ldcg(P.rowflag + s) != 0);
-    if (any_flag) {
-      const float *Xz = X + z * x_stride;
-      for (uint32_t r = 0; r < 16u; r++) {
-        const uint32_t o = rt * 16u + r;
-        if (o >= out) break;
-        float acc8[8];
-        const uint32_t *Wrow = Wz + (uint64_t)o * wng;
-        for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
-          const int ns = (int)min(8u, seq - s0);
-          ternary_row_generic<8>(Xz, Wrow, nullptr, false, __ldg(Sz + o), (int)s0, ns, cols,
-                                 nblk, wng, acc8);
-          if (lane == 0) {
-            for (int k = 0; k < ns; k++) {
-              const uint32_t s = s0 + k;
-              const uint64_t oi = (uint64_t)s * out + o;
-              if (__ldcg(P.rowflag + s) && oi < limit)
-                Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
-            }
+  if (kw == 0 && any_flag) {
+    const float *Xz = X + z * x_stride;
+    const float *Sz = SCALE + z * s_stride;
+    for (uint32_t r = 0; r < 16u; r++) {
+      const uint32_t o = rt * 16u + r;
+      if (o >= out) break;
+      float acc8[8];
+      const uint32_t *Wrow = Wz + (uint64_t)o * wng;
+      for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
+        const int ns = (int)min(8u, seq - s0);
+        ternary_row_generic<8>(Xz, Wrow, nullptr, false, __ldg(Sz + o), (int)s0, ns, cols,
+                               nblk, wng, acc8);
+        if (lane == 0) {
+          for (int k = 0; k < ns; k++) {
+            const uint32_t s = s0 + k;
+            const uint64_t oi = (uint64_t)s * out + o;
+            if (__ldcg(P.rowflag + s) && oi < limit)
+              Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
           }
         }
       }
@@ -978,12 +993,18 @@ bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   }();
   const uint32_t tiles = (out + 15u) / 16u;
   if (!mode || per_block || (uint64_t)tiles * count > kDecMaxTiles) return false;
-  const dim3 grid(tiles * count), block(kDecWarps * 32);
-  switch (n_tiles((int)seq)) {
+  const int NTs = n_tiles((int)seq);
+  // Tiles per CTA: the fewest that keep the grid within one wave of the
+  // resident CTAs (2 per SM), keeping at least two warps per tile.
+  const uint32_t total = tiles * count, wave = 2u * 148u;
+  int lg = 0;
+  while (lg < (NTs >= 5 ? 2 : 3) && (total + (1u << lg) - 1) >> lg > wave) lg++;
+  const dim3 grid((total + (1u << lg) - 1) >> lg), block(kDecWarps * 32);
+  switch (NTs) {
 #define NL_DEC(N)                                                                            \
   case N:                                                                                    \
     *err = launch_pdl(ternary_dec_kernel<N>, grid, block, 0, st, X, xs, WP, wst, S, ss, B, Y, \
-                      ys, seq, out, cols, limit, ws, tiles);                                 \
+                      ys, seq, out, cols, limit, ws, tiles, count, lg);                      \
     return true;
     NL_DEC(1) NL_DEC(2) NL_DEC(3) NL_DEC(4) NL_DEC(5) NL_DEC(6)
 #undef NL_DEC

@@ -225,7 +225,6 @@ __global__ void __launch_bounds__(kAttnWarps * 32)
 attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
                          float *__restrict__ CV, const int *__restrict__ POS, AttnGeom g,
                          const float2 *__restrict__ rope, float *__restrict__ part) {
-  pdl_trigger();
   pdl_wait();
   constexpr int DPL = HD / 32;   // dims per lane; lanes 0-15 hold the first half
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -367,7 +366,6 @@ attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
 template <int HD>
 __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
                                     float *__restrict__ C, uint64_t limit) {
-  pdl_trigger();
   pdl_wait();
   const uint32_t bh = blockIdx.x;
   const uint32_t bb = bh / g.heads, h = bh % g.heads;

@@ -824,7 +824,7 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
                    const float *__restrict__ SCALE, uint64_t s_stride,
                    const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
                    uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
-                   uint32_t tiles, uint32_t count, int rt_log2) {
+                   uint32_t tiles, uint32_t count, int rt_log2, PeerOut po) {
   constexpr int KB = NT == 1 ? 4 : (NT <= 4 ? 2 : 1);   // blocks per warp in flight
   constexpr int CH = NT <= 2 ? 4 : 1;                   // accumulator chains per n-tile
   constexpr int kMaxRT = NT >= 5 ? 4 : 8;
@@ -935,45 +935,56 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   __syncthreads();
 
   // Epilogue: warp kw of tile tl covers outputs kw*32 + lane, step wpt*32.
-  if (!live) return;
-  float *Yz = Y + z * y_stride;
-  const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
-  for (uint32_t k = (uint32_t)kw; k * 32u < 16u * seq; k += (uint32_t)wpt) {   // warp-uniform
-    const uint32_t idx = (uint32_t)lane + 32u * k;
-    const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
-    const float sc = __shfl_sync(0xffffffffu, e_scale, (int)r);
-    const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
-    const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
-    const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
-    const uint32_t o = rt * 16u + r;
-    if (idx >= 16u * seq || o >= out || fl) continue;
-    long long tot = (long long)s_acc[tl][r][3 * s] + 256ll * s_acc[tl][r][3 * s + 1] +
-                    65536ll * s_acc[tl][r][3 * s + 2];
-    tot >>= 6;                                   // the operands carried 64 * t: exact
-    float yv = ((float)tot * ri) * sc;
-    if (BIAS) yv = bi + yv;
-    const uint64_t oi = (uint64_t)s * out + o;
-    if (oi < limit) Yz[oi] = yv;
-  }
-  // Rows the prep flagged (non-finite or unrepresentable) on the CUDA cores.
-  if (kw == 0 && any_flag) {
-    const float *Xz = X + z * x_stride;
-    const float *Sz = SCALE + z * s_stride;
-    for (uint32_t r = 0; r < 16u; r++) {
+  // With peer outputs every value goes to each rank's slot.
+  const unsigned long long tag =
+      po.n ? (unsigned long long)(uint32_t)(*po.ep * po.tmul + po.tadd) << 32 : 0ull;
+  auto store = [&](uint64_t oi, float v) {
+    if (po.n == 0) {
+      Y[z * y_stride + oi] = v;
+    } else {
+      const unsigned long long word = tag | __float_as_uint(v);
+      for (int r = 0; r < po.n; r++) po.dst[r][z * y_stride + oi] = word;
+    }
+  };
+  if (live) {
+    const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
+    for (uint32_t k = (uint32_t)kw; k * 32u < 16u * seq; k += (uint32_t)wpt) {   // warp-uniform
+      const uint32_t idx = (uint32_t)lane + 32u * k;
+      const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
+      const float sc = __shfl_sync(0xffffffffu, e_scale, (int)r);
+      const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
+      const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
+      const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
       const uint32_t o = rt * 16u + r;
-      if (o >= out) break;
-      float acc8[8];
-      const uint32_t *Wrow = Wz + (uint64_t)o * wng;
-      for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
-        const int ns = (int)min(8u, seq - s0);
-        ternary_row_generic<8>(Xz, Wrow, nullptr, false, __ldg(Sz + o), (int)s0, ns, cols,
-                               nblk, wng, acc8);
-        if (lane == 0) {
-          for (int k = 0; k < ns; k++) {
-            const uint32_t s = s0 + k;
-            const uint64_t oi = (uint64_t)s * out + o;
-            if (__ldcg(P.rowflag + s) && oi < limit)
-              Yz[oi] = (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k];
+      if (idx >= 16u * seq || o >= out || fl) continue;
+      long long tot = (long long)s_acc[tl][r][3 * s] + 256ll * s_acc[tl][r][3 * s + 1] +
+                      65536ll * s_acc[tl][r][3 * s + 2];
+      tot >>= 6;                                   // the operands carried 64 * t: exact
+      float yv = ((float)tot * ri) * sc;
+      if (BIAS) yv = bi + yv;
+      const uint64_t oi = (uint64_t)s * out + o;
+      if (oi < limit) store(oi, yv);
+    }
+    // Rows the prep flagged (non-finite or unrepresentable) on the CUDA cores.
+    if (kw == 0 && any_flag) {
+      const float *Xz = X + z * x_stride;
+      const float *Sz = SCALE + z * s_stride;
+      for (uint32_t r = 0; r < 16u; r++) {
+        const uint32_t o = rt * 16u + r;
+        if (o >= out) break;
+        float acc8[8];
+        const uint32_t *Wrow = Wz + (uint64_t)o * wng;
+        for (uint32_t s0 = 0; s0 < seq; s0 += 8) {
+          const int ns = (int)min(8u, seq - s0);
+          ternary_row_generic<8>(Xz, Wrow, nullptr, false, __ldg(Sz + o), (int)s0, ns, cols,
+                                 nblk, wng, acc8);
+          if (lane == 0) {
+            for (int k = 0; k < ns; k++) {
+              const uint32_t s = s0 + k;
+              const uint64_t oi = (uint64_t)s * out + o;
+              if (__ldcg(P.rowflag + s) && oi < limit)
+                store(oi, (BIAS ? __ldg(BIAS + o) : 0.0f) + acc8[k]);
+            }
           }
         }
       }
@@ -983,10 +994,20 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
 
 // Launch the decode GEMV when the problem has few row tiles; false when the
 // streaming kernels should run instead.
+// Tiles per CTA (log 2) of the decode GEMV: the fewest that keep the grid
+// within one wave of the resident CTAs (2 per SM), at least two warps a tile.
+int dec_rt_log2(uint32_t total, int NTs) {
+  const uint32_t wave = 2u * 148u;
+  int lg = 0;
+  while (lg < (NTs >= 5 ? 2 : 3) && (total + (1u << lg) - 1) >> lg > wave) lg++;
+  return lg;
+}
+
 bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t *WP,
                     uint64_t wst, const float *S, uint64_t ss, const float *B, float *Y,
                     uint64_t ys, uint32_t seq, uint32_t out, uint32_t cols, bool per_block,
-                    uint64_t limit, void *ws, cudaStream_t st, cudaError_t *err) {
+                    uint64_t limit, void *ws, cudaStream_t st, cudaError_t *err,
+                    const PeerOut *po = nullptr) {
   static const int mode = [] {
     const char *v = getenv("NELISP_TERNARY_PATH");
     return v && (strcmp(v, "ring") == 0 || strcmp(v, "tma") == 0) ? 0 : 1;
@@ -994,17 +1015,16 @@ bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   const uint32_t tiles = (out + 15u) / 16u;
   if (!mode || per_block || (uint64_t)tiles * count > kDecMaxTiles) return false;
   const int NTs = n_tiles((int)seq);
-  // Tiles per CTA: the fewest that keep the grid within one wave of the
-  // resident CTAs (2 per SM), keeping at least two warps per tile.
-  const uint32_t total = tiles * count, wave = 2u * 148u;
-  int lg = 0;
-  while (lg < (NTs >= 5 ? 2 : 3) && (total + (1u << lg) - 1) >> lg > wave) lg++;
+  const uint32_t total = tiles * count;
+  const int lg = dec_rt_log2(total, NTs);
   const dim3 grid((total + (1u << lg) - 1) >> lg), block(kDecWarps * 32);
+  PeerOut pov = {};
+  if (po) pov = *po;
   switch (NTs) {
 #define NL_DEC(N)                                                                            \
   case N:                                                                                    \
     *err = launch_pdl(ternary_dec_kernel<N>, grid, block, 0, st, X, xs, WP, wst, S, ss, B, Y, \
-                      ys, seq, out, cols, limit, ws, tiles, count, lg);                      \
+                      ys, seq, out, cols, limit, ws, tiles, count, lg, pov);                 \
     return true;
     NL_DEC(1) NL_DEC(2) NL_DEC(3) NL_DEC(4) NL_DEC(5) NL_DEC(6)
 #undef NL_DEC
@@ -1165,6 +1185,13 @@ bool ternary_fast_shape(uint32_t cols, uint32_t nblk, uint32_t wng,
   return true;
 }
 
+uint32_t ternary_dec_ctas(uint32_t count, uint32_t out, uint32_t cols, uint32_t seq) {
+  const uint32_t tiles = (out + 15u) / 16u, total = tiles * count;
+  if (seq == 0 || seq > (uint32_t)kMaxFastSeq || total > kDecMaxTiles || cols % 128u) return 0;
+  const int lg = dec_rt_log2(total, n_tiles((int)seq));
+  return (total + (1u << lg) - 1) >> lg;
+}
+
 size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols) {
   int s = (int)(seq < (uint32_t)kMaxFastSeq ? seq : (uint32_t)kMaxFastSeq);
   if (s < 1) s = 1;
@@ -1255,9 +1282,21 @@ cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_strid
                                 const uint32_t *WP, uint64_t w_stride, const float *SCALE,
                                 uint64_t s_stride, const float *BIAS, float *Y,
                                 uint64_t y_stride, uint32_t seq, uint32_t out, uint32_t cols,
-                                bool per_block, void *ws, cudaStream_t stream) {
+                                bool per_block, void *ws, cudaStream_t stream,
+                                const PeerOut *po) {
   if (count == 0 || seq == 0 || out == 0) return cudaSuccess;
   const uint32_t nblk = (cols + 127) / 128, wng = (cols + 15) / 16;
+  if (po && po->n) {
+    // Peer outputs exist only on the decode kernel.
+    cudaError_t e = cudaErrorNotSupported;
+    if (ws && seq <= (uint32_t)kMaxFastSeq && ternary_fast_shape(cols, nblk, wng, per_block) &&
+        try_launch_dec(count, X, x_stride, WP, w_stride, SCALE, s_stride, BIAS, Y, y_stride, seq,
+                       out, cols, per_block, UINT64_MAX, ws, stream, &e, po)) {
+      count_launches(1);
+      return e;
+    }
+    return cudaErrorNotSupported;
+  }
   if (!ws || seq > (uint32_t)kMaxFastSeq || !ternary_fast_shape(cols, nblk, wng, per_block)) {
     dim3 grid(ceil_div((int)out, 8), count);
     ternary_generic_kernel<<<grid, 256, 0, stream>>>(X, x_stride, WP, w_stride, SCALE, s_stride,

@@ -49,13 +49,16 @@ namespace {
 typedef struct ncclComm *ncclComm_t;
 typedef struct { char internal[128]; } ncclUniqueId;
 typedef int ncclResult_t;
-constexpr int kNcclSum = 0, kNcclMax = 2, kNcclUint64 = 5, kNcclFloat32 = 7;
+constexpr int kNcclSum = 0, kNcclMax = 2, kNcclMin = 3, kNcclInt8 = 0, kNcclInt32 = 2,
+              kNcclUint64 = 5, kNcclFloat32 = 7;
 
 struct Nccl {
   void *h = nullptr;
   ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
   ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
   ncclResult_t (*AllReduce)(const void *, void *, size_t, int, int, ncclComm_t, cudaStream_t) =
+      nullptr;
+  ncclResult_t (*AllGather)(const void *, void *, size_t, int, ncclComm_t, cudaStream_t) =
       nullptr;
   ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
   const char *(*GetErrorString)(ncclResult_t) = nullptr;
@@ -72,6 +75,7 @@ Nccl *nccl() {
       n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(n.h, "ncclGetUniqueId");
       n.CommInitRank = (decltype(n.CommInitRank))dlsym(n.h, "ncclCommInitRank");
       n.AllReduce = (decltype(n.AllReduce))dlsym(n.h, "ncclAllReduce");
+      n.AllGather = (decltype(n.AllGather))dlsym(n.h, "ncclAllGather");
       n.CommDestroy = (decltype(n.CommDestroy))dlsym(n.h, "ncclCommDestroy");
       n.GetErrorString = (decltype(n.GetErrorString))dlsym(n.h, "ncclGetErrorString");
     }
@@ -127,6 +131,83 @@ __global__ void gen_embed_kernel(float *E, uint64_t n, uint64_t key) {
 // ---- step kernels ---------------------------------------------------------------------
 namespace cg = cooperative_groups;
 
+// ---- peer all-reduce (tensor parallelism over NVLink) ---------------------------------
+// Each rank's O / down GEMV writes its partial rows into its slot of every
+// rank's receive buffer (peer stores), every value a 64-bit word tagged with
+// the index of this use of the slots (PeerOut); the next kernel on each rank
+// polls each word until the tag shows up and sums the slots in rank order
+// (so all ranks get the same bits).  The argmax keys go the same way with an
+// arrival counter: the LM head's last CTA adds 1 to every rank's counter.  A
+// rank cannot overwrite a slot for use u + 1 before every peer has read use
+// u: writing use u + 1 needs results each peer computes only after its read
+// of use u.  Every wait is bounded; one that gives up sets ERR, which the
+// host reports after the generation.
+constexpr uint32_t kPeerSpin = 1u << 22;   // polls (~100 ns apart) before giving up
+
+struct PeerSig {
+  unsigned long long *ctr[8];
+  unsigned int *done;
+  int n;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ bool wait_count(const unsigned long long *ctr, unsigned long long target, int *err) {
+  if (*reinterpret_cast<volatile int *>(err)) return false;   // an earlier wait gave up
+  for (uint32_t i = 0; i < kPeerSpin; i++) {
+    if (ld_acquire_sys(ctr) >= target) return true;
+    __nanosleep(100);
+  }
+  atomicExch(err, 1);
+  return false;
+}
+// The last CTA of the grid to get here arrives at every rank of SIG.
+__device__ __forceinline__ void peer_signal(const PeerSig &sig) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicInc(sig.done, gridDim.x - 1u) == gridDim.x - 1u) {
+      __threadfence_system();
+      for (int r = 0; r < sig.n; r++) atomicAdd_system(sig.ctr[r], 1ull);
+    }
+  }
+}
+
+// A reduction input: either DELTA (already summed) or the TP slots of this
+// rank's receive buffer, whose words carry the tag *EP * TMUL + TADD once
+// written for this use.
+struct PeerIn {
+  const unsigned long long *slots;   // nullptr: use delta
+  uint32_t tp, slot_stride;          // slot r at slots + r * slot_stride
+  const unsigned long long *ep;
+  unsigned int tmul, tadd;
+  int *err;
+};
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// The f32 in word P once its tag is TAG (bounded poll; ERR on giving up).
+__device__ __forceinline__ float tagged_value(const unsigned long long *p, uint32_t tag,
+                                              int *err) {
+  unsigned long long w = ld_relaxed_sys(p);
+  if ((uint32_t)(w >> 32) != tag) {
+    for (uint32_t i = 0; i < kPeerSpin; i++) {
+      if (*reinterpret_cast<volatile int *>(err)) break;
+      __nanosleep(32);
+      w = ld_relaxed_sys(p);
+      if ((uint32_t)(w >> 32) == tag) break;
+      if (i + 1 == kPeerSpin) atomicExch(err, 1);
+    }
+  }
+  return __uint_as_float((uint32_t)w);
+}
+
 enum { kNormGather = 0, kNormAdd = 1 };
 constexpr int kNormThreads = 128;   // per CTA of a row cluster
 
@@ -178,9 +259,10 @@ template <int MODE>
 __global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kNormThreads)
 k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restrict__ h,
        const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
-       void *ws, uint32_t B, uint32_t H, float eps) {
+       void *ws, uint32_t B, uint32_t H, float eps, PeerIn pin) {
   pdl_trigger();                 // the next GEMV may start streaming its weights
   pdl_wait();
+  const uint32_t tag = pin.slots ? (uint32_t)(*pin.ep * pin.tmul + pin.tadd) : 0u;
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[32];
   __shared__ RowStats st[2];
@@ -196,7 +278,18 @@ k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restri
     const float *src = MODE == kNormGather ? E + (size_t)__ldg(tok + b) * H : nullptr;
     float ss = 0.0f;
     for (uint32_t i = sl.c0 + threadIdx.x; i < sl.c1; i += blockDim.x) {
-      float v = MODE == kNormGather ? __ldg(src + i) : __fadd_rn(hb[i], delta[(size_t)b * H + i]);
+      float v;
+      if (MODE == kNormGather) {
+        v = __ldg(src + i);
+      } else if (pin.slots) {
+        const unsigned long long *sl = pin.slots + (size_t)b * H + i;
+        float sum = tagged_value(sl, tag, pin.err);
+        for (uint32_t r = 1; r < pin.tp; r++)
+          sum = __fadd_rn(sum, tagged_value(sl + (size_t)r * pin.slot_stride, tag, pin.err));
+        v = __fadd_rn(hb[i], sum);
+      } else {
+        v = __fadd_rn(hb[i], delta[(size_t)b * H + i]);
+      }
       hb[i] = v;
       xs[i - sl.c0] = v;
       ss = fmaf(v, v, ss);
@@ -280,10 +373,13 @@ __global__ void __launch_bounds__(256)
 k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
          unsigned long long *__restrict__ keys, float *__restrict__ logits,
          const int *__restrict__ pos, uint32_t B, uint32_t vr, uint32_t v0, uint32_t H,
-         uint32_t logit_stride) {
+         uint32_t logit_stride, const unsigned long long *ep, uint32_t key_stride,
+         PeerSig sig) {
   pdl_trigger();
   pdl_wait();
   constexpr int RPW = 4;
+  // Keys of this step: slot ep % 2 when the ranks exchange them peer to peer.
+  if (sig.n) keys += (*ep & 1ull) * key_stride;
   extern __shared__ __align__(16) float xs[];   // [NB][H]
   for (uint32_t i = threadIdx.x; i < NB * H; i += blockDim.x)
     xs[i] = (i / H) < B ? x[i] : 0.0f;
@@ -340,18 +436,44 @@ k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
   if (lane == 0)
     for (int b = 0; b < NB; b++)
       if ((uint32_t)b < B && best[b]) atomicMax(keys + b, best[b]);
+  if (sig.n) peer_signal(sig);
 }
 
 // Next token: from the prompt while it lasts, else the argmax; reset the
 // keys and advance the position.  One CTA.
+// With peer keys (PK.n > 0): wait for every rank's LM head of this step, take
+// the maximum of the ranks' keys, clear this rank's keys of the next step.
+struct PeerKeys {
+  const unsigned long long *keys[8];   // every rank's two key slots
+  int n;
+  uint32_t stride;                     // keys per slot
+  const unsigned long long *ctr;
+  int *err;
+};
 __global__ void k_next(unsigned long long *keys, const int *prompt, uint32_t P, int *tok,
-                       int *out_tok, int *pos, float *posf, uint32_t B) {
+                       int *out_tok, int *pos, float *posf, uint32_t B, unsigned long long *ep,
+                       PeerKeys pk) {
   pdl_trigger();
   pdl_wait();
   const int p = *pos;
+  const unsigned long long e = *ep;
   const uint32_t b = threadIdx.x;
+  if (pk.n) {
+    if (threadIdx.x == 0) wait_count(pk.ctr, (e + 1ull) * (unsigned long long)pk.n, pk.err);
+    __syncthreads();
+  }
   if (b < B) {
-    const uint32_t idx = 0xFFFFFFFFu - (uint32_t)(keys[b] & 0xFFFFFFFFull);
+    unsigned long long key;
+    if (pk.n) {
+      key = 0ull;
+      for (int r = 0; r < pk.n; r++) {
+        const unsigned long long k = ld_acquire_sys(pk.keys[r] + (e & 1ull) * pk.stride + b);
+        key = k > key ? k : key;
+      }
+    } else {
+      key = keys[b];
+    }
+    const uint32_t idx = 0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull);
     int nt;
     if ((uint32_t)p + 1 < P) {
       nt = prompt[(size_t)b * P + p + 1];
@@ -360,12 +482,15 @@ __global__ void k_next(unsigned long long *keys, const int *prompt, uint32_t P, 
       out_tok[(size_t)(p + 1 - P) * B + b] = nt;
     }
     tok[b] = nt;
-    keys[b] = 0ull;
+    if (!pk.n) keys[b] = 0ull;
   }
+  // the next step's slot, for every batch row a later generation may use
+  if (pk.n && b < pk.stride) keys[((e + 1ull) & 1ull) * pk.stride + b] = 0ull;
   __syncthreads();
   if (threadIdx.x == 0) {
     *pos = p + 1;
     *posf = (float)(p + 1);
+    *ep = e + 1ull;
   }
 }
 
@@ -374,7 +499,7 @@ __global__ void k_init(const int *prompt, uint32_t P, int *tok, unsigned long lo
   const uint32_t b = threadIdx.x;
   if (b < B) {
     tok[b] = prompt[(size_t)b * P];
-    keys[b] = 0ull;
+    if (keys) keys[b] = 0ull;   // peer-exchanged keys are cleared by k_next only
   }
   if (threadIdx.x == 0) {
     *pos = 0;
@@ -410,6 +535,14 @@ struct nl_decoder {
   unsigned long long *keys = nullptr;
   void *ws_qkv = nullptr, *ws_o = nullptr, *ws_gu = nullptr, *ws_d = nullptr, *attn_scr = nullptr;
   float2 *rope = nullptr;   // [max_seq][head_dim / 2] (cos, sin)
+  // Peer all-reduce (tensor parallelism): this rank's block of counters,
+  // key slots and receive slots, exported to the peers; every rank's block
+  // mapped here (own included).
+  bool par = false;
+  char *par_local = nullptr;
+  char *par_peer[8] = {};
+  unsigned long long *ep = nullptr;   // decode steps completed
+  int *err = nullptr;                 // a peer wait gave up
   bool keep_logits = false;
   std::map<uint32_t, cudaGraphExec_t> graphs;   // by batch
   uint64_t kernels_per_step = 0;
@@ -463,6 +596,29 @@ int allreduce(nl_decoder *D, void *buf, size_t count, int dtype, int op) {
   return NL_OK;
 }
 
+// Layout of a rank's peer block: arrival counters (set 2: argmax keys), CTA
+// completion counters, two slots of argmax keys, then the receive slots of
+// sets 0 (O-proj) and 1 (down): [rank][max_batch][hidden] tagged words.
+constexpr size_t kParCtr = 0, kParDone = 64, kParKeys = 256, kParSlots = 1024;
+size_t par_set_bytes(const nl_decoder *D) {
+  return align256((size_t)D->size * D->cfg.max_batch * D->cfg.hidden * 8u);
+}
+size_t par_bytes(const nl_decoder *D) { return kParSlots + 2 * par_set_bytes(D); }
+unsigned long long *par_slot(const nl_decoder *D, char *base, int set, int rank) {
+  return reinterpret_cast<unsigned long long *>(base + kParSlots +
+                                                (size_t)set * par_set_bytes(D)) +
+         (size_t)rank * D->cfg.max_batch * D->cfg.hidden;
+}
+unsigned long long *par_ctr(char *base, int set) {
+  return reinterpret_cast<unsigned long long *>(base + kParCtr) + set;
+}
+unsigned int *par_done(char *base, int set) {
+  return reinterpret_cast<unsigned int *>(base + kParDone) + set;
+}
+unsigned long long *par_keys(char *base) {
+  return reinterpret_cast<unsigned long long *>(base + kParKeys);
+}
+
 // Enqueue one decode step for batch B on D->stream.
 int enqueue_step(nl_decoder *D, uint32_t B) {
   const nl_decoder_config &c = D->cfg;
@@ -482,11 +638,29 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   e = launch_pdl(k_norm<kNormGather>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
                  (const int *)D->tok, (const float *)D->embed, D->h, (const float *)nullptr,
                  (const float *)D->layers[0].gattn, D->x, fast_h ? D->ws_qkv : nullptr, B, H,
-                 eps);
+                 eps, PeerIn{});
   count_launches(1);
   if (e != cudaSuccess) return cuda_status(e, "step: embed");
   const AttnGeom geom = attn_geom(B, D->hr * hd, D->hr, D->kvr, c.max_seq,
                                   (uint64_t)c.max_batch * c.max_seq * D->kvr * hd);
+  // Tensor parallelism: O / down partials go peer to peer (D->par), or
+  // through NCCL all-reduces.
+  PeerOut po[2] = {};
+  PeerIn pin[2] = {};
+  if (D->par) {
+    for (int set = 0; set < 2; set++) {
+      for (int r = 0; r < D->size; r++) po[set].dst[r] = par_slot(D, D->par_peer[r], set, D->rank);
+      po[set].n = D->size;
+      po[set].ep = D->ep;
+      po[set].tmul = c.layers;
+      pin[set].slots = par_slot(D, D->par_local, set, 0);
+      pin[set].tp = (uint32_t)D->size;
+      pin[set].slot_stride = c.max_batch * H;
+      pin[set].ep = D->ep;
+      pin[set].tmul = c.layers;
+      pin[set].err = D->err;
+    }
+  }
   for (uint32_t l = 0; l < c.layers; l++) {
     Layer &L = D->layers[l];
     e = ternary_main_launch(1, D->x, 0, L.wqkv, 0, L.sqkv, 0, nullptr, D->qkv, 0, B, D->qkv_rows,
@@ -501,13 +675,15 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
       e = ternary_prep_launch(D->ctx, 0, 1, B, D->hr * hd, D->ws_o, st, true);
       if (e != cudaSuccess) return cuda_status(e, "step: o prep");
     }
+    po[0].tadd = po[1].tadd = pin[0].tadd = pin[1].tadd = l + 1;
     e = ternary_main_launch(1, D->ctx, 0, L.wo, 0, L.so, 0, nullptr, D->o, 0, B, H, D->hr * hd,
-                            false, fast_o ? D->ws_o : nullptr, st);
+                            false, fast_o ? D->ws_o : nullptr, st, D->par ? &po[0] : nullptr);
     if (e != cudaSuccess) return cuda_status(e, "step: o");
-    if ((rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+    if (!D->par && (rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+    // tag of this layer's use: ep * layers + l + 1 (never 0: the slots start zeroed)
     e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
                    (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
-                   (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps);
+                   (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps, pin[0]);
     count_launches(1);
     if (e != cudaSuccess) return cuda_status(e, "step: ffn norm");
     e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
@@ -519,14 +695,14 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
     count_launches(1);
     if (e != cudaSuccess) return cuda_status(e, "step: swiglu");
     e = ternary_main_launch(1, D->a, 0, L.wd, 0, L.sd, 0, nullptr, D->d, 0, B, H, D->fr, false,
-                            fast_d ? D->ws_d : nullptr, st);
+                            fast_d ? D->ws_d : nullptr, st, D->par ? &po[1] : nullptr);
     if (e != cudaSuccess) return cuda_status(e, "step: down");
-    if ((rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+    if (!D->par && (rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
     const bool last = l + 1 == c.layers;
     e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
                    (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
                    (const float *)(last ? D->gfinal : D->layers[l + 1].gattn), D->x,
-                   (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps);
+                   (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps, pin[1]);
     count_launches(1);
     if (e != cudaSuccess) return cuda_status(e, "step: attn norm");
   }
@@ -536,9 +712,24 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   const float *E = D->embed + (size_t)D->v0 * H;
   float *lg = D->keep_logits ? D->logits : nullptr;
   const uint32_t lstride = c.max_batch * D->vr;
+  unsigned long long *keys = D->par ? par_keys(D->par_local) : D->keys;
+  PeerSig sig = {};
+  PeerKeys pk = {};
+  if (D->par) {
+    for (int r = 0; r < D->size; r++) {
+      sig.ctr[r] = par_ctr(D->par_peer[r], 2);
+      pk.keys[r] = par_keys(D->par_peer[r]);
+    }
+    sig.done = par_done(D->par_local, 2);
+    sig.n = pk.n = D->size;
+    pk.stride = c.max_batch;
+    pk.ctr = par_ctr(D->par_local, 2);
+    pk.err = D->err;
+  }
 #define NL_LM(NB)                                                                         \
   e = launch_pdl(k_lmhead<NB>, dim3(lmgrid), dim3(256), smem_lm, st, E, (const float *)D->x, \
-                 D->keys, lg, (const int *)D->pos, B, D->vr, D->v0, H, lstride)
+                 keys, lg, (const int *)D->pos, B, D->vr, D->v0, H, lstride,              \
+                 (const unsigned long long *)D->ep, c.max_batch, sig)
   if (B <= 1) NL_LM(1);
   else if (B <= 2) NL_LM(2);
   else if (B <= 4) NL_LM(4);
@@ -547,9 +738,9 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
 #undef NL_LM
   count_launches(1);
   if (e != cudaSuccess) return cuda_status(e, "step: lm head");
-  if ((rc = allreduce(D, D->keys, B, kNcclUint64, kNcclMax))) return rc;
-  e = launch_pdl(k_next, dim3(1), dim3(32), 0, st, D->keys, (const int *)D->prompt,
-                 D->last_positions, D->tok, D->out_tok, D->pos, D->posf, B);
+  if (!D->par && (rc = allreduce(D, D->keys, B, kNcclUint64, kNcclMax))) return rc;
+  e = launch_pdl(k_next, dim3(1), dim3(32), 0, st, keys, (const int *)D->prompt,
+                 D->last_positions, D->tok, D->out_tok, D->pos, D->posf, B, D->ep, pk);
   count_launches(1);
   return cuda_status(e, "step: next");
 }
@@ -596,6 +787,17 @@ extern "C" void nl_decoder_destroy(nl_decoder *D) {
   if (D->stream) cudaStreamSynchronize(D->stream);
   for (auto &kv : D->graphs) cudaGraphExecDestroy(kv.second);
   D->graphs.clear();
+  if (D->par) {
+    // Peers may still read this rank's keys: free only after every rank has
+    // finished its generation (an NCCL all-reduce as the barrier).
+    Nccl *n = nccl();
+    if (n && D->comm && D->ep &&
+        n->AllReduce(D->ep, D->ep, 1, kNcclUint64, kNcclMax, D->comm, D->stream) == 0)
+      cudaStreamSynchronize(D->stream);
+    for (int q = 0; q < D->size; q++)
+      if (q != D->rank && D->par_peer[q]) cudaIpcCloseMemHandle(D->par_peer[q]);
+    if (D->par_local) cudaFree(D->par_local);
+  }
   if (D->comm && nccl()) nccl()->CommDestroy(D->comm);
   for (void *p : D->allocs) cudaFree(p);
   if (D->stream) cudaStreamDestroy(D->stream);
@@ -692,6 +894,11 @@ static int decoder_build(nl_decoder *D) {
   DALLOC(D->pos, 16);
   DALLOC(D->tok, (size_t)B * 4);
   DALLOC(D->keys, (size_t)B * 8);
+  DALLOC(D->ep, 8);
+  DALLOC(D->err, 4);
+  if ((e = cudaMemsetAsync(D->ep, 0, 8, D->stream)) != cudaSuccess ||
+      (e = cudaMemsetAsync(D->err, 0, 4, D->stream)) != cudaSuccess)
+    return cuda_status(e, "decoder: counters");
   DALLOC(D->prompt, (size_t)B * c.max_seq * 4);
   DALLOC(D->out_tok, (size_t)B * c.max_seq * 4);
   DALLOC(D->ws_qkv, ternary_ws_bytes(1, B, H));
@@ -708,6 +915,101 @@ static int decoder_build(nl_decoder *D) {
   if (D->keep_logits) DALLOC(D->logits, (size_t)c.max_seq * B * D->vr * 4);
   if ((rc = set_smem_limits(D))) return rc;
   return cuda_status(cudaStreamSynchronize(D->stream), "decoder: build");
+}
+
+// Map every rank's peer block into this process (CUDA IPC handles exchanged
+// with an NCCL all-gather) and agree, with an NCCL min-reduction, on whether
+// every rank managed it; otherwise every rank keeps the NCCL all-reduces.
+// NELISP_DECODER_ALLREDUCE=nccl keeps them too.
+static int setup_peer_allreduce(nl_decoder *D) {
+  Nccl *n = nccl();
+  if (D->size <= 1 || D->size > 8 || !n || !n->AllGather) return NL_OK;
+  const char *v = getenv("NELISP_DECODER_ALLREDUCE");
+  const bool want = !(v && strcmp(v, "nccl") == 0);   // same on every rank
+  if (!want) return NL_OK;
+  cudaStream_t st = D->stream;
+  int ok = 1;
+  const size_t bytes = par_bytes(D);
+  if (cudaMalloc(&D->par_local, bytes) != cudaSuccess) { D->par_local = nullptr; ok = 0; }
+  cudaGetLastError();
+  if (ok && cudaMemset(D->par_local, 0, bytes) != cudaSuccess) ok = 0;
+  // What each rank publishes: its block's IPC handle and its device's UUID
+  // (ranks that wait on one another must not share a GPU).
+  struct Pub {
+    cudaIpcMemHandle_t h;
+    char uuid[16];
+    char pad[16];
+  };
+  Pub mine;
+  memset(&mine, 0, sizeof(mine));
+  if (ok && cudaIpcGetMemHandle(&mine.h, D->par_local) != cudaSuccess) ok = 0;
+  cudaGetLastError();
+  {
+    int devn = 0;
+    cudaDeviceProp prop;
+    if (cudaGetDevice(&devn) == cudaSuccess && cudaGetDeviceProperties(&prop, devn) == cudaSuccess)
+      memcpy(mine.uuid, &prop.uuid, 16);
+    else
+      ok = 0;
+    cudaGetLastError();
+  }
+  char *dev = nullptr;
+  int *flag = nullptr;
+  if (cudaMalloc(&dev, (size_t)D->size * sizeof(Pub)) != cudaSuccess ||
+      cudaMalloc(&flag, sizeof(int)) != cudaSuccess) {
+    if (dev) cudaFree(dev);
+    return set_error(NL_ERROR, "decoder: peer setup buffers");
+  }
+  std::vector<Pub> all(D->size);
+  ncclResult_t r = 0;
+  cudaError_t e = cudaMemcpy(dev + (size_t)D->rank * sizeof(Pub), &mine, sizeof(Pub),
+                             cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    r = n->AllGather(dev + (size_t)D->rank * sizeof(Pub), dev, sizeof(Pub), kNcclInt8, D->comm,
+                     st);
+  if (e == cudaSuccess && r == 0) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && r == 0)
+    e = cudaMemcpy(all.data(), dev, (size_t)D->size * sizeof(Pub), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess || r != 0) {
+    cudaFree(dev);
+    cudaFree(flag);
+    return set_error(NL_ERROR, "decoder: peer handle exchange failed");
+  }
+  for (int a = 0; a < D->size; a++)
+    for (int b = a + 1; b < D->size; b++)
+      if (memcmp(all[a].uuid, all[b].uuid, 16) == 0) ok = 0;   // two ranks on one GPU
+  for (int q = 0; q < D->size && ok; q++) {
+    if (q == D->rank) {
+      D->par_peer[q] = D->par_local;
+      continue;
+    }
+    void *ptr = nullptr;
+    if (cudaIpcOpenMemHandle(&ptr, all[q].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = 0;
+      break;
+    }
+    D->par_peer[q] = static_cast<char *>(ptr);
+  }
+  // every rank takes the same path
+  cudaMemcpy(flag, &ok, sizeof(int), cudaMemcpyHostToDevice);
+  r = n->AllReduce(flag, flag, 1, kNcclInt32, kNcclMin, D->comm, st);
+  int agreed = 0;
+  if (r == 0 && cudaStreamSynchronize(st) == cudaSuccess)
+    cudaMemcpy(&agreed, flag, sizeof(int), cudaMemcpyDeviceToHost);
+  cudaFree(dev);
+  cudaFree(flag);
+  if (!agreed) {
+    for (int q = 0; q < D->size; q++)
+      if (q != D->rank && D->par_peer[q]) cudaIpcCloseMemHandle(D->par_peer[q]);
+    for (int q = 0; q < 8; q++) D->par_peer[q] = nullptr;
+    if (D->par_local) cudaFree(D->par_local);
+    D->par_local = nullptr;
+    cudaGetLastError();
+    return r == 0 ? NL_OK : set_error(NL_ERROR, "decoder: peer setup agreement failed");
+  }
+  D->par = true;
+  return NL_OK;
 }
 
 extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int tp_size,
@@ -743,7 +1045,7 @@ extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int 
       return set_error(NL_ERROR, "ncclCommInitRank: %s", n->GetErrorString ? n->GetErrorString(r) : "?");
     }
   }
-  if ((rc = decoder_build(D))) {
+  if ((rc = decoder_build(D)) || (rc = setup_peer_allreduce(D))) {
     nl_decoder_destroy(D);
     return rc;
   }
@@ -771,7 +1073,8 @@ extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t promp
   auto it = D->graphs.find(batch * 100000u + prompt_len);
   if (it == D->graphs.end()) {
     // One eager step first (kernel attributes, NCCL connections), then capture.
-    k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->keys, D->pos, D->posf, batch);
+    k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->par ? nullptr : D->keys, D->pos,
+                             D->posf, batch);
     if ((rc = enqueue_step(D, batch))) return rc;
     if ((rc = cuda_status(cudaStreamSynchronize(st), "generate: warm-up"))) return rc;
     uint64_t before = nl_launch_count();
@@ -790,7 +1093,8 @@ extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t promp
     it = D->graphs.emplace(batch * 100000u + prompt_len, exec).first;
   }
   cudaGraphExec_t exec = it->second;
-  k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->keys, D->pos, D->posf, batch);
+  k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->par ? nullptr : D->keys, D->pos,
+                           D->posf, batch);
   cudaEvent_t e0, e1, e2;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
@@ -808,6 +1112,12 @@ extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t promp
   cudaEventDestroy(e1);
   cudaEventDestroy(e2);
   if (rc) return rc;
+  if (D->par) {
+    int herr = 0;
+    if ((rc = cuda_status(cudaMemcpy(&herr, D->err, 4, cudaMemcpyDeviceToHost), "generate: err")))
+      return rc;
+    if (herr) return set_error(NL_ERROR, "generate: a tensor-parallel peer exchange timed out");
+  }
   count_launches(D->kernels_per_step * (prompt_len - 1 + steps));
   if (prefill_ms) *prefill_ms = a;
   if (decode_ms) *decode_ms = b;

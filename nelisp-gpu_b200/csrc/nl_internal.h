@@ -94,11 +94,26 @@ size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols);
 cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t count,
                                 uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream,
                                 bool pdl = false);
+// Outputs of a tensor-parallel partial GEMV written straight into every
+// rank's receive slot (peer memory over NVLink, own slot included), each
+// value as one 64-bit word (tag << 32 | f32 bits) with tag = *ep * tmul +
+// tadd, the index of this use of the slots: a reader polls each word until
+// its tag shows up, so no fence or counter is needed.  n = 0: the plain
+// output Y.
+struct PeerOut {
+  unsigned long long *dst[8];
+  const unsigned long long *ep;
+  unsigned int tmul, tadd;
+  int n;
+};
+// CTAs of the decode GEMV for this shape (0 when another kernel would run).
+uint32_t ternary_dec_ctas(uint32_t count, uint32_t out, uint32_t cols, uint32_t seq);
 cudaError_t ternary_main_launch(uint32_t count, const float *X, uint64_t x_stride,
                                 const uint32_t *WP, uint64_t w_stride, const float *SCALE,
                                 uint64_t s_stride, const float *BIAS, float *Y,
                                 uint64_t y_stride, uint32_t seq, uint32_t out, uint32_t cols,
-                                bool per_block, void *ws, cudaStream_t stream);
+                                bool per_block, void *ws, cudaStream_t stream,
+                                const PeerOut *po = nullptr);
 bool ternary_fast_shape(uint32_t cols, uint32_t nblk, uint32_t wng,
                         bool per_block);
 

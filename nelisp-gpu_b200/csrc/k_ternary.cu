@@ -1192,6 +1192,15 @@ uint32_t ternary_dec_ctas(uint32_t count, uint32_t out, uint32_t cols, uint32_t 
   return (total + (1u << lg) - 1) >> lg;
 }
 
+size_t ternary_ws_bytes_best(uint32_t count, uint32_t seq, uint32_t cols, bool per_block) {
+  size_t b = ternary_ws_bytes(count, seq, cols);
+  if (ternary_umma_applies(count, seq, cols, per_block)) {
+    const size_t u = ternary_umma_ws_bytes(seq, cols);
+    if (u > b) b = u;
+  }
+  return b;
+}
+
 size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols) {
   int s = (int)(seq < (uint32_t)kMaxFastSeq ? seq : (uint32_t)kMaxFastSeq);
   if (s < 1) s = 1;
@@ -1219,6 +1228,19 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
         out, cols, nblk, wng, per_block ? 1 : 0, limit);
     count_launches(1);
     return cudaPeekAtLastError();
+  }
+  // Many sequence rows of one problem: the tcgen05 GEMM, when the workspace
+  // holds its int8 limb matrix.
+  static const bool umma_on = [] {
+    const char *v = getenv("NELISP_TERNARY_PATH");   // ring / tma: the chunked kernels
+    return !(v && (strcmp(v, "ring") == 0 || strcmp(v, "tma") == 0));
+  }();
+  if (umma_on && seq > (uint32_t)kMaxFastSeq && limit == UINT64_MAX &&
+      ternary_umma_applies(count, seq, cols, per_block)) {
+    bool launched = false;
+    cudaError_t e = ternary_umma_launch(X, WP, SCALE, BIAS, Y, seq, out, cols, ws, ws_bytes,
+                                        stream, &launched);
+    if (launched || e != cudaSuccess) return e;
   }
   // Sequences in chunks of 16 (one prep + one main launch per chunk); the
   // workspace is reused chunk to chunk, ordered by the stream.

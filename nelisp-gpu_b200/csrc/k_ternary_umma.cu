@@ -1,0 +1,430 @@
+// k_ternary_umma.cu -- the ternary GEMM for many sequence rows (prefill) on
+// the 5th-generation tensor cores (tcgen05, accumulators in TMEM).
+//
+// Y[s, o] = S[o] * sum_k t(o, k) X[s, k] (+ BIAS[o]) for seq > 16 rows, the
+// per-row-scale form of ternary-rows (lisp/nelisp-gpu-kernels.el:713-746)
+// computed exactly: every activation row is scaled by a power of two and
+// split into three int8 limbs (as in the GEMV's prep), the products are
+// summed in int32 by tcgen05.mma.kind::i8, and the limbs are recombined in
+// int64 -- so the result is the exact sum rounded once per row scale.
+//
+// One CTA computes a tile of 128 output rows x 80 sequence rows (N = 240
+// columns = 80 rows x 3 limbs) over the whole K:
+//   warp 0      TMA producer: the packed weight tile (128 rows x 128 columns,
+//               two bits each, 4 KB) and the int8 limb tile (240 x 128 B,
+//               128-byte swizzle) per stage, S-stage mbarrier ring;
+//   warps 2-5   expand the two-bit codes into the int8 A tile in shared
+//               memory (one thread per weight row; one shift and one mask per
+//               four weights, 64 * t per byte), then arrive;
+//   warp 1      allocates TMEM and issues four 128x240x32 MMAs per stage from
+//               one thread; tcgen05.commit frees the stage;
+//   warps 2-5   finally read the accumulators back (tcgen05.ld) and write Y.
+// The shift-and-mask expansion leaves the 16 codes of a packed word in the
+// order P = {3,7,11,15, 2,6,10,14, 1,5,9,13, 0,4,8,12}; the limb tile is
+// written in the same order, so the K index of A and B agrees.
+// Every mbarrier wait is bounded; one that gives up flags g_umma_error.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "nl_internal.h"
+#include "ternary_prep.cuh"
+
+namespace nl {
+namespace {
+
+constexpr int kUmmaM = 128;              // output rows per CTA
+constexpr int kUmmaTok = 80;             // sequence rows per CTA
+constexpr int kUmmaN = 3 * kUmmaTok;     // MMA N: (row, limb) columns
+constexpr int kUmmaK = 128;              // K per stage (bytes of int8)
+constexpr int kUmmaStages = 4;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kWBytes = kUmmaM * kUmmaK / 4;      // packed weights per stage
+constexpr uint32_t kABytes = kUmmaM * kUmmaK;           // int8 A per stage
+constexpr uint32_t kBBytes = kUmmaN * kUmmaK;           // int8 B per stage
+constexpr uint32_t kWaitRounds = 4096;
+constexpr uint32_t kSuspendNs = 1000000;
+constexpr uint32_t kTop2 = 0xC0C0C0C0u;
+
+__device__ int g_umma_error;
+
+__device__ __forceinline__ uint32_t su32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void bar_init(uint64_t *b, uint32_t n) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void bar_expect(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(su32(b)),
+               "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitRounds; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(su32(b)), "r"(parity), "r"(kSuspendNs) : "memory");
+    if (done) return true;
+  }
+  atomicExch(&g_umma_error, 1);
+  return false;
+}
+__device__ __forceinline__ void tma2d(void *dst, const CUtensorMap *map, int x, int y,
+                                      uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(su32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand in the 128-byte-swizzle
+// canonical layout (rows of 128 bytes, 8-row groups 1024 bytes apart).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor: s8 x s8 -> s32, both K-major, M = 128, N = kUmmaN.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kUmmaN >> 3) << 17) |
+                            ((uint32_t)(kUmmaM >> 4) << 24);
+
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                   su32(bar)) : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+
+// ---- prep: activation rows -> scale, flag and the K-permuted int8 limb rows --
+// Row s of X becomes rows 3s, 3s+1, 3s+2 of XB (limbs l0, l1, l2 with
+// xq = l0 + 256 l1 + 65536 l2 and xq = round(x * 2^e), max|x * 2^e| in
+// [2^21, 2^22)); byte p of each 16-column group holds column P[p].
+__global__ void __launch_bounds__(256)
+umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict__ XB,
+                 float *__restrict__ rowinv, int *__restrict__ rowflag) {
+  __shared__ float red[8];
+  __shared__ int sbad;
+  const uint32_t s = blockIdx.x;
+  const float *xr = X + (size_t)s * cols;
+  float m = 0.0f;
+  int bad = 0;
+  for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = xr[i];
+    m = fmaxf(m, fabsf(v));
+    bad |= !isfinite(v);
+  }
+  bad = __syncthreads_or(bad);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  if (threadIdx.x == 0) sbad = bad;
+  __syncthreads();
+  float mm = 0.0f;
+  for (int w = 0; w < 8; w++) mm = fmaxf(mm, red[w]);
+  // the exponent of the GEMV's prep (ternary_prep.cuh, row_scale)
+  bool ok = sbad == 0;
+  float mul = 0.0f, inv = 0.0f;
+  if (ok && mm > 0.0f) {
+    int E;
+    frexpf(mm, &E);
+    const int e = 22 - E;
+    if (e > 126 || e < -126) {
+      ok = false;
+    } else {
+      mul = ldexpf(1.0f, e);
+      inv = ldexpf(1.0f, -e);
+    }
+  }
+  if (threadIdx.x == 0) {
+    rowinv[s] = ok ? inv : 0.0f;
+    rowflag[s] = !ok;
+  }
+  const int P[16] = {3, 7, 11, 15, 2, 6, 10, 14, 1, 5, 9, 13, 0, 4, 8, 12};
+  int8_t *o0 = XB + (size_t)(3 * s) * cols, *o1 = o0 + cols, *o2 = o1 + cols;
+  for (uint32_t w = threadIdx.x; w < cols / 16u; w += blockDim.x) {
+    uint32_t b0[4] = {0, 0, 0, 0}, b1[4] = {0, 0, 0, 0}, b2[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < 16; p++) {
+      int l0 = 0, l1 = 0, l2 = 0;
+      if (ok) {
+        const int qv = __float2int_rn(xr[16u * w + P[p]] * mul);
+        l0 = (int)(int8_t)(qv & 0xff);
+        const int r = (qv - l0) >> 8;
+        l1 = (int)(int8_t)(r & 0xff);
+        l2 = (r - l1) >> 8;
+      }
+      b0[p >> 2] |= (uint32_t)(l0 & 0xff) << (8 * (p & 3));
+      b1[p >> 2] |= (uint32_t)(l1 & 0xff) << (8 * (p & 3));
+      b2[p >> 2] |= (uint32_t)(l2 & 0xff) << (8 * (p & 3));
+    }
+    reinterpret_cast<uint4 *>(o0)[w] = make_uint4(b0[0], b0[1], b0[2], b0[3]);
+    reinterpret_cast<uint4 *>(o1)[w] = make_uint4(b1[0], b1[1], b1[2], b1[3]);
+    reinterpret_cast<uint4 *>(o2)[w] = make_uint4(b2[0], b2[1], b2[2], b2[3]);
+  }
+}
+
+// ---- the GEMM ------------------------------------------------------------------
+__global__ void __launch_bounds__(192, 1)
+ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
+                    const float *__restrict__ S, const float *__restrict__ BIAS,
+                    const float *__restrict__ rowinv, const int *__restrict__ rowflag,
+                    float *__restrict__ Y, uint32_t seq, uint32_t out, uint32_t cols) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t *sA = base;                                   // stages x 16 KB (1024-aligned)
+  uint8_t *sB = sA + kUmmaStages * kABytes;             // stages x 30 KB (1024-aligned)
+  uint8_t *sW = sB + kUmmaStages * kBBytes;             // stages x 4 KB
+  uint64_t *full = reinterpret_cast<uint64_t *>(sW + kUmmaStages * kWBytes);
+  uint64_t *aready = full + kUmmaStages;
+  uint64_t *empty = aready + kUmmaStages;
+  uint64_t *done = empty + kUmmaStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t m0 = blockIdx.x * kUmmaM, t0 = blockIdx.y * kUmmaTok;
+  const uint32_t nk = cols / kUmmaK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kUmmaStages; i++) {
+      bar_init(&full[i], 1);
+      bar_init(&aready[i], 4);
+      bar_init(&empty[i], 1);
+    }
+    bar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     su32(tmem_slot)), "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      for (uint32_t kt = 0; kt < nk; kt++) {
+        const int st = (int)(kt % kUmmaStages);
+        if (kt >= (uint32_t)kUmmaStages &&
+            !bar_wait(&empty[st], ((kt / kUmmaStages) - 1) & 1))
+          break;
+        bar_expect(&full[st], kWBytes + kBBytes);
+        tma2d(sW + st * kWBytes, &tmW, (int)(kt * (kUmmaK / 16)), (int)m0, &full[st]);
+        tma2d(sB + st * kBBytes, &tmB, (int)(kt * kUmmaK), (int)(3 * t0), &full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      for (uint32_t kt = 0; kt < nk; kt++) {
+        const int st = (int)(kt % kUmmaStages);
+        const uint32_t ph = (kt / kUmmaStages) & 1;
+        if (!bar_wait(&full[st], ph) || !bar_wait(&aready[st], ph)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        const uint32_t a0 = su32(sA + st * kABytes), b0 = su32(sB + st * kBBytes);
+#pragma unroll
+        for (int k = 0; k < kUmmaK / 32; k++)
+          umma_i8(tmem, smem_desc(a0 + 32u * k), smem_desc(b0 + 32u * k),
+                  (kt > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty[st]);      // the stage is free once these MMAs are done
+      }
+      umma_commit(done);
+    }
+  } else {
+    // ---- expand the weights (warps 2-5, one thread per A row) ----
+    const uint32_t r = threadIdx.x - 64;          // 0..127
+    for (uint32_t kt = 0; kt < nk; kt++) {
+      const int st = (int)(kt % kUmmaStages);
+      if (!bar_wait(&full[st], (kt / kUmmaStages) & 1)) break;
+      const uint4 *wr = reinterpret_cast<const uint4 *>(sW + st * kWBytes + r * 32u);
+      const uint4 lo = wr[0], hi = wr[1];
+      const uint32_t w8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+      uint8_t *arow = sA + st * kABytes + (r >> 3) * 1024u + (r & 7u) * 128u;
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        const uint32_t w = w8[c];
+        const uint4 v = make_uint4(w & kTop2, (w << 2) & kTop2, (w << 4) & kTop2, (w << 6) & kTop2);
+        *reinterpret_cast<uint4 *>(arow + (((uint32_t)c ^ (r & 7u)) << 4)) = v;
+      }
+      // generic-proxy writes, read by the tensor cores (async proxy)
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      __syncwarp();
+      if (lane == 0) bar_arrive(&aready[st]);
+    }
+    // ---- epilogue: accumulators -> Y ----
+    if (bar_wait(done, 0)) {
+      asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+      const uint32_t q = (uint32_t)(warp & 3);      // TMEM lane quarter of this warp
+      const uint32_t o = m0 + q * 32u + (uint32_t)lane;
+      const float sc = o < out ? __ldg(S + o) : 0.0f;
+      const float bi = (BIAS && o < out) ? __ldg(BIAS + o) : 0.0f;
+      for (uint32_t c0 = 0; c0 < (uint32_t)kUmmaN; c0 += 48) {   // 16 rows per round
+        uint32_t v[48];
+        tmem_ld16(tmem + ((q * 32u) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
+        tmem_ld16(tmem + ((q * 32u) << 16) + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+        tmem_ld16(tmem + ((q * 32u) << 16) + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
+        asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const uint32_t s = t0 + c0 / 3u + (uint32_t)j;
+          if (o >= out || s >= seq || rowflag[s]) continue;
+          long long tot = (long long)(int)v[3 * j] + 256ll * (int)v[3 * j + 1] +
+                          65536ll * (int)v[3 * j + 2];
+          tot >>= 6;                                 // the operands carried 64 * t: exact
+          float y = ((float)tot * rowinv[s]) * sc;
+          if (BIAS) y = bi + y;
+          Y[(size_t)s * out + o] = y;
+        }
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+// Rows the prep flagged (non-finite or unrepresentable): y on the CUDA cores,
+// in f32, one warp per output row.
+__global__ void umma_flagged_kernel(const float *__restrict__ X, const uint32_t *__restrict__ WP,
+                                    const float *__restrict__ S, const float *__restrict__ BIAS,
+                                    const int *__restrict__ rowflag, float *__restrict__ Y,
+                                    uint32_t seq, uint32_t out, uint32_t cols) {
+  const uint32_t s = blockIdx.y;
+  if (!rowflag[s]) return;
+  const uint32_t o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (o >= out) return;
+  const uint32_t wng = cols / 16u;
+  const uint32_t *wr = WP + (size_t)o * wng;
+  const float *xr = X + (size_t)s * cols;
+  float acc = 0.0f;
+  for (uint32_t wi = lane; wi < wng; wi += 32) {
+    const uint32_t w = wr[wi];
+    for (int f = 0; f < 16; f++) {
+      const int t = (int)(w << (30 - 2 * f)) >> 30;   // sign-extended two-bit field
+      acc = fmaf((float)t, xr[16u * wi + f], acc);    // every field: 0 * inf is NaN
+    }
+  }
+  for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+  if (lane == 0) Y[(size_t)s * out + o] = (BIAS ? BIAS[o] : 0.0f) + acc * S[o];
+}
+
+typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                             const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                             const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                             CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+    cudaGetLastError();
+  }
+  return fn;
+}
+
+size_t umma_smem_bytes() {
+  return 1024 + (size_t)kUmmaStages * (kABytes + kBBytes + kWBytes) + 3 * kUmmaStages * 8 + 8 + 16;
+}
+
+}  // namespace
+
+uint32_t umma_cols_padded(uint32_t seq) {
+  const uint32_t tiles = (seq + kUmmaTok - 1) / kUmmaTok;
+  return tiles * kUmmaN;
+}
+
+size_t ternary_umma_ws_bytes(uint32_t seq, uint32_t cols) {
+  return align256((size_t)umma_cols_padded(seq) * cols) + align256((size_t)seq * 4) * 2;
+}
+
+bool ternary_umma_applies(uint32_t count, uint32_t seq, uint32_t cols, bool per_block) {
+  return count == 1 && !per_block && seq > 16 && cols % kUmmaK == 0 && cols >= kUmmaK;
+}
+
+cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float *S,
+                                const float *BIAS, float *Y, uint32_t seq, uint32_t out,
+                                uint32_t cols, void *ws, size_t ws_bytes, cudaStream_t st,
+                                bool *launched) {
+  *launched = false;
+  EncodeFn enc = encode_fn();
+  if (!enc || !ws || ws_bytes < ternary_umma_ws_bytes(seq, cols) || ((uintptr_t)WP & 15u) ||
+      ((uintptr_t)X & 15u))
+    return cudaSuccess;
+  const uint32_t ncol = umma_cols_padded(seq);
+  int8_t *XB = reinterpret_cast<int8_t *>(ws);
+  float *rowinv = reinterpret_cast<float *>((char *)ws + align256((size_t)ncol * cols));
+  int *rowflag = reinterpret_cast<int *>((char *)rowinv + align256((size_t)seq * 4));
+  CUtensorMap mw, mb;
+  {
+    const cuuint64_t dims[2] = {cols / 16u, out}, strides[1] = {(cuuint64_t)cols / 16u * 4u};
+    const cuuint32_t box[2] = {kUmmaK / 16, kUmmaM}, es[2] = {1, 1};
+    if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t *>(WP), dims, strides,
+            box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaSuccess;
+  }
+  {
+    const cuuint64_t dims[2] = {cols, ncol}, strides[1] = {cols};
+    const cuuint32_t box[2] = {kUmmaK, kUmmaN}, es[2] = {1, 1};
+    if (enc(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, XB, dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaSuccess;
+  }
+  static bool configured = false;
+  const size_t smem = umma_smem_bytes();
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(ternary_umma_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  *launched = true;
+  // rows 3*seq .. ncol of XB feed only MMA columns no output reads
+  umma_prep_kernel<<<seq, 256, 0, st>>>(X, cols, XB, rowinv, rowflag);
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return e;
+  const dim3 grid((out + kUmmaM - 1) / kUmmaM, (seq + kUmmaTok - 1) / kUmmaTok);
+  ternary_umma_kernel<<<grid, 192, smem, st>>>(mw, mb, S, BIAS, rowinv, rowflag, Y, seq, out,
+                                                cols);
+  if ((e = cudaPeekAtLastError()) != cudaSuccess) return e;
+  umma_flagged_kernel<<<dim3((out + 7) / 8, seq), 256, 0, st>>>(X, WP, S, BIAS, rowflag, Y, seq,
+                                                               out, cols);
+  count_launches(3);
+  return cudaPeekAtLastError();
+}
+
+}  // namespace nl

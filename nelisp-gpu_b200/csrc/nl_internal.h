@@ -87,6 +87,18 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
                                 void *ws, size_t ws_bytes,
                                 cudaStream_t stream);
 size_t ternary_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols);
+// The tcgen05 GEMM for seq > 16 sequence rows of one problem
+// (k_ternary_umma.cu): its workspace, whether it applies, and the launch
+// (prep + GEMM + flagged rows); *LAUNCHED false: it did not apply.
+size_t ternary_umma_ws_bytes(uint32_t seq, uint32_t cols);
+bool ternary_umma_applies(uint32_t count, uint32_t seq, uint32_t cols, bool per_block);
+cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float *S,
+                                const float *BIAS, float *Y, uint32_t seq, uint32_t out,
+                                uint32_t cols, void *ws, size_t ws_bytes, cudaStream_t st,
+                                bool *launched);
+// Workspace for the fastest path of (count, seq, cols): the larger of the
+// two.
+size_t ternary_ws_bytes_best(uint32_t count, uint32_t seq, uint32_t cols, bool per_block);
 // The two halves of the fast path, for callers that fuse the prep into the
 // kernel producing the activations: the prep alone, and the GEMV alone on a
 // workspace the prep has filled (seq <= 16; shapes the fast path does not

@@ -774,7 +774,7 @@ extern "C" int nl_dispatch_dev(const char *name, uint32_t nbuf, void *const *buf
 
 // ---- typed entry points -------------------------------------------------------------
 extern "C" size_t nl_ternary_workspace_bytes(uint32_t seq, uint32_t cols) {
-  return ternary_ws_bytes(1, seq, cols);
+  return ternary_ws_bytes_best(1, seq, cols, false);
 }
 
 static int ternary_common(uint32_t count, const float *X, uint64_t xs, const uint32_t *WP,
@@ -786,7 +786,7 @@ static int ternary_common(uint32_t count, const float *X, uint64_t xs, const uin
   if (rc) return rc;
   cudaStream_t st = (cudaStream_t)stream;
   if (!ws && ternary_fast_shape(cols, nblk, wng, per_block)) {
-    ws_bytes = ternary_ws_bytes(count, seq, cols);
+    ws_bytes = ternary_ws_bytes_best(count, seq, cols, per_block);
     ws = library_workspace(ws_bytes, st);
     if (!ws) ws_bytes = 0;   // the generic kernel needs none
   }

@@ -253,10 +253,11 @@ def test_gemv_batched_matches_single():
         assert nlo.tk_err(y[z], want[z]) < TOL
 
 
-# ---- the three fast-path kernels agree bit for bit ----------------------------
-# The decode kernel (row tiles split over warps), the persistent TMA kernel and
-# the register-ring kernel sum the same exact int32 products and share the
-# epilogue, so they must give identical bits.  NELISP_TERNARY_PATH is read once
+# ---- the fast-path kernels agree bit for bit ------------------------------------
+# The decode kernel (row tiles split over warps), the persistent TMA kernel,
+# the register-ring kernel and, for more than 16 sequence rows, the tcgen05
+# GEMM sum the same exact integer products and scale them the same way, so
+# they must give identical bits.  NELISP_TERNARY_PATH is read once
 # per process, hence one subprocess per path.
 
 _PATH_SCRIPT = r"""
@@ -277,7 +278,8 @@ def pack_trits(t):
 out_path = sys.argv[1]
 rng = np.random.default_rng(4242)
 res = {{}}
-for (seq, out, cols) in [(1, 4096, 4096), (4, 2560, 6912), (16, 1000, 2560), (7, 3840, 2560)]:
+for (seq, out, cols) in [(1, 4096, 4096), (4, 2560, 6912), (16, 1000, 2560), (7, 3840, 2560),
+                         (100, 1000, 2560), (17, 300, 512)]:
     t = rng.integers(-1, 2, size=(out, cols))
     WP = pack_trits(t)
     S = rng.uniform(0.5, 1.5, out).astype(np.float32)
@@ -285,7 +287,8 @@ for (seq, out, cols) in [(1, 4096, 4096), (4, 2560, 6912), (16, 1000, 2560), (7,
     d = torch.device("cuda")
     tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X, WP.view(np.int32), S))
     tY = torch.empty(seq * out, dtype=torch.float32, device=d)
-    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols)
+    ws = torch.empty(dev.ternary_workspace_bytes(seq, cols), dtype=torch.uint8, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols, workspace=ws)
     torch.cuda.synchronize()
     res[f"{{seq}}_{{out}}_{{cols}}"] = tY.cpu().numpy()
     res[f"x_{{seq}}_{{out}}_{{cols}}"] = X
@@ -323,3 +326,31 @@ def test_fast_path_kernels_agree_bitwise(tmp_path):
         want = nlo.ternary_gemv_rows(ref["x_" + key], ref["w_" + key], ref["s_" + key], seq,
                                      out, cols)
         assert nlo.tk_err(ref[key], want) < TOL, key
+
+
+@pytest.mark.parametrize("seq,out,cols", [(17, 128, 128), (80, 256, 2560), (81, 200, 1024),
+                                          (300, 700, 2560), (512, 2560, 6912)])
+def test_tcgen05_gemm_matches_oracle(seq, out, cols):
+    """Many sequence rows (the prefill shape): the tcgen05 GEMM, exact up to
+    the per-row power-of-two scaling, against the oracle."""
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(seq + out + cols)
+    t = rng.integers(-1, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, out).astype(np.float32)
+    X = rng.standard_normal(seq * cols).astype(np.float32)
+    X[3 * cols + 5] = np.inf if seq > 3 else X[3 * cols + 5]   # one flagged row
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X, WP.view(np.int32), S))
+    tY = torch.full((seq * out,), float("nan"), dtype=torch.float32, device=d)
+    ws = torch.empty(dev.ternary_workspace_bytes(seq, cols), dtype=torch.uint8, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols, workspace=ws)
+    torch.cuda.synchronize()
+    got = tY.cpu().numpy().reshape(seq, out)
+    want = nlo.ternary_gemv_rows(X, WP, S, seq, out, cols).reshape(seq, out)
+    ok_rows = [s for s in range(seq) if s != 3]
+    assert nlo.tk_err(got[ok_rows], want[ok_rows]) < TOL
+    if seq > 3:   # the row holding inf goes through the CUDA-core path, as the reference
+        assert np.array_equal(np.isnan(got[3]), np.isnan(want[3]))
+        assert np.array_equal(np.isinf(got[3]), np.isinf(want[3]))

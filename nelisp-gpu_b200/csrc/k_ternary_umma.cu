@@ -311,29 +311,30 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
 }
 
 // Rows the prep flagged (non-finite or unrepresentable): y on the CUDA cores,
-// in f32, one warp per output row.
+// in f32.  One CTA per sequence row, which returns at once unless flagged;
+// its warps then take the output rows in turn.
 __global__ void umma_flagged_kernel(const float *__restrict__ X, const uint32_t *__restrict__ WP,
                                     const float *__restrict__ S, const float *__restrict__ BIAS,
                                     const int *__restrict__ rowflag, float *__restrict__ Y,
                                     uint32_t seq, uint32_t out, uint32_t cols) {
-  const uint32_t s = blockIdx.y;
+  const uint32_t s = blockIdx.x;
   if (!rowflag[s]) return;
-  const uint32_t o = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (o >= out) return;
   const uint32_t wng = cols / 16u;
-  const uint32_t *wr = WP + (size_t)o * wng;
   const float *xr = X + (size_t)s * cols;
-  float acc = 0.0f;
-  for (uint32_t wi = lane; wi < wng; wi += 32) {
-    const uint32_t w = wr[wi];
-    for (int f = 0; f < 16; f++) {
-      const int t = (int)(w << (30 - 2 * f)) >> 30;   // sign-extended two-bit field
-      acc = fmaf((float)t, xr[16u * wi + f], acc);    // every field: 0 * inf is NaN
+  for (uint32_t o = threadIdx.x >> 5; o < out; o += blockDim.x >> 5) {
+    const uint32_t *wr = WP + (size_t)o * wng;
+    float acc = 0.0f;
+    for (uint32_t wi = lane; wi < wng; wi += 32) {
+      const uint32_t w = wr[wi];
+      for (int f = 0; f < 16; f++) {
+        const int t = (int)(w << (30 - 2 * f)) >> 30;   // sign-extended two-bit field
+        acc = fmaf((float)t, xr[16u * wi + f], acc);    // every field: 0 * inf is NaN
+      }
     }
+    for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
+    if (lane == 0) Y[(size_t)s * out + o] = (BIAS ? BIAS[o] : 0.0f) + acc * S[o];
   }
-  for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-  if (lane == 0) Y[(size_t)s * out + o] = (BIAS ? BIAS[o] : 0.0f) + acc * S[o];
 }
 
 typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
@@ -421,8 +422,7 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   ternary_umma_kernel<<<grid, 192, smem, st>>>(mw, mb, S, BIAS, rowinv, rowflag, Y, seq, out,
                                                 cols);
   if ((e = cudaPeekAtLastError()) != cudaSuccess) return e;
-  umma_flagged_kernel<<<dim3((out + 7) / 8, seq), 256, 0, st>>>(X, WP, S, BIAS, rowflag, Y, seq,
-                                                               out, cols);
+  umma_flagged_kernel<<<seq, 256, 0, st>>>(X, WP, S, BIAS, rowflag, Y, seq, out, cols);
   count_launches(3);
   return cudaPeekAtLastError();
 }

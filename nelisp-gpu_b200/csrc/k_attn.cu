@@ -362,6 +362,217 @@ attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
   }
 }
 
+// ---- causal attention over a whole sequence (attn-causal-gqa, prefill) --------
+// Reference: lisp/nelisp-gpu-kernels.el:949-990 -- for every (head h, row i),
+// softmax over keys j <= i of (q_i . k_j) / sqrt(hd), context = sum p_j v_j,
+// kv head h / (heads / kvheads).  Here, flash-style in f32 on the CUDA cores
+// (TF32 products would miss the 1e-4 bar): one CTA per (sequence, head,
+// 64-row query block) walks 64-key tiles up to the diagonal with an online
+// softmax.  Threads ty*16 .. ty*16+15 own query rows 4ty .. 4ty+3: their
+// scores (4 rows x 4 keys each) and their context columns (4 rows x HD/16),
+// so the running max / sum stay in registers; keys are transposed in shared
+// memory for conflict-free score loads.
+constexpr int kCausalBQ = 64, kCausalBK = 64;
+
+struct CausalGeom {
+  uint32_t seq, heads, kvheads;
+  uint64_t q_row, kv_row;           // row strides (floats) of Q / CTX and of K / V
+  uint64_t q_batch, kv_batch;       // sequence strides (floats), grid z
+  uint64_t limit;                   // invocations (h * seq + i) to compute
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256)
+attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
+                   const float *__restrict__ V, float *__restrict__ CTX, CausalGeom g) {
+  constexpr int DPT = HD / 16;                     // context columns per thread
+  extern __shared__ __align__(16) float smc[];
+  float *Qs = smc;                                 // [BQ][HD]
+  float *Kt = Qs + kCausalBQ * HD;                 // [HD][BK]
+  float *Vs = Kt + HD * kCausalBK;                 // [BK][HD]
+  float *Ps = Vs + kCausalBK * HD;                 // [BQ][BK + 1]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const uint32_t q0 = blockIdx.x * kCausalBQ, h = blockIdx.y, bz = blockIdx.z;
+  const uint32_t kvh = h / (g.heads / g.kvheads);
+  const float *Qb = Q + bz * g.q_batch + (uint64_t)h * HD;
+  const float *Kb = K + bz * g.kv_batch + (uint64_t)kvh * HD;
+  const float *Vb = V + bz * g.kv_batch + (uint64_t)kvh * HD;
+  const float scale = 1.0f / sqrtf((float)HD);
+  for (int e = tid; e < kCausalBQ * HD / 4; e += 256) {
+    const int r = e / (HD / 4), c4 = e % (HD / 4);
+    const uint32_t i = q0 + r;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < g.seq) v = *reinterpret_cast<const float4 *>(Qb + i * g.q_row + 4 * c4);
+    reinterpret_cast<float4 *>(Qs + r * HD)[c4] = v;
+  }
+  float m[4], l[4], o[4][DPT];
+#pragma unroll
+  for (int a = 0; a < 4; a++) {
+    m[a] = -INFINITY;
+    l[a] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
+  }
+  const uint32_t kend = min(g.seq, q0 + kCausalBQ);        // keys past the block's last row
+  for (uint32_t k0 = 0; k0 < kend; k0 += kCausalBK) {
+    __syncthreads();
+    for (int e = tid; e < kCausalBK * HD / 4; e += 256) {
+      const int r = e / (HD / 4), c4 = e % (HD / 4);
+      const uint32_t j = k0 + r;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (j < g.seq) {
+        kv = *reinterpret_cast<const float4 *>(Kb + j * g.kv_row + 4 * c4);
+        vv = *reinterpret_cast<const float4 *>(Vb + j * g.kv_row + 4 * c4);
+      }
+      Kt[(4 * c4 + 0) * kCausalBK + r] = kv.x;
+      Kt[(4 * c4 + 1) * kCausalBK + r] = kv.y;
+      Kt[(4 * c4 + 2) * kCausalBK + r] = kv.z;
+      Kt[(4 * c4 + 3) * kCausalBK + r] = kv.w;
+      reinterpret_cast<float4 *>(Vs + r * HD)[c4] = vv;
+    }
+    __syncthreads();
+    // scores: rows 4ty + a, keys 4tx + b
+    float sc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int b = 0; b < 4; b++) sc[a][b] = 0.0f;
+#pragma unroll 8
+    for (int d = 0; d < HD; d++) {
+      const float4 kk = *reinterpret_cast<const float4 *>(Kt + d * kCausalBK + 4 * tx);
+      float qa[4];
+#pragma unroll
+      for (int a = 0; a < 4; a++) qa[a] = Qs[(4 * ty + a) * HD + d];
+#pragma unroll
+      for (int a = 0; a < 4; a++) {
+        sc[a][0] = fmaf(qa[a], kk.x, sc[a][0]);
+        sc[a][1] = fmaf(qa[a], kk.y, sc[a][1]);
+        sc[a][2] = fmaf(qa[a], kk.z, sc[a][2]);
+        sc[a][3] = fmaf(qa[a], kk.w, sc[a][3]);
+      }
+    }
+    // causal mask, online softmax per row (reductions over the 16 threads of a row)
+#pragma unroll
+    for (int a = 0; a < 4; a++) {
+      const uint32_t i = q0 + 4 * ty + a;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int b = 0; b < 4; b++) {
+        const uint32_t j = k0 + 4 * tx + b;
+        sc[a][b] = (j <= i && j < g.seq) ? sc[a][b] * scale : -INFINITY;
+        rmax = fmaxf(rmax, sc[a][b]);
+      }
+      for (int off = 8; off > 0; off >>= 1)
+        rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+      const float mn = fmaxf(m[a], rmax);
+      const float corr = mn == -INFINITY ? 1.0f : expf(m[a] - mn);   // exp(-inf) = 0
+      float rsum = 0.0f;
+#pragma unroll
+      for (int b = 0; b < 4; b++) {
+        const float p = mn == -INFINITY ? 0.0f : expf(sc[a][b] - mn);
+        Ps[(4 * ty + a) * (kCausalBK + 1) + 4 * tx + b] = p;
+        rsum += p;
+      }
+      for (int off = 8; off > 0; off >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
+      l[a] = l[a] * corr + rsum;
+      m[a] = mn;
+#pragma unroll
+      for (int c = 0; c < DPT; c++) o[a][c] *= corr;
+    }
+    __syncwarp();
+    // context: rows 4ty + a, columns tx*DPT .. tx*DPT + DPT-1
+    const int jn = (int)min((uint32_t)kCausalBK, kend - k0);
+    for (int j = 0; j < jn; j++) {
+      float vv[DPT];
+#pragma unroll
+      for (int c = 0; c < DPT; c++) vv[c] = Vs[j * HD + tx * DPT + c];
+#pragma unroll
+      for (int a = 0; a < 4; a++) {
+        const float p = Ps[(4 * ty + a) * (kCausalBK + 1) + j];
+#pragma unroll
+        for (int c = 0; c < DPT; c++) o[a][c] = fmaf(p, vv[c], o[a][c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; a++) {
+    const uint32_t i = q0 + 4 * ty + a;
+    if (i >= g.seq || (uint64_t)h * g.seq + i >= g.limit) continue;
+    float *cr = CTX + bz * g.q_batch + i * g.q_row + (uint64_t)h * HD + tx * DPT;
+#pragma unroll
+    for (int c = 0; c < DPT; c++) cr[c] = o[a][c] / l[a];
+  }
+}
+
+// Any head size: the reference's three passes, one thread per (head, row).
+__global__ void attn_causal_simple_kernel(const float *__restrict__ Q, const float *__restrict__ K,
+                                          const float *__restrict__ V, float *__restrict__ CTX,
+                                          CausalGeom g, uint32_t hd) {
+  const uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (uint64_t)g.heads * g.seq || idx >= g.limit) return;
+  const uint32_t h = (uint32_t)(idx / g.seq), i = (uint32_t)(idx % g.seq);
+  const uint32_t kvh = h / (g.heads / g.kvheads);
+  const float *q = Q + i * g.q_row + (uint64_t)h * hd;
+  const float scale = 1.0f / sqrtf((float)hd);
+  auto score = [&](uint32_t j) {
+    const float *k = K + j * g.kv_row + (uint64_t)kvh * hd;
+    float acc = 0.0f;
+    for (uint32_t t = 0; t < hd; t++) acc = fmaf(q[t], k[t], acc);
+    return acc * scale;
+  };
+  float mx = -1.0e30f;
+  for (uint32_t j = 0; j <= i; j++) mx = fmaxf(mx, score(j));
+  float sm = 0.0f;
+  for (uint32_t j = 0; j <= i; j++) sm += expf(score(j) - mx);
+  float *c = CTX + i * g.q_row + (uint64_t)h * hd;
+  for (uint32_t t = 0; t < hd; t++) c[t] = 0.0f;
+  for (uint32_t j = 0; j <= i; j++) {
+    const float p = expf(score(j) - mx) / sm;
+    const float *v = V + j * g.kv_row + (uint64_t)kvh * hd;
+    for (uint32_t t = 0; t < hd; t++) c[t] = fmaf(p, v[t], c[t]);
+  }
+}
+
+size_t causal_smem(int hd) {
+  return ((size_t)kCausalBQ * hd + (size_t)hd * kCausalBK + (size_t)kCausalBK * hd +
+          (size_t)kCausalBQ * (kCausalBK + 1)) * sizeof(float);
+}
+
+cudaError_t causal_launch(const float *Q, const float *K, const float *V, float *CTX,
+                          const CausalGeom &g, uint32_t hd, uint32_t batch, cudaStream_t st) {
+  if (g.seq == 0 || g.heads == 0 || batch == 0) return cudaSuccess;
+  const bool fast = (hd == 64 || hd == 128) && aligned16(Q) && aligned16(K) && aligned16(V) &&
+                    aligned16(CTX) && g.q_row % 4 == 0 && g.kv_row % 4 == 0 &&
+                    g.q_batch % 4 == 0 && g.kv_batch % 4 == 0;
+  cudaError_t e;
+  if (fast) {
+    static bool configured = false;
+    if (!configured) {
+      if ((e = cudaFuncSetAttribute(attn_causal_kernel<128>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)causal_smem(128))) != cudaSuccess ||
+          (e = cudaFuncSetAttribute(attn_causal_kernel<64>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)causal_smem(64))) != cudaSuccess)
+        return e;
+      configured = true;
+    }
+    const dim3 grid((g.seq + kCausalBQ - 1) / kCausalBQ, g.heads, batch);
+    if (hd == 128)
+      attn_causal_kernel<128><<<grid, 256, causal_smem(128), st>>>(Q, K, V, CTX, g);
+    else
+      attn_causal_kernel<64><<<grid, 256, causal_smem(64), st>>>(Q, K, V, CTX, g);
+    count_launches(1);
+    return cudaPeekAtLastError();
+  }
+  for (uint32_t b = 0; b < batch; b++) {
+    attn_causal_simple_kernel<<<(unsigned)ceil_div64((uint64_t)g.heads * g.seq, 128), 128, 0, st>>>(
+        Q + b * g.q_batch, K + b * g.kv_batch, V + b * g.kv_batch, CTX + b * g.q_batch, g, hd);
+    count_launches(1);
+  }
+  return cudaPeekAtLastError();
+}
+
 // One CTA per (b, h): merge the splits and write C.
 template <int HD>
 __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
@@ -607,7 +818,49 @@ cudaError_t run_attn(const OpArgs &a) {
                      a.stream);
 }
 
+// attn-causal-gqa: buffers Q K V CTX, push (seq heads kvheads hd).
+const char *chk_causal(const OpArgs &a) {
+  const uint64_t seq = a.push[0], heads = a.push[1], kvheads = a.push[2], hd = a.push[3];
+  if (heads == 0 || kvheads == 0 || heads % kvheads || hd == 0)
+    return fmt_msg("attn-causal-gqa: heads %u, kvheads %u, hd %u do not divide", a.push[1],
+                   a.push[2], a.push[3]);
+  const char *m;
+  if ((m = need_words(a, 0, seq * heads * hd, "Q"))) return m;
+  if ((m = need_words(a, 1, seq * kvheads * hd, "K"))) return m;
+  if ((m = need_words(a, 2, seq * kvheads * hd, "V"))) return m;
+  return need_words(a, 3, seq * heads * hd, "CTX");
+}
+cudaError_t run_causal(const OpArgs &a) {
+  CausalGeom g;
+  g.seq = a.push[0];
+  g.heads = a.push[1];
+  g.kvheads = a.push[2];
+  const uint32_t hd = a.push[3];
+  g.q_row = (uint64_t)g.heads * hd;
+  g.kv_row = (uint64_t)g.kvheads * hd;
+  g.q_batch = g.kv_batch = 0;
+  g.limit = invocations(a.groups, 64);
+  return causal_launch((const float *)a.buf[0], (const float *)a.buf[1], (const float *)a.buf[2],
+                       (float *)a.buf[3], g, hd, 1, a.stream);
+}
+
 }  // namespace
+
+cudaError_t attn_causal_prefill_launch(const float *Q, const float *CK, const float *CV,
+                                       float *CTX, uint32_t B, uint32_t seq, uint32_t heads,
+                                       uint32_t kvheads, uint32_t hd, uint64_t q_batch,
+                                       uint64_t kv_batch, cudaStream_t st) {
+  CausalGeom g;
+  g.seq = seq;
+  g.heads = heads;
+  g.kvheads = kvheads;
+  g.q_row = (uint64_t)heads * hd;
+  g.kv_row = (uint64_t)kvheads * hd;
+  g.q_batch = q_batch;
+  g.kv_batch = kv_batch;
+  g.limit = UINT64_MAX;
+  return causal_launch(Q, CK, CV, CTX, g, hd, B, st);
+}
 
 AttnGeom attn_geom(uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads,
                    uint32_t maxseq, uint64_t cache_words) {
@@ -693,6 +946,7 @@ const OpSpec kAttnOps[] = {
     {"cache-append-b", 3, 3, chk_cache_append<true>, no_scratch, run_cache_append<true>},
     {"decode-attn", 5, 3, chk_attn<false>, scr_attn<false>, run_attn<false>},
     {"decode-attn-b", 5, 5, chk_attn<true>, scr_attn<true>, run_attn<true>},
+    {"attn-causal-gqa", 4, 4, chk_causal, no_scratch, run_causal},
 };
 const int kAttnOpsCount = sizeof(kAttnOps) / sizeof(kAttnOps[0]);
 

@@ -191,6 +191,13 @@ cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, cons
                                     float *C, const AttnGeom &g, const float2 *rope,
                                     void *scratch, cudaStream_t st);
 size_t attn_rope_scratch_bytes(const AttnGeom &g);   // 0: shape not covered
+// Causal attention over rows 0..seq-1 of B sequences (attn-causal-gqa per
+// sequence): Q / CTX rows of heads*hd floats, K / V rows of kvheads*hd,
+// sequence b at + b * q_batch / + b * kv_batch floats.
+cudaError_t attn_causal_prefill_launch(const float *Q, const float *CK, const float *CV,
+                                       float *CTX, uint32_t B, uint32_t seq, uint32_t heads,
+                                       uint32_t kvheads, uint32_t hd, uint64_t q_batch,
+                                       uint64_t kv_batch, cudaStream_t st);
 
 // Library workspace for typed calls that pass no workspace (nl_runtime.cu).
 void *library_workspace(size_t bytes, cudaStream_t stream);

@@ -68,6 +68,7 @@ def _declare(L):
         "nlo_decode_rope_b": [_F] * 6 + [_u32] * 3,
         "nlo_cache_append_b": [_F, _F, _F] + [_u32] * 3,
         "nlo_decode_attn_b": [_F] * 5 + [_u32] * 5,
+        "nlo_attn_causal_gqa": [_F] * 4 + [_u32] * 4,
         "nlo_embed_gather": [_F, _F, _F, _u32, _u32],
         "nlo_matmul_sample_ref": [_u32] * 4,
         "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
@@ -254,6 +255,14 @@ def decode_attn_b(Q, CK, CV, POS, B, dim, heads, kvheads, maxseq):
     lib().nlo_decode_attn_b(_f(Q), _f(CK), _f(CV), _f(POS), _f(C),
                             B, dim, heads, kvheads, maxseq)
     return C
+
+
+def attn_causal_gqa(Q, K, V, seq, heads, kvheads, hd):
+    """attn-causal-gqa (lisp/nelisp-gpu-kernels.el:949-990): CTX [seq x heads*hd]."""
+    Q, K, V = f32(Q), f32(K), f32(V)
+    CTX = np.zeros(seq * heads * hd, np.float32)
+    lib().nlo_attn_causal_gqa(_f(Q), _f(K), _f(V), _f(CTX), seq, heads, kvheads, hd)
+    return CTX
 
 
 def embed_gather(TOK, WTE, seq, dim):

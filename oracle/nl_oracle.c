@@ -451,6 +451,45 @@ void nlo_decode_attn_b(const float *Q, const float *CK, const float *CV,
   }
 }
 
+/* lisp/nelisp-gpu-kernels.el:949-990 (attn-causal-gqa): one invocation per
+ * (head h, row i), idx = h * seq + i; three passes over keys j <= i -- the
+ * maximum (starting at -1e30), the normaliser, then the context accumulated
+ * into CTX in key order with p_j = exp(s_j - mx) / sm. */
+void nlo_attn_causal_gqa(const float *Q, const float *K, const float *V, float *CTX,
+                         uint32_t seq, uint32_t heads, uint32_t kvheads, uint32_t hd) {
+  uint32_t qdim = heads * hd, kvdim = kvheads * hd, grp = heads / kvheads;
+  float scale = 1.0f / sqrtf((float)hd);
+  long long total = (long long)heads * seq;
+#pragma omp parallel for schedule(dynamic, 16)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t h = (uint32_t)(idx / seq), i = (uint32_t)(idx % seq);
+    uint32_t qb = i * qdim + h * hd, kc = (h / grp) * hd, n = i + 1;
+    float mx = -1.0e30f;
+    for (uint32_t j = 0; j < n; j++) {
+      uint32_t kb = j * kvdim + kc;
+      float acc = 0.0f;
+      for (uint32_t t = 0; t < hd; t++) acc = acc + Q[qb + t] * K[kb + t];
+      acc = acc * scale;
+      if (acc > mx) mx = acc;
+    }
+    float sm = 0.0f;
+    for (uint32_t j = 0; j < n; j++) {
+      uint32_t kb = j * kvdim + kc;
+      float acc = 0.0f;
+      for (uint32_t t = 0; t < hd; t++) acc = acc + Q[qb + t] * K[kb + t];
+      sm = sm + expf(acc * scale - mx);
+    }
+    for (uint32_t t = 0; t < hd; t++) CTX[qb + t] = 0.0f;
+    for (uint32_t j = 0; j < n; j++) {
+      uint32_t kb = j * kvdim + kc;
+      float acc = 0.0f;
+      for (uint32_t t = 0; t < hd; t++) acc = acc + Q[qb + t] * K[kb + t];
+      float pj = expf(acc * scale - mx) / sm;
+      for (uint32_t t = 0; t < hd; t++) CTX[qb + t] = CTX[qb + t] + pj * V[kb + t];
+    }
+  }
+}
+
 /* lisp/nelisp-gpu-kernels.el:1385-1392 (embed-gather) */
 void nlo_embed_gather(const float *TOK, const float *WTE, float *C,
                       uint32_t seq, uint32_t dim) {

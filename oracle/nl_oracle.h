@@ -80,6 +80,8 @@ void nlo_decode_rope_b(const float *X, const float *CO, const float *SI,
 void nlo_cache_append_b(const float *SRC, const float *POS, float *CACHE,
                         uint32_t B, uint32_t kvdim, uint32_t maxseq);
 /* decode-attn-b :368-390 (decode-attn :317-338 is B=1) */
+void nlo_attn_causal_gqa(const float *Q, const float *K, const float *V, float *CTX,
+                         uint32_t seq, uint32_t heads, uint32_t kvheads, uint32_t hd);
 void nlo_decode_attn_b(const float *Q, const float *CK, const float *CV,
                        const float *POS, float *C, uint32_t B, uint32_t dim,
                        uint32_t heads, uint32_t kvheads, uint32_t maxseq);

@@ -57,7 +57,7 @@ def test_registry_names_the_reference_kernels(lib):
            "pack-act-rows", "bitlinear-dp4a-rows", "bitlinear-dp4a-1f", "matmul",
            "matmul-tiled", "matmul-reg", "linear", "softmax", "silu-mul", "add2",
            "rmsnorm-istd", "rmsnorm-fwd", "rope-half", "decode-rope", "decode-rope-b",
-           "cache-append", "cache-append-b", "decode-attn", "decode-attn-b",
+           "cache-append", "cache-append-b", "decode-attn", "decode-attn-b", "attn-causal-gqa",
            "embed-gather", "scale"}
     assert hot <= names
     nb, npush = ctypes.c_uint32(), ctypes.c_uint32()

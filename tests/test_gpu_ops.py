@@ -301,3 +301,36 @@ def test_resident_table_order_and_readback(host):
     assert np.array_equal(host.read_resident(h, 8), np.arange(8))
     for x in (hs[0], h, hs[2]):
         host.free(x)
+
+
+# ---- attn-causal-gqa (prefill attention, kernels.el:949-990) -----------------
+
+@pytest.mark.parametrize("seq,heads,kvheads,hd", [
+    (1, 4, 4, 128), (5, 8, 2, 128), (64, 4, 4, 128), (65, 4, 1, 128), (130, 20, 20, 128),
+    (300, 8, 4, 64), (47, 6, 3, 32),        # hd 32: the three-pass fallback
+])
+def test_attn_causal_gqa(host, seq, heads, kvheads, hd):
+    rng = np.random.default_rng(seq * 7 + heads + hd)
+    Q = rng.standard_normal(seq * heads * hd).astype(np.float32)
+    K = rng.standard_normal(seq * kvheads * hd).astype(np.float32)
+    V = rng.standard_normal(seq * kvheads * hd).astype(np.float32)
+    C = host.run2("attn-causal-gqa", [("in", Q), ("in", K), ("in", V), ("out", seq * heads * hd)],
+                  [seq, heads, kvheads, hd], g64(heads * seq))[0]
+    want = nlo.attn_causal_gqa(Q, K, V, seq, heads, kvheads, hd)
+    assert nlo.tk_err(C, want) < 1e-4
+
+
+def test_attn_causal_gqa_short_grid(host):
+    # groups cover the first 64 (head, row) invocations, h-major: head 0 rows
+    # 0..39 and head 1 rows 0..23; the rest of CTX stays zero
+    seq, heads, kvheads, hd = 40, 2, 1, 128
+    rng = np.random.default_rng(3)
+    Q = rng.standard_normal(seq * heads * hd).astype(np.float32)
+    K = rng.standard_normal(seq * kvheads * hd).astype(np.float32)
+    V = rng.standard_normal(seq * kvheads * hd).astype(np.float32)
+    C = host.run2("attn-causal-gqa", [("in", Q), ("in", K), ("in", V), ("out", seq * heads * hd)],
+                  [seq, heads, kvheads, hd], 1)[0].reshape(seq, heads, hd)
+    want = nlo.attn_causal_gqa(Q, K, V, seq, heads, kvheads, hd).reshape(seq, heads, hd)
+    assert nlo.tk_err(C[:, 0], want[:, 0]) < 1e-4
+    assert nlo.tk_err(C[:24, 1], want[:24, 1]) < 1e-4
+    assert not C[24:, 1].any()

@@ -181,3 +181,37 @@ def test_rope_half_against_numpy():
     want = np.concatenate([x[..., :half] * c - x[..., half:] * s,
                            x[..., half:] * c + x[..., :half] * s], axis=-1)
     assert np.max(np.abs(Y - want)) < 1e-5
+
+
+def test_oracle_attn_causal_gqa_follows_the_reference_loop():
+    """nlo_attn_causal_gqa against a direct Python transcription of
+    kernels.el:949-990 (three passes per (head, row), f32 arithmetic)."""
+    rng = np.random.default_rng(11)
+    seq, heads, kvh, hd = 6, 4, 2, 8
+    Q = rng.standard_normal(seq * heads * hd).astype(np.float32)
+    K = rng.standard_normal(seq * kvh * hd).astype(np.float32)
+    V = rng.standard_normal(seq * kvh * hd).astype(np.float32)
+    got = nlo.attn_causal_gqa(Q, K, V, seq, heads, kvh, hd)
+    f = np.float32
+    want = np.zeros(seq * heads * hd, np.float32)
+    qdim, kvdim, grp, scale = heads * hd, kvh * hd, heads // kvh, f(1.0) / np.sqrt(f(hd))
+    for idx in range(heads * seq):
+        h, i = idx // seq, idx % seq
+        qb, kc = i * qdim + h * hd, (h // grp) * hd
+
+        def score(j):
+            acc = f(0.0)
+            for t in range(hd):
+                acc = f(acc + f(Q[qb + t] * K[j * kvdim + kc + t]))
+            return f(acc * scale)
+        mx = f(-1.0e30)
+        for j in range(i + 1):
+            mx = max(mx, score(j))
+        sm = f(0.0)
+        for j in range(i + 1):
+            sm = f(sm + f(np.exp(f(score(j) - mx))))
+        for j in range(i + 1):
+            pj = f(f(np.exp(f(score(j) - mx))) / sm)
+            for t in range(hd):
+                want[qb + t] = f(want[qb + t] + f(pj * V[j * kvdim + kc + t]))
+    assert np.max(np.abs(got - want)) < 2e-6

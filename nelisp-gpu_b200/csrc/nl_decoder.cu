@@ -507,6 +507,64 @@ __global__ void k_init(const int *prompt, uint32_t P, int *tok, unsigned long lo
   }
 }
 
+// ---- batched prefill ----------------------------------------------------------------
+// Positions 0 .. P-2 of every sequence in one pass per layer (rows r = b * n + t,
+// n = P - 1): the same layer math as the decode step, with the GEMMs on the
+// tcgen05 kernel and causal attention over the prompt; it fills the KV cache,
+// and decoding continues with the last prompt token at position P - 1.
+
+// Row r's token: prompt[b * P + t].
+__global__ void k_pf_tokens(const int *prompt, uint32_t P, uint32_t n, uint32_t B, int *tok) {
+  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < B * n; i += gridDim.x * blockDim.x)
+    tok[i] = prompt[(size_t)(i / n) * P + i % n];
+}
+
+// RoPE of q and k at position t (the decode step's cos/sin table) and the
+// cache append of k and v, for every prefill row.
+__global__ void k_pf_rope(const float *__restrict__ qkv, float *__restrict__ q,
+                          float *__restrict__ ck, float *__restrict__ cv,
+                          const float2 *__restrict__ rope, uint32_t B, uint32_t n, uint32_t hr,
+                          uint32_t kvr, uint32_t hd, uint32_t maxseq) {
+  const uint32_t half = hd / 2, nh = hr + 2 * kvr, rowlen = nh * hd, kvdim = kvr * hd;
+  const uint64_t total = (uint64_t)B * n * nh * half;
+  for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t m = (uint32_t)(idx % half);
+    const uint32_t head = (uint32_t)((idx / half) % nh);
+    const uint32_t r = (uint32_t)(idx / ((uint64_t)half * nh));
+    const uint32_t b = r / n, t = r % n;
+    const float *src = qkv + (size_t)r * rowlen + (size_t)head * hd;
+    const float a0 = src[m], a1 = src[m + half];
+    if (head < hr + kvr) {
+      const float2 cs = rope[(size_t)t * half + m];
+      const float y0 = __fsub_rn(__fmul_rn(a0, cs.x), __fmul_rn(a1, cs.y));
+      const float y1 = __fadd_rn(__fmul_rn(a1, cs.x), __fmul_rn(a0, cs.y));
+      float *dst = head < hr ? q + (size_t)r * hr * hd + (size_t)head * hd
+                             : ck + ((size_t)b * maxseq + t) * kvdim + (size_t)(head - hr) * hd;
+      dst[m] = y0;
+      dst[m + half] = y1;
+    } else {
+      float *dst = cv + ((size_t)b * maxseq + t) * kvdim + (size_t)(head - hr - kvr) * hd;
+      dst[m] = a0;
+      dst[m + half] = a1;
+    }
+  }
+}
+
+// After the batched prefill: position P - 1 and its token.
+__global__ void k_pf_init(const int *prompt, uint32_t P, int *tok, unsigned long long *keys,
+                          int *pos, float *posf, uint32_t B) {
+  const uint32_t b = threadIdx.x;
+  if (b < B) {
+    tok[b] = prompt[(size_t)b * P + P - 1];
+    if (keys) keys[b] = 0ull;
+  }
+  if (threadIdx.x == 0) {
+    *pos = (int)P - 1;
+    *posf = (float)(P - 1);
+  }
+}
+
 }  // namespace
 
 // ---- the decoder object -------------------------------------------------------------------
@@ -538,6 +596,14 @@ struct nl_decoder {
   // Peer all-reduce (tensor parallelism): this rank's block of counters,
   // key slots and receive slots, exported to the peers; every rank's block
   // mapped here (own included).
+  // batched prefill buffers (rows = batch * (prompt - 1)), grown on demand
+  uint32_t pf_cap = 0;
+  std::vector<void *> pf_allocs;
+  int *pf_tok = nullptr;
+  float *pf_h = nullptr, *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_ctx = nullptr,
+        *pf_o = nullptr, *pf_gu = nullptr, *pf_a = nullptr, *pf_d = nullptr;
+  void *pf_ws = nullptr;
+  size_t pf_ws_bytes = 0;
   bool par = false;
   char *par_local = nullptr;
   char *par_peer[8] = {};
@@ -800,6 +866,7 @@ extern "C" void nl_decoder_destroy(nl_decoder *D) {
   }
   if (D->comm && nccl()) nccl()->CommDestroy(D->comm);
   for (void *p : D->allocs) cudaFree(p);
+  for (void *p : D->pf_allocs) cudaFree(p);
   if (D->stream) cudaStreamDestroy(D->stream);
   delete D;
 }
@@ -1053,6 +1120,105 @@ extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int 
   return NL_OK;
 }
 
+// Buffers for a batched prefill of ROWS rows (reallocated when larger).
+static int prefill_buffers(nl_decoder *D, uint32_t rows) {
+  if (rows <= D->pf_cap) return NL_OK;
+  cudaStreamSynchronize(D->stream);
+  for (void *p : D->pf_allocs) cudaFree(p);
+  D->pf_allocs.clear();
+  D->pf_cap = 0;
+  const nl_decoder_config &c = D->cfg;
+  const size_t R = rows, H = c.hidden, hq = (size_t)D->hr * c.head_dim;
+  size_t ws = ternary_ws_bytes_best(1, rows, c.hidden, false);
+  if (ternary_ws_bytes_best(1, rows, (uint32_t)hq, false) > ws)
+    ws = ternary_ws_bytes_best(1, rows, (uint32_t)hq, false);
+  if (ternary_ws_bytes_best(1, rows, D->fr, false) > ws)
+    ws = ternary_ws_bytes_best(1, rows, D->fr, false);
+  struct {
+    void **p;
+    size_t bytes;
+  } want[] = {{(void **)&D->pf_tok, R * 4},          {(void **)&D->pf_h, R * H * 4},
+              {(void **)&D->pf_x, R * H * 4},          {(void **)&D->pf_qkv, R * D->qkv_rows * 4},
+              {(void **)&D->pf_q, R * hq * 4},         {(void **)&D->pf_ctx, R * hq * 4},
+              {(void **)&D->pf_o, R * H * 4},          {(void **)&D->pf_gu, R * 2 * D->fr * 4},
+              {(void **)&D->pf_a, R * D->fr * 4},      {(void **)&D->pf_d, R * H * 4},
+              {&D->pf_ws, ws}};
+  for (auto &w : want) {
+    cudaError_t e = cudaMalloc(w.p, w.bytes ? w.bytes : 16);
+    if (e != cudaSuccess) {
+      for (void *p : D->pf_allocs) cudaFree(p);
+      D->pf_allocs.clear();
+      return cuda_status(e, "prefill: cudaMalloc");
+    }
+    D->pf_allocs.push_back(*w.p);
+  }
+  D->pf_ws_bytes = ws;
+  D->pf_cap = rows;
+  return NL_OK;
+}
+
+// Positions 0 .. P-2 of BATCH sequences in one pass per layer (see k_pf_tokens).
+static int run_prefill(nl_decoder *D, uint32_t B, uint32_t P) {
+  const nl_decoder_config &c = D->cfg;
+  const uint32_t n = P - 1, rows = B * n, H = c.hidden, hd = c.head_dim, hq = D->hr * hd;
+  const float eps = c.rms_eps;
+  cudaStream_t st = D->stream;
+  int rc;
+  if ((rc = prefill_buffers(D, rows))) return rc;
+  cudaError_t e;
+  k_pf_tokens<<<grid_for(rows, 256), 256, 0, st>>>(D->prompt, P, n, B, D->pf_tok);
+  const dim3 gnorm(rows * kRowCluster);
+  const size_t smem_h = (size_t)row_slice_cols(H) * sizeof(float);
+  k_norm<kNormGather><<<gnorm, kNormThreads, smem_h, st>>>(
+      D->pf_tok, D->embed, D->pf_h, nullptr, D->layers[0].gattn, D->pf_x, nullptr, rows, H, eps,
+      PeerIn{});
+  count_launches(2);
+  if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "prefill: embed");
+  auto gemm = [&](const float *X, const uint32_t *W, const float *S, float *Y, uint32_t out,
+                  uint32_t cols) {
+    return ternary_gemv_launch(1, X, 0, W, 0, S, 0, nullptr, Y, 0, rows, out, cols, cols / 128,
+                               cols / 16, false, UINT64_MAX, D->pf_ws, D->pf_ws_bytes, st);
+  };
+  for (uint32_t l = 0; l < c.layers; l++) {
+    Layer &L = D->layers[l];
+    if ((e = gemm(D->pf_x, L.wqkv, L.sqkv, D->pf_qkv, D->qkv_rows, H)) != cudaSuccess)
+      return cuda_status(e, "prefill: qkv");
+    const uint64_t nrope = (uint64_t)rows * (D->hr + 2 * D->kvr) * (hd / 2);
+    k_pf_rope<<<grid_for(nrope, 256), 256, 0, st>>>(D->pf_qkv, D->pf_q, L.ck, L.cv, D->rope, B, n,
+                                                    D->hr, D->kvr, hd, c.max_seq);
+    count_launches(1);
+    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "prefill: rope");
+    if ((e = attn_causal_prefill_launch(D->pf_q, L.ck, L.cv, D->pf_ctx, B, n, D->hr, D->kvr, hd,
+                                        (uint64_t)n * hq, (uint64_t)c.max_seq * D->kvr * hd,
+                                        st)) != cudaSuccess)
+      return cuda_status(e, "prefill: attention");
+    if ((e = gemm(D->pf_ctx, L.wo, L.so, D->pf_o, H, hq)) != cudaSuccess)
+      return cuda_status(e, "prefill: o");
+    if ((rc = allreduce(D, D->pf_o, (size_t)rows * H, kNcclFloat32, kNcclSum))) return rc;
+    if (l + 1 == c.layers) break;   // the last layer's FFN feeds no cache
+    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->pf_h, D->pf_o,
+                                                           L.gffn, D->pf_x, nullptr, rows, H,
+                                                           eps, PeerIn{});
+    count_launches(1);
+    if ((e = gemm(D->pf_x, L.wgu, L.sgu, D->pf_gu, 2 * D->fr, H)) != cudaSuccess)
+      return cuda_status(e, "prefill: gate/up");
+    k_silu_prep<<<gnorm, kNormThreads, (size_t)row_slice_cols(D->fr) * sizeof(float), st>>>(
+        D->pf_gu, D->pf_a, nullptr, rows, D->fr);
+    count_launches(1);
+    if ((e = gemm(D->pf_a, L.wd, L.sd, D->pf_d, H, D->fr)) != cudaSuccess)
+      return cuda_status(e, "prefill: down");
+    if ((rc = allreduce(D, D->pf_d, (size_t)rows * H, kNcclFloat32, kNcclSum))) return rc;
+    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->pf_h, D->pf_d,
+                                                           D->layers[l + 1].gattn, D->pf_x,
+                                                           nullptr, rows, H, eps, PeerIn{});
+    count_launches(1);
+    if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "prefill: norms");
+  }
+  k_pf_init<<<1, 32, 0, st>>>(D->prompt, P, D->tok, D->par ? nullptr : D->keys, D->pos, D->posf, B);
+  count_launches(1);
+  return cuda_status(cudaPeekAtLastError(), "prefill: init");
+}
+
 extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t prompt_len,
                                    const int32_t *prompt, uint32_t steps, int32_t *out_tokens,
                                    double *prefill_ms, double *decode_ms) {
@@ -1093,14 +1259,28 @@ extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t promp
     it = D->graphs.emplace(batch * 100000u + prompt_len, exec).first;
   }
   cudaGraphExec_t exec = it->second;
-  k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->par ? nullptr : D->keys, D->pos,
-                           D->posf, batch);
+  // Prompts of more than 16 rows in all: the batched prefill; shorter ones
+  // step through the prompt with the decode graph (teacher forcing).
+  const bool batched = prompt_len >= 2 && (uint64_t)batch * (prompt_len - 1) > 16;
+  if (batched && (rc = prefill_buffers(D, batch * (prompt_len - 1)))) return rc;
+  if (!batched)
+    k_init<<<1, 32, 0, st>>>(D->prompt, prompt_len, D->tok, D->par ? nullptr : D->keys, D->pos,
+                             D->posf, batch);
   cudaEvent_t e0, e1, e2;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
   cudaEventCreate(&e2);
   cudaEventRecord(e0, st);
-  for (uint32_t i = 0; i + 1 < prompt_len; i++) cudaGraphLaunch(exec, st);
+  if (batched) {
+    if ((rc = run_prefill(D, batch, prompt_len))) {
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      cudaEventDestroy(e2);
+      return rc;
+    }
+  } else {
+    for (uint32_t i = 0; i + 1 < prompt_len; i++) cudaGraphLaunch(exec, st);
+  }
   cudaEventRecord(e1, st);
   for (uint32_t i = 0; i < steps; i++) cudaGraphLaunch(exec, st);
   cudaEventRecord(e2, st);
@@ -1118,7 +1298,7 @@ extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t promp
       return rc;
     if (herr) return set_error(NL_ERROR, "generate: a tensor-parallel peer exchange timed out");
   }
-  count_launches(D->kernels_per_step * (prompt_len - 1 + steps));
+  count_launches(D->kernels_per_step * ((batched ? 0u : prompt_len - 1) + steps));
   if (prefill_ms) *prefill_ms = a;
   if (decode_ms) *decode_ms = b;
   D->last_batch = batch;

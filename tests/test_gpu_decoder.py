@@ -74,3 +74,32 @@ def test_decoder_rejects_bad_requests():
     with pytest.raises(NlError):
         dec.generate(np.full((1, 2), SMALL["vocab"]), 2)     # token out of range
     dec.close()
+
+
+def test_decoder_batched_prefill_matches_cpu_model():
+    """Prompts of more than 16 rows in all take the batched prefill (tcgen05
+    GEMMs, causal attention over the prompt); the generated tokens and the
+    logits from the last prompt position on match the CPU model, which steps
+    through the prompt one position at a time."""
+    from nelisp_cuda.decoder import Decoder
+    cfg = dict(SMALL, heads=8, kv_heads=4, head_dim=64, hidden=512, ffn=1024, seed=23)
+    rng = np.random.default_rng(9)
+    B, P, steps, max_seq = 3, 40, 5, 48
+    prompt = rng.integers(0, cfg["vocab"], size=(B, P))
+    dec = Decoder(cfg, max_batch=B, max_seq=max_seq, keep_logits=True)
+    toks, pf, dc = dec.generate(prompt, steps)
+    lg = dec.logits()
+    dec.close()
+    want_t, want_lg = nlo.decoder_generate(dict(cfg, max_batch=B, max_seq=max_seq), prompt, steps,
+                                           keep_logits=True)
+    for p in range(P - 1, P + steps - 1):
+        for b in range(B):
+            err = nlo.tk_err(lg[p, b], want_lg[p, b])
+            assert err < 1e-4, (p, b, err)
+    for b in range(B):
+        for i in range(steps):
+            row = want_lg[P - 1 + i, b]
+            top2 = np.sort(row)[-2:]
+            if top2[1] - top2[0] < 1e-3 * max(1.0, abs(top2[1])):
+                break
+            assert toks[b, i] == want_t[b, i], (b, i)

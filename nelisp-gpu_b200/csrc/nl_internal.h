@@ -54,6 +54,8 @@ extern const OpSpec kRowOps[];
 extern const int kRowOpsCount;
 extern const OpSpec kAttnOps[];
 extern const int kAttnOpsCount;
+extern const OpSpec kKvOps[];
+extern const int kKvOpsCount;
 
 // Error reporting (nl_runtime.cu).
 int set_error(int code, const char *fmt, ...);

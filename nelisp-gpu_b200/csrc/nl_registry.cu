@@ -19,7 +19,7 @@ struct Table {
 const Table kTables[] = {
     {kTernaryOps, &kTernaryOpsCount}, {kInt8Ops, &kInt8OpsCount},
     {kDenseOps, &kDenseOpsCount},     {kRowOps, &kRowOpsCount},
-    {kAttnOps, &kAttnOpsCount},
+    {kAttnOps, &kAttnOpsCount},       {kKvOps, &kKvOpsCount},
 };
 
 }  // namespace

@@ -69,6 +69,14 @@ def _declare(L):
         "nlo_cache_append_b": [_F, _F, _F] + [_u32] * 3,
         "nlo_decode_attn_b": [_F] * 5 + [_u32] * 5,
         "nlo_attn_causal_gqa": [_F] * 4 + [_u32] * 4,
+        "nlo_cache_append_ring": [_F] * 3 + [_u32] * 3,
+        "nlo_qkv_append": [_F] * 3 + [_u32] * 3,
+        "nlo_cache_append_paged": [_F] * 5 + [_u32] * 4,
+        "nlo_block_copy": [_F] + [_u32] * 4,
+        "nlo_decode_rope_b_v": [_F] * 6 + [_u32] * 3,
+        "nlo_decode_attn_stream": [_F] * 7 + [_u32] * 5,
+        "nlo_attn_stream_entries": [_F] * 7 + [_u32] * 5,
+        "nlo_decode_attn_paged": [_F] * 7 + [_u32] * 6,
         "nlo_embed_gather": [_F, _F, _F, _u32, _u32],
         "nlo_matmul_sample_ref": [_u32] * 4,
         "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
@@ -263,6 +271,66 @@ def attn_causal_gqa(Q, K, V, seq, heads, kvheads, hd):
     CTX = np.zeros(seq * heads * hd, np.float32)
     lib().nlo_attn_causal_gqa(_f(Q), _f(K), _f(V), _f(CTX), seq, heads, kvheads, hd)
     return CTX
+
+
+def _fz(a):
+    return _f(a) if a is not None else None
+
+
+def cache_append_ring(SRC, POS, CACHE, kvdim, nsink, win):
+    out = f32(CACHE).copy()
+    lib().nlo_cache_append_ring(_f(f32(SRC)), _f(f32(POS)), _f(out), kvdim, nsink, win)
+    return out
+
+
+def qkv_append(QKV, CK, CV, dim, kvdim, wbase):
+    ck, cv = f32(CK).copy(), f32(CV).copy()
+    lib().nlo_qkv_append(_f(f32(QKV)), _f(ck), _f(cv), dim, kvdim, wbase)
+    return ck, cv
+
+
+def cache_append_paged(SRC, POS, LENS, TABLE, POOL, B, kvdim, bs, mbps):
+    out = f32(POOL).copy()
+    lib().nlo_cache_append_paged(_f(f32(SRC)), _fz(None if POS is None else f32(POS)),
+                                 _fz(None if LENS is None else f32(LENS)), _f(f32(TABLE)),
+                                 _f(out), B, kvdim, bs, mbps)
+    return out
+
+
+def block_copy(POOL, bs, kvdim, src, dst):
+    out = f32(POOL).copy()
+    lib().nlo_block_copy(_f(out), bs, kvdim, src, dst)
+    return out
+
+
+def decode_rope_b_v(X, CO, SI, SG, LENS, B, cols, heads):
+    C = np.zeros(B * cols, np.float32)
+    lib().nlo_decode_rope_b_v(_f(f32(X)), _f(f32(CO)), _f(f32(SI)), _f(f32(SG)), _f(f32(LENS)),
+                              _f(C), B, cols, heads)
+    return C
+
+
+def decode_attn_stream(Q, CK, CV, POS, CO, SI, dim, heads, kvheads, nsink, win):
+    C = np.zeros(dim, np.float32)
+    lib().nlo_decode_attn_stream(_f(f32(Q)), _f(f32(CK)), _f(f32(CV)), _f(f32(POS)), _f(f32(CO)),
+                                 _f(f32(SI)), _f(C), dim, heads, kvheads, nsink, win)
+    return C
+
+
+def attn_stream_entries(Q, CK, CV, ENT, CO, SI, dim, heads, kvheads, ne, qcrel):
+    C = np.zeros(dim, np.float32)
+    lib().nlo_attn_stream_entries(_f(f32(Q)), _f(f32(CK)), _f(f32(CV)), _f(f32(ENT)),
+                                  _f(f32(CO)), _f(f32(SI)), _f(C), dim, heads, kvheads, ne, qcrel)
+    return C
+
+
+def decode_attn_paged(Q, CK, CV, POS, LENS, TABLE, B, dim, heads, kvheads, bs, mbps):
+    C = np.zeros(B * dim, np.float32)
+    lib().nlo_decode_attn_paged(_f(f32(Q)), _f(f32(CK)), _f(f32(CV)),
+                                _fz(None if POS is None else f32(POS)),
+                                _fz(None if LENS is None else f32(LENS)), _f(f32(TABLE)), _f(C),
+                                B, dim, heads, kvheads, bs, mbps)
+    return C
 
 
 def embed_gather(TOK, WTE, seq, dim):

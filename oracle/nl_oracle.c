@@ -490,6 +490,173 @@ void nlo_attn_causal_gqa(const float *Q, const float *K, const float *V, float *
   }
 }
 
+/* ---- paged / ring / entry-list KV caches (kernels.el:396-451, 1044-1246) ---- */
+
+static uint32_t u_of(float v) { return v > 0.0f ? (uint32_t)v : 0u; }
+
+/* :396-404 cache-append-ring */
+void nlo_cache_append_ring(const float *SRC, const float *POS, float *CACHE, uint32_t kvdim,
+                           uint32_t nsink, uint32_t win) {
+  uint32_t pos = u_of(POS[0]), slot = pos;
+  if (pos >= nsink) slot = nsink + (pos - nsink) % win;
+  for (uint32_t i = 0; i < kvdim; i++) CACHE[(size_t)slot * kvdim + i] = SRC[i];
+}
+
+/* :1044-1050 qkv-append */
+void nlo_qkv_append(const float *QKV, float *CK, float *CV, uint32_t dim, uint32_t kvdim,
+                    uint32_t wbase) {
+  for (uint32_t i = 0; i < kvdim; i++) {
+    CK[(size_t)wbase + i] = QKV[(size_t)dim + i];
+    CV[(size_t)wbase + i] = QKV[(size_t)dim + kvdim + i];
+  }
+}
+
+/* :1099-1108 / :1210-1218 cache-append-paged(-v); LENS NULL: POS[0] */
+void nlo_cache_append_paged(const float *SRC, const float *POS, const float *LENS,
+                            const float *TABLE, float *POOL, uint32_t B, uint32_t kvdim,
+                            uint32_t bs, uint32_t mbps) {
+  for (uint32_t s = 0; s < B; s++) {
+    uint32_t pos = u_of(LENS ? LENS[s] : POS[0]);
+    uint32_t phys = u_of(TABLE[(size_t)s * mbps + pos / bs]);
+    for (uint32_t t = 0; t < kvdim; t++)
+      POOL[((size_t)phys * bs + pos % bs) * kvdim + t] = SRC[(size_t)s * kvdim + t];
+  }
+}
+
+/* :1184-1190 block-copy */
+void nlo_block_copy(float *POOL, uint32_t bs, uint32_t kvdim, uint32_t src, uint32_t dst) {
+  size_t bn = (size_t)bs * kvdim;
+  for (size_t i = 0; i < bn; i++) POOL[dst * bn + i] = POOL[src * bn + i];
+}
+
+/* :1195-1207 decode-rope-b-v (adjacent pairs, SI scaled by SG[0]) */
+void nlo_decode_rope_b_v(const float *X, const float *CO, const float *SI, const float *SG,
+                         const float *LENS, float *C, uint32_t B, uint32_t cols,
+                         uint32_t heads) {
+  uint32_t hd = cols / heads, half = hd / 2;
+  for (uint32_t bb = 0; bb < B; bb++)
+    for (uint32_t h = 0; h < heads; h++)
+      for (uint32_t m = 0; m < half; m++) {
+        size_t ci = (size_t)u_of(LENS[bb]) * half + m;
+        float cc = CO[ci], ss = SI[ci] * SG[0];
+        size_t i0 = (size_t)bb * cols + (size_t)h * hd + 2 * m, i1 = i0 + 1;
+        float a0 = X[i0], a1 = X[i1];
+        C[i0] = a0 * cc - a1 * ss;
+        C[i1] = a0 * ss + a1 * cc;
+      }
+}
+
+/* The decode attentions over a gathered cache: key j of sequence s lives at
+ * float offset row(j) (+ kvh * hd); rotated modes rotate keys by crel(j) and
+ * the query by qcrel with pairs (2m, 2m+1).  Two passes, as the reference. */
+typedef struct {
+  int mode; /* 0 paged, 1 paged-v, 2 ring, 3 entries */
+  const float *pos, *table, *ent, *co, *si;
+  uint32_t bs, mbps, nsink, win, ne, qcrel;
+} gather_t;
+
+static uint32_t g_count(const gather_t *g, uint32_t s) {
+  if (g->mode == 0) return u_of(g->pos[0]) + 1;
+  if (g->mode == 1) return u_of(g->pos[s]) + 1;
+  if (g->mode == 2) {
+    uint32_t cap = g->nsink + g->win, len = u_of(g->pos[0]) + 1;
+    return len > cap ? cap : len;
+  }
+  return g->ne;
+}
+static size_t g_row(const gather_t *g, uint32_t s, uint32_t j, uint32_t kvdim, uint32_t *crel) {
+  if (g->mode <= 1) {
+    uint32_t phys = u_of(g->table[(size_t)s * g->mbps + j / g->bs]);
+    return ((size_t)phys * g->bs + j % g->bs) * kvdim;
+  }
+  if (g->mode == 2) {
+    uint32_t pos = u_of(g->pos[0]), cap = g->nsink + g->win, start = g->nsink;
+    if (pos >= cap) start = pos - g->win + 1;
+    uint32_t woff = (start - g->nsink) % g->win, slot = j;
+    if (j >= g->nsink) slot = g->nsink + (woff + (j - g->nsink)) % g->win;
+    *crel = j;
+    return (size_t)slot * kvdim;
+  }
+  *crel = u_of(g->ent[2 * j + 1]);
+  return u_of(g->ent[2 * j]);
+}
+static float g_score(const gather_t *g, const float *q, const float *CK, size_t kb, uint32_t crel,
+                     uint32_t qcrel, uint32_t hd, float coef) {
+  float acc = 0.0f;
+  if (g->mode >= 2) {
+    uint32_t half = hd / 2;
+    for (uint32_t m = 0; m < half; m++) {
+      float cc = g->co[(size_t)crel * half + m], ss = g->si[(size_t)crel * half + m];
+      float k0 = CK[kb + 2 * m], k1 = CK[kb + 2 * m + 1];
+      float kr0 = k0 * cc - k1 * ss, kr1 = k0 * ss + k1 * cc;
+      float qcc = g->co[(size_t)qcrel * half + m], qss = g->si[(size_t)qcrel * half + m];
+      float q0 = q[2 * m], q1 = q[2 * m + 1];
+      float qr0 = q0 * qcc - q1 * qss, qr1 = q0 * qss + q1 * qcc;
+      acc = acc + (qr0 * kr0 + qr1 * kr1);
+    }
+  } else {
+    for (uint32_t t = 0; t < hd; t++) acc = acc + q[t] * CK[kb + t];
+  }
+  return acc * coef;
+}
+static void g_attn(const gather_t *g, const float *Q, const float *CK, const float *CV, float *C,
+                   uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads) {
+  uint32_t hd = dim / heads, grp = heads / kvheads, kvdim = kvheads * hd;
+  float coef = 1.0f / sqrtf((float)hd);
+  long long total = (long long)B * dim;
+#pragma omp parallel for schedule(static)
+  for (long long idx = 0; idx < total; idx++) {
+    uint32_t s = (uint32_t)(idx / dim), c = (uint32_t)(idx % dim);
+    uint32_t h = c / hd, t = c % hd, kvh = h / grp, len = g_count(g, s);
+    uint32_t qcrel = g->qcrel;
+    if (g->mode == 2) {
+      uint32_t cap = g->nsink + g->win;
+      qcrel = u_of(g->pos[0]);
+      if (qcrel >= cap) qcrel = cap - 1;
+    }
+    const float *q = Q + (size_t)s * dim + (size_t)h * hd;
+    float mx = -1.0e30f;
+    for (uint32_t j = 0; j < len; j++) {
+      uint32_t crel = 0;
+      size_t kb = g_row(g, s, j, kvdim, &crel) + (size_t)kvh * hd;
+      float sc = g_score(g, q, CK, kb, crel, qcrel, hd, coef);
+      if (sc > mx) mx = sc;
+    }
+    float z = 0.0f, ctx = 0.0f;
+    for (uint32_t j = 0; j < len; j++) {
+      uint32_t crel = 0;
+      size_t kb = g_row(g, s, j, kvdim, &crel) + (size_t)kvh * hd;
+      float e = expf(g_score(g, q, CK, kb, crel, qcrel, hd, coef) - mx);
+      z = z + e;
+      ctx = ctx + e * CV[kb + t];
+    }
+    C[idx] = ctx / z;
+  }
+}
+
+/* :409-451 decode-attn-stream */
+void nlo_decode_attn_stream(const float *Q, const float *CK, const float *CV, const float *POS,
+                            const float *CO, const float *SI, float *C, uint32_t dim,
+                            uint32_t heads, uint32_t kvheads, uint32_t nsink, uint32_t win) {
+  gather_t g = {2, POS, NULL, NULL, CO, SI, 0, 0, nsink, win, 0, 0};
+  g_attn(&g, Q, CK, CV, C, 1, dim, heads, kvheads);
+}
+/* :1057-1092 attn-stream-entries */
+void nlo_attn_stream_entries(const float *Q, const float *CK, const float *CV, const float *ENT,
+                             const float *CO, const float *SI, float *C, uint32_t dim,
+                             uint32_t heads, uint32_t kvheads, uint32_t ne, uint32_t qcrel) {
+  gather_t g = {3, NULL, NULL, ENT, CO, SI, 0, 0, 0, 0, ne, qcrel};
+  g_attn(&g, Q, CK, CV, C, 1, dim, heads, kvheads);
+}
+/* :1111-1137 / :1221-1246 decode-attn-paged(-v); LENS NULL: POS[0] */
+void nlo_decode_attn_paged(const float *Q, const float *CK, const float *CV, const float *POS,
+                           const float *LENS, const float *TABLE, float *C, uint32_t B,
+                           uint32_t dim, uint32_t heads, uint32_t kvheads, uint32_t bs,
+                           uint32_t mbps) {
+  gather_t g = {LENS ? 1 : 0, LENS ? LENS : POS, TABLE, NULL, NULL, NULL, bs, mbps, 0, 0, 0, 0};
+  g_attn(&g, Q, CK, CV, C, B, dim, heads, kvheads);
+}
+
 /* lisp/nelisp-gpu-kernels.el:1385-1392 (embed-gather) */
 void nlo_embed_gather(const float *TOK, const float *WTE, float *C,
                       uint32_t seq, uint32_t dim) {

@@ -82,6 +82,26 @@ void nlo_cache_append_b(const float *SRC, const float *POS, float *CACHE,
 /* decode-attn-b :368-390 (decode-attn :317-338 is B=1) */
 void nlo_attn_causal_gqa(const float *Q, const float *K, const float *V, float *CTX,
                          uint32_t seq, uint32_t heads, uint32_t kvheads, uint32_t hd);
+void nlo_cache_append_ring(const float *SRC, const float *POS, float *CACHE, uint32_t kvdim,
+                           uint32_t nsink, uint32_t win);
+void nlo_qkv_append(const float *QKV, float *CK, float *CV, uint32_t dim, uint32_t kvdim,
+                    uint32_t wbase);
+void nlo_cache_append_paged(const float *SRC, const float *POS, const float *LENS,
+                            const float *TABLE, float *POOL, uint32_t B, uint32_t kvdim,
+                            uint32_t bs, uint32_t mbps);
+void nlo_block_copy(float *POOL, uint32_t bs, uint32_t kvdim, uint32_t src, uint32_t dst);
+void nlo_decode_rope_b_v(const float *X, const float *CO, const float *SI, const float *SG,
+                         const float *LENS, float *C, uint32_t B, uint32_t cols, uint32_t heads);
+void nlo_decode_attn_stream(const float *Q, const float *CK, const float *CV, const float *POS,
+                            const float *CO, const float *SI, float *C, uint32_t dim,
+                            uint32_t heads, uint32_t kvheads, uint32_t nsink, uint32_t win);
+void nlo_attn_stream_entries(const float *Q, const float *CK, const float *CV, const float *ENT,
+                             const float *CO, const float *SI, float *C, uint32_t dim,
+                             uint32_t heads, uint32_t kvheads, uint32_t ne, uint32_t qcrel);
+void nlo_decode_attn_paged(const float *Q, const float *CK, const float *CV, const float *POS,
+                           const float *LENS, const float *TABLE, float *C, uint32_t B,
+                           uint32_t dim, uint32_t heads, uint32_t kvheads, uint32_t bs,
+                           uint32_t mbps);
 void nlo_decode_attn_b(const float *Q, const float *CK, const float *CV,
                        const float *POS, float *C, uint32_t B, uint32_t dim,
                        uint32_t heads, uint32_t kvheads, uint32_t maxseq);

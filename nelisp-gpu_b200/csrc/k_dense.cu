@@ -23,7 +23,7 @@ namespace {
 
 enum Cover { kElem = 0, kTile16 = 1, kReg4 = 2 };
 
-template <int BM, int BN, int BK, int TM, int TN, bool TRANS_B>
+template <int BM, int BN, int BK, int TM, int TN, bool TRANS_B, bool TRANS_A = false>
 __global__ void __launch_bounds__((BM / TM) * (BN / TN))
 sgemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
              const float *__restrict__ bias, float *__restrict__ C,
@@ -40,10 +40,19 @@ sgemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
     for (int j = 0; j < TN; j++) acc[i][j] = 0.0f;
 
   for (uint32_t k0 = 0; k0 < K; k0 += BK) {
-    for (int e = tid; e < BM * BK; e += NT) {
-      int r = e / BK, kk = e % BK;
-      uint32_t gr = m0 + r, gk = k0 + kk;
-      As[kk][r] = (gr < M && gk < K) ? __ldg(A + (uint64_t)gr * K + gk) : 0.0f;
+    if (TRANS_A) {
+      // A is [K x M] (matmul-at); tile element (kk, r) = A[k0 + kk, m0 + r]
+      for (int e = tid; e < BM * BK; e += NT) {
+        int kk = e / BM, r = e % BM;
+        uint32_t gr = m0 + r, gk = k0 + kk;
+        As[kk][r] = (gr < M && gk < K) ? __ldg(A + (uint64_t)gk * M + gr) : 0.0f;
+      }
+    } else {
+      for (int e = tid; e < BM * BK; e += NT) {
+        int r = e / BK, kk = e % BK;
+        uint32_t gr = m0 + r, gk = k0 + kk;
+        As[kk][r] = (gr < M && gk < K) ? __ldg(A + (uint64_t)gr * K + gk) : 0.0f;
+      }
     }
     if (TRANS_B) {
       // B is [N x K] (a linear layer's weight); tile element (kk, c) = B[c, kk]
@@ -95,7 +104,7 @@ sgemm_kernel(const float *__restrict__ A, const float *__restrict__ B,
   }
 }
 
-template <bool TRANS_B>
+template <bool TRANS_B, bool TRANS_A = false>
 cudaError_t sgemm(const float *A, const float *B, const float *bias, float *C,
                   uint32_t M, uint32_t K, uint32_t N, int cover,
                   uint64_t limit, cudaStream_t st) {
@@ -103,13 +112,13 @@ cudaError_t sgemm(const float *A, const float *B, const float *bias, float *C,
   uint64_t big = (uint64_t)M * N;
   if (big >= (uint64_t)148 * 64 * 64) {
     dim3 grid((N + 63) / 64, (M + 63) / 64);
-    sgemm_kernel<64, 64, 16, 4, 4, TRANS_B><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
+    sgemm_kernel<64, 64, 16, 4, 4, TRANS_B, TRANS_A><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
   } else if (big >= (uint64_t)148 * 32 * 32) {
     dim3 grid((N + 31) / 32, (M + 31) / 32);
-    sgemm_kernel<32, 32, 32, 2, 2, TRANS_B><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
+    sgemm_kernel<32, 32, 32, 2, 2, TRANS_B, TRANS_A><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
   } else {
     dim3 grid((N + 15) / 16, (M + 15) / 16);
-    sgemm_kernel<16, 16, 32, 1, 1, TRANS_B><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
+    sgemm_kernel<16, 16, 32, 1, 1, TRANS_B, TRANS_A><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
   }
   count_launches(1);
   return cudaPeekAtLastError();
@@ -156,7 +165,23 @@ cudaError_t run_linear(const OpArgs &a) {
 
 }  // namespace
 
+// matmul-at (kernels.el:177-186): C[m, n] = sum_k A[k, m] B[k, n], A [K x M].
+const char *chk_matmul_at(const OpArgs &a) {
+  const uint64_t M = a.push[0], K = a.push[1], N = a.push[2];
+  const char *m;
+  const bool any = M != 0 && N != 0;
+  if ((m = need_words(a, 0, any ? K * M : 0, "A"))) return m;
+  if ((m = need_words(a, 1, any ? K * N : 0, "B"))) return m;
+  return need_words(a, 2, M * N, "C");
+}
+cudaError_t run_matmul_at(const OpArgs &a) {
+  return sgemm<false, true>((const float *)a.buf[0], (const float *)a.buf[1], nullptr,
+                            (float *)a.buf[2], a.push[0], a.push[1], a.push[2], kElem,
+                            invocations(a.groups, 64), a.stream);
+}
+
 const OpSpec kDenseOps[] = {
+    {"matmul-at", 3, 3, chk_matmul_at, no_scratch, run_matmul_at},
     {"matmul", 3, 3, chk_matmul, no_scratch, run_matmul<kElem>},
     {"matmul-tiled", 3, 3, chk_matmul, no_scratch, run_matmul<kTile16>},
     {"matmul-reg", 3, 3, chk_matmul_reg, no_scratch, run_matmul<kReg4>},

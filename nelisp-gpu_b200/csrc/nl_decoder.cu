@@ -69,8 +69,14 @@ Nccl *nccl() {
   static bool tried = false;
   if (!tried) {
     tried = true;
-    n.h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
-    if (!n.h) n.h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    // An NCCL already in the process (PyTorch's) is reused; otherwise the
+    // library is opened RTLD_LOCAL so that its symbols never shadow those a
+    // later-loaded library (libtorch_cuda) expects from a newer NCCL.
+    const char *env = getenv("NELISP_NCCL_LIB");
+    if (env && *env) n.h = dlopen(env, RTLD_NOW | RTLD_LOCAL);
+    if (!n.h) n.h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!n.h) n.h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!n.h) n.h = dlopen("libnccl.so", RTLD_NOW | RTLD_LOCAL);
     if (n.h) {
       n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(n.h, "ncclGetUniqueId");
       n.CommInitRank = (decltype(n.CommInitRank))dlsym(n.h, "ncclCommInitRank");

@@ -56,6 +56,8 @@ extern const OpSpec kAttnOps[];
 extern const int kAttnOpsCount;
 extern const OpSpec kKvOps[];
 extern const int kKvOpsCount;
+extern const OpSpec kMiscOps[];
+extern const int kMiscOpsCount;
 
 // Error reporting (nl_runtime.cu).
 int set_error(int code, const char *fmt, ...);

@@ -94,6 +94,26 @@ SIGNATURES = {
 _lib = None
 
 
+def _prefer_bundled_nccl() -> None:
+    """Point the decoder's NCCL loader at the NCCL that ships with PyTorch
+    (the `nvidia-nccl` wheel) when there is one.  The dynamic linker matches a
+    dependency by soname against libraries already in the process, so an
+    older system libnccl.so.2 opened first would be handed to libtorch_cuda
+    later and fail its symbol lookups."""
+    if os.environ.get("NELISP_NCCL_LIB"):
+        return
+    import importlib.util
+    try:
+        spec = importlib.util.find_spec("nvidia.nccl")
+    except (ImportError, ValueError):
+        return
+    for d in (spec.submodule_search_locations or []) if spec else []:
+        cand = os.path.join(d, "lib", "libnccl.so.2")
+        if os.path.exists(cand):
+            os.environ["NELISP_NCCL_LIB"] = cand
+            return
+
+
 def load(path: str = LIB_PATH):
     """Load libnelisp_cuda; raises if it is missing (no CPU fallback)."""
     global _lib
@@ -103,6 +123,7 @@ def load(path: str = LIB_PATH):
         raise ImportError(
             f"libnelisp_cuda is not built ({path} missing); run "
             "`python -c 'import __graft_entry__ as g; g.build()'` or `make -C nelisp-gpu_b200`")
+    _prefer_bundled_nccl()
     lib = ctypes.CDLL(path)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)

@@ -78,6 +78,17 @@ def _declare(L):
         "nlo_attn_stream_entries": [_F] * 7 + [_u32] * 5,
         "nlo_decode_attn_paged": [_F] * 7 + [_u32] * 6,
         "nlo_embed_gather": [_F, _F, _F, _u32, _u32],
+        "nlo_matmul_at": [_F, _F, _F] + [_u32] * 3,
+        "nlo_causal_mask": [_F, _u32],
+        "nlo_attn_scores": [_F] * 3 + [_u32] * 4,
+        "nlo_attn_context": [_F] * 3 + [_u32] * 4,
+        "nlo_dp4a_dot": [_F] * 5 + [_u32],
+        "nlo_bitlinear_dp4a": [_F] * 8 + [_u32] * 3,
+        "nlo_dp4a_rows_t": [_F] * 4 + [_u32] * 4,
+        "nlo_rmsnorm_heads": [_F] * 3 + [_u32] * 3,
+        "nlo_rope_apply": [_F] * 5 + [_u32] * 3,
+        "nlo_silu": [_F, _F, _u32],
+        "nlo_scale_rows": [_F] * 3 + [_u32] * 2,
         "nlo_matmul_sample_ref": [_u32] * 4,
         "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
         "nlo_set_threads": [ctypes.c_int],
@@ -337,6 +348,83 @@ def embed_gather(TOK, WTE, seq, dim):
     TOK, WTE = f32(TOK), f32(WTE)
     C = np.zeros(seq * dim, np.float32)
     lib().nlo_embed_gather(_f(TOK), _f(WTE), _f(C), seq, dim)
+    return C
+
+
+def matmul_at(A, B, M, K, N):
+    return _mm(lib().nlo_matmul_at, A, B, M, K, N)
+
+
+def causal_mask(S, n):
+    S = f32(S).copy()
+    lib().nlo_causal_mask(_f(S), n)
+    return S
+
+
+def attn_scores(Q, K, seq, dim, heads, kvheads):
+    Q, K = f32(Q), f32(K)
+    S = np.zeros(heads * seq * seq, np.float32)
+    lib().nlo_attn_scores(_f(Q), _f(K), _f(S), seq, dim, heads, kvheads)
+    return S
+
+
+def attn_context(P, V, seq, dim, heads, kvheads):
+    P, V = f32(P), f32(V)
+    C = np.zeros(seq * dim, np.float32)
+    lib().nlo_attn_context(_f(P), _f(V), _f(C), seq, dim, heads, kvheads)
+    return C
+
+
+def dp4a_dot(ALO, AHI, BLO, BHI, n):
+    a = [f32(x) for x in (ALO, AHI, BLO, BHI)]
+    out = np.zeros(n, np.float32)
+    lib().nlo_dp4a_dot(*[_f(x) for x in a], _f(out), n)
+    return out
+
+
+def bitlinear_dp4a(ALO, AHI, WLO, WHI, BIAS, BETA, GAMMA, seq, out, ng):
+    a = [f32(x) for x in (ALO, AHI, WLO, WHI, BIAS, BETA, GAMMA)]
+    Y = np.zeros(seq * out, np.float32)
+    lib().nlo_bitlinear_dp4a(*[_f(x) for x in a], _f(Y), seq, out, ng)
+    return Y
+
+
+def dp4a_rows_t(WP, BETA, G, out, cols, ng, seq):
+    """WP: the packed int8 words (uint32) or their f32 bit-casts."""
+    WP = np.ascontiguousarray(WP)
+    if WP.dtype != np.float32:
+        WP = np.ascontiguousarray(WP, np.uint32).view(np.float32)
+    BETA, G = f32(BETA), f32(G)
+    X = np.zeros(seq * cols, np.float32)
+    lib().nlo_dp4a_rows_t(_f(WP), _f(BETA), _f(G), _f(X), out, cols, ng, seq)
+    return X
+
+
+def rmsnorm_heads(X, G, seq, nheads, hd):
+    X, G = f32(X), f32(G)
+    Y = np.zeros(seq * nheads * hd, np.float32)
+    lib().nlo_rmsnorm_heads(_f(X), _f(G), _f(Y), seq, nheads, hd)
+    return Y
+
+
+def rope_apply(X, CO, SI, SG, seq, dim, heads):
+    X, CO, SI, SG = f32(X), f32(CO), f32(SI), f32(SG)
+    C = np.zeros(seq * dim, np.float32)
+    lib().nlo_rope_apply(_f(X), _f(CO), _f(SI), _f(SG), _f(C), seq, dim, heads)
+    return C
+
+
+def silu(X, n):
+    X = f32(X)
+    C = np.zeros(n, np.float32)
+    lib().nlo_silu(_f(X), _f(C), n)
+    return C
+
+
+def scale_rows(Y, S, M, N):
+    Y, S = f32(Y), f32(S)
+    C = np.zeros(M * N, np.float32)
+    lib().nlo_scale_rows(_f(Y), _f(S), _f(C), M, N)
     return C
 
 

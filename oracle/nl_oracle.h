@@ -109,6 +109,31 @@ void nlo_decode_attn_b(const float *Q, const float *CK, const float *CV,
 void nlo_embed_gather(const float *TOK, const float *WTE, float *C,
                       uint32_t seq, uint32_t dim);
 
+/* nl_oracle_misc.c: matmul-at :177-186, causal-mask :148-155, attn-scores
+ * :208-221, attn-context :224-235, dp4a-dot :592-602, bitlinear-dp4a :606-620,
+ * dp4a-rows-t :792-810, rmsnorm-heads :828-845, rope-apply :1290-1303, silu
+ * :1306-1312, scale-rows :1365-1372 */
+void nlo_matmul_at(const float *A, const float *B, float *C, uint32_t M, uint32_t K,
+                   uint32_t N);
+void nlo_causal_mask(float *S, uint32_t n);
+void nlo_attn_scores(const float *Q, const float *K, float *S, uint32_t seq, uint32_t dim,
+                     uint32_t heads, uint32_t kvheads);
+void nlo_attn_context(const float *P, const float *V, float *C, uint32_t seq, uint32_t dim,
+                      uint32_t heads, uint32_t kvheads);
+void nlo_dp4a_dot(const float *ALO, const float *AHI, const float *BLO, const float *BHI,
+                  float *OUT, uint32_t n);
+void nlo_bitlinear_dp4a(const float *ALO, const float *AHI, const float *WLO, const float *WHI,
+                        const float *BIAS, const float *BETA, const float *GAMMA, float *Y,
+                        uint32_t seq, uint32_t out, uint32_t ng);
+void nlo_dp4a_rows_t(const float *WP, const float *BETA, const float *G, float *X, uint32_t out,
+                     uint32_t cols, uint32_t ng, uint32_t seq);
+void nlo_rmsnorm_heads(const float *X, const float *G, float *Y, uint32_t seq, uint32_t nheads,
+                       uint32_t hd);
+void nlo_rope_apply(const float *X, const float *CO, const float *SI, const float *SG, float *C,
+                    uint32_t seq, uint32_t dim, uint32_t heads);
+void nlo_silu(const float *X, float *C, uint32_t n);
+void nlo_scale_rows(const float *Y, const float *S, float *C, uint32_t M, uint32_t N);
+
 /* Double-precision references used by the reference's own self-checks. */
 double nlo_matmul_sample_ref(uint32_t r, uint32_t c, uint32_t K, uint32_t N);
 void   nlo_softmax_ref_f64(const double *A, double *C, uint32_t M, uint32_t N);

@@ -58,13 +58,24 @@ def test_registry_names_the_reference_kernels(lib):
            "matmul-tiled", "matmul-reg", "linear", "softmax", "silu-mul", "add2",
            "rmsnorm-istd", "rmsnorm-fwd", "rope-half", "decode-rope", "decode-rope-b",
            "cache-append", "cache-append-b", "decode-attn", "decode-attn-b", "attn-causal-gqa",
-           "embed-gather", "scale"}
+           "embed-gather", "scale",
+           # paged / streaming KV caches
+           "cache-append-ring", "decode-attn-stream", "qkv-append", "attn-stream-entries",
+           "cache-append-paged", "decode-attn-paged", "block-copy", "decode-rope-b-v",
+           "cache-append-paged-v", "decode-attn-paged-v",
+           # unfused prefill attention, QK-norm, RoPE, DP4A spikes, backward GEMMs
+           "matmul-at", "causal-mask", "attn-scores", "attn-context", "dp4a-dot",
+           "bitlinear-dp4a", "dp4a-rows-t", "rmsnorm-heads", "rope-apply", "silu", "scale-rows"}
     assert hot <= names
     nb, npush = ctypes.c_uint32(), ctypes.c_uint32()
     assert lib.nl_kernel_arity(b"ternary-rows", ctypes.byref(nb), ctypes.byref(npush)) == 0
     assert (nb.value, npush.value) == (5, 5)      # (X WP BIAS BETA Y) (seq out cols nblk wng)
     assert lib.nl_kernel_arity(b"decode-attn-b", ctypes.byref(nb), ctypes.byref(npush)) == 0
     assert (nb.value, npush.value) == (5, 5)
+    for name, arity in [(b"bitlinear-dp4a", (8, 3)), (b"dp4a-rows-t", (4, 4)),
+                        (b"attn-scores", (3, 4)), (b"rope-apply", (5, 3))]:
+        assert lib.nl_kernel_arity(name, ctypes.byref(nb), ctypes.byref(npush)) == 0
+        assert (nb.value, npush.value) == arity, name
     assert lib.nl_kernel_arity(b"no-such-kernel", None, None) == 1
 
 

@@ -212,6 +212,26 @@ int nl_ternary_gemv_batched_dev(uint32_t count, const float *X,
                                 uint32_t cols, void *workspace,
                                 size_t ws_bytes, void *stream);
 
+/* nl_ternary_gemv_batched_dev end to end on host buffers: copies the COUNT
+ * activation blocks in from X_HOST, runs the GEMVs on the device-resident
+ * weights WP and scales S (device pointers, e.g. from nl_resident_info) and
+ * copies the outputs back to Y_HOST, returning once they are there.  The
+ * per-call shape of the reference's RUN (inline inputs copied in, outputs
+ * copied back; host/vkserver.c:274-334) for a resident-weight GEMV batch.
+ * Copies run on their own streams; with NELISP_HOST_CHUNKS=n (1..8, default
+ * 1) the problems go in n chunks whose copies overlap the other chunks'
+ * kernels.  X_HOST and Y_HOST should be pinned (cudaHostAlloc / torch
+ * pin_memory) for the copies to run at full speed.
+ * Problem z reads X_HOST + z*x_stride (seq*cols values) and writes
+ * Y_HOST + z*y_stride (seq*out values).  Device staging is owned by the
+ * library. */
+int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
+                                 uint64_t x_stride, const uint32_t *WP,
+                                 uint64_t w_stride, const float *S,
+                                 uint64_t s_stride, float *Y_host,
+                                 uint64_t y_stride, uint32_t seq, uint32_t out,
+                                 uint32_t cols);
+
 /* Size of the file-scope device workspace of nl_ternary_gemv_static_dev. */
 #define NL_TERNARY_STATIC_WS_BYTES (2u << 20)
 

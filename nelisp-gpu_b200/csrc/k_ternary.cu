@@ -51,70 +51,6 @@ namespace {
 
 constexpr int kDepth = 8;        // 128-column blocks in flight per warp
 
-__device__ __forceinline__ float trit_of(uint32_t w, uint32_t f) {
-  return (float)(((int32_t)(w << (30u - 2u * f))) >> 30);
-}
-
-// ---------------------------------------------------------------------------
-// Generic CUDA-core path: any shape, the reference's semantics exactly
-// (blocks b < nblk, words wi < min(wng, 8*nblk), fields i < cols).  One warp
-// per output row; lanes take words, groups of eight lanes form a block.
-// ---------------------------------------------------------------------------
-template <int SB>
-__device__ void ternary_row_generic(const float *__restrict__ X,
-                                    const uint32_t *__restrict__ Wrow,
-                                    const float *__restrict__ beta_row,
-                                    bool per_block, float row_scale,
-                                    int s0, int ns, uint32_t cols,
-                                    uint32_t nblk, uint32_t wng,
-                                    float acc[SB]) {
-  const int lane = threadIdx.x & 31;
-  for (int s = 0; s < SB; s++) acc[s] = 0.0f;
-  const uint32_t nwords = 8u * nblk;
-  for (uint32_t base = 0; base < nwords; base += 32) {
-    uint32_t wi = base + lane;
-    uint32_t w = (wi < wng && wi < nwords) ? __ldg(Wrow + wi) : 0u;
-    float part[SB];
-#pragma unroll
-    for (int s = 0; s < SB; s++) part[s] = 0.0f;
-    // Every field is multiplied, zeros included: 0 * inf is NaN in the
-    // reference's arithmetic too.
-    if (wi < wng && wi < nwords) {
-      for (uint32_t f = 0; f < 16; f++) {
-        uint32_t i = wi * 16u + f;
-        if (i < cols) {
-          float t = trit_of(w, f);
-#pragma unroll
-          for (int s = 0; s < SB; s++)
-            if (s < ns) part[s] = fmaf(t, __ldg(X + (size_t)(s0 + s) * cols + i), part[s]);
-        }
-      }
-    }
-    // Sum within each group of eight lanes = one 128-column block.
-#pragma unroll
-    for (int s = 0; s < SB; s++) {
-      float v = part[s];
-      v += __shfl_xor_sync(0xffffffffu, v, 1);
-      v += __shfl_xor_sync(0xffffffffu, v, 2);
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      part[s] = v;
-    }
-    uint32_t b = wi / 8u;
-    if ((lane & 7) == 0 && b < nblk) {
-      float sc = per_block ? __ldg(beta_row + b) : 1.0f;
-#pragma unroll
-      for (int s = 0; s < SB; s++) acc[s] = fmaf(sc, part[s], acc[s]);
-    }
-  }
-#pragma unroll
-  for (int s = 0; s < SB; s++) {
-    float v = acc[s];
-    v += __shfl_xor_sync(0xffffffffu, v, 8);
-    v += __shfl_xor_sync(0xffffffffu, v, 16);
-    acc[s] = per_block ? v : v * row_scale;
-  }
-}
-
 // One warp per (problem z, output row o), sequences in chunks of 8.
 __global__ void __launch_bounds__(256)
 ternary_generic_kernel(const float *__restrict__ X, uint64_t x_stride,
@@ -1194,6 +1130,10 @@ uint32_t ternary_dec_ctas(uint32_t count, uint32_t out, uint32_t cols, uint32_t 
 
 size_t ternary_ws_bytes_best(uint32_t count, uint32_t seq, uint32_t cols, bool per_block) {
   size_t b = ternary_ws_bytes(count, seq, cols);
+  if (!per_block && seq <= 16u) {
+    const size_t t = ternary_tc_ws_bytes(count, seq, cols);
+    if (t > b) b = t;
+  }
   if (ternary_umma_applies(count, seq, cols, per_block)) {
     const size_t u = ternary_umma_ws_bytes(seq, cols);
     if (u > b) b = u;
@@ -1228,6 +1168,16 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
         out, cols, nblk, wng, per_block ? 1 : 0, limit);
     count_launches(1);
     return cudaPeekAtLastError();
+  }
+  // Streaming shapes (more 16-row tiles than the decode kernel takes): the
+  // tcgen05 GEMV with the weights expanded into tensor memory.
+  if (ternary_tc_applies(count, seq, out, cols, per_block, w_stride) &&
+      ternary_dec_ctas(count, out, cols, seq) == 0) {
+    bool launched = false;
+    cudaError_t e = ternary_tc_launch(count, X, x_stride, WP, w_stride, SCALE, s_stride, BIAS, Y,
+                                      y_stride, seq, out, cols, limit, ws, ws_bytes, stream,
+                                      &launched);
+    if (launched || e != cudaSuccess) return e;
   }
   // Many sequence rows of one problem: the tcgen05 GEMM, when the workspace
   // holds its int8 limb matrix.

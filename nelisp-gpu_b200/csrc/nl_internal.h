@@ -63,6 +63,18 @@ extern const int kMiscOpsCount;
 int set_error(int code, const char *fmt, ...);
 int cuda_status(cudaError_t e, const char *what);
 
+// Bounded waits.  A kernel whose bounded wait gives up records it in a
+// host-mapped flag (wait_flag_device(), allocated by nl_init before any
+// capture); the synchronising entry points report and clear it.
+int *wait_flag_device();
+bool take_wait_timeout();
+__device__ __forceinline__ void report_wait_timeout(int *err) {
+  if (err) {
+    *(volatile int *)err = 1;
+    __threadfence_system();
+  }
+}
+
 // Launch accounting: every kernel the library enqueues is counted.
 void count_launches(uint64_t n);
 
@@ -202,6 +214,16 @@ cudaError_t attn_causal_prefill_launch(const float *Q, const float *CK, const fl
                                        float *CTX, uint32_t B, uint32_t seq, uint32_t heads,
                                        uint32_t kvheads, uint32_t hd, uint64_t q_batch,
                                        uint64_t kv_batch, cudaStream_t st);
+
+// The tcgen05 GEMV for up to 16 sequence rows (k_ternary_tc.cu).
+size_t ternary_tc_ws_bytes(uint32_t count, uint32_t seq, uint32_t cols);
+bool ternary_tc_applies(uint32_t count, uint32_t seq, uint32_t out, uint32_t cols,
+                        bool per_block, uint64_t w_stride);
+cudaError_t ternary_tc_launch(uint32_t count, const float *X, uint64_t x_stride,
+                              const uint32_t *WP, uint64_t w_stride, const float *SCALE,
+                              uint64_t s_stride, const float *BIAS, float *Y, uint64_t y_stride,
+                              uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
+                              size_t ws_bytes, cudaStream_t st, bool *launched);
 
 // Library workspace for typed calls that pass no workspace (nl_runtime.cu).
 void *library_workspace(size_t bytes, cudaStream_t stream);

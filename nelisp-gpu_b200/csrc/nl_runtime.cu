@@ -65,6 +65,11 @@ struct Context {
   uint64_t launches = 0;
   bool capturing = false;
   uint64_t capture_launches = 0;
+  // nl_ternary_gemv_batched_host: copy streams, events, device staging
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev[2 * 8] = {};
+  void *hbuf = nullptr;
+  size_t hbuf_bytes = 0;
 };
 
 Context g;
@@ -119,7 +124,11 @@ void free_words(void *p, bool host) {
 int ensure_ready() { return g.ready ? NL_OK : nl_init(-1); }
 
 int sync_status(const char *what) {
-  return cuda_status(cudaStreamSynchronize(g.stream), what);
+  const int rc = cuda_status(cudaStreamSynchronize(g.stream), what);
+  if (rc == NL_OK && take_wait_timeout())
+    return set_error(NL_ERROR, "%s: a kernel's bounded wait timed out; its outputs are invalid",
+                     what);
+  return rc;
 }
 
 void *arena_get(size_t bytes) {
@@ -306,6 +315,38 @@ void *library_workspace(size_t bytes, cudaStream_t stream) {
   return g.ws;
 }
 
+// ---- bounded-wait flag ----------------------------------------------------------
+namespace {
+int *g_wait_host = nullptr, *g_wait_dev = nullptr;
+}  // namespace
+
+int *wait_flag_device() {
+  if (!g_wait_host) {
+    int *h = nullptr;
+    if (cudaHostAlloc((void **)&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    *h = 0;
+    int *d = nullptr;
+    if (cudaHostGetDevicePointer((void **)&d, h, 0) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFreeHost(h);
+      return nullptr;
+    }
+    g_wait_dev = d;
+    g_wait_host = h;
+  }
+  return g_wait_dev;
+}
+
+bool take_wait_timeout() {
+  if (!g_wait_host || !*(volatile int *)g_wait_host) return false;
+  *(volatile int *)g_wait_host = 0;
+  return true;
+}
+
 }  // namespace nl
 
 using namespace nl;
@@ -331,6 +372,7 @@ extern "C" int nl_init(int device) {
   if (cudaGetDeviceProperties(&prop, pick) == cudaSuccess)
     snprintf(g.devname, sizeof(g.devname), "%s", prop.name);
   g.device = pick;
+  wait_flag_device();             // before any stream capture
   g.ready = true;
   return NL_OK;
 }
@@ -343,6 +385,15 @@ extern "C" void nl_shutdown(void) {
   g.nres = 0;
   if (g.arena) cudaFree(g.arena);
   if (g.ws) cudaFree(g.ws);
+  if (g.hbuf) cudaFree(g.hbuf);
+  g.hbuf = nullptr;
+  g.hbuf_bytes = 0;
+  if (g.h2d) {
+    cudaStreamDestroy(g.h2d);
+    cudaStreamDestroy(g.d2h);
+    for (cudaEvent_t &ev : g.ev) cudaEventDestroy(ev);
+    g.h2d = g.d2h = nullptr;
+  }
   if (g.stage) cudaFreeHost(g.stage);
   g.arena = g.ws = g.stage = nullptr;
   g.arena_bytes = g.ws_bytes = 0;
@@ -810,6 +861,84 @@ extern "C" int nl_ternary_gemv_dev(const float *X, const uint32_t *WP, const flo
                                    void *stream) {
   return ternary_common(1, X, 0, WP, 0, S, 0, BIAS, Y, 0, seq, out, cols, (cols + 127) / 128,
                         (cols + 15) / 16, false, workspace, ws_bytes, stream);
+}
+
+extern "C" int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
+                                            uint64_t x_stride, const uint32_t *WP,
+                                            uint64_t w_stride, const float *S, uint64_t s_stride,
+                                            float *Y_host, uint64_t y_stride, uint32_t seq,
+                                            uint32_t out, uint32_t cols) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  if (count == 0 || seq == 0 || out == 0) return NL_OK;
+  if (!X_host || !Y_host || !WP || !S)
+    return set_error(NL_ERROR, "ternary-gemv-host: null buffer");
+  if (count > 1 && (x_stride < (uint64_t)seq * cols || y_stride < (uint64_t)seq * out))
+    return set_error(NL_ERROR, "ternary-gemv-host: strides overlap the problems");
+  cudaError_t e = cudaSuccess;
+  if (!g.h2d) {
+    if ((e = cudaStreamCreateWithFlags(&g.h2d, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaStreamCreateWithFlags(&g.d2h, cudaStreamNonBlocking)) != cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host: streams");
+    for (cudaEvent_t &ev : g.ev)
+      if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
+        return cuda_status(e, "ternary-gemv-host: events");
+  }
+  const uint64_t xs = count > 1 ? x_stride : (uint64_t)seq * cols;
+  const uint64_t ys = count > 1 ? y_stride : (uint64_t)seq * out;
+  const size_t xbytes = align256(((count - 1) * xs + (uint64_t)seq * cols) * 4u);
+  const size_t ybytes = align256(((count - 1) * ys + (uint64_t)seq * out) * 4u);
+  if (g.hbuf_bytes < xbytes + ybytes) {
+    cudaStreamSynchronize(g.stream);
+    if (g.hbuf) cudaFree(g.hbuf);
+    g.hbuf = nullptr;
+    g.hbuf_bytes = 0;
+    if ((e = cudaMalloc(&g.hbuf, xbytes + ybytes)) != cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host: staging");
+    g.hbuf_bytes = xbytes + ybytes;
+  }
+  float *dx = (float *)g.hbuf, *dy = (float *)((char *)g.hbuf + xbytes);
+  const uint32_t nblk = (cols + 127) / 128, wng = (cols + 15) / 16;
+  size_t wsb = ternary_ws_bytes_best(count, seq, cols, false);
+  void *ws = ternary_fast_shape(cols, nblk, wng, false) ? library_workspace(wsb, g.stream) : nullptr;
+  if (!ws) wsb = 0;
+  // NELISP_HOST_CHUNKS (1..8) splits the problems into chunks whose copies
+  // overlap the other chunks' kernels.  The default is one chunk: at 64 x
+  // 4096^2 (1 MB each way, 23 us per copy) every extra chunk's prep launch
+  // cost more than the overlap saved (measured on B200: 123 us at 1 chunk,
+  // 122 at 2, 133 at 4, 184 at 8).
+  static const uint32_t want_chunks = [] {
+    const char *v = getenv("NELISP_HOST_CHUNKS");
+    const int n = v ? atoi(v) : 0;
+    return (uint32_t)(n >= 1 && n <= 8 ? n : 1);
+  }();
+  uint32_t nch = want_chunks;
+  if (nch > count) nch = count;
+  const uint32_t per = (count + nch - 1) / nch;
+  for (uint32_t c = 0, z0 = 0; z0 < count; c++, z0 += per) {
+    const uint32_t z1 = z0 + per < count ? z0 + per : count, n = z1 - z0;
+    const size_t xin = ((n - 1) * xs + (uint64_t)seq * cols) * 4u;
+    const size_t yout = ((n - 1) * ys + (uint64_t)seq * out) * 4u;
+    if ((e = cudaMemcpyAsync(dx + z0 * xs, X_host + z0 * xs, xin, cudaMemcpyHostToDevice,
+                             g.h2d)) != cudaSuccess ||
+        (e = cudaEventRecord(g.ev[2 * c], g.h2d)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(g.stream, g.ev[2 * c], 0)) != cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host: copy in");
+    if ((e = ternary_gemv_launch(n, dx + z0 * xs, xs, WP + z0 * w_stride, w_stride,
+                                 S + z0 * s_stride, s_stride, nullptr, dy + z0 * ys, ys, seq, out,
+                                 cols, nblk, wng, false, UINT64_MAX, ws, wsb, g.stream)) !=
+        cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host");
+    if ((e = cudaEventRecord(g.ev[2 * c + 1], g.stream)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(g.d2h, g.ev[2 * c + 1], 0)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(Y_host + z0 * ys, dy + z0 * ys, yout, cudaMemcpyDeviceToHost,
+                             g.d2h)) != cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host: copy out");
+  }
+  rc = cuda_status(cudaStreamSynchronize(g.d2h), "ternary-gemv-host");
+  if (rc == NL_OK && take_wait_timeout())
+    return set_error(NL_ERROR, "ternary-gemv-host: a kernel's bounded wait timed out");
+  return rc;
 }
 
 extern "C" int nl_ternary_gemv_batched_dev(uint32_t count, const float *X, uint64_t x_stride,

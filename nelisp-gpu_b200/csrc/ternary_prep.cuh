@@ -174,4 +174,69 @@ __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, flo
   }
 }
 
+// ---- the generic CUDA-core row ------------------------------------------------
+__device__ __forceinline__ float trit_of(uint32_t w, uint32_t f) {
+  return (float)(((int32_t)(w << (30u - 2u * f))) >> 30);
+}
+
+// ---------------------------------------------------------------------------
+// Generic CUDA-core path: any shape, the reference's semantics exactly
+// (blocks b < nblk, words wi < min(wng, 8*nblk), fields i < cols).  One warp
+// per output row; lanes take words, groups of eight lanes form a block.
+// ---------------------------------------------------------------------------
+template <int SB>
+__device__ inline void ternary_row_generic(const float *__restrict__ X,
+                                    const uint32_t *__restrict__ Wrow,
+                                    const float *__restrict__ beta_row,
+                                    bool per_block, float row_scale,
+                                    int s0, int ns, uint32_t cols,
+                                    uint32_t nblk, uint32_t wng,
+                                    float acc[SB]) {
+  const int lane = threadIdx.x & 31;
+  for (int s = 0; s < SB; s++) acc[s] = 0.0f;
+  const uint32_t nwords = 8u * nblk;
+  for (uint32_t base = 0; base < nwords; base += 32) {
+    uint32_t wi = base + lane;
+    uint32_t w = (wi < wng && wi < nwords) ? __ldg(Wrow + wi) : 0u;
+    float part[SB];
+#pragma unroll
+    for (int s = 0; s < SB; s++) part[s] = 0.0f;
+    // Every field is multiplied, zeros included: 0 * inf is NaN in the
+    // reference's arithmetic too.
+    if (wi < wng && wi < nwords) {
+      for (uint32_t f = 0; f < 16; f++) {
+        uint32_t i = wi * 16u + f;
+        if (i < cols) {
+          float t = trit_of(w, f);
+#pragma unroll
+          for (int s = 0; s < SB; s++)
+            if (s < ns) part[s] = fmaf(t, __ldg(X + (size_t)(s0 + s) * cols + i), part[s]);
+        }
+      }
+    }
+    // Sum within each group of eight lanes = one 128-column block.
+#pragma unroll
+    for (int s = 0; s < SB; s++) {
+      float v = part[s];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      part[s] = v;
+    }
+    uint32_t b = wi / 8u;
+    if ((lane & 7) == 0 && b < nblk) {
+      float sc = per_block ? __ldg(beta_row + b) : 1.0f;
+#pragma unroll
+      for (int s = 0; s < SB; s++) acc[s] = fmaf(sc, part[s], acc[s]);
+    }
+  }
+#pragma unroll
+  for (int s = 0; s < SB; s++) {
+    float v = acc[s];
+    v += __shfl_xor_sync(0xffffffffu, v, 8);
+    v += __shfl_xor_sync(0xffffffffu, v, 16);
+    acc[s] = per_block ? v : v * row_scale;
+  }
+}
+
 }  // namespace nl

@@ -255,9 +255,10 @@ def test_gemv_batched_matches_single():
 
 # ---- the fast-path kernels agree bit for bit ------------------------------------
 # The decode kernel (row tiles split over warps), the persistent TMA kernel,
-# the register-ring kernel and, for more than 16 sequence rows, the tcgen05
-# GEMM sum the same exact integer products and scale them the same way, so
-# they must give identical bits.  NELISP_TERNARY_PATH is read once
+# the register-ring kernel, the tcgen05 GEMV (NELISP_TERNARY_PATH=tc forces
+# it from one row up) and, for more than 16 sequence rows, the tcgen05 GEMM
+# sum the same exact integer products and scale them the same way, so they
+# must give identical bits.  NELISP_TERNARY_PATH is read once
 # per process, hence one subprocess per path.
 
 _PATH_SCRIPT = r"""
@@ -279,7 +280,9 @@ out_path = sys.argv[1]
 rng = np.random.default_rng(4242)
 res = {{}}
 for (seq, out, cols) in [(1, 4096, 4096), (4, 2560, 6912), (16, 1000, 2560), (7, 3840, 2560),
-                         (100, 1000, 2560), (17, 300, 512)]:
+                         (100, 1000, 2560), (17, 300, 512),
+                         # more 16-row tiles than the decode kernel takes: tcgen05 GEMV
+                         (1, 33024, 1024), (3, 40000, 640), (9, 32800, 512), (16, 34000, 256)]:
     t = rng.integers(-1, 2, size=(out, cols))
     WP = pack_trits(t)
     S = rng.uniform(0.5, 1.5, out).astype(np.float32)
@@ -294,6 +297,21 @@ for (seq, out, cols) in [(1, 4096, 4096), (4, 2560, 6912), (16, 1000, 2560), (7,
     res[f"x_{{seq}}_{{out}}_{{cols}}"] = X
     res[f"w_{{seq}}_{{out}}_{{cols}}"] = WP
     res[f"s_{{seq}}_{{out}}_{{cols}}"] = S
+# a batch of problems through one call (the benchmark's shape, smaller)
+count, seq, out, cols = 9, 2, 4096, 1024
+Ws = [pack_trits(rng.integers(-1, 2, size=(out, cols))) for _ in range(count)]
+S = rng.uniform(0.5, 1.5, count * out).astype(np.float32)
+X = rng.standard_normal(count * seq * cols).astype(np.float32)
+d = torch.device("cuda")
+tX = torch.from_numpy(X).to(d)
+tW = torch.from_numpy(np.concatenate(Ws).view(np.int32)).to(d)
+tS = torch.from_numpy(S).to(d)
+tY = torch.zeros(count * seq * out, dtype=torch.float32, device=d)
+dev.ternary_gemv_batched(count, tX, seq * cols, tW, out * cols // 16, tS, out, tY, seq * out,
+                         seq, out, cols)
+torch.cuda.synchronize()
+res["batched"] = tY.cpu().numpy()
+res["xb"], res["wb"], res["sb"] = X, np.concatenate(Ws), S
 np.savez(out_path, **res)
 """
 
@@ -306,7 +324,7 @@ def test_fast_path_kernels_agree_bitwise(tmp_path):
     script = tmp_path / "paths.py"
     script.write_text(_PATH_SCRIPT.format(root=ROOT, pkg=PKG))
     results = {}
-    for path in ("auto", "tma", "ring"):
+    for path in ("auto", "tma", "ring", "tc"):
         env = dict(os.environ)
         env.pop("NELISP_TERNARY_PATH", None)
         if path != "auto":
@@ -316,10 +334,18 @@ def test_fast_path_kernels_agree_bitwise(tmp_path):
                        cwd=ROOT, timeout=300)
         results[path] = np.load(outp)
     ref = results["auto"]
+    for path in ("tma", "ring", "tc"):
+        assert np.array_equal(ref["batched"].view(np.uint32), results[path]["batched"].view(np.uint32))
+    count, seq, out, cols = 9, 2, 4096, 1024
+    for z in range(count):
+        want = nlo.ternary_gemv_rows(ref["xb"][z * seq * cols:(z + 1) * seq * cols],
+                                     ref["wb"][z * out * cols // 16:(z + 1) * out * cols // 16],
+                                     ref["sb"][z * out:(z + 1) * out], seq, out, cols)
+        assert nlo.tk_err(ref["batched"][z * seq * out:(z + 1) * seq * out], want) < TOL
     for key in ref.files:
-        if key[0] in "xws":
+        if key[0] in "xws" or key == "batched":
             continue
-        for path in ("tma", "ring"):
+        for path in ("tma", "ring", "tc"):
             assert np.array_equal(ref[key].view(np.uint32), results[path][key].view(np.uint32)), \
                 (path, key)
         seq, out, cols = (int(v) for v in key.split("_"))
@@ -354,3 +380,72 @@ def test_tcgen05_gemm_matches_oracle(seq, out, cols):
     if seq > 3:   # the row holding inf goes through the CUDA-core path, as the reference
         assert np.array_equal(np.isnan(got[3]), np.isnan(want[3]))
         assert np.array_equal(np.isinf(got[3]), np.isinf(want[3]))
+
+
+@pytest.mark.parametrize("seq", [6, 9, 13, 16])
+def test_tcgen05_gemv_flagged_rows(seq):
+    """The tcgen05 GEMV (more 16-row tiles than the decode kernel takes) with a
+    row holding inf and one holding only zeros: the exact path for the others,
+    the CUDA-core arithmetic (NaN and inf where the reference has them) for the
+    flagged row."""
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(seq)
+    out, cols = 33000, 384
+    t = rng.integers(-1, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, out).astype(np.float32)
+    X = rng.standard_normal(seq * cols).astype(np.float32)
+    flagged = seq // 2
+    X[flagged * cols + 7] = np.inf
+    zero = seq - 1 if seq > 2 else None
+    if zero is not None:
+        X[zero * cols:(zero + 1) * cols] = 0.0
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X, WP.view(np.int32), S))
+    tY = torch.full((seq * out,), 7.0, dtype=torch.float32, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols)
+    torch.cuda.synchronize()
+    got = tY.cpu().numpy().reshape(seq, out)
+    want = nlo.ternary_gemv_rows(X, WP, S, seq, out, cols).reshape(seq, out)
+    ok = [s for s in range(seq) if s != flagged]
+    if ok:
+        assert nlo.tk_err(got[ok], want[ok]) < TOL
+    if zero is not None:
+        assert not got[zero].any()
+    assert np.array_equal(np.isnan(got[flagged]), np.isnan(want[flagged]))
+    assert np.array_equal(np.isinf(got[flagged]), np.isinf(want[flagged]))
+    fin = np.isfinite(want[flagged])
+    assert np.allclose(got[flagged][fin], want[flagged][fin], rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("count,seq,out,cols", [(64, 1, 1024, 1024), (9, 3, 2560, 512),
+                                                (1, 2, 300, 256), (40, 16, 512, 768)])
+def test_batched_host_entry_matches_device_entry(count, seq, out, cols):
+    """nl_ternary_gemv_batched_host (copies in, chunked GEMVs, copies out)
+    gives the bits of nl_ternary_gemv_batched_dev on the same inputs."""
+    import ctypes
+    import torch
+    from nelisp_cuda import _lib as L
+    from nelisp_cuda import dev
+    lib = L.load()
+    rng = np.random.default_rng(count + seq)
+    Ws = np.concatenate([pack_trits(rng.integers(-1, 2, size=(out, cols))) for _ in range(count)])
+    S = rng.uniform(0.5, 1.5, count * out).astype(np.float32)
+    X = rng.standard_normal(count * seq * cols).astype(np.float32)
+    d = torch.device("cuda")
+    tW = torch.from_numpy(Ws.view(np.int32)).to(d)
+    tS = torch.from_numpy(S).to(d)
+    tX = torch.from_numpy(X).to(d)
+    tY = torch.zeros(count * seq * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv_batched(count, tX, seq * cols, tW, out * cols // 16, tS, out, tY, seq * out,
+                             seq, out, cols)
+    torch.cuda.synchronize()
+    Xp = torch.from_numpy(X).pin_memory()
+    Yp = torch.full((count * seq * out,), 5.0, dtype=torch.float32).pin_memory()
+    L.check(lib.nl_ternary_gemv_batched_host(count, Xp.data_ptr(), seq * cols, tW.data_ptr(),
+                                             out * cols // 16, tS.data_ptr(), out,
+                                             Yp.data_ptr(), seq * out, seq, out, cols))
+    assert np.array_equal(Yp.numpy().view(np.uint32), tY.cpu().numpy().view(np.uint32))
+    want = nlo.ternary_gemv_rows(X[:seq * cols], Ws[:out * cols // 16], S[:out], seq, out, cols)
+    assert nlo.tk_err(Yp.numpy()[:seq * out], want) < TOL

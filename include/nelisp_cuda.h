@@ -232,6 +232,22 @@ int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
                                  uint64_t y_stride, uint32_t seq, uint32_t out,
                                  uint32_t cols);
 
+/* Bounded waits.  The library's kernels that wait on mbarriers (the TMA and
+ * tcgen05 ternary kernels) give up after a bounded time and record it in a
+ * host-mapped flag; their outputs are then invalid.  The synchronising entry
+ * points (nl_run, nl_batch, nl_run_compiled, nl_ternary_gemv_batched_host)
+ * report it as NL_ERROR.  Callers of the asynchronous *_dev entry points
+ * synchronise their stream and then call nl_wait_status: NL_ERROR (with a
+ * message) if a wait gave up since the last report, else NL_OK; the flag is
+ * cleared.  No reference counterpart (vkserver has no device-side waits). */
+int nl_wait_status(void);
+
+/* Self-test of the bounded-wait report: one thread waits on an mbarrier that
+ * nothing completes, gives up after a few milliseconds and sets the flag;
+ * synchronises and returns what nl_wait_status returns (NL_ERROR when the
+ * report works).  The context stays usable. */
+int nl_selftest_wait_timeout(void);
+
 /* Size of the file-scope device workspace of nl_ternary_gemv_static_dev. */
 #define NL_TERNARY_STATIC_WS_BYTES (2u << 20)
 

@@ -411,7 +411,6 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
 // ---------------------------------------------------------------------------
 constexpr int kTmaBlocks = 4;                 // 128-column blocks per stage
 
-__device__ int g_tma_error;                   // set by a wait that gave up
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -429,10 +428,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 // Bounded wait for the phase of parity PARITY to complete.  Each try_wait
 // suspends the thread in hardware until the phase completes or kSuspendNs
 // pass, so a waiting warp takes no issue slots; after kWaitRounds rounds
-// (seconds) the wait gives up and flags the error.
+// (seconds) the wait gives up and records it in the host-visible flag ERR.
 constexpr uint32_t kSuspendNs = 1000000;
 constexpr uint32_t kWaitRounds = 4096;
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
   const uint32_t a = smem_u32(bar);
   for (uint32_t i = 0; i < kWaitRounds; i++) {
     uint32_t done;
@@ -442,12 +441,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         : "=r"(done) : "r"(a), "r"(parity), "r"(kSuspendNs) : "memory");
     if (done) return true;
   }
-  atomicExch(&g_tma_error, 1);
+  report_wait_timeout(err);
   return false;
-}
-// The producer's wait for a free stage (the same bounded, suspending wait).
-__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity) {
-  return mbar_wait(bar, parity);
 }
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y,
                                             uint64_t *bar) {
@@ -499,7 +494,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
                    const float *__restrict__ SCALE, uint64_t s_stride,
                    const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
                    uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
-                   uint32_t count) {
+                   uint32_t count, int *err) {
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = (blockDim.x >> 5) - 1;            // consumer warps; warp nw produces
@@ -543,7 +538,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       uint32_t ph = 0;                             // parity of the current lap
       uint32_t g = 0;
       for (; g < total; g++) {
-        if (g >= (uint32_t)S && !mbar_wait_backoff(&empty[st], ph ^ 1u)) break;
+        if (g >= (uint32_t)S && !mbar_wait(&empty[st], ph ^ 1u, err)) break;
         const uint32_t it = blockIdx.x + (g / nchunk) * gridDim.x, c = g % nchunk;
         const uint32_t z = it / tpp, tile = it % tpp;
         const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
@@ -570,7 +565,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       }
       // Leave only when the last copies have landed (bounded).
       for (uint32_t k = g > (uint32_t)S ? g - S : 0; k < g; k++)
-        mbar_wait(&full[k % S], (k / S) & 1);
+        mbar_wait(&full[k % S], (k / S) & 1, err);
     }
     return;
   }
@@ -626,7 +621,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     // partial chunk hold TMA's zero fill, and a zero weight operand adds an
     // exact 0 whatever the stale fragments beside it.
     for (uint32_t c = 0; c < nchunk; c++) {
-      if (!mbar_wait(&full[cst], cph)) return;
+      if (!mbar_wait(&full[cst], cph, err)) return;
       const uint32_t wt = wsm + (uint32_t)cst * wbytes;
       const uint32_t fb = fsm + (uint32_t)cst * (fstage * 8u) + (uint32_t)lane * 16u;
 #pragma unroll
@@ -1039,7 +1034,7 @@ cudaError_t launch_tma_nt(const CUtensorMap &map, uint32_t items, int nw, cudaSt
   // kernel with the prep fused in), launched without the attribute.
   return launch_pdl(ternary_tma_kernel<NT, PB>, dim3(grid), dim3(32 * (nw + 1)),
                     tma_smem_bytes(NT, nw), st, map, X, xs, WP, wst, S, ss, B, Y, ys, seq,
-                    out, cols, limit, ws, count);
+                    out, cols, limit, ws, count, wait_flag_device());
 }
 
 // Launch the TMA variant when the weights of all COUNT problems form one
@@ -1130,7 +1125,7 @@ uint32_t ternary_dec_ctas(uint32_t count, uint32_t out, uint32_t cols, uint32_t 
 
 size_t ternary_ws_bytes_best(uint32_t count, uint32_t seq, uint32_t cols, bool per_block) {
   size_t b = ternary_ws_bytes(count, seq, cols);
-  if (!per_block && seq <= 16u) {
+  if (ternary_tc_applies(1, seq, 1, cols, per_block, 0)) {   // the shapes the tcgen05 GEMV takes
     const size_t t = ternary_tc_ws_bytes(count, seq, cols);
     if (t > b) b = t;
   }

@@ -22,7 +22,8 @@
 // The shift-and-mask expansion leaves the 16 codes of a packed word in the
 // order P = {3,7,11,15, 2,6,10,14, 1,5,9,13, 0,4,8,12}; the limb tile is
 // written in the same order, so the K index of A and B agrees.
-// Every mbarrier wait is bounded; one that gives up flags g_umma_error.
+// Every mbarrier wait is bounded; one that gives up sets the library's
+// host-mapped wait flag, which the synchronising entry points report.
 
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -48,7 +49,6 @@ constexpr uint32_t kWaitRounds = 4096;
 constexpr uint32_t kSuspendNs = 1000000;
 constexpr uint32_t kTop2 = 0xC0C0C0C0u;
 
-__device__ int g_umma_error;
 
 __device__ __forceinline__ uint32_t su32(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -63,7 +63,7 @@ __device__ __forceinline__ void bar_expect(uint64_t *b, uint32_t bytes) {
 __device__ __forceinline__ void bar_arrive(uint64_t *b) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(su32(b)) : "memory");
 }
-__device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity) {
+__device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity, int *err) {
   for (uint32_t i = 0; i < kWaitRounds; i++) {
     uint32_t done;
     asm volatile(
@@ -72,7 +72,7 @@ __device__ __forceinline__ bool bar_wait(uint64_t *b, uint32_t parity) {
         : "=r"(done) : "r"(su32(b)), "r"(parity), "r"(kSuspendNs) : "memory");
     if (done) return true;
   }
-  atomicExch(&g_umma_error, 1);
+  report_wait_timeout(err);
   return false;
 }
 __device__ __forceinline__ void tma2d(void *dst, const CUtensorMap *map, int x, int y,
@@ -187,7 +187,8 @@ __global__ void __launch_bounds__(192, 1)
 ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
                     const float *__restrict__ S, const float *__restrict__ BIAS,
                     const float *__restrict__ rowinv, const int *__restrict__ rowflag,
-                    float *__restrict__ Y, uint32_t seq, uint32_t out, uint32_t cols) {
+                    float *__restrict__ Y, uint32_t seq, uint32_t out, uint32_t cols,
+                    int *err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -229,7 +230,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       for (uint32_t kt = 0; kt < nk; kt++) {
         const int st = (int)(kt % kUmmaStages);
         if (kt >= (uint32_t)kUmmaStages &&
-            !bar_wait(&empty[st], ((kt / kUmmaStages) - 1) & 1))
+            !bar_wait(&empty[st], ((kt / kUmmaStages) - 1) & 1, err))
           break;
         bar_expect(&full[st], kWBytes + kBBytes);
         tma2d(sW + st * kWBytes, &tmW, (int)(kt * (kUmmaK / 16)), (int)m0, &full[st]);
@@ -242,7 +243,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       for (uint32_t kt = 0; kt < nk; kt++) {
         const int st = (int)(kt % kUmmaStages);
         const uint32_t ph = (kt / kUmmaStages) & 1;
-        if (!bar_wait(&full[st], ph) || !bar_wait(&aready[st], ph)) break;
+        if (!bar_wait(&full[st], ph, err) || !bar_wait(&aready[st], ph, err)) break;
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
         const uint32_t a0 = su32(sA + st * kABytes), b0 = su32(sB + st * kBBytes);
 #pragma unroll
@@ -258,7 +259,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     const uint32_t r = threadIdx.x - 64;          // 0..127
     for (uint32_t kt = 0; kt < nk; kt++) {
       const int st = (int)(kt % kUmmaStages);
-      if (!bar_wait(&full[st], (kt / kUmmaStages) & 1)) break;
+      if (!bar_wait(&full[st], (kt / kUmmaStages) & 1, err)) break;
       const uint4 *wr = reinterpret_cast<const uint4 *>(sW + st * kWBytes + r * 32u);
       const uint4 lo = wr[0], hi = wr[1];
       const uint32_t w8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
@@ -275,7 +276,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       if (lane == 0) bar_arrive(&aready[st]);
     }
     // ---- epilogue: accumulators -> Y ----
-    if (bar_wait(done, 0)) {
+    if (bar_wait(done, 0, err)) {
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
       const uint32_t q = (uint32_t)(warp & 3);      // TMEM lane quarter of this warp
       const uint32_t o = m0 + q * 32u + (uint32_t)lane;
@@ -420,7 +421,7 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   if (e != cudaSuccess) return e;
   const dim3 grid((out + kUmmaM - 1) / kUmmaM, (seq + kUmmaTok - 1) / kUmmaTok);
   ternary_umma_kernel<<<grid, 192, smem, st>>>(mw, mb, S, BIAS, rowinv, rowflag, Y, seq, out,
-                                                cols);
+                                                cols, wait_flag_device());
   if ((e = cudaPeekAtLastError()) != cudaSuccess) return e;
   umma_flagged_kernel<<<seq, 256, 0, st>>>(X, WP, S, BIAS, rowflag, Y, seq, out, cols);
   count_launches(3);

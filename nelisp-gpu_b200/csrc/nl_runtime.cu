@@ -863,6 +863,46 @@ extern "C" int nl_ternary_gemv_dev(const float *X, const uint32_t *WP, const flo
                         (cols + 15) / 16, false, workspace, ws_bytes, stream);
 }
 
+extern "C" int nl_wait_status(void) {
+  if (take_wait_timeout())
+    return set_error(NL_ERROR, "a kernel's bounded wait timed out; its outputs are invalid");
+  return NL_OK;
+}
+
+namespace nl {
+namespace {
+// One thread waits on an mbarrier that expects two arrivals and gets one: the
+// phase never completes, the wait gives up after ROUNDS rounds of at most
+// 100 us each and reports.
+__global__ void selftest_wait_kernel(int *err, uint32_t rounds) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(&bar);
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(a), "r"(2u));
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(a) : "memory");
+  for (uint32_t i = 0; i < rounds; i++) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done) : "r"(a), "r"(0u), "r"(100000u) : "memory");
+    if (done) return;
+  }
+  report_wait_timeout(err);
+}
+}  // namespace
+}  // namespace nl
+
+extern "C" int nl_selftest_wait_timeout(void) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  int *err = wait_flag_device();
+  if (!err) return set_error(NL_ERROR, "no host-mapped wait flag");
+  selftest_wait_kernel<<<1, 1, 0, g.stream>>>(err, 64);
+  count_launches(1);
+  if ((rc = cuda_status(cudaStreamSynchronize(g.stream), "selftest-wait"))) return rc;
+  return nl_wait_status();
+}
+
 extern "C" int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
                                             uint64_t x_stride, const uint32_t *WP,
                                             uint64_t w_stride, const float *S, uint64_t s_stride,

@@ -81,6 +81,8 @@ SIGNATURES = {
     "nl_ternary_gemv_batched_dev": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
                                          _u32, _u32, _u32, _vp, _sz, _vp]),
     "nl_ternary_gemv_static_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "nl_wait_status": (_i, []),
+    "nl_selftest_wait_timeout": (_i, []),
     "nl_ternary_gemv_batched_host": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
                                           _u32, _u32, _u32]),
     "nl_launch_count": (_u64, []),

@@ -131,3 +131,20 @@ def test_cli_vkmatmul_vksoftmax_vkrun(tmp_path):
     r = subprocess.run([os.path.join(BIN_DIR, "vkrun"), "/tmp/nlgpu123.spv", str(inp), str(outp),
                         "64", "1", "-", "4"], capture_output=True, timeout=120)
     assert r.returncode == 2                             # unknown kernel name
+
+
+def test_bounded_wait_timeout_is_reported():
+    """A kernel wait that can never complete gives up after its bound, sets the
+    host-mapped flag, and the host reads it as an error; the context stays
+    usable and the flag is cleared by the report."""
+    from nelisp_cuda import _lib as L
+    lib = L.load()
+    L.check(lib.nl_init(-1))
+    assert lib.nl_wait_status() == L.NL_OK
+    assert lib.nl_selftest_wait_timeout() == L.NL_ERROR
+    assert b"timed out" in lib.nl_last_error()
+    assert lib.nl_wait_status() == L.NL_OK          # cleared
+    from nelisp_cuda.host import Host
+    h = Host()
+    got = h.run2("add2", [("in", [1.0, 2.0]), ("in", [3.0, 4.0]), ("out", 2)], [2], 1)[0]
+    assert list(got) == [4.0, 6.0]

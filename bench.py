@@ -568,6 +568,77 @@ def run_kernel_rows(device, peak, with_cpu):
         rows["decode-attn-b B8 H32 ctx4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
     del Q, CK, CV, Cq, flush
     torch.cuda.empty_cache()
+    rows.update(upload_rows())
+    return rows
+
+
+def upload_rows():
+    """OP_UPLOAD_FILE of a 1 GiB file (the pipelined reader: parallel preads,
+    O_DIRECT where the file system takes it, copies overlapping reads) and the
+    f32 -> two-bit repacking of a 6912 x 2560 weight matrix from a file."""
+    import ctypes
+    import os
+    import tempfile
+
+    import numpy as np
+
+    from nelisp_cuda import _lib as L
+    lib = L.load()
+    rows = {}
+    d = tempfile.mkdtemp(prefix="nl_upload_")
+    try:
+        path = os.path.join(d, "weights.bin")
+        nbytes = 1 << 30
+        blk = np.random.default_rng(3).integers(0, 2 ** 32, size=(16 << 20) // 4,
+                                                 dtype=np.uint64).astype(np.uint32).tobytes()
+        with open(path, "wb") as f:
+            for _ in range(nbytes // len(blk)):
+                f.write(blk)
+            f.flush()
+            os.fsync(f.fileno())
+        try:
+            fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+            os.close(fd)
+            direct = True
+        except (OSError, AttributeError):
+            direct = False
+        h = ctypes.c_uint32()
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            L.check(lib.nl_upload_file(path.encode(), 0, nbytes // 4, ctypes.byref(h)))
+            times.append(time.perf_counter() - t0)
+            lib.nl_free(h.value)
+        t = min(times)
+        rows["upload-file 1 GiB"] = {
+            "ms": round(t * 1e3, 1), "GB/s": round(nbytes / t / 1e9, 2),
+            "o_direct": direct,
+            "note": "file -> device through 4 x 16 MiB pinned slots, 4 parallel preads per slot; "
+                    "with O_DIRECT the reads bypass the page cache and come from the disk"}
+        rws, cls = 6912, 2560
+        w = (np.random.default_rng(4).standard_normal((rws, cls)) * 0.02).astype(np.float32)
+        wpath = os.path.join(d, "ffn_f32.bin")
+        with open(wpath, "wb") as f:
+            f.write(w.tobytes())
+            os.fsync(f.fileno())
+        hw, hs = ctypes.c_uint32(), ctypes.c_uint32()
+        times = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            L.check(lib.nl_upload_file_ternary(wpath.encode(), 0, rws, cls, 1, ctypes.byref(hw),
+                                               ctypes.byref(hs)))
+            times.append(time.perf_counter() - t0)
+            lib.nl_free(hw.value)
+            lib.nl_free(hs.value)
+        t = min(times)
+        rows["upload-file-ternary 6912x2560 f32"] = {
+            "ms": round(t * 1e3, 2), "GB/s_f32_read": round(w.nbytes / t / 1e9, 2),
+            "note": "read the f32 matrix, per-row absmean, quant-w thresholds, pack to 2 bits "
+                    "(70.8 MB in, 4.4 MB packed + scales out)"}
+    finally:
+        for fn in os.listdir(d):
+            os.remove(os.path.join(d, fn))
+        os.rmdir(d)
     return rows
 
 

@@ -114,9 +114,26 @@ int nl_kernel_arity(const char *name, uint32_t *nbuf, uint32_t *npush);
 int nl_upload(const void *words, uint32_t nwords, uint32_t *handle);
 /* OP_UPLOAD_FILE (host/vkserver.c:371-410): read NWORDS words at byte
  * OFFSET of PATH straight into a new resident buffer.  Status 1 (and no
- * handle allocated) on open, seek or short-read failure. */
+ * handle allocated) on open, seek or short-read failure.  The region streams
+ * through four 16 MiB pinned slots, each filled by four parallel preads
+ * (O_DIRECT where the file system allows) while the previous slot is copied
+ * to the device. */
 int nl_upload_file(const char *path, uint64_t offset, uint32_t nwords,
                    uint32_t *handle);
+
+/* OP_UPLOAD_FILE with on-device repacking: reads an f32 weight matrix
+ * [rows x cols] (row-major, the importer's dense layout) at OFFSET of PATH
+ * through the same pipelined reader, ternarizes it on the device with the
+ * reference's quant-w rule (lisp/nelisp-gpu-kernels.el:516-561: beta = mean
+ * |W|, per tensor or, with PER_ROW, per row; t = +1 where W/beta >= 0.5, -1
+ * where <= -0.5, else 0) and packs it into the two-bit GEMV format (field i
+ * of word i/16 at bits 2(i%16); 00 -> 0, 01 -> +1, 11 -> -1).  Returns two
+ * resident handles: *H_WP, rows x ceil(cols/16) words, and *H_S, the rows
+ * scales (beta of each row).  diag(S) (T x) equals quant-w's fake-quantized
+ * weights times x.  Short files and open errors: NL_ERROR, no handles. */
+int nl_upload_file_ternary(const char *path, uint64_t offset, uint32_t rows,
+                           uint32_t cols, int per_row, uint32_t *h_wp,
+                           uint32_t *h_s);
 /* OP_WRITE_RESIDENT (host/vkserver.c:356-367): overwrite in place.  Status 1
  * for a bad handle or more words than the buffer holds. */
 int nl_write_resident(uint32_t handle, const void *words, uint32_t nwords);

@@ -58,6 +58,8 @@ extern const OpSpec kKvOps[];
 extern const int kKvOpsCount;
 extern const OpSpec kMiscOps[];
 extern const int kMiscOpsCount;
+extern const OpSpec kQuantOps[];
+extern const int kQuantOpsCount;
 
 // Error reporting (nl_runtime.cu).
 int set_error(int code, const char *fmt, ...);
@@ -224,6 +226,19 @@ cudaError_t ternary_tc_launch(uint32_t count, const float *X, uint64_t x_stride,
                               uint64_t s_stride, const float *BIAS, float *Y, uint64_t y_stride,
                               uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
                               size_t ws_bytes, cudaStream_t st, bool *launched);
+
+// Copies NBYTES at OFFSET of PATH into device memory DST through the pipelined
+// pinned-slot reader (nl_runtime.cu).  NL_OK, or NL_ERROR with a message
+// (*MISSING_WORDS set when the file is short).
+int file_to_device(const char *path, uint64_t offset, size_t nbytes, void *dst,
+                   uint64_t *missing_words);
+
+// Ternarization of an f32 weight matrix with the reference's quant-w rule,
+// packed into the two-bit GEMV format (k_quant.cu).  SCRATCH holds
+// quant_w_scratch_bytes(rows) bytes.
+size_t quant_w_scratch_bytes(uint32_t rows);
+cudaError_t quant_w_pack_launch(const float *W, uint32_t rows, uint32_t cols, bool per_row,
+                                uint32_t *WP, float *S, void *scratch, cudaStream_t st);
 
 // Library workspace for typed calls that pass no workspace (nl_runtime.cu).
 void *library_workspace(size_t bytes, cudaStream_t stream);

@@ -20,7 +20,7 @@ const Table kTables[] = {
     {kTernaryOps, &kTernaryOpsCount}, {kInt8Ops, &kInt8OpsCount},
     {kDenseOps, &kDenseOpsCount},     {kRowOps, &kRowOpsCount},
     {kAttnOps, &kAttnOpsCount},       {kKvOps, &kKvOpsCount},
-    {kMiscOps, &kMiscOpsCount},
+    {kMiscOps, &kMiscOpsCount},       {kQuantOps, &kQuantOpsCount},
 };
 
 }  // namespace

@@ -16,10 +16,14 @@
 
 #include <cuda_runtime.h>
 #include <errno.h>
+#include <fcntl.h>
 #include <stdarg.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
+
+#include <thread>
 
 #include <vector>
 
@@ -445,56 +449,234 @@ extern "C" int nl_upload(const void *words, uint32_t nwords, uint32_t *handle) {
   return NL_OK;
 }
 
-extern "C" int nl_upload_file(const char *path, uint64_t offset, uint32_t nwords,
-                              uint32_t *handle) {
-  int rc = ensure_ready();
-  if (rc) return rc;
-  FILE *f = fopen(path, "rb");
-  if (!f) return set_error(NL_ERROR, "cannot open %s: %s", path, strerror(errno));
-  if (fseeko(f, (off_t)offset, SEEK_SET) != 0) {
-    fclose(f);
-    return set_error(NL_ERROR, "seek %s", path);
+namespace nl {
+namespace {
+
+// ---- file -> device at NVMe speed ---------------------------------------------
+// host/vkserver.c:371-410 freads the region into mapped memory in one call.
+// Here the region streams through kReadSlots pinned slots of kReadSlot bytes:
+// each slot is filled by kReadThreads parallel preads (several requests in
+// flight keep an NVMe queue busy) and copied to the device asynchronously, so
+// the copy of one slot overlaps the reads of the next.  The file is opened
+// with O_DIRECT where the file system takes it (no page-cache copy); reads
+// then start on a 4 KiB boundary and the slot's leading bytes are skipped.
+constexpr size_t kReadSlot = 16u << 20;
+constexpr int kReadSlots = 4;                  // kReadSlots * kReadSlot = kStageBytes
+constexpr int kReadThreads = 4;
+constexpr size_t kDirectAlign = 4096;
+static_assert(kReadSlots * kReadSlot == kStageBytes, "staging layout");
+
+struct FileReader {
+  int fd = -1;
+  bool direct = false;
+  ~FileReader() {
+    if (fd >= 0) close(fd);
   }
-  uint32_t h = 0;
-  if ((rc = alloc_slot(&h))) { fclose(f); return rc; }
-  Resident &r = g.res[h];
-  r.ptr = alloc_words(nwords, &r.host);
-  if (!r.ptr) { fclose(f); return set_error(NL_ERROR, "upload-file: cannot allocate %u words", nwords); }
-  r.words = nwords;
-  r.used = true;
+  bool open_path(const char *path) {
+#ifdef O_DIRECT
+    fd = open(path, O_RDONLY | O_DIRECT);
+    if (fd >= 0) {
+      direct = true;
+      return true;
+    }
+#endif
+    fd = open(path, O_RDONLY);
+    direct = false;
+    return fd >= 0;
+  }
+  void reopen_buffered(const char *path) {
+    if (fd >= 0) close(fd);
+    fd = open(path, O_RDONLY);
+    direct = false;
+  }
+};
+
+// Reads [off, off + len) into buf with kReadThreads parallel preads; returns
+// the bytes read before the first short read (EOF), or -1 on an I/O error.
+long long read_span(int fd, char *buf, uint64_t off, size_t len, int *err_no) {
+  const size_t part = ((len + kReadThreads - 1) / kReadThreads + kDirectAlign - 1) &
+                      ~(kDirectAlign - 1);
+  long long got[kReadThreads] = {0};
+  int errs[kReadThreads] = {0};
+  std::thread th[kReadThreads];
+  int nth = 0;
+  for (int t = 0; t < kReadThreads; t++) {
+    const size_t b = (size_t)t * part;
+    if (b >= len) break;
+    const size_t n = b + part <= len ? part : len - b;
+    th[nth++] = std::thread([=, &got, &errs] {
+      size_t done = 0;
+      while (done < n) {
+        const ssize_t r = pread(fd, buf + b + done, n - done, (off_t)(off + b + done));
+        if (r < 0) {
+          if (errno == EINTR) continue;
+          errs[t] = errno;
+          break;
+        }
+        if (r == 0) break;
+        done += (size_t)r;
+      }
+      got[t] = (long long)done;
+    });
+  }
+  for (int t = 0; t < nth; t++) th[t].join();
+  long long total = 0;
+  for (int t = 0; t < nth; t++) {
+    if (errs[t]) {
+      *err_no = errs[t];
+      return -1;
+    }
+    total += got[t];
+    const size_t b = (size_t)t * part, n = b + part <= len ? part : len - b;
+    if ((size_t)got[t] < n) break;            // EOF inside this part
+  }
+  return total;
+}
+
+}  // namespace
+
+// Copies NBYTES at OFFSET of PATH to device memory DST.  Returns NL_OK, or
+// NL_ERROR with a message (*MISSING_WORDS set on a short file).
+namespace {
+int file_to_device_impl(const char *path, uint64_t offset, size_t nbytes, void *dst,
+                        uint64_t *missing_words, bool allow_direct) {
+  *missing_words = 0;
+  FileReader fr;
+  if (allow_direct ? !fr.open_path(path) : (fr.reopen_buffered(path), fr.fd < 0))
+    return set_error(NL_ERROR, "cannot open %s: %s", path, strerror(errno));
+  if (nbytes == 0) return NL_OK;
   if (!g.stage && cudaHostAlloc(&g.stage, kStageBytes, cudaHostAllocDefault) != cudaSuccess) {
     cudaGetLastError();
     g.stage = nullptr;
   }
-  // Pinned staging when it could be had, pageable memory otherwise.
-  void *stage = g.stage ? g.stage : malloc(kStageBytes);
-  if (!stage) { fclose(f); nl_free(h); return set_error(NL_ERROR, "upload-file: no staging memory"); }
-  size_t want = (size_t)nwords * 4u, done = 0;
-  uint64_t missing = 0;
-  while (done < want) {
-    size_t n = want - done;
-    if (n > kStageBytes) n = kStageBytes;
-    size_t got = fread(stage, 1, n, f);
-    if (got) {
-      cudaError_t e = cudaMemcpy((char *)r.ptr + done, stage, got, cudaMemcpyHostToDevice);
-      if (e != cudaSuccess) {
-        if (stage != g.stage) free(stage);
-        fclose(f);
-        nl_free(h);
+  if (!g.stage) return set_error(NL_ERROR, "upload-file: no pinned staging memory");
+  if (!g.h2d && cudaStreamCreateWithFlags(&g.h2d, cudaStreamNonBlocking) != cudaSuccess)
+    return cuda_status(cudaGetLastError(), "upload-file: stream");
+  static cudaEvent_t slot_ev[kReadSlots] = {};
+  for (cudaEvent_t &ev : slot_ev)
+    if (!ev && cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess)
+      return cuda_status(cudaGetLastError(), "upload-file: events");
+  const uint64_t start = fr.direct ? offset & ~(uint64_t)(kDirectAlign - 1) : offset;
+  const size_t skew = (size_t)(offset - start);
+  const uint64_t span = skew + nbytes;           // bytes of file from START that matter
+  uint64_t done = 0;                              // file bytes consumed from START
+  for (int slot = 0; done < span; slot = (slot + 1) % kReadSlots) {
+    char *buf = (char *)g.stage + (size_t)slot * kReadSlot;
+    cudaError_t e = cudaEventSynchronize(slot_ev[slot]);   // its previous copy is done
+    if (e != cudaSuccess) return cuda_status(e, "upload-file");
+    size_t want = span - done < kReadSlot ? (size_t)(span - done) : kReadSlot;
+    size_t req = fr.direct ? (want + kDirectAlign - 1) & ~(kDirectAlign - 1) : want;
+    int err_no = 0;
+    long long got = read_span(fr.fd, buf, start + done, req, &err_no);
+    if (got < 0 && fr.direct && err_no == EINVAL && done == 0)   // O_DIRECT refused
+      return file_to_device_impl(path, offset, nbytes, dst, missing_words, false);
+    if (got < 0) return set_error(NL_ERROR, "read %s: %s", path, strerror(err_no));
+    const size_t use = (size_t)got < want ? (size_t)got : want;
+    // device bytes: file [start + done + lo, start + done + use) minus the skew
+    const size_t lo = done < skew ? (size_t)(skew - done) : 0;
+    if (use > lo) {
+      const uint64_t dpos = done + lo - skew;
+      if ((e = cudaMemcpyAsync((char *)dst + dpos, buf + lo, use - lo, cudaMemcpyHostToDevice,
+                               g.h2d)) != cudaSuccess ||
+          (e = cudaEventRecord(slot_ev[slot], g.h2d)) != cudaSuccess)
         return cuda_status(e, "upload-file");
-      }
     }
-    done += got;
-    if (got != n) { missing = (want - done + 3) / 4u; break; }
+    done += use;
+    if (use < want) {                            // short file
+      const uint64_t have = done > skew ? done - skew : 0;
+      *missing_words = (nbytes - have + 3) / 4u;
+      cudaStreamSynchronize(g.h2d);
+      return set_error(NL_ERROR, "%s short read, %llu words missing", path,
+                       (unsigned long long)*missing_words);
+    }
   }
-  if (stage != g.stage) free(stage);
-  fclose(f);
-  if (missing) {
+  return cuda_status(cudaStreamSynchronize(g.h2d), "upload-file");
+}
+}  // namespace
+
+int file_to_device(const char *path, uint64_t offset, size_t nbytes, void *dst,
+                   uint64_t *missing_words) {
+  return file_to_device_impl(path, offset, nbytes, dst, missing_words, true);
+}
+
+}  // namespace nl
+
+extern "C" int nl_upload_file(const char *path, uint64_t offset, uint32_t nwords,
+                              uint32_t *handle) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  {
+    // the reference opens and seeks before allocating (host/vkserver.c:384-386)
+    FileReader probe;
+    if (!probe.open_path(path))
+      return set_error(NL_ERROR, "cannot open %s: %s", path, strerror(errno));
+  }
+  uint32_t h = 0;
+  if ((rc = alloc_slot(&h))) return rc;
+  Resident &r = g.res[h];
+  r.ptr = alloc_words(nwords, &r.host);
+  if (!r.ptr && nwords) return set_error(NL_ERROR, "upload-file: cannot allocate %u words", nwords);
+  r.words = nwords;
+  r.used = true;
+  uint64_t missing = 0;
+  rc = file_to_device(path, offset, (size_t)nwords * 4u, r.ptr, &missing);
+  if (rc != NL_OK) {
+    char msg[1024];
+    snprintf(msg, sizeof(msg), "%s", nl_last_error());
     nl_free(h);
-    return set_error(NL_ERROR, "%s short read, %llu words missing", path,
-                     (unsigned long long)missing);
+    return set_error(rc, "%s", msg);
   }
   *handle = h;
+  return NL_OK;
+}
+
+extern "C" int nl_upload_file_ternary(const char *path, uint64_t offset, uint32_t rows,
+                                      uint32_t cols, int per_row, uint32_t *h_wp,
+                                      uint32_t *h_s) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  if (!h_wp || !h_s) return set_error(NL_ERROR, "upload-file-ternary: null handle pointer");
+  if (!rows || !cols) return set_error(NL_ERROR, "upload-file-ternary: empty matrix");
+  const uint64_t wng = (cols + 15u) / 16u, wwords = (uint64_t)rows * wng;
+  if (wwords > 0xffffffffull) return set_error(NL_ERROR, "upload-file-ternary: too large");
+  const size_t fbytes = (size_t)rows * cols * 4u;
+  void *tmp = nullptr;
+  const size_t scratch = quant_w_scratch_bytes(rows);
+  cudaError_t e = cudaMalloc(&tmp, align256(fbytes) + scratch);
+  if (e != cudaSuccess) return cuda_status(e, "upload-file-ternary: f32 staging");
+  uint64_t missing = 0;
+  if ((rc = file_to_device(path, offset, fbytes, tmp, &missing)) != NL_OK) {
+    cudaFree(tmp);
+    return rc;
+  }
+  uint32_t hw = 0, hs = 0;
+  if ((rc = alloc_slot(&hw))) { cudaFree(tmp); return rc; }
+  Resident &rw = g.res[hw];
+  rw.ptr = alloc_words((uint32_t)wwords, &rw.host);
+  rw.words = (uint32_t)wwords;
+  rw.used = true;
+  if ((rc = alloc_slot(&hs))) { nl_free(hw); cudaFree(tmp); return rc; }
+  Resident &rs = g.res[hs];
+  rs.ptr = alloc_words(rows, &rs.host);
+  rs.words = rows;
+  rs.used = true;
+  if (!rw.ptr || !rs.ptr) {
+    nl_free(hw);
+    nl_free(hs);
+    cudaFree(tmp);
+    return set_error(NL_ERROR, "upload-file-ternary: cannot allocate the packed weights");
+  }
+  e = quant_w_pack_launch((const float *)tmp, rows, cols, per_row != 0, (uint32_t *)rw.ptr,
+                          (float *)rs.ptr, (char *)tmp + align256(fbytes), g.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+  cudaFree(tmp);
+  if (e != cudaSuccess) {
+    nl_free(hw);
+    nl_free(hs);
+    return cuda_status(e, "upload-file-ternary");
+  }
+  *h_wp = hw;
+  *h_s = hs;
   return NL_OK;
 }
 

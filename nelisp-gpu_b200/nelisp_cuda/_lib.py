@@ -82,6 +82,8 @@ SIGNATURES = {
                                          _u32, _u32, _u32, _vp, _sz, _vp]),
     "nl_ternary_gemv_static_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
     "nl_wait_status": (_i, []),
+    "nl_upload_file_ternary": (_i, [ctypes.c_char_p, _u64, _u32, _u32, ctypes.c_int,
+                                    ctypes.POINTER(_u32), ctypes.POINTER(_u32)]),
     "nl_selftest_wait_timeout": (_i, []),
     "nl_ternary_gemv_batched_host": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
                                           _u32, _u32, _u32]),

@@ -89,6 +89,12 @@ def _declare(L):
         "nlo_rope_apply": [_F] * 5 + [_u32] * 3,
         "nlo_silu": [_F, _F, _u32],
         "nlo_scale_rows": [_F] * 3 + [_u32] * 2,
+        "nlo_sumsq_acc": [_F, _F, _u32],
+        "nlo_absmean_acc": [_F, _F, _u32],
+        "nlo_clip_scale": [_F, _F, _F],
+        "nlo_quant_act": [_F, _F, _u32, _u32],
+        "nlo_quant_w": [_F, _F, _F, _u32],
+        "nlo_quant_w_pack": [_F, _u32, _u32, ctypes.c_int, _U, _F],
         "nlo_matmul_sample_ref": [_u32] * 4,
         "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
         "nlo_set_threads": [ctypes.c_int],
@@ -426,6 +432,47 @@ def scale_rows(Y, S, M, N):
     C = np.zeros(M * N, np.float32)
     lib().nlo_scale_rows(_f(Y), _f(S), _f(C), M, N)
     return C
+
+
+def sumsq_acc(G, acc0, n):
+    G, A = f32(G), np.array([acc0], np.float32)
+    lib().nlo_sumsq_acc(_f(G), _f(A), n)
+    return A[0]
+
+
+def absmean_acc(G, acc0, n):
+    G, A = f32(G), np.array([acc0], np.float32)
+    lib().nlo_absmean_acc(_f(G), _f(A), n)
+    return A[0]
+
+
+def clip_scale(gsq, cfg):
+    G, C, S = (np.array([v], np.float32) for v in (gsq, cfg, 0.0))
+    lib().nlo_clip_scale(_f(G), _f(C), _f(S))
+    return S[0]
+
+
+def quant_act(X, seq, cols):
+    X = f32(X)
+    XQ = np.zeros(seq * cols, np.float32)
+    lib().nlo_quant_act(_f(X), _f(XQ), seq, cols)
+    return XQ
+
+
+def quant_w(W, S0, n):
+    W, S = f32(W), np.array([S0], np.float32)
+    WQ = np.zeros(n, np.float32)
+    lib().nlo_quant_w(_f(W), _f(S), _f(WQ), n)
+    return WQ
+
+
+def quant_w_pack(W, rows, cols, per_row):
+    W = f32(W)
+    wng = (cols + 15) // 16
+    WP = np.zeros(rows * wng, np.uint32)
+    S = np.zeros(rows, np.float32)
+    lib().nlo_quant_w_pack(_f(W), rows, cols, int(per_row), _u(WP), _f(S))
+    return WP, S
 
 
 def matmul_sample_ref(r, c, K, N) -> float:

@@ -133,6 +133,16 @@ void nlo_rope_apply(const float *X, const float *CO, const float *SI, const floa
                     uint32_t seq, uint32_t dim, uint32_t heads);
 void nlo_silu(const float *X, float *C, uint32_t n);
 void nlo_scale_rows(const float *Y, const float *S, float *C, uint32_t M, uint32_t N);
+/* nl_oracle_misc.c: sumsq-acc :496-503, clip-scale :505-512, absmean-acc
+ * :516-526, quant-act :529-548, quant-w :550-561, and the repacking of
+ * nl_upload_file_ternary */
+void nlo_sumsq_acc(const float *G, float *ACC, uint32_t n);
+void nlo_absmean_acc(const float *G, float *ACC, uint32_t n);
+void nlo_clip_scale(const float *GSQ, const float *CFG, float *SCALE);
+void nlo_quant_act(const float *X, float *XQ, uint32_t seq, uint32_t cols);
+void nlo_quant_w(const float *W, const float *S, float *WQ, uint32_t n);
+void nlo_quant_w_pack(const float *W, uint32_t rows, uint32_t cols, int per_row, uint32_t *WP,
+                      float *S);
 
 /* Double-precision references used by the reference's own self-checks. */
 double nlo_matmul_sample_ref(uint32_t r, uint32_t c, uint32_t K, uint32_t N);

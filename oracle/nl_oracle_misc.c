@@ -1,11 +1,13 @@
 /* nl_oracle_misc.c -- CPU restatements (test infrastructure only: the parity
  * checker for libnelisp_cuda, never a product path) of the reference
  * operators for the unfused prefill attention pieces, QK-norm, adjacent-pair
- * RoPE, SiLU, row scaling, the DP4A spikes and the backward GEMMs.  One loop
+ * RoPE, SiLU, row scaling, the DP4A spikes, the backward GEMMs and the BitNet
+ * quantization family (with the on-device repacking of upload-file).  One loop
  * iteration per reference invocation (gid-x), the reference's f32 operation
  * order, no contraction (built with -ffp-contract=off). */
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "nl_oracle.h"
@@ -166,4 +168,93 @@ void nlo_silu(const float *X, float *C, uint32_t n) {
 /* :1365-1372 (scale-rows) */
 void nlo_scale_rows(const float *Y, const float *S, float *C, uint32_t M, uint32_t N) {
   for (uint64_t idx = 0; idx < (uint64_t)M * N; idx++) C[idx] = Y[idx] * S[idx / N];
+}
+
+/* :496-503 (sumsq-acc) and :516-526 (absmean-acc): serial f32 sums, as the
+ * reference's single thread does them. */
+void nlo_sumsq_acc(const float *G, float *ACC, uint32_t n) {
+  float acc = 0.0f;
+  for (uint32_t i = 0; i < n; i++) acc = acc + G[i] * G[i];
+  ACC[0] = ACC[0] + acc;
+}
+void nlo_absmean_acc(const float *G, float *ACC, uint32_t n) {
+  float acc = 0.0f;
+  for (uint32_t i = 0; i < n; i++) acc = acc + (G[i] < 0.0f ? 0.0f - G[i] : G[i]);
+  ACC[0] = ACC[0] + acc;
+}
+
+/* :505-512 (clip-scale) */
+void nlo_clip_scale(const float *GSQ, const float *CFG, float *SCALE) {
+  float s = CFG[0] / sqrtf(GSQ[0] + 1.0e-12f);
+  SCALE[0] = 1.0f;
+  if (s < 1.0f) SCALE[0] = s;
+}
+
+/* :529-548 (quant-act) */
+void nlo_quant_act(const float *X, float *XQ, uint32_t seq, uint32_t cols) {
+  for (uint32_t row = 0; row < seq; row++) {
+    const float *x = X + (size_t)row * cols;
+    float amax = 0.0f;
+    for (uint32_t c = 0; c < cols; c++) {
+      float av = x[c] < 0.0f ? 0.0f - x[c] : x[c];
+      if (av > amax) amax = av;
+    }
+    float gamma = amax / 127.0f;
+    for (uint32_t c = 0; c < cols; c++) {
+      float xq = 0.0f;
+      if (gamma > 0.0f) {
+        float q = x[c] / gamma, sgn = 1.0f, aq = q;
+        if (q < 0.0f) { sgn = -1.0f; aq = 0.0f - q; }
+        uint32_t ri = (uint32_t)(aq + 0.5f);
+        float rf = (float)ri;
+        if (rf > 127.0f) rf = 127.0f;
+        xq = gamma * (sgn * rf);
+      }
+      XQ[(size_t)row * cols + c] = xq;
+    }
+  }
+}
+
+static int trit_q(float w, float beta) {
+  if (!(beta > 0.0f)) return 0;
+  float q = w / beta;
+  return q >= 0.5f ? 1 : (q <= -0.5f ? -1 : 0);
+}
+
+/* :550-561 (quant-w) */
+void nlo_quant_w(const float *W, const float *S, float *WQ, uint32_t n) {
+  float beta = S[0] / (float)n;
+  for (uint32_t i = 0; i < n; i++) WQ[i] = beta * (float)trit_q(W[i], beta);
+}
+
+/* The on-device repacking of nl_upload_file_ternary: quant-w's rule with
+ * beta = mean |W| per tensor or per row, the sum of |W| taken in f64 (as the
+ * device does; the reference's absmean-acc sums serially in f32), written as
+ * packed two-bit codes (01 -> +1, 11 -> -1, 00 -> 0) and per-row scales. */
+void nlo_quant_w_pack(const float *W, uint32_t rows, uint32_t cols, int per_row, uint32_t *WP,
+                      float *S) {
+  uint32_t wng = (cols + 15) / 16;
+  double total = 0.0;
+  double *rs = (double *)malloc(sizeof(double) * (rows ? rows : 1));
+  for (uint32_t o = 0; o < rows; o++) {
+    double s = 0.0;
+    for (uint32_t c = 0; c < cols; c++) s += fabs((double)W[(size_t)o * cols + c]);
+    rs[o] = s;
+    total += s;
+  }
+  float tbeta = (float)(total / ((double)rows * cols));
+  for (uint32_t o = 0; o < rows; o++) {
+    float beta = per_row ? (float)(rs[o] / (double)cols) : tbeta;
+    S[o] = beta;
+    for (uint32_t wi = 0; wi < wng; wi++) {
+      uint32_t word = 0;
+      for (uint32_t f = 0; f < 16; f++) {
+        uint32_t c = 16 * wi + f;
+        int t = c < cols ? trit_q(W[(size_t)o * cols + c], beta) : 0;
+        word |= (uint32_t)(t == 1 ? 1 : (t == -1 ? 3 : 0)) << (2 * f);
+      }
+      WP[(size_t)o * wng + wi] = word;
+    }
+  }
+  free(rs);
 }

@@ -65,7 +65,9 @@ def test_registry_names_the_reference_kernels(lib):
            "cache-append-paged-v", "decode-attn-paged-v",
            # unfused prefill attention, QK-norm, RoPE, DP4A spikes, backward GEMMs
            "matmul-at", "causal-mask", "attn-scores", "attn-context", "dp4a-dot",
-           "bitlinear-dp4a", "dp4a-rows-t", "rmsnorm-heads", "rope-apply", "silu", "scale-rows"}
+           "bitlinear-dp4a", "dp4a-rows-t", "rmsnorm-heads", "rope-apply", "silu", "scale-rows",
+           # BitNet quantization family
+           "sumsq-acc", "clip-scale", "absmean-acc", "quant-act", "quant-w"}
     assert hot <= names
     nb, npush = ctypes.c_uint32(), ctypes.c_uint32()
     assert lib.nl_kernel_arity(b"ternary-rows", ctypes.byref(nb), ctypes.byref(npush)) == 0

@@ -123,3 +123,61 @@ def test_rmsnorm_heads_rope_silu_scale_rows():
     Yr = rng.standard_normal((7, 5)).astype(np.float32)
     S = rng.standard_normal(7).astype(np.float32)
     assert np.array_equal(nlo.scale_rows(Yr.ravel(), S, 7, 5).reshape(7, 5), Yr * S[:, None])
+
+
+def test_quantization_family_restatements():
+    rng = np.random.default_rng(11)
+    # :550-561 quant-w, beta = S[0] / n, thresholds at +-0.5
+    W = rng.standard_normal(200).astype(np.float32)
+    S0 = np.float32(np.abs(W).sum())
+    WQ = nlo.quant_w(W, S0, 200)
+    beta = np.float32(S0 / np.float32(200))
+    q = W / beta
+    want = beta * np.where(q >= 0.5, 1.0, np.where(q <= -0.5, -1.0, 0.0)).astype(np.float32)
+    assert np.array_equal(WQ, want.astype(np.float32))
+    assert not nlo.quant_w(W, 0.0, 200).any()                 # beta 0: all zero
+    # :529-548 quant-act: gamma = max|x|/127, round by truncating |q| + 0.5
+    X = (rng.standard_normal((3, 50)) * 3).astype(np.float32)
+    XQ = nlo.quant_act(X.ravel(), 3, 50).reshape(3, 50)
+    for r in range(3):
+        g = np.float32(np.abs(X[r]).max() / np.float32(127.0))
+        qq = X[r] / g
+        rf = np.minimum(np.floor(np.abs(qq) + np.float32(0.5)), 127).astype(np.float32)
+        assert np.array_equal(XQ[r], (g * (np.sign(qq) * rf)).astype(np.float32))
+    # :505-512 clip-scale and the accumulators
+    assert nlo.clip_scale(4.0, 1.0) == np.float32(1.0) / np.sqrt(np.float32(4.0) + np.float32(1e-12))
+    assert nlo.clip_scale(0.25, 1.0) == 1.0
+    G = rng.standard_normal(1000).astype(np.float32)
+    assert abs(nlo.absmean_acc(G, 2.0, 1000) - (2.0 + np.abs(G.astype(np.float64)).sum())) < 1e-3
+    assert abs(nlo.sumsq_acc(G, 0.0, 1000) - (G.astype(np.float64) ** 2).sum()) < 1e-2
+
+
+@pytest.mark.parametrize("per_row", [False, True])
+def test_quant_w_pack_decodes_to_quant_w(per_row):
+    """The repacked weights decode (two-bit codes x row scale) to quant-w's
+    fake-quantized values with beta = mean |W| of the tensor or the row."""
+    rng = np.random.default_rng(12 + per_row)
+    rows, cols = 9, 37
+    W = rng.standard_normal((rows, cols)).astype(np.float32)
+    WP, S = nlo.quant_w_pack(W.ravel(), rows, cols, per_row)
+    wng = (cols + 15) // 16
+    codes = np.zeros((rows, wng * 16), np.int64)
+    w = WP.reshape(rows, wng)
+    for f in range(16):
+        c = (w >> np.uint32(2 * f)) & 3
+        codes[:, f::16] = np.where(c == 1, 1, np.where(c == 3, -1, 0))
+    assert not codes[:, cols:].any()
+    dec = codes[:, :cols] * S[:, None]
+    for o in range(rows):
+        n = cols if per_row else rows * cols
+        S0 = np.abs(W[o] if per_row else W).astype(np.float64).sum()
+        want = nlo.quant_w(W[o], np.float32(S0), n) if per_row else None
+        if per_row:
+            # beta rounds the f64 mean once; quant-w divides two f32 values:
+            # the scales may differ in the last bit, the trits may not
+            assert abs(S[o] - np.float32(S0 / n)) <= 1e-6 * S[o]
+            assert np.array_equal(codes[o, :cols], np.sign(want).astype(np.int64))
+        else:
+            assert S[o] == S[0]
+    if not per_row:
+        assert abs(S[0] - np.abs(W.astype(np.float64)).mean()) <= 1e-6 * S[0]

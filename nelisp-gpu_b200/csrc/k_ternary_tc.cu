@@ -194,7 +194,49 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *v) {
 }
 
 // ---- prep ------------------------------------------------------------------------
-// grid (kRowCluster * seq, count), clusters of kRowCluster CTAs per row (the
+// Packed word W (16 columns) of a row: xq = round(x * mul) (zeros when !OK),
+// the four field-scaled limb rows at XB (row stride COLS) in the K order of
+// the file comment; returns the sum of the sixteen xq.
+__device__ __forceinline__ long long tc_quantize_word(const float *xr, uint32_t W, bool ok,
+                                                      float mul, int8_t *xb, uint32_t cols) {
+  int q[16];
+  const float4 *src = reinterpret_cast<const float4 *>(xr + 16u * W);
+#pragma unroll
+  for (int v4 = 0; v4 < 4; v4++) {
+    const float4 f = ok ? src[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
+    q[4 * v4] = __float2int_rn(f.x * mul);       // exact scaling, one rounding
+    q[4 * v4 + 1] = __float2int_rn(f.y * mul);
+    q[4 * v4 + 2] = __float2int_rn(f.z * mul);
+    q[4 * v4 + 3] = __float2int_rn(f.w * mul);
+  }
+  long long part = 0;
+  uint32_t bw[4][4] = {};                        // [limb][byte group f]
+#pragma unroll
+  for (int f = 0; f < 4; f++) {
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+      const int v = q[4 * b + f] * (1 << (2 * (3 - f)));   // |v| <= 2^28
+      part += q[4 * b + f];
+      const int l0 = (int)(int8_t)(v & 0xff);
+      int r = (v - l0) >> 8;
+      const int l1 = (int)(int8_t)(r & 0xff);
+      r = (r - l1) >> 8;
+      const int l2 = (int)(int8_t)(r & 0xff);
+      const int l3 = (r - l2) >> 8;
+      bw[0][f] |= (uint32_t)(l0 & 0xff) << (8 * b);
+      bw[1][f] |= (uint32_t)(l1 & 0xff) << (8 * b);
+      bw[2][f] |= (uint32_t)(l2 & 0xff) << (8 * b);
+      bw[3][f] |= (uint32_t)(l3 & 0xff) << (8 * b);
+    }
+  }
+#pragma unroll
+  for (int l = 0; l < 4; l++)
+    *reinterpret_cast<uint4 *>(xb + (size_t)l * cols + 16u * W) =
+        make_uint4(bw[l][0], bw[l][1], bw[l][2], bw[l][3]);
+  return part;
+}
+
+// Few rows: grid (kRowCluster * seq, count), clusters of kRowCluster CTAs per row (the
 // row maximum is combined through distributed shared memory in rank order, as
 // in the chunked kernels' prep).  Each CTA quantizes its column slice, writes
 // its four limb rows and its partial sum of xq.
@@ -245,47 +287,63 @@ tc_prep_kernel(const float *__restrict__ X, uint64_t x_stride, uint32_t seq, uin
   }
   int8_t *xb = P.xb + ((size_t)z * tc_rows_b(seq) + 4u * s) * cols;
   long long part = 0;
-  for (uint32_t W = sl.c0 / 16u + threadIdx.x; W < sl.c1 / 16u; W += blockDim.x) {
-    int q[16];
-    const float4 *src = reinterpret_cast<const float4 *>(xr + 16u * W);
-#pragma unroll
-    for (int v4 = 0; v4 < 4; v4++) {
-      const float4 f = ok ? src[v4] : make_float4(0.f, 0.f, 0.f, 0.f);
-      q[4 * v4] = __float2int_rn(f.x * mul);       // exact scaling, one rounding
-      q[4 * v4 + 1] = __float2int_rn(f.y * mul);
-      q[4 * v4 + 2] = __float2int_rn(f.z * mul);
-      q[4 * v4 + 3] = __float2int_rn(f.w * mul);
-    }
-    uint32_t bw[4][4] = {};                        // [limb][byte group f]
-#pragma unroll
-    for (int f = 0; f < 4; f++) {
-#pragma unroll
-      for (int b = 0; b < 4; b++) {
-        const int v = q[4 * b + f] * (1 << (2 * (3 - f)));   // |v| <= 2^28
-        part += q[4 * b + f];
-        const int l0 = (int)(int8_t)(v & 0xff);
-        int r = (v - l0) >> 8;
-        const int l1 = (int)(int8_t)(r & 0xff);
-        r = (r - l1) >> 8;
-        const int l2 = (int)(int8_t)(r & 0xff);
-        const int l3 = (r - l2) >> 8;
-        bw[0][f] |= (uint32_t)(l0 & 0xff) << (8 * b);
-        bw[1][f] |= (uint32_t)(l1 & 0xff) << (8 * b);
-        bw[2][f] |= (uint32_t)(l2 & 0xff) << (8 * b);
-        bw[3][f] |= (uint32_t)(l3 & 0xff) << (8 * b);
-      }
-    }
-#pragma unroll
-    for (int l = 0; l < 4; l++)
-      *reinterpret_cast<uint4 *>(xb + (size_t)l * cols + 16u * W) =
-          make_uint4(bw[l][0], bw[l][1], bw[l][2], bw[l][3]);
-  }
+  for (uint32_t W = sl.c0 / 16u + threadIdx.x; W < sl.c1 / 16u; W += blockDim.x)
+    part += tc_quantize_word(xr, W, ok, mul, xb, cols);
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   if ((threadIdx.x & 31) == 0) lred[threadIdx.x >> 5] = part;
   __syncthreads();
   if (threadIdx.x == 0)
     P.rowsum[(z * 16 + s) * kRowCluster + rank] = lred[0] + lred[1] + lred[2] + lred[3];
   cl.sync();                      // no CTA leaves while its maximum is read
+}
+
+// Many rows (enough to fill the GPU without splitting a row): one CTA of
+// kTcRowThreads per row, no cluster; the row's sum of xq goes to partial slot
+// 0 and the other slots are zeroed, so the GEMV reads the same layout.
+constexpr int kTcRowThreads = 256;
+__global__ void __launch_bounds__(kTcRowThreads)
+tc_prep_rows_kernel(const float *__restrict__ X, uint64_t x_stride, uint32_t seq, uint32_t cols,
+                    uint32_t count, void *ws) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float red[kTcRowThreads / 32];
+  __shared__ long long lred[kTcRowThreads / 32];
+  const uint32_t s = blockIdx.x, z = blockIdx.y;
+  const float *xr = X + z * x_stride + (size_t)s * cols;
+  float m = 0.0f;
+  int bad = 0;
+  for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = xr[i];
+    m = fmaxf(m, fabsf(v));
+    bad |= !isfinite(v);
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  bad = __syncthreads_or(bad);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  float mm = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kTcRowThreads / 32; w++) mm = fmaxf(mm, red[w]);
+  float mul = 0.0f, inv = 0.0f;
+  const bool ok = row_scale(mm, bad != 0, &mul, &inv);
+  TcPrep P = tc_prep_at(ws, count, seq, cols);
+  if (threadIdx.x == 0) {
+    P.rowinv[z * 16 + s] = inv;
+    P.rowflag[z * 16 + s] = !ok;
+  }
+  int8_t *xb = P.xb + ((size_t)z * tc_rows_b(seq) + 4u * s) * cols;
+  long long part = 0;
+  for (uint32_t W = threadIdx.x; W < cols / 16u; W += blockDim.x)
+    part += tc_quantize_word(xr, W, ok, mul, xb, cols);
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) lred[threadIdx.x >> 5] = part;
+  __syncthreads();
+  if (threadIdx.x < kRowCluster) {
+    long long t = 0;
+    if (threadIdx.x == 0)
+      for (int w = 0; w < kTcRowThreads / 32; w++) t += lred[w];
+    P.rowsum[(z * 16 + s) * kRowCluster + threadIdx.x] = t;
+  }
 }
 
 // ---- the GEMV ---------------------------------------------------------------------
@@ -685,9 +743,15 @@ cudaError_t ternary_tc_launch(uint32_t count, const float *X, uint64_t x_stride,
       return cudaSuccess;
   }
   *launched = true;
-  const dim3 pgrid(kRowCluster * seq, count);
-  cudaError_t e = launch_k(tc_prep_kernel, pgrid, dim3(kTcPrepThreads), 0, st, false, X,
-                           x_stride, seq, cols, count, ws);
+  // Few rows: a cluster per row splits it over 8 SMs; enough rows to fill
+  // the GPU: a CTA per row.
+  cudaError_t e;
+  if ((uint64_t)seq * count >= 2u * 148u)
+    e = launch_k(tc_prep_rows_kernel, dim3(seq, count), dim3(kTcRowThreads), 0, st, false, X,
+                 x_stride, seq, cols, count, ws);
+  else
+    e = launch_k(tc_prep_kernel, dim3(kRowCluster * seq, count), dim3(kTcPrepThreads), 0, st,
+                 false, X, x_stride, seq, cols, count, ws);
   if (e != cudaSuccess) return e;
   const uint32_t items = ((out + kTcM - 1) / kTcM) * count;
   switch (tc_mma_n(seq)) {

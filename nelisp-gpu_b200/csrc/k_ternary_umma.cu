@@ -9,16 +9,21 @@
 // int64 -- so the result is the exact sum rounded once per row scale.
 //
 // One CTA computes a tile of 128 output rows x 80 sequence rows (N = 240
-// columns = 80 rows x 3 limbs) over the whole K:
+// columns = 80 rows x 3 limbs) over the whole K, 7 warps:
 //   warp 0      TMA producer: the packed weight tile (128 rows x 128 columns,
 //               two bits each, 4 KB) and the int8 limb tile (240 x 128 B,
-//               128-byte swizzle) per stage, S-stage mbarrier ring;
+//               128-byte swizzle) per stage, S-stage mbarrier ring; the
+//               weights of the first stages are requested before waiting
+//               for the prep kernel (programmatic dependent launch);
 //   warps 2-5   expand the two-bit codes into the int8 A tile in shared
 //               memory (one thread per weight row; one shift and one mask per
 //               four weights, 64 * t per byte), then arrive;
-//   warp 1      allocates TMEM and issues four 128x240x32 MMAs per stage from
-//               one thread; tcgen05.commit frees the stage;
-//   warps 2-5   finally read the accumulators back (tcgen05.ld) and write Y.
+//   warps 1, 6  two MMA issuers taking the stages in turn, four 128x240x32
+//               MMAs per stage each into its own TMEM accumulator (warp 1
+//               also allocates TMEM); tcgen05.commit frees the stage;
+//   warps 2-5   finally read both accumulators back (tcgen05.ld), add them,
+//               recombine the limbs and write Y; rows the prep flagged are
+//               computed there on the CUDA cores.
 // The shift-and-mask expansion leaves the 16 codes of a packed word in the
 // order P = {3,7,11,15, 2,6,10,14, 1,5,9,13, 0,4,8,12}; the limb tile is
 // written in the same order, so the K index of A and B agrees.
@@ -41,7 +46,8 @@ constexpr int kUmmaTok = 80;             // sequence rows per CTA
 constexpr int kUmmaN = 3 * kUmmaTok;     // MMA N: (row, limb) columns
 constexpr int kUmmaK = 128;              // K per stage (bytes of int8)
 constexpr int kUmmaStages = 4;
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;      // two 240-column accumulators
+constexpr int kUmmaThreads = 224;        // 7 warps
 constexpr uint32_t kWBytes = kUmmaM * kUmmaK / 4;      // packed weights per stage
 constexpr uint32_t kABytes = kUmmaM * kUmmaK;           // int8 A per stage
 constexpr uint32_t kBBytes = kUmmaN * kUmmaK;           // int8 B per stage
@@ -122,16 +128,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 __global__ void __launch_bounds__(256)
 umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict__ XB,
                  float *__restrict__ rowinv, int *__restrict__ rowflag) {
+  pdl_trigger();                 // the GEMM may start streaming its weights
+  pdl_wait();                    // X may come from the preceding kernel
   __shared__ float red[8];
   __shared__ int sbad;
   const uint32_t s = blockIdx.x;
   const float *xr = X + (size_t)s * cols;
+  const float4 *x4 = reinterpret_cast<const float4 *>(xr);
   float m = 0.0f;
   int bad = 0;
-  for (uint32_t i = threadIdx.x; i < cols; i += blockDim.x) {
-    const float v = xr[i];
-    m = fmaxf(m, fabsf(v));
-    bad |= !isfinite(v);
+  for (uint32_t i = threadIdx.x; i < cols / 4u; i += blockDim.x) {
+    const float4 v = __ldg(x4 + i);
+    m = fmaxf(fmaxf(m, fmaxf(fabsf(v.x), fabsf(v.y))), fmaxf(fabsf(v.z), fabsf(v.w)));
+    bad |= !isfinite(v.x) | !isfinite(v.y) | !isfinite(v.z) | !isfinite(v.w);
   }
   bad = __syncthreads_or(bad);
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -141,37 +150,30 @@ umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict_
   float mm = 0.0f;
   for (int w = 0; w < 8; w++) mm = fmaxf(mm, red[w]);
   // the exponent of the GEMV's prep (ternary_prep.cuh, row_scale)
-  bool ok = sbad == 0;
   float mul = 0.0f, inv = 0.0f;
-  if (ok && mm > 0.0f) {
-    int E;
-    frexpf(mm, &E);
-    const int e = 22 - E;
-    if (e > 126 || e < -126) {
-      ok = false;
-    } else {
-      mul = ldexpf(1.0f, e);
-      inv = ldexpf(1.0f, -e);
-    }
-  }
+  const bool ok = row_scale(mm, sbad != 0, &mul, &inv);
   if (threadIdx.x == 0) {
-    rowinv[s] = ok ? inv : 0.0f;
+    rowinv[s] = inv;
     rowflag[s] = !ok;
   }
-  const int P[16] = {3, 7, 11, 15, 2, 6, 10, 14, 1, 5, 9, 13, 0, 4, 8, 12};
+  // Byte p of a 16-column group holds column P[p] = 4 (p % 4) + 3 - p / 4:
+  // {3,7,11,15, 2,6,10,14, 1,5,9,13, 0,4,8,12}.
   int8_t *o0 = XB + (size_t)(3 * s) * cols, *o1 = o0 + cols, *o2 = o1 + cols;
   for (uint32_t w = threadIdx.x; w < cols / 16u; w += blockDim.x) {
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+      const float4 f = ok ? __ldg(x4 + 4u * w + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * q] = f.x; v[4 * q + 1] = f.y; v[4 * q + 2] = f.z; v[4 * q + 3] = f.w;
+    }
     uint32_t b0[4] = {0, 0, 0, 0}, b1[4] = {0, 0, 0, 0}, b2[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int p = 0; p < 16; p++) {
-      int l0 = 0, l1 = 0, l2 = 0;
-      if (ok) {
-        const int qv = __float2int_rn(xr[16u * w + P[p]] * mul);
-        l0 = (int)(int8_t)(qv & 0xff);
-        const int r = (qv - l0) >> 8;
-        l1 = (int)(int8_t)(r & 0xff);
-        l2 = (r - l1) >> 8;
-      }
+      const int qv = __float2int_rn(v[4 * (p % 4) + 3 - p / 4] * mul);
+      const int l0 = (int)(int8_t)(qv & 0xff);
+      const int r = (qv - l0) >> 8;
+      const int l1 = (int)(int8_t)(r & 0xff);
+      const int l2 = (r - l1) >> 8;
       b0[p >> 2] |= (uint32_t)(l0 & 0xff) << (8 * (p & 3));
       b1[p >> 2] |= (uint32_t)(l1 & 0xff) << (8 * (p & 3));
       b2[p >> 2] |= (uint32_t)(l2 & 0xff) << (8 * (p & 3));
@@ -183,8 +185,12 @@ umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict_
 }
 
 // ---- the GEMM ------------------------------------------------------------------
-__global__ void __launch_bounds__(192, 1)
+// Two MMA issuers take the K stages in turn (one thread issues a tcgen05.mma
+// only every ~50-170 cycles, a 128 x 240 x 32 MMA takes the tensor core ~120),
+// each into its own accumulator; the epilogue adds the two exactly.
+__global__ void __launch_bounds__(kUmmaThreads, 1)
 ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
+                    const float *__restrict__ X, const uint32_t *__restrict__ WP,
                     const float *__restrict__ S, const float *__restrict__ BIAS,
                     const float *__restrict__ rowinv, const int *__restrict__ rowflag,
                     float *__restrict__ Y, uint32_t seq, uint32_t out, uint32_t cols,
@@ -198,8 +204,8 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   uint64_t *full = reinterpret_cast<uint64_t *>(sW + kUmmaStages * kWBytes);
   uint64_t *aready = full + kUmmaStages;
   uint64_t *empty = aready + kUmmaStages;
-  uint64_t *done = empty + kUmmaStages;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  uint64_t *done = empty + kUmmaStages;                 // one per issuer
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t m0 = blockIdx.x * kUmmaM, t0 = blockIdx.y * kUmmaTok;
@@ -211,7 +217,8 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       bar_init(&aready[i], 4);
       bar_init(&empty[i], 1);
     }
-    bar_init(done, 1);
+    bar_init(&done[0], 1);
+    bar_init(&done[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 1) {
@@ -222,11 +229,13 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = *tmem_slot;               // accumulators at columns 0 and 256
 
   if (warp == 0) {
-    // ---- producer ----
+    // ---- producer: the weights of the first stages before the wait for
+    // the prep kernel (launch_pdl), which does not write them ----
     if (lane == 0) {
+      const uint32_t pre = nk < (uint32_t)kUmmaStages ? nk : (uint32_t)kUmmaStages;
       for (uint32_t kt = 0; kt < nk; kt++) {
         const int st = (int)(kt % kUmmaStages);
         if (kt >= (uint32_t)kUmmaStages &&
@@ -234,13 +243,22 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
           break;
         bar_expect(&full[st], kWBytes + kBBytes);
         tma2d(sW + st * kWBytes, &tmW, (int)(kt * (kUmmaK / 16)), (int)m0, &full[st]);
-        tma2d(sB + st * kBBytes, &tmB, (int)(kt * kUmmaK), (int)(3 * t0), &full[st]);
+        if (kt >= pre) {
+          tma2d(sB + st * kBBytes, &tmB, (int)(kt * kUmmaK), (int)(3 * t0), &full[st]);
+        } else if (kt + 1 == pre) {
+          pdl_wait();
+          for (uint32_t k = 0; k < pre; k++)
+            tma2d(sB + k * kBBytes, &tmB, (int)(k * kUmmaK), (int)(3 * t0), &full[k]);
+        }
       }
     }
-  } else if (warp == 1) {
-    // ---- MMA issuer ----
+  } else if (warp == 1 || warp == 6) {
+    // ---- MMA issuers: issuer p takes the stages kt with kt % 2 == p ----
     if (lane == 0) {
-      for (uint32_t kt = 0; kt < nk; kt++) {
+      const uint32_t p = warp == 1 ? 0u : 1u;
+      const uint32_t acc_d = tmem + 256u * p;
+      bool first = true;
+      for (uint32_t kt = p; kt < nk; kt += 2) {
         const int st = (int)(kt % kUmmaStages);
         const uint32_t ph = (kt / kUmmaStages) & 1;
         if (!bar_wait(&full[st], ph, err) || !bar_wait(&aready[st], ph, err)) break;
@@ -248,11 +266,12 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         const uint32_t a0 = su32(sA + st * kABytes), b0 = su32(sB + st * kBBytes);
 #pragma unroll
         for (int k = 0; k < kUmmaK / 32; k++)
-          umma_i8(tmem, smem_desc(a0 + 32u * k), smem_desc(b0 + 32u * k),
-                  (kt > 0 || k > 0) ? 1u : 0u);
+          umma_i8(acc_d, smem_desc(a0 + 32u * k), smem_desc(b0 + 32u * k),
+                  (!first || k > 0) ? 1u : 0u);
+        first = false;
         umma_commit(&empty[st]);      // the stage is free once these MMAs are done
       }
-      umma_commit(done);
+      umma_commit(&done[p]);
     }
   } else {
     // ---- expand the weights (warps 2-5, one thread per A row) ----
@@ -276,18 +295,27 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       if (lane == 0) bar_arrive(&aready[st]);
     }
     // ---- epilogue: accumulators -> Y ----
-    if (bar_wait(done, 0, err)) {
+    const bool two = nk >= 2;                     // issuer 1 wrote an accumulator
+    if (bar_wait(&done[0], 0, err) && (!two || bar_wait(&done[1], 0, err))) {
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
       const uint32_t q = (uint32_t)(warp & 3);      // TMEM lane quarter of this warp
       const uint32_t o = m0 + q * 32u + (uint32_t)lane;
       const float sc = o < out ? __ldg(S + o) : 0.0f;
       const float bi = (BIAS && o < out) ? __ldg(BIAS + o) : 0.0f;
+      const uint32_t lb = (q * 32u) << 16;
       for (uint32_t c0 = 0; c0 < (uint32_t)kUmmaN; c0 += 48) {   // 16 rows per round
-        uint32_t v[48];
-        tmem_ld16(tmem + ((q * 32u) << 16) + c0, *reinterpret_cast<uint32_t(*)[16]>(v));
-        tmem_ld16(tmem + ((q * 32u) << 16) + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
-        tmem_ld16(tmem + ((q * 32u) << 16) + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(v + 32));
+        uint32_t v[48], u[48];
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+          tmem_ld16(tmem + lb + c0 + 16u * j, *reinterpret_cast<uint32_t(*)[16]>(v + 16 * j));
+          if (two)
+            tmem_ld16(tmem + lb + 256u + c0 + 16u * j, *reinterpret_cast<uint32_t(*)[16]>(u + 16 * j));
+        }
         asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+        if (two) {
+#pragma unroll
+          for (int j = 0; j < 48; j++) v[j] += u[j];   // exact int32 partial sums
+        }
 #pragma unroll
         for (int j = 0; j < 16; j++) {
           const uint32_t s = t0 + c0 / 3u + (uint32_t)j;
@@ -300,6 +328,22 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
           Y[(size_t)s * out + o] = y;
         }
       }
+      // Rows the prep flagged (non-finite or unrepresentable): the generic
+      // CUDA-core arithmetic, one output row of this warp's 32 at a time.
+      const uint32_t wng = cols / 16u, nblk = cols / 128u;
+      for (uint32_t j = 0; j < (uint32_t)kUmmaTok; j++) {
+        const uint32_t s = t0 + j;
+        if (s >= seq) break;
+        if (!rowflag[s]) continue;
+        for (uint32_t rr = 0; rr < 32u; rr++) {
+          const uint32_t orow = m0 + q * 32u + rr;
+          if (orow >= out) break;
+          float acc1[1];
+          ternary_row_generic<1>(X, WP + (size_t)orow * wng, nullptr, false, __ldg(S + orow),
+                                 (int)s, 1, cols, nblk, wng, acc1);
+          if (lane == 0) Y[(size_t)s * out + orow] = (BIAS ? __ldg(BIAS + orow) : 0.0f) + acc1[0];
+        }
+      }
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
@@ -308,33 +352,6 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
                  "r"(kTmemCols));
-  }
-}
-
-// Rows the prep flagged (non-finite or unrepresentable): y on the CUDA cores,
-// in f32.  One CTA per sequence row, which returns at once unless flagged;
-// its warps then take the output rows in turn.
-__global__ void umma_flagged_kernel(const float *__restrict__ X, const uint32_t *__restrict__ WP,
-                                    const float *__restrict__ S, const float *__restrict__ BIAS,
-                                    const int *__restrict__ rowflag, float *__restrict__ Y,
-                                    uint32_t seq, uint32_t out, uint32_t cols) {
-  const uint32_t s = blockIdx.x;
-  if (!rowflag[s]) return;
-  const int lane = threadIdx.x & 31;
-  const uint32_t wng = cols / 16u;
-  const float *xr = X + (size_t)s * cols;
-  for (uint32_t o = threadIdx.x >> 5; o < out; o += blockDim.x >> 5) {
-    const uint32_t *wr = WP + (size_t)o * wng;
-    float acc = 0.0f;
-    for (uint32_t wi = lane; wi < wng; wi += 32) {
-      const uint32_t w = wr[wi];
-      for (int f = 0; f < 16; f++) {
-        const int t = (int)(w << (30 - 2 * f)) >> 30;   // sign-extended two-bit field
-        acc = fmaf((float)t, xr[16u * wi + f], acc);    // every field: 0 * inf is NaN
-      }
-    }
-    for (int d = 16; d > 0; d >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, d);
-    if (lane == 0) Y[(size_t)s * out + o] = (BIAS ? BIAS[o] : 0.0f) + acc * S[o];
   }
 }
 
@@ -358,7 +375,7 @@ EncodeFn encode_fn() {
 }
 
 size_t umma_smem_bytes() {
-  return 1024 + (size_t)kUmmaStages * (kABytes + kBBytes + kWBytes) + 3 * kUmmaStages * 8 + 8 + 16;
+  return 1024 + (size_t)kUmmaStages * (kABytes + kBBytes + kWBytes) + 3 * kUmmaStages * 8 + 16 + 16;
 }
 
 }  // namespace
@@ -416,16 +433,15 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   }
   *launched = true;
   // rows 3*seq .. ncol of XB feed only MMA columns no output reads
-  umma_prep_kernel<<<seq, 256, 0, st>>>(X, cols, XB, rowinv, rowflag);
-  cudaError_t e = cudaPeekAtLastError();
+  cudaError_t e = launch_k(umma_prep_kernel, dim3(seq), dim3(256), 0, st, false, X, cols, XB,
+                           rowinv, rowflag);
   if (e != cudaSuccess) return e;
   const dim3 grid((out + kUmmaM - 1) / kUmmaM, (seq + kUmmaTok - 1) / kUmmaTok);
-  ternary_umma_kernel<<<grid, 192, smem, st>>>(mw, mb, S, BIAS, rowinv, rowflag, Y, seq, out,
-                                                cols, wait_flag_device());
-  if ((e = cudaPeekAtLastError()) != cudaSuccess) return e;
-  umma_flagged_kernel<<<seq, 256, 0, st>>>(X, WP, S, BIAS, rowflag, Y, seq, out, cols);
-  count_launches(3);
-  return cudaPeekAtLastError();
+  e = launch_pdl(ternary_umma_kernel, grid, dim3(kUmmaThreads), smem, st, mw, mb, X, WP, S, BIAS,
+                 (const float *)rowinv, (const int *)rowflag, Y, seq, out, cols,
+                 wait_flag_device());
+  count_launches(2);
+  return e != cudaSuccess ? e : cudaPeekAtLastError();
 }
 
 }  // namespace nl

@@ -363,6 +363,62 @@ k_silu_prep(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint3
   cl.sync();
 }
 
+// Prefill rows (hundreds of them fill the GPU without splitting a row): one
+// CTA per row, float4 streams.  The same per-element arithmetic as k_norm /
+// k_silu_prep; the sum of squares is reduced in a different order.
+constexpr int kRowThreads = 256;
+__global__ void __launch_bounds__(kRowThreads)
+k_rows_add_norm(float *__restrict__ h, const float *__restrict__ delta,
+                const float *__restrict__ g, float *__restrict__ x, uint32_t H, float eps) {
+  __shared__ float red[kRowThreads / 32];
+  const size_t base = (size_t)blockIdx.x * H;
+  float4 *h4 = reinterpret_cast<float4 *>(h + base);
+  const float4 *d4 = reinterpret_cast<const float4 *>(delta + base);
+  float ss = 0.0f;
+  for (uint32_t i = threadIdx.x; i < H / 4u; i += blockDim.x) {
+    const float4 a = h4[i], b = __ldg(d4 + i);
+    const float4 v = make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z),
+                                 __fadd_rn(a.w, b.w));
+    h4[i] = v;
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; w++) tot += red[w];
+  const float rinv = 1.0f / sqrtf(tot / (float)H + eps);
+  float4 *x4 = reinterpret_cast<float4 *>(x + base);
+  const float4 *g4 = reinterpret_cast<const float4 *>(g);
+  for (uint32_t i = threadIdx.x; i < H / 4u; i += blockDim.x) {
+    const float4 v = h4[i], gv = __ldg(g4 + i);   // this thread's own writes above
+    x4[i] = make_float4(__fmul_rn(__fmul_rn(v.x, rinv), gv.x), __fmul_rn(__fmul_rn(v.y, rinv), gv.y),
+                        __fmul_rn(__fmul_rn(v.z, rinv), gv.z), __fmul_rn(__fmul_rn(v.w, rinv), gv.w));
+  }
+}
+__global__ void __launch_bounds__(kRowThreads)
+k_rows_silu(const float *__restrict__ gu, float *__restrict__ a, uint32_t fr) {
+  const float *gr = gu + (size_t)blockIdx.x * 2 * fr;
+  const float4 *g4 = reinterpret_cast<const float4 *>(gr);
+  const float4 *u4 = reinterpret_cast<const float4 *>(gr + fr);
+  float4 *a4 = reinterpret_cast<float4 *>(a + (size_t)blockIdx.x * fr);
+  for (uint32_t i = threadIdx.x; i < fr / 4u; i += blockDim.x) {
+    const float4 gv = __ldg(g4 + i), uv = __ldg(u4 + i);
+    const float gg[4] = {gv.x, gv.y, gv.z, gv.w}, uu[4] = {uv.x, uv.y, uv.z, uv.w};
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float sg = 1.0f / (1.0f + expf(-gg[e]));
+      r[e] = __fmul_rn(__fmul_rn(gg[e], sg), uu[e]);
+    }
+    a4[i] = make_float4(r[0], r[1], r[2], r[3]);
+  }
+}
+
 // Order-preserving 64-bit argmax key: larger logit first, then lower index.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
   uint32_t u = __float_as_uint(v);
@@ -1202,22 +1258,30 @@ static int run_prefill(nl_decoder *D, uint32_t B, uint32_t P) {
       return cuda_status(e, "prefill: o");
     if ((rc = allreduce(D, D->pf_o, (size_t)rows * H, kNcclFloat32, kNcclSum))) return rc;
     if (l + 1 == c.layers) break;   // the last layer's FFN feeds no cache
-    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->pf_h, D->pf_o,
-                                                           L.gffn, D->pf_x, nullptr, rows, H,
-                                                           eps, PeerIn{});
-    count_launches(1);
+    // Enough rows to fill the GPU: a CTA per row; else the row clusters.
+    const bool by_row = rows >= 2u * 148u && H % 4u == 0 && D->fr % 4u == 0;
+    auto add_norm = [&](const float *delta, const float *g) {
+      if (by_row)
+        k_rows_add_norm<<<rows, kRowThreads, 0, st>>>(D->pf_h, delta, g, D->pf_x, H, eps);
+      else
+        k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->pf_h, delta, g,
+                                                               D->pf_x, nullptr, rows, H, eps,
+                                                               PeerIn{});
+      count_launches(1);
+    };
+    add_norm(D->pf_o, L.gffn);
     if ((e = gemm(D->pf_x, L.wgu, L.sgu, D->pf_gu, 2 * D->fr, H)) != cudaSuccess)
       return cuda_status(e, "prefill: gate/up");
-    k_silu_prep<<<gnorm, kNormThreads, (size_t)row_slice_cols(D->fr) * sizeof(float), st>>>(
-        D->pf_gu, D->pf_a, nullptr, rows, D->fr);
+    if (by_row)
+      k_rows_silu<<<rows, kRowThreads, 0, st>>>(D->pf_gu, D->pf_a, D->fr);
+    else
+      k_silu_prep<<<gnorm, kNormThreads, (size_t)row_slice_cols(D->fr) * sizeof(float), st>>>(
+          D->pf_gu, D->pf_a, nullptr, rows, D->fr);
     count_launches(1);
     if ((e = gemm(D->pf_a, L.wd, L.sd, D->pf_d, H, D->fr)) != cudaSuccess)
       return cuda_status(e, "prefill: down");
     if ((rc = allreduce(D, D->pf_d, (size_t)rows * H, kNcclFloat32, kNcclSum))) return rc;
-    k_norm<kNormAdd><<<gnorm, kNormThreads, smem_h, st>>>(nullptr, nullptr, D->pf_h, D->pf_d,
-                                                           D->layers[l + 1].gattn, D->pf_x,
-                                                           nullptr, rows, H, eps, PeerIn{});
-    count_launches(1);
+    add_norm(D->pf_d, D->layers[l + 1].gattn);
     if ((e = cudaPeekAtLastError()) != cudaSuccess) return cuda_status(e, "prefill: norms");
   }
   k_pf_init<<<1, 32, 0, st>>>(D->prompt, P, D->tok, D->par ? nullptr : D->keys, D->pos, D->posf, B);

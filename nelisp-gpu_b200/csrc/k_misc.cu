@@ -5,6 +5,7 @@
 //   causal-mask     :148-155    S[i, j] = -1e30 for j > i (in place)
 //   attn-scores     :208-221    S[h, i, j] = <q_i^h, k_j^kvh> / sqrt(hd), -1e30 past i
 //   attn-context    :224-235    C[i, h*hd+t] = sum_j P[h, i, j] V[j, kvh*hd+t]
+//   attn-sc-dq/-dk, attn-ctx-dp/-dv :237-290  their gradients
 //   dp4a-dot        :592-602    OUT[i] = sdot4x8(A, B), the words rebuilt from two
 //                               f32 halves (lo + hi * 65536)
 //   bitlinear-dp4a  :606-620    Y = BIAS[o] + (BETA[0] GAMMA[s]) float(sum sdot)
@@ -54,6 +55,9 @@ cudaError_t run_causal_mask(const OpArgs &a) {
 
 // ---- attn-scores: per head a [seq x seq] tile product, 32 x 32 per CTA --------------
 constexpr int kSc = 32, kScK = 32;
+// CAUSAL: attn-scores (scaled by 1/sqrt(hd), -1e30 above the diagonal);
+// otherwise attn-ctx-dp (DP[h,i,j] = sum_t DC[i,h,t] V[j,kvh,t], every (i, j)).
+template <bool CAUSAL = true>
 __global__ void __launch_bounds__(256)
 k_attn_scores(const float *__restrict__ Q, const float *__restrict__ K, float *__restrict__ S,
               uint32_t seq, uint32_t dim, uint32_t heads, uint32_t kvheads, uint64_t limit) {
@@ -62,7 +66,7 @@ k_attn_scores(const float *__restrict__ Q, const float *__restrict__ K, float *_
   const uint32_t h = blockIdx.z, i0 = blockIdx.y * kSc, j0 = blockIdx.x * kSc;
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;   // 8 row groups of 4
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const bool live = j0 <= i0 + kSc - 1;                     // a tile above the diagonal is all masked
+  const bool live = !CAUSAL || j0 <= i0 + kSc - 1;          // a tile above the diagonal is all masked
   if (live) {
     for (uint32_t t0 = 0; t0 < hd; t0 += kScK) {
       for (int e = threadIdx.x; e < kSc * kScK; e += 256) {
@@ -88,7 +92,7 @@ k_attn_scores(const float *__restrict__ Q, const float *__restrict__ K, float *_
     if (i >= seq || j >= seq) continue;
     const uint64_t idx = (uint64_t)h * seq * seq + (uint64_t)i * seq + j;
     if (idx >= limit) continue;
-    S[idx] = j > i ? -1.0e30f : acc[a] * scale;
+    S[idx] = CAUSAL ? (j > i ? -1.0e30f : acc[a] * scale) : acc[a];
   }
 }
 const char *chk_scores(const OpArgs &a) {
@@ -105,7 +109,7 @@ cudaError_t run_scores(const OpArgs &a) {
   const uint32_t seq = a.push[0];
   if (!seq) return cudaSuccess;
   const dim3 grid((seq + kSc - 1) / kSc, (seq + kSc - 1) / kSc, a.push[2]);
-  k_attn_scores<<<grid, 256, 0, a.stream>>>((const float *)a.buf[0], (const float *)a.buf[1],
+  k_attn_scores<true><<<grid, 256, 0, a.stream>>>((const float *)a.buf[0], (const float *)a.buf[1],
                                            (float *)a.buf[2], seq, a.push[1], a.push[2],
                                            a.push[3], invocations(a.groups, 64));
   count_launches(1);
@@ -113,6 +117,9 @@ cudaError_t run_scores(const OpArgs &a) {
 }
 
 // ---- attn-context: per head C_h = P_h [seq x seq] V_kvh [seq x hd] --------------------
+// SCALED: attn-sc-dq (DQ = (sum_j DS[h,i,j] K[j,kvh,t]) / sqrt(hd)); else
+// attn-context.
+template <bool SCALED = false>
 __global__ void __launch_bounds__(256)
 k_attn_context(const float *__restrict__ P, const float *__restrict__ V, float *__restrict__ C,
                uint32_t seq, uint32_t dim, uint32_t heads, uint32_t kvheads, uint64_t limit) {
@@ -144,7 +151,7 @@ k_attn_context(const float *__restrict__ P, const float *__restrict__ V, float *
     const uint32_t i = i0 + ty * 4 + a, t = t0 + tx;
     if (i >= seq || t >= hd) continue;
     const uint64_t idx = (uint64_t)i * dim + (uint64_t)h * hd + t;
-    if (idx < limit) C[idx] = acc[a];
+    if (idx < limit) C[idx] = SCALED ? acc[a] * (1.0f / sqrtf((float)hd)) : acc[a];
   }
 }
 const char *chk_context(const OpArgs &a) {
@@ -161,9 +168,101 @@ cudaError_t run_context(const OpArgs &a) {
   const uint32_t seq = a.push[0], hd = a.push[2] ? a.push[1] / a.push[2] : 0;
   if (!seq || !hd) return cudaSuccess;
   const dim3 grid((hd + kSc - 1) / kSc, (seq + kSc - 1) / kSc, a.push[2]);
-  k_attn_context<<<grid, 256, 0, a.stream>>>((const float *)a.buf[0], (const float *)a.buf[1],
+  k_attn_context<false><<<grid, 256, 0, a.stream>>>((const float *)a.buf[0], (const float *)a.buf[1],
                                             (float *)a.buf[2], seq, a.push[1], a.push[2],
                                             a.push[3], invocations(a.groups, 64));
+  count_launches(1);
+  return cudaPeekAtLastError();
+}
+
+// ---- attention backward (kernels.el:237-290) ------------------------------------
+// attn-sc-dq (DS K DQ) and attn-ctx-dp (DC V DP) are the tiled products above;
+// attn-sc-dk (DS Q DK) and attn-ctx-dv (DC P DV) sum over the query rows i and
+// the heads of a kv group, one thread per output as the reference does.
+const char *chk_dq(const OpArgs &a) {
+  const uint64_t seq = a.push[0], dim = a.push[1], heads = a.push[2], kvheads = a.push[3];
+  if (!heads || !kvheads || dim % heads || heads % kvheads)
+    return fmt_msg("attention: dim %u, heads %u, kvheads %u do not divide", a.push[1], a.push[2],
+                   a.push[3]);
+  const char *m;
+  if ((m = need_words(a, 0, heads * seq * seq, "DS"))) return m;
+  if ((m = need_words(a, 1, seq * kvheads * (dim / heads), "K"))) return m;
+  return need_words(a, 2, seq * dim, "DQ");
+}
+cudaError_t run_dq(const OpArgs &a) {
+  const uint32_t seq = a.push[0], hd = a.push[2] ? a.push[1] / a.push[2] : 0;
+  if (!seq || !hd) return cudaSuccess;
+  const dim3 grid((hd + kSc - 1) / kSc, (seq + kSc - 1) / kSc, a.push[2]);
+  k_attn_context<true><<<grid, 256, 0, a.stream>>>((const float *)a.buf[0], (const float *)a.buf[1],
+                                                  (float *)a.buf[2], seq, a.push[1], a.push[2],
+                                                  a.push[3], invocations(a.groups, 64));
+  count_launches(1);
+  return cudaPeekAtLastError();
+}
+const char *chk_dp(const OpArgs &a) {
+  const uint64_t seq = a.push[0], dim = a.push[1], heads = a.push[2], kvheads = a.push[3];
+  if (!heads || !kvheads || dim % heads || heads % kvheads)
+    return fmt_msg("attention: dim %u, heads %u, kvheads %u do not divide", a.push[1], a.push[2],
+                   a.push[3]);
+  const char *m;
+  if ((m = need_words(a, 0, seq * dim, "DC"))) return m;
+  if ((m = need_words(a, 1, seq * kvheads * (dim / heads), "V"))) return m;
+  return need_words(a, 2, heads * seq * seq, "DP");
+}
+cudaError_t run_dp(const OpArgs &a) {
+  const uint32_t seq = a.push[0];
+  if (!seq) return cudaSuccess;
+  const dim3 grid((seq + kSc - 1) / kSc, (seq + kSc - 1) / kSc, a.push[2]);
+  k_attn_scores<false><<<grid, 256, 0, a.stream>>>((const float *)a.buf[0], (const float *)a.buf[1],
+                                                  (float *)a.buf[2], seq, a.push[1], a.push[2],
+                                                  a.push[3], invocations(a.groups, 64));
+  count_launches(1);
+  return cudaPeekAtLastError();
+}
+// DK[j,kvh,t] = scale * sum_{h in group} sum_i DS[h,i,j] Q[i,h,t] (DV: P, DC, no scale)
+template <bool SCALED>
+__global__ void k_attn_kv_grad(const float *__restrict__ D, const float *__restrict__ X,
+                               float *__restrict__ OUT, uint32_t seq, uint32_t dim, uint32_t heads,
+                               uint32_t kvheads, uint64_t limit) {
+  const uint32_t hd = dim / heads, grp = heads / kvheads, kvdim = kvheads * hd;
+  const uint64_t total = (uint64_t)seq * kvdim;
+  for (uint64_t idx = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total && idx < limit;
+       idx += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t j = (uint32_t)(idx / kvdim), rem = (uint32_t)(idx % kvdim);
+    const uint32_t kvh = rem / hd, t = rem % hd;
+    float acc = 0.0f;
+    for (uint32_t hh = 0; hh < grp; hh++) {
+      const uint32_t h = kvh * grp + hh;
+      const float *dcol = D + (uint64_t)h * seq * seq + j;
+      const float *xcol = X + (uint64_t)h * hd + t;
+      for (uint32_t i = 0; i < seq; i++)
+        acc = __fadd_rn(acc, __fmul_rn(__ldg(dcol + (uint64_t)i * seq), __ldg(xcol + (uint64_t)i * dim)));
+    }
+    OUT[idx] = SCALED ? acc * (1.0f / sqrtf((float)hd)) : acc;
+  }
+}
+template <bool SCALED>
+const char *chk_kv_grad(const OpArgs &a) {
+  const uint64_t seq = a.push[0], dim = a.push[1], heads = a.push[2], kvheads = a.push[3];
+  if (!heads || !kvheads || dim % heads || heads % kvheads)
+    return fmt_msg("attention: dim %u, heads %u, kvheads %u do not divide", a.push[1], a.push[2],
+                   a.push[3]);
+  const char *m;
+  // buffer 0 is DS (attn-sc-dk) or DC (attn-ctx-dv); buffer 1 is Q or P
+  if ((m = need_words(a, SCALED ? 0 : 1, heads * seq * seq, SCALED ? "DS" : "P"))) return m;
+  if ((m = need_words(a, SCALED ? 1 : 0, seq * dim, SCALED ? "Q" : "DC"))) return m;
+  return need_words(a, 2, seq * kvheads * (dim / heads), SCALED ? "DK" : "DV");
+}
+template <bool SCALED>
+cudaError_t run_kv_grad(const OpArgs &a) {
+  const uint64_t n = (uint64_t)a.push[0] * (a.push[2] ? a.push[3] * (a.push[1] / a.push[2]) : 0);
+  if (!n) return cudaSuccess;
+  // attn-sc-dk: (DS Q DK); attn-ctx-dv: (DC P DV) -- the score-shaped operand first
+  const float *Dm = (const float *)a.buf[SCALED ? 0 : 1];
+  const float *Xm = (const float *)a.buf[SCALED ? 1 : 0];
+  k_attn_kv_grad<SCALED><<<blocks_for(n), 256, 0, a.stream>>>(Dm, Xm, (float *)a.buf[2], a.push[0],
+                                                              a.push[1], a.push[2], a.push[3],
+                                                              invocations(a.groups, 64));
   count_launches(1);
   return cudaPeekAtLastError();
 }
@@ -386,6 +485,10 @@ const OpSpec kMiscOps[] = {
     {"causal-mask", 1, 1, chk_causal_mask, no_scr, run_causal_mask},
     {"attn-scores", 3, 4, chk_scores, no_scr, run_scores},
     {"attn-context", 3, 4, chk_context, no_scr, run_context},
+    {"attn-sc-dq", 3, 4, chk_dq, no_scr, run_dq},
+    {"attn-sc-dk", 3, 4, chk_kv_grad<true>, no_scr, run_kv_grad<true>},
+    {"attn-ctx-dp", 3, 4, chk_dp, no_scr, run_dp},
+    {"attn-ctx-dv", 3, 4, chk_kv_grad<false>, no_scr, run_kv_grad<false>},
     {"dp4a-dot", 5, 1, chk_dp4a_dot, no_scr, run_dp4a_dot},
     {"bitlinear-dp4a", 8, 3, chk_bitlinear_dp4a, no_scr, run_bitlinear_dp4a},
     {"dp4a-rows-t", 4, 4, chk_dp4a_rows_t, no_scr, run_dp4a_rows_t},

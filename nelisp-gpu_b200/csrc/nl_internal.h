@@ -60,6 +60,8 @@ extern const OpSpec kMiscOps[];
 extern const int kMiscOpsCount;
 extern const OpSpec kQuantOps[];
 extern const int kQuantOpsCount;
+extern const OpSpec kTrainOps[];
+extern const int kTrainOpsCount;
 
 // Error reporting (nl_runtime.cu).
 int set_error(int code, const char *fmt, ...);

@@ -21,6 +21,7 @@ const Table kTables[] = {
     {kDenseOps, &kDenseOpsCount},     {kRowOps, &kRowOpsCount},
     {kAttnOps, &kAttnOpsCount},       {kKvOps, &kKvOpsCount},
     {kMiscOps, &kMiscOpsCount},       {kQuantOps, &kQuantOpsCount},
+    {kTrainOps, &kTrainOpsCount},
 };
 
 }  // namespace

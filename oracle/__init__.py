@@ -95,6 +95,31 @@ def _declare(L):
         "nlo_quant_act": [_F, _F, _u32, _u32],
         "nlo_quant_w": [_F, _F, _F, _u32],
         "nlo_quant_w_pack": [_F, _u32, _u32, ctypes.c_int, _U, _F],
+        "nlo_transpose": [_F, _F, _u32, _u32],
+        "nlo_slice_cols": [_F, _F] + [_u32] * 4,
+        "nlo_set_cols": [_F, _F] + [_u32] * 4,
+        "nlo_silu_mul_bwd": [_F] * 5 + [_u32],
+        "nlo_silu_bwd": [_F] * 3 + [_u32],
+        "nlo_gelu_bwd": [_F] * 3 + [_u32],
+        "nlo_sub_scale": [_F] * 4 + [_u32],
+        "nlo_sgd": [_F] * 4 + [_u32],
+        "nlo_adam": [_F] * 6 + [_u32],
+        "nlo_colsum": [_F, _F, _u32, _u32],
+        "nlo_rmsnorm_dgamma": [_F] * 4 + [_u32, _u32],
+        "nlo_rmsnorm_dx": [_F] * 5 + [_u32, _u32],
+        "nlo_softmax_bwd": [_F] * 3 + [_u32, _u32],
+        "nlo_rowdot": [_F] * 3 + [_u32, _u32],
+        "nlo_ce_grad": [_F] * 3 + [_u32, _u32, ctypes.c_int],
+        "nlo_topk_mask": [_F, _F] + [_u32] * 3,
+        "nlo_embed_bwd": [_F] * 3 + [_u32] * 3,
+        "nlo_gather_spike": [_F] * 3 + [_u32, _u32, ctypes.c_uint64],
+        "nlo_scatter_spike": [_F] * 3 + [_u32, _u32, ctypes.c_uint64],
+        "nlo_gdn_step": [_F] * 7 + [_u32] * 4,
+        "nlo_attn_sc_dq": [_F] * 3 + [_u32] * 4,
+        "nlo_attn_sc_dk": [_F] * 3 + [_u32] * 4,
+        "nlo_attn_ctx_dp": [_F] * 3 + [_u32] * 4,
+        "nlo_attn_ctx_dv": [_F] * 3 + [_u32] * 4,
+        "nlo_tree_attn": [_F] * 8 + [_u32] * 5,
         "nlo_matmul_sample_ref": [_u32] * 4,
         "nlo_softmax_ref_f64": [_D, _D, _u32, _u32],
         "nlo_set_threads": [ctypes.c_int],
@@ -473,6 +498,18 @@ def quant_w_pack(W, rows, cols, per_row):
     S = np.zeros(rows, np.float32)
     lib().nlo_quant_w_pack(_f(W), rows, cols, int(per_row), _u(WP), _f(S))
     return WP, S
+
+
+def call(name, *args):
+    """Call oracle function nlo_NAME: float32 arrays go as pointers (modified
+    in place where the function writes them), everything else as integers."""
+    conv = []
+    for a in args:
+        if isinstance(a, np.ndarray):
+            conv.append(_f(a))
+        else:
+            conv.append(int(a))
+    getattr(lib(), "nlo_" + name)(*conv)
 
 
 def matmul_sample_ref(r, c, K, N) -> float:

@@ -143,6 +143,45 @@ void nlo_quant_act(const float *X, float *XQ, uint32_t seq, uint32_t cols);
 void nlo_quant_w(const float *W, const float *S, float *WQ, uint32_t n);
 void nlo_quant_w_pack(const float *W, uint32_t rows, uint32_t cols, int per_row, uint32_t *WP,
                       float *S);
+/* nl_oracle_misc.c: the training-side operators */
+void nlo_transpose(const float *A, float *C, uint32_t R, uint32_t Co);
+void nlo_slice_cols(const float *A, float *C, uint32_t seq, uint32_t dim, uint32_t hd, uint32_t c0);
+void nlo_set_cols(float *D, const float *S, uint32_t seq, uint32_t dim, uint32_t hd, uint32_t c0);
+void nlo_silu_mul_bwd(const float *G, const float *A, const float *B, float *DA, float *DB, uint32_t n);
+void nlo_silu_bwd(const float *G, const float *X, float *D, uint32_t n);
+void nlo_gelu_bwd(const float *G, const float *H, float *D, uint32_t n);
+void nlo_sub_scale(const float *A, const float *B, const float *S, float *C, uint32_t n);
+void nlo_sgd(float *W, const float *G, const float *L, const float *S, uint32_t n);
+void nlo_adam(float *W, const float *G, float *M, float *V, const float *H, const float *S,
+              uint32_t n);
+void nlo_colsum(const float *G, float *D, uint32_t M, uint32_t N);
+void nlo_rmsnorm_dgamma(const float *DY, const float *X, const float *S, float *DG, uint32_t M,
+                        uint32_t N);
+void nlo_rmsnorm_dx(const float *DY, const float *X, const float *S, const float *G, float *DX,
+                    uint32_t M, uint32_t N);
+void nlo_softmax_bwd(const float *P, const float *G, float *DS, uint32_t M, uint32_t N);
+void nlo_rowdot(const float *G, const float *Y, float *D, uint32_t M, uint32_t N);
+void nlo_ce_grad(const float *LG, const float *T, float *G, uint32_t M, uint32_t V, int idx);
+void nlo_topk_mask(const float *LG, float *MK, uint32_t M, uint32_t E, uint32_t K);
+void nlo_embed_bwd(const float *TOK, const float *GX, float *DW, uint32_t seq, uint32_t dim,
+                   uint32_t vocab);
+void nlo_gather_spike(const float *TABLE, const float *POOL, float *OUT, uint32_t n, uint32_t bs,
+                      uint64_t pool_words);
+void nlo_scatter_spike(const float *TABLE, const float *SRC, float *POOL, uint32_t n, uint32_t bs,
+                       uint64_t pool_words);
+void nlo_gdn_step(float *S, const float *Q, const float *K, const float *V, const float *G,
+                  const float *B, float *OUT, uint32_t nv, uint32_t dk, uint32_t dv, uint32_t t);
+void nlo_attn_sc_dq(const float *DS, const float *K, float *DQ, uint32_t seq, uint32_t dim,
+                    uint32_t heads, uint32_t kvheads);
+void nlo_attn_sc_dk(const float *DS, const float *Q, float *DK, uint32_t seq, uint32_t dim,
+                    uint32_t heads, uint32_t kvheads);
+void nlo_attn_ctx_dp(const float *DC, const float *V, float *DP, uint32_t seq, uint32_t dim,
+                     uint32_t heads, uint32_t kvheads);
+void nlo_attn_ctx_dv(const float *DC, const float *P, float *DV, uint32_t seq, uint32_t dim,
+                     uint32_t heads, uint32_t kvheads);
+void nlo_tree_attn(const float *Q, const float *CK, const float *CV, const float *NK,
+                   const float *NV, const float *PAR, const float *LEN, float *C, uint32_t M,
+                   uint32_t dim, uint32_t heads, uint32_t kvheads, uint32_t maxdepth);
 
 /* Double-precision references used by the reference's own self-checks. */
 double nlo_matmul_sample_ref(uint32_t r, uint32_t c, uint32_t K, uint32_t N);

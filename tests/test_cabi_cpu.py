@@ -67,7 +67,13 @@ def test_registry_names_the_reference_kernels(lib):
            "matmul-at", "causal-mask", "attn-scores", "attn-context", "dp4a-dot",
            "bitlinear-dp4a", "dp4a-rows-t", "rmsnorm-heads", "rope-apply", "silu", "scale-rows",
            # BitNet quantization family
-           "sumsq-acc", "clip-scale", "absmean-acc", "quant-act", "quant-w"}
+           "sumsq-acc", "clip-scale", "absmean-acc", "quant-act", "quant-w",
+           # training-side operators
+           "transpose", "slice-cols", "set-cols", "silu-mul-bwd", "silu-bwd", "gelu-bwd",
+           "sub-scale", "sgd", "adam", "colsum", "rmsnorm-dgamma", "rmsnorm-dx", "softmax-bwd",
+           "rowdot", "ce-grad", "ce-grad-idx", "topk-mask", "embed-bwd", "gather-spike",
+           "scatter-spike", "gdn-step", "tree-attn", "attn-sc-dq", "attn-sc-dk", "attn-ctx-dp",
+           "attn-ctx-dv"}
     assert hot <= names
     nb, npush = ctypes.c_uint32(), ctypes.c_uint32()
     assert lib.nl_kernel_arity(b"ternary-rows", ctypes.byref(nb), ctypes.byref(npush)) == 0

@@ -212,7 +212,7 @@ def run_gpu(args):
             step()
         torch.cuda.synchronize()
         if rank == 0:
-            print(json.dumps({"profile_run": True, "steps": args.steps}), flush=True)
+            emit({"profile_run": True, "steps": args.steps})
         return
     # the clock record covers load only: 0.5 s before the timed region, the
     # region itself and 1 s after it, all running this same step
@@ -347,7 +347,8 @@ def run_gpu(args):
 
     kernels = None
     if not args.no_kernels:
-        kernels = run_kernel_rows(device, peak, rank == 0 and ws == 1 and not args.no_cpu)
+        kernels = run_kernel_rows(device, peak, rank == 0 and ws == 1 and not args.no_cpu,
+                                  with_upload=rank == 0)
 
     decode = None
     if not args.no_decode:
@@ -395,7 +396,7 @@ def run_gpu(args):
             line["kernels"] = kernels
         if decode:
             line["decode"] = decode
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -457,7 +458,7 @@ def run_decoder(dist, ws, rank, local, peak):
     return res
 
 
-def run_kernel_rows(device, peak, with_cpu):
+def run_kernel_rows(device, peak, with_cpu, with_upload=True):
     """The other hot-path kernels at BASELINE.json's configs (0, 2, 3):
     f32 matmul 256^3, row softmax 4096x4096 ~ N(0, 4), SwiGLU 16x11008 and
     decode attention (B 8, 32 heads x 128, context 4096), each through the
@@ -568,7 +569,8 @@ def run_kernel_rows(device, peak, with_cpu):
         rows["decode-attn-b B8 H32 ctx4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
     del Q, CK, CV, Cq, flush
     torch.cuda.empty_cache()
-    rows.update(upload_rows())
+    if with_upload:            # one process reads the disk; the other ranks skip it
+        rows.update(upload_rows())
     return rows
 
 
@@ -671,8 +673,8 @@ def run_decode_profile(args):
     dec = Decoder(BITNET_2B, max_batch=8, max_seq=64, device=0)
     prompt = np.random.default_rng(5).integers(0, BITNET_2B["vocab"], size=(args.batch, 4))
     toks, pf, dc = dec.generate(prompt, 4)
-    print(json.dumps({"decode_profile": True, "batch": args.batch, "ms_per_step": dc / 4,
-                      "kernels_per_step": dec.info()["kernels_per_step"]}), flush=True)
+    emit({"decode_profile": True, "batch": args.batch, "ms_per_step": dc / 4,
+                      "kernels_per_step": dec.info()["kernels_per_step"]})
     dec.close()
 
 
@@ -747,10 +749,28 @@ def run_reference(args):
         "note": "the reference's own path (Elisp DSL -> SPIR-V -> Vulkan) cannot run: no "
                 "Emacs, no Vulkan loader or ICD (unavailable on this box)",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_OUT = None
+
+
+def emit(obj):
+    """The result line: the only thing this program writes to standard output."""
+    out = _RESULT_OUT or sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
 
 
 def main():
+    global _RESULT_OUT
+    # Libraries write to file descriptor 1 too (NCCL's version banner, for
+    # one); keep the real standard output for the result line and send
+    # everything else to standard error.
+    sys.stdout.flush()
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)

@@ -235,13 +235,11 @@ int nl_ternary_gemv_batched_dev(uint32_t count, const float *X,
  * copies the outputs back to Y_HOST, returning once they are there.  The
  * per-call shape of the reference's RUN (inline inputs copied in, outputs
  * copied back; host/vkserver.c:274-334) for a resident-weight GEMV batch.
- * Copies run on their own streams; with NELISP_HOST_CHUNKS=n (1..8, default
- * 1) the problems go in n chunks whose copies overlap the other chunks'
- * kernels.  X_HOST and Y_HOST should be pinned (cudaHostAlloc / torch
- * pin_memory) for the copies to run at full speed.
- * Problem z reads X_HOST + z*x_stride (seq*cols values) and writes
- * Y_HOST + z*y_stride (seq*out values).  Device staging is owned by the
- * library. */
+ * X_HOST and Y_HOST should be pinned (cudaHostAlloc / torch pin_memory) for
+ * the copies to run at full speed.  Problem z reads X_HOST + z*x_stride
+ * (seq*cols values) and writes Y_HOST + z*y_stride (seq*out values).  Device
+ * staging is owned by the library.  Equivalent to nl_ternary_gemv_host_submit
+ * followed by nl_host_wait. */
 int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
                                  uint64_t x_stride, const uint32_t *WP,
                                  uint64_t w_stride, const float *S,
@@ -249,11 +247,31 @@ int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
                                  uint64_t y_stride, uint32_t seq, uint32_t out,
                                  uint32_t cols);
 
+/* The same call without waiting: queues the copy in, the GEMVs and the copy
+ * out, and returns a TICKET (1, 2, 3, ... per call; 0 for an empty call).
+ * The caller keeps X_HOST and Y_HOST untouched until nl_host_wait(TICKET)
+ * returns.  Calls' copies and kernels overlap on the device, so a serving
+ * loop that keeps two or three requests in flight hides the copies behind
+ * the kernels.  The library keeps eight staging slots; the ninth call in
+ * flight reuses the first call's slot, and nl_host_wait on the first ticket
+ * then also waits for the ninth call. */
+int nl_ternary_gemv_host_submit(uint32_t count, const float *X_host,
+                                uint64_t x_stride, const uint32_t *WP,
+                                uint64_t w_stride, const float *S,
+                                uint64_t s_stride, float *Y_host,
+                                uint64_t y_stride, uint32_t seq, uint32_t out,
+                                uint32_t cols, uint64_t *ticket);
+
+/* Waits until call TICKET's outputs are in its Y_HOST (and every earlier
+ * call's too).  Returns NL_ERROR for a ticket never issued, or when a
+ * kernel's bounded wait timed out (see nl_wait_status). */
+int nl_host_wait(uint64_t ticket);
+
 /* Bounded waits.  The library's kernels that wait on mbarriers (the TMA and
  * tcgen05 ternary kernels) give up after a bounded time and record it in a
  * host-mapped flag; their outputs are then invalid.  The synchronising entry
- * points (nl_run, nl_batch, nl_run_compiled, nl_ternary_gemv_batched_host)
- * report it as NL_ERROR.  Callers of the asynchronous *_dev entry points
+ * points (nl_run, nl_batch, nl_run_compiled, nl_ternary_gemv_batched_host,
+ * nl_host_wait) report it as NL_ERROR.  Callers of the asynchronous *_dev entry points
  * synchronise their stream and then call nl_wait_status: NL_ERROR (with a
  * message) if a wait gave up since the last report, else NL_OK; the flag is
  * cleared.  No reference counterpart (vkserver has no device-side waits). */

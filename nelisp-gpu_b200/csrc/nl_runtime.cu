@@ -53,6 +53,11 @@ struct Compiled {
   uint64_t kernels = 0;          // kernels per replay
 };
 
+// staging slots of the host-buffer GEMV entry: calls that may be in flight at
+// once.  A call beyond that reuses the slot of the call kHostSlots before it,
+// whose nl_host_wait then also waits for the newer call.
+constexpr int kHostSlots = 8;
+
 struct Context {
   bool ready = false;
   int device = -1;
@@ -69,11 +74,16 @@ struct Context {
   uint64_t launches = 0;
   bool capturing = false;
   uint64_t capture_launches = 0;
-  // nl_ternary_gemv_batched_host: copy streams, events, device staging
+  // host-buffer GEMV entry: copy streams and device staging slots.  Ticket t
+  // (1-based) uses slot (t-1) % kHostSlots; the slot's events order its reuse.
   cudaStream_t h2d = nullptr, d2h = nullptr;
-  cudaEvent_t ev[2 * 8] = {};
-  void *hbuf = nullptr;
-  size_t hbuf_bytes = 0;
+  struct HostSlot {
+    void *buf = nullptr;
+    size_t bytes = 0;
+    bool used = false;
+    cudaEvent_t in_done = nullptr, k_done = nullptr, out_done = nullptr;
+  } hs[kHostSlots];
+  uint64_t host_tickets = 0;
 };
 
 Context g;
@@ -389,15 +399,16 @@ extern "C" void nl_shutdown(void) {
   g.nres = 0;
   if (g.arena) cudaFree(g.arena);
   if (g.ws) cudaFree(g.ws);
-  if (g.hbuf) cudaFree(g.hbuf);
-  g.hbuf = nullptr;
-  g.hbuf_bytes = 0;
-  if (g.h2d) {
-    cudaStreamDestroy(g.h2d);
-    cudaStreamDestroy(g.d2h);
-    for (cudaEvent_t &ev : g.ev) cudaEventDestroy(ev);
-    g.h2d = g.d2h = nullptr;
+  for (Context::HostSlot &hs : g.hs) {
+    if (hs.buf) cudaFree(hs.buf);
+    for (cudaEvent_t *ev : {&hs.in_done, &hs.k_done, &hs.out_done})
+      if (*ev) cudaEventDestroy(*ev);
+    hs = Context::HostSlot();
   }
+  g.host_tickets = 0;
+  if (g.h2d) cudaStreamDestroy(g.h2d);
+  if (g.d2h) cudaStreamDestroy(g.d2h);
+  g.h2d = g.d2h = nullptr;
   if (g.stage) cudaFreeHost(g.stage);
   g.arena = g.ws = g.stage = nullptr;
   g.arena_bytes = g.ws_bytes = 0;
@@ -1085,82 +1096,98 @@ extern "C" int nl_selftest_wait_timeout(void) {
   return nl_wait_status();
 }
 
-extern "C" int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
-                                            uint64_t x_stride, const uint32_t *WP,
-                                            uint64_t w_stride, const float *S, uint64_t s_stride,
-                                            float *Y_host, uint64_t y_stride, uint32_t seq,
-                                            uint32_t out, uint32_t cols) {
+extern "C" int nl_ternary_gemv_host_submit(uint32_t count, const float *X_host,
+                                           uint64_t x_stride, const uint32_t *WP,
+                                           uint64_t w_stride, const float *S, uint64_t s_stride,
+                                           float *Y_host, uint64_t y_stride, uint32_t seq,
+                                           uint32_t out, uint32_t cols, uint64_t *ticket) {
   int rc = ensure_ready();
   if (rc) return rc;
+  if (!ticket) return set_error(NL_ERROR, "ternary-gemv-host: null ticket");
+  *ticket = 0;
   if (count == 0 || seq == 0 || out == 0) return NL_OK;
   if (!X_host || !Y_host || !WP || !S)
     return set_error(NL_ERROR, "ternary-gemv-host: null buffer");
   if (count > 1 && (x_stride < (uint64_t)seq * cols || y_stride < (uint64_t)seq * out))
     return set_error(NL_ERROR, "ternary-gemv-host: strides overlap the problems");
   cudaError_t e = cudaSuccess;
-  if (!g.h2d) {
-    if ((e = cudaStreamCreateWithFlags(&g.h2d, cudaStreamNonBlocking)) != cudaSuccess ||
-        (e = cudaStreamCreateWithFlags(&g.d2h, cudaStreamNonBlocking)) != cudaSuccess)
-      return cuda_status(e, "ternary-gemv-host: streams");
-    for (cudaEvent_t &ev : g.ev)
-      if ((e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming)) != cudaSuccess)
-        return cuda_status(e, "ternary-gemv-host: events");
-  }
+  if (!g.h2d && (e = cudaStreamCreateWithFlags(&g.h2d, cudaStreamNonBlocking)) != cudaSuccess)
+    return cuda_status(e, "ternary-gemv-host: streams");
+  if (!g.d2h && (e = cudaStreamCreateWithFlags(&g.d2h, cudaStreamNonBlocking)) != cudaSuccess)
+    return cuda_status(e, "ternary-gemv-host: streams");
+  Context::HostSlot &hs = g.hs[g.host_tickets % kHostSlots];
+  for (cudaEvent_t *ev : {&hs.in_done, &hs.k_done, &hs.out_done})
+    if (!*ev && (e = cudaEventCreateWithFlags(ev, cudaEventDisableTiming)) != cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host: events");
   const uint64_t xs = count > 1 ? x_stride : (uint64_t)seq * cols;
   const uint64_t ys = count > 1 ? y_stride : (uint64_t)seq * out;
-  const size_t xbytes = align256(((count - 1) * xs + (uint64_t)seq * cols) * 4u);
-  const size_t ybytes = align256(((count - 1) * ys + (uint64_t)seq * out) * 4u);
-  if (g.hbuf_bytes < xbytes + ybytes) {
-    cudaStreamSynchronize(g.stream);
-    if (g.hbuf) cudaFree(g.hbuf);
-    g.hbuf = nullptr;
-    g.hbuf_bytes = 0;
-    if ((e = cudaMalloc(&g.hbuf, xbytes + ybytes)) != cudaSuccess)
+  const size_t xin = ((count - 1) * xs + (uint64_t)seq * cols) * 4u;
+  const size_t yout = ((count - 1) * ys + (uint64_t)seq * out) * 4u;
+  const size_t xbytes = align256(xin);
+  if (hs.bytes < xbytes + yout) {
+    // the slot's previous call must be done with it before it is replaced
+    if (hs.used && (e = cudaEventSynchronize(hs.out_done)) != cudaSuccess)
       return cuda_status(e, "ternary-gemv-host: staging");
-    g.hbuf_bytes = xbytes + ybytes;
+    if (hs.buf) cudaFree(hs.buf);
+    hs.buf = nullptr;
+    hs.bytes = 0;
+    hs.used = false;
+    if ((e = cudaMalloc(&hs.buf, xbytes + align256(yout))) != cudaSuccess)
+      return cuda_status(e, "ternary-gemv-host: staging");
+    hs.bytes = xbytes + align256(yout);
   }
-  float *dx = (float *)g.hbuf, *dy = (float *)((char *)g.hbuf + xbytes);
+  float *dx = (float *)hs.buf, *dy = (float *)((char *)hs.buf + xbytes);
   const uint32_t nblk = (cols + 127) / 128, wng = (cols + 15) / 16;
   size_t wsb = ternary_ws_bytes_best(count, seq, cols, false);
   void *ws = ternary_fast_shape(cols, nblk, wng, false) ? library_workspace(wsb, g.stream) : nullptr;
   if (!ws) wsb = 0;
-  // NELISP_HOST_CHUNKS (1..8) splits the problems into chunks whose copies
-  // overlap the other chunks' kernels.  The default is one chunk: at 64 x
-  // 4096^2 (1 MB each way, 23 us per copy) every extra chunk's prep launch
-  // cost more than the overlap saved (measured on B200: 123 us at 1 chunk,
-  // 122 at 2, 133 at 4, 184 at 8).
-  static const uint32_t want_chunks = [] {
-    const char *v = getenv("NELISP_HOST_CHUNKS");
-    const int n = v ? atoi(v) : 0;
-    return (uint32_t)(n >= 1 && n <= 8 ? n : 1);
-  }();
-  uint32_t nch = want_chunks;
-  if (nch > count) nch = count;
-  const uint32_t per = (count + nch - 1) / nch;
-  for (uint32_t c = 0, z0 = 0; z0 < count; c++, z0 += per) {
-    const uint32_t z1 = z0 + per < count ? z0 + per : count, n = z1 - z0;
-    const size_t xin = ((n - 1) * xs + (uint64_t)seq * cols) * 4u;
-    const size_t yout = ((n - 1) * ys + (uint64_t)seq * out) * 4u;
-    if ((e = cudaMemcpyAsync(dx + z0 * xs, X_host + z0 * xs, xin, cudaMemcpyHostToDevice,
-                             g.h2d)) != cudaSuccess ||
-        (e = cudaEventRecord(g.ev[2 * c], g.h2d)) != cudaSuccess ||
-        (e = cudaStreamWaitEvent(g.stream, g.ev[2 * c], 0)) != cudaSuccess)
-      return cuda_status(e, "ternary-gemv-host: copy in");
-    if ((e = ternary_gemv_launch(n, dx + z0 * xs, xs, WP + z0 * w_stride, w_stride,
-                                 S + z0 * s_stride, s_stride, nullptr, dy + z0 * ys, ys, seq, out,
-                                 cols, nblk, wng, false, UINT64_MAX, ws, wsb, g.stream)) !=
-        cudaSuccess)
-      return cuda_status(e, "ternary-gemv-host");
-    if ((e = cudaEventRecord(g.ev[2 * c + 1], g.stream)) != cudaSuccess ||
-        (e = cudaStreamWaitEvent(g.d2h, g.ev[2 * c + 1], 0)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(Y_host + z0 * ys, dy + z0 * ys, yout, cudaMemcpyDeviceToHost,
-                             g.d2h)) != cudaSuccess)
-      return cuda_status(e, "ternary-gemv-host: copy out");
-  }
-  rc = cuda_status(cudaStreamSynchronize(g.d2h), "ternary-gemv-host");
+  // copy in once the slot's previous kernel has read its inputs; run once the
+  // inputs are there and the slot's previous outputs have been copied out;
+  // copy out once the kernel is done
+  if ((hs.used && (e = cudaStreamWaitEvent(g.h2d, hs.k_done, 0)) != cudaSuccess) ||
+      (e = cudaMemcpyAsync(dx, X_host, xin, cudaMemcpyHostToDevice, g.h2d)) != cudaSuccess ||
+      (e = cudaEventRecord(hs.in_done, g.h2d)) != cudaSuccess ||
+      (e = cudaStreamWaitEvent(g.stream, hs.in_done, 0)) != cudaSuccess ||
+      (hs.used && (e = cudaStreamWaitEvent(g.stream, hs.out_done, 0)) != cudaSuccess))
+    return cuda_status(e, "ternary-gemv-host: copy in");
+  if ((e = ternary_gemv_launch(count, dx, xs, WP, w_stride, S, s_stride, nullptr, dy, ys, seq,
+                               out, cols, nblk, wng, false, UINT64_MAX, ws, wsb, g.stream)) !=
+      cudaSuccess)
+    return cuda_status(e, "ternary-gemv-host");
+  if ((e = cudaEventRecord(hs.k_done, g.stream)) != cudaSuccess ||
+      (e = cudaStreamWaitEvent(g.d2h, hs.k_done, 0)) != cudaSuccess ||
+      (e = cudaMemcpyAsync(Y_host, dy, yout, cudaMemcpyDeviceToHost, g.d2h)) != cudaSuccess ||
+      (e = cudaEventRecord(hs.out_done, g.d2h)) != cudaSuccess)
+    return cuda_status(e, "ternary-gemv-host: copy out");
+  hs.used = true;
+  *ticket = ++g.host_tickets;
+  return NL_OK;
+}
+
+extern "C" int nl_host_wait(uint64_t ticket) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  if (ticket == 0) return NL_OK;          // an empty call's ticket
+  if (ticket > g.host_tickets) return set_error(NL_ERROR, "host-wait: unknown ticket %llu",
+                                                (unsigned long long)ticket);
+  // copies out complete in ticket order on one stream: the slot's latest
+  // copy-out is this ticket's or a later one
+  Context::HostSlot &hs = g.hs[(ticket - 1) % kHostSlots];
+  rc = cuda_status(cudaEventSynchronize(hs.out_done), "host-wait");
   if (rc == NL_OK && take_wait_timeout())
-    return set_error(NL_ERROR, "ternary-gemv-host: a kernel's bounded wait timed out");
+    return set_error(NL_ERROR, "host-wait: a kernel's bounded wait timed out");
   return rc;
+}
+
+extern "C" int nl_ternary_gemv_batched_host(uint32_t count, const float *X_host,
+                                            uint64_t x_stride, const uint32_t *WP,
+                                            uint64_t w_stride, const float *S, uint64_t s_stride,
+                                            float *Y_host, uint64_t y_stride, uint32_t seq,
+                                            uint32_t out, uint32_t cols) {
+  uint64_t t = 0;
+  const int rc = nl_ternary_gemv_host_submit(count, X_host, x_stride, WP, w_stride, S, s_stride,
+                                             Y_host, y_stride, seq, out, cols, &t);
+  return rc ? rc : nl_host_wait(t);
 }
 
 extern "C" int nl_ternary_gemv_batched_dev(uint32_t count, const float *X, uint64_t x_stride,

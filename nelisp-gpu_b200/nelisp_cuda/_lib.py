@@ -87,6 +87,9 @@ SIGNATURES = {
     "nl_selftest_wait_timeout": (_i, []),
     "nl_ternary_gemv_batched_host": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
                                           _u32, _u32, _u32]),
+    "nl_ternary_gemv_host_submit": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
+                                         _u32, _u32, _u32, ctypes.POINTER(_u64)]),
+    "nl_host_wait": (_i, [_u64]),
     "nl_launch_count": (_u64, []),
     # decoder (nelisp_cuda.decoder rebinds these with the config struct)
     "nl_nccl_unique_id": (_i, [_vp]),

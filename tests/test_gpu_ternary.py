@@ -422,7 +422,7 @@ def test_tcgen05_gemv_flagged_rows(seq):
 @pytest.mark.parametrize("count,seq,out,cols", [(64, 1, 1024, 1024), (9, 3, 2560, 512),
                                                 (1, 2, 300, 256), (40, 16, 512, 768)])
 def test_batched_host_entry_matches_device_entry(count, seq, out, cols):
-    """nl_ternary_gemv_batched_host (copies in, chunked GEMVs, copies out)
+    """nl_ternary_gemv_batched_host (copies in, GEMVs, copies out)
     gives the bits of nl_ternary_gemv_batched_dev on the same inputs."""
     import ctypes
     import torch
@@ -449,3 +449,45 @@ def test_batched_host_entry_matches_device_entry(count, seq, out, cols):
     assert np.array_equal(Yp.numpy().view(np.uint32), tY.cpu().numpy().view(np.uint32))
     want = nlo.ternary_gemv_rows(X[:seq * cols], Ws[:out * cols // 16], S[:out], seq, out, cols)
     assert nlo.tk_err(Yp.numpy()[:seq * out], want) < TOL
+
+
+def test_host_submit_overlaps_calls_and_waits_in_order():
+    """Five nl_ternary_gemv_host_submit calls in flight at once (more than the
+    library's three staging slots), each on its own activations and output
+    buffer: one nl_host_wait on the last ticket completes them all, each with
+    the bits of the device entry; an unissued ticket is an error."""
+    import ctypes
+    import torch
+    from nelisp_cuda import _lib as L
+    from nelisp_cuda import dev
+    lib = L.load()
+    count, seq, out, cols = 12, 2, 1024, 1536
+    rng = np.random.default_rng(77)
+    Ws = np.concatenate([pack_trits(rng.integers(-1, 2, size=(out, cols))) for _ in range(count)])
+    S = rng.uniform(0.5, 1.5, count * out).astype(np.float32)
+    d = torch.device("cuda")
+    tW = torch.from_numpy(Ws.view(np.int32)).to(d)
+    tS = torch.from_numpy(S).to(d)
+    calls = 5
+    Xs = [torch.from_numpy(rng.standard_normal(count * seq * cols).astype(np.float32)).pin_memory()
+          for _ in range(calls)]
+    Ys = [torch.full((count * seq * out,), 7.0, dtype=torch.float32).pin_memory()
+          for _ in range(calls)]
+    tickets = []
+    for X, Y in zip(Xs, Ys):
+        t = ctypes.c_uint64()
+        L.check(lib.nl_ternary_gemv_host_submit(count, X.data_ptr(), seq * cols, tW.data_ptr(),
+                                                out * cols // 16, tS.data_ptr(), out,
+                                                Y.data_ptr(), seq * out, seq, out, cols,
+                                                ctypes.byref(t)))
+        tickets.append(t.value)
+    assert all(b == a + 1 for a, b in zip(tickets, tickets[1:]))
+    L.check(lib.nl_host_wait(tickets[-1]))
+    for X, Y in zip(Xs, Ys):
+        tY = torch.zeros(count * seq * out, dtype=torch.float32, device=d)
+        dev.ternary_gemv_batched(count, X.to(d), seq * cols, tW, out * cols // 16, tS, out, tY,
+                                 seq * out, seq, out, cols)
+        assert np.array_equal(Y.numpy().view(np.uint32), tY.cpu().numpy().view(np.uint32))
+    assert lib.nl_host_wait(0) == 0
+    assert lib.nl_host_wait(tickets[-1] + 1) != 0
+    assert b"unknown ticket" in lib.nl_last_error()

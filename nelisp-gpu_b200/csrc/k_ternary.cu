@@ -42,6 +42,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+
 #include "nl_internal.h"
 #include "ternary_prep.cuh"
 
@@ -140,7 +141,7 @@ ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
     mm = fmaxf(mm, *cl.map_shared_rank(&s_max, k));
     anybad |= *cl.map_shared_rank(&s_bad, k);
   }
-  quantize_slice(xr + sl.c0, sl, mm, anybad != 0, live, rank == 0, s, seq,
+  quantize_slice(xr + sl.c0, sl, mm, anybad != 0, live, rank, s, seq,
                  prep_at(ws, (int)seq, cols, z));
   cl.sync();                      // no CTA leaves while its maximum is read
 }
@@ -177,31 +178,105 @@ __host__ __device__ inline size_t mma_smem_bytes(int NT) {
   return (size_t)2 * kChunk * NT * 128 * sizeof(uint2);   // double-buffered chunk
 }
 
-// Two-bit codes -> int8 operands of four m16n8k32 steps, with no lookup: a
-// code moved to bits 6..7 of a byte, the bits below cleared, IS the int8
-// value 64*t of its trit (00 -> 0, 01 -> 64, 10 -> -128 = 64*(-2),
-// 11 -> -64), the reference's sign-extending decode scaled by 64.  Byte j of
-// word w holds codes 4j..4j+3; (w << 2(3-k)) & 0xC0C0C0C0 is the operand
-// register of codes {k, 4+k, 8+k, 12+k}.  The dot products come out
-// multiplied by 64, which the epilogue removes exactly.
-//   MMA j = 0: codes {0,4,8,12} | {1,5,9,13} of the lane's first word
-//   MMA j = 1: codes {2,6,10,14} | {3,7,11,15} of the first word
-//   MMA j = 2, 3: the same of the second word
-// (a0/a2 = rows g, a1/a3 = rows g+8; the activation fragments follow the
-// same column order, see ternary_prep.cuh).
+// Two-bit codes -> int8 operands of four m16n8k32 steps, with no lookup.
+// Byte b of word w holds codes 4b..4b+3, code i in field i % 4 (bits
+// 2(i%4)..2(i%4)+1 of the byte).  MMA step j takes field j of every byte of
+// the lane's two words (a0/a2 = the first / second word of row g, a1/a3 the
+// same of row g+8; the activation fragments follow the same column order,
+// see ternary_prep.cuh).  Two forms:
+//
+// unpack_signed: a code moved to bits 6..7 of a byte, the bits below
+//   cleared, IS the int8 value 64*t of its trit (00 -> 0, 01 -> 64,
+//   10 -> -128 = 64*(-2), 11 -> -64), the reference's sign-extending decode
+//   scaled by 64: (w << 2(3-j)) & 0xC0C0C0C0, two instructions a register.
+//   Every step carries 64*t, so the dot products come out multiplied by 64.
+//
+// unpack_offset: one LOP3 a register.  A code XOR 0b10 is t + 2 (00 -> 2,
+//   01 -> 3, 11 -> 1, 10 -> 0), so (w ^ 0xAAAAAAAA) & (3 << 2j) * 0x01010101
+//   gives bytes 4^j (t + 2) <= 48 for fields j = 0..2, still non-negative
+//   int8; field 3 keeps the signed form 64 t (w & 0xC0C0C0C0, one AND).  Each
+//   step accumulates into its own chain, whose sum is an exact multiple of
+//   4^j; chain j >> 2j then holds sum (t + 2) x (j < 3) or sum t x (j = 3),
+//   and the epilogue removes 2 * sum x over fields 0..2 exactly with the
+//   prep's XSUM.
 constexpr uint32_t kTop2 = 0xC0C0C0C0u;
 __device__ __forceinline__ uint2 lo2(uint4 v) { return make_uint2(v.x, v.y); }
 __device__ __forceinline__ uint2 hi2(uint4 v) { return make_uint2(v.z, v.w); }
-__device__ __forceinline__ void unpack_block(uint2 a, uint2 c, uint32_t (&A)[4][4]) {
-  A[0][0] = (a.x << 6) & kTop2; A[0][1] = (c.x << 6) & kTop2;
-  A[0][2] = (a.x << 4) & kTop2; A[0][3] = (c.x << 4) & kTop2;
-  A[1][0] = (a.x << 2) & kTop2; A[1][1] = (c.x << 2) & kTop2;
-  A[1][2] = a.x & kTop2;        A[1][3] = c.x & kTop2;
-  A[2][0] = (a.y << 6) & kTop2; A[2][1] = (c.y << 6) & kTop2;
-  A[2][2] = (a.y << 4) & kTop2; A[2][3] = (c.y << 4) & kTop2;
-  A[3][0] = (a.y << 2) & kTop2; A[3][1] = (c.y << 2) & kTop2;
-  A[3][2] = a.y & kTop2;        A[3][3] = c.y & kTop2;
+__device__ __forceinline__ void unpack_signed(uint2 a, uint2 c, uint32_t (&A)[4][4]) {
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int sh = 6 - 2 * j;
+    A[j][0] = (a.x << sh) & kTop2;
+    A[j][1] = (c.x << sh) & kTop2;
+    A[j][2] = (a.y << sh) & kTop2;
+    A[j][3] = (c.y << sh) & kTop2;
+  }
 }
+// (w ^ x) & M in one instruction: lop3 with the truth table of (a ^ c) & b
+// (0x48 for a = 0xF0, b = 0xCC, c = 0xAA).
+template <uint32_t M>
+__device__ __forceinline__ uint32_t xor_and(uint32_t w, uint32_t x) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x48;\n" : "=r"(d) : "r"(w), "n"(M), "r"(x));
+  return d;
+}
+// X holds 0xAAAAAAAA (kept in a register by the caller: lop3 takes one
+// immediate).
+__device__ __forceinline__ void unpack_offset(uint2 a, uint2 c, uint32_t x,
+                                              uint32_t (&A)[4][4]) {
+  A[0][0] = xor_and<0x03030303u>(a.x, x); A[0][1] = xor_and<0x03030303u>(c.x, x);
+  A[0][2] = xor_and<0x03030303u>(a.y, x); A[0][3] = xor_and<0x03030303u>(c.y, x);
+  A[1][0] = xor_and<0x0C0C0C0Cu>(a.x, x); A[1][1] = xor_and<0x0C0C0C0Cu>(c.x, x);
+  A[1][2] = xor_and<0x0C0C0C0Cu>(a.y, x); A[1][3] = xor_and<0x0C0C0C0Cu>(c.y, x);
+  A[2][0] = xor_and<0x30303030u>(a.x, x); A[2][1] = xor_and<0x30303030u>(c.x, x);
+  A[2][2] = xor_and<0x30303030u>(a.y, x); A[2][3] = xor_and<0x30303030u>(c.y, x);
+  A[3][0] = a.x & kTop2; A[3][1] = c.x & kTop2;
+  A[3][2] = a.y & kTop2; A[3][3] = c.y & kTop2;
+}
+__device__ __forceinline__ uint32_t offset_key() {
+  uint32_t x;
+  asm("mov.b32 %0, 0xAAAAAAAA;\n" : "=r"(x));
+  return x;
+}
+// The four step chains of one output column of unpack_offset, unscaled:
+// sum (t + 2) x over fields 0..2 plus sum t x over field 3 (exact).
+__device__ __forceinline__ int offset_combine(int a0, int a1, int a2, int a3) {
+  return a0 + (a1 >> 2) + (a2 >> 4) + (a3 >> 6);
+}
+// XSUM of a problem's rows spread over a warp: in pass p, lane l holds
+// partial l % 8 of row 4p + l / 8 (zero past SEQ).  The loads are issued
+// early, one or a few per lane, and combined late: total() leaves row l's
+// sum in lane l.  NT n-tiles hold at most 8 NT / 3 rows.
+template <int NT>
+struct XsumLanes {
+  static constexpr int kPasses = (8 * NT / 3 + 3) / 4;
+  long long v[kPasses];
+  __device__ __forceinline__ void load(const PrepOut &P, uint32_t seq, int lane) {
+#pragma unroll
+    for (int p = 0; p < kPasses; p++) {
+      const uint32_t s = 4u * p + (uint32_t)(lane >> 3);
+      v[p] = s < seq ? __ldcg(P.xsum + s * kRowCluster + (lane & 7)) : 0ll;
+    }
+  }
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int p = 0; p < kPasses; p++) v[p] = 0ll;
+  }
+  // All 32 lanes call it.
+  __device__ __forceinline__ long long total(int lane) const {
+    long long mine = 0;
+#pragma unroll
+    for (int p = 0; p < kPasses; p++) {
+      long long t = v[p];
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      t += __shfl_xor_sync(0xffffffffu, t, 4);
+      const long long r = __shfl_sync(0xffffffffu, t, (lane & 3) * 8);   // row 4p + lane % 4
+      if ((lane >> 2) == p) mine = r;
+    }
+    return mine;
+  }
+};
 
 // One chunk of kChunk blocks for one warp: consume the weight registers,
 // refill them with the blocks kChunk further on, run the MMAs against the
@@ -222,7 +297,7 @@ __device__ __forceinline__ void mma_chunk(int (&acc)[NT][2][4], float (&yf)[NT][
       wb[u] = __ldcs(pb + 4 * (u + kChunk));
     }
     uint32_t A[4][4];
-    unpack_block(a, c, A);
+    unpack_signed(a, c, A);
     const uint2 *fu = fb + u * NT * 128;
     // Two accumulator chains per n-tile, so consecutive MMAs do not wait on
     // each other's results.
@@ -410,6 +485,9 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
 // records an error and returns.
 // ---------------------------------------------------------------------------
 constexpr int kTmaBlocks = 4;                 // 128-column blocks per stage
+// Zero activation fragments for the blocks past the row end of a partial
+// stage (at most kTmaBlocks - 1 blocks of 6 n-tiles).
+__device__ __align__(128) unsigned char g_zero_frags[(kTmaBlocks - 1) * 6 * 1024];
 
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -542,9 +620,12 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
         const uint32_t it = blockIdx.x + (g / nchunk) * gridDim.x, c = g % nchunk;
         const uint32_t z = it / tpp, tile = it % tpp;
         const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
-        mbar_expect_tx(&full[st], wbytes + nb * NT * 1024u);
+        mbar_expect_tx(&full[st], wbytes + (uint32_t)kTmaBlocks * NT * 1024u);
         tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u),
                     (int)(z * out + tile * 16u * nw), &full[st]);
+        if (nb < (uint32_t)kTmaBlocks)             // the blocks past the row end
+          bulk_load(fbuf + (size_t)st * fstage + (size_t)nb * NT * 128u, g_zero_frags,
+                    ((uint32_t)kTmaBlocks - nb) * NT * 1024u, &full[st]);
         if (g >= pre) {
           bulk_load(fbuf + (size_t)st * fstage, prep_at(ws, (int)seq, cols, z).frag +
                     (size_t)c * fstage, nb * NT * 1024u, &full[st]);
@@ -571,7 +652,12 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   }
 
   // ---- consumers ----
+  // One n-tile (one or two sequence rows) takes the one-LOP3 offset operands;
+  // more n-tiles keep the signed ones, whose extra chains would not fit the
+  // register budget of two CTAs per SM without spilling.
+  constexpr bool OFF = !PER_BLOCK && NT == 1;
   pdl_wait();                                      // the epilogue reads the prep's flags
+  const uint32_t xkey = offset_key();
   const int gq = lane >> 2, q = lane & 3;
   // Byte offsets of this lane's 8-byte words in a stage's weight tile: row r
   // of the tile holds 128 bytes; the 16-byte chunk k of row r sits at chunk
@@ -605,6 +691,11 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     const float e_bias = BIAS ? __ldg(BIAS + erow) : 0.0f;
     const float e_rinv = (uint32_t)lane < seq ? P.rowinv[lane] : 0.0f;
     const int e_flag = (uint32_t)lane < seq ? P.rowflag[lane] : 0;
+    XsumLanes<NT> xl;
+    if (OFF)
+      xl.load(P, seq, lane);
+    else
+      xl.zero();
 
     int acc[NT][4][4];                    // [n-tile][k-step][reg]: independent chains
     float yf[NT][4];
@@ -617,9 +708,10 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
         for (int j = 0; j < 4; j++) acc[t][j][r] = 0;
       }
 
-    // Whole chunks without a per-block test: blocks past the row end of a
-    // partial chunk hold TMA's zero fill, and a zero weight operand adds an
-    // exact 0 whatever the stale fragments beside it.
+    // Chunks run without a per-block test: in the row's last chunk, when
+    // nblk is not a multiple of kTmaBlocks, the blocks past the row end hold
+    // TMA's zero fill and zero fragments (the producer copies them), so they
+    // add an exact 0 with either operand form.
     for (uint32_t c = 0; c < nchunk; c++) {
       if (!mbar_wait(&full[cst], cph, err)) return;
       const uint32_t wt = wsm + (uint32_t)cst * wbytes;
@@ -629,7 +721,10 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
         const uint2 a = lds64(wt + offA[b]);
         const uint2 cw = lds64(wt + offB[b]);
         uint32_t A[4][4];
-        unpack_block(a, cw, A);
+        if (OFF)
+          unpack_offset(a, cw, xkey, A);
+        else
+          unpack_signed(a, cw, A);
 #pragma unroll
         for (int t = 0; t < NT; t++) {
           const uint32_t ft = fb + (uint32_t)(b * NT + t) * 1024u;
@@ -671,7 +766,8 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
 #pragma unroll
       for (int r = 0; r < 4; r++)
         v[r] = PER_BLOCK ? __float_as_int(yf[t][r])
-                         : acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
+                 : OFF ? offset_combine(acc[t][0][r], acc[t][1][r], acc[t][2][r], acc[t][3][r])
+                       : acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
       s_acc[gq][8 * t + 2 * q] = v[0];
       s_acc[gq][8 * t + 2 * q + 1] = v[1];
       s_acc[gq + 8][8 * t + 2 * q] = v[2];
@@ -681,6 +777,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     const uint32_t *Wz = WP + z * w_stride;
     float *Yz = Y + z * y_stride;
     const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
+    const long long e_xsum = OFF ? xl.total(lane) : 0ll;
     for (uint32_t k = 0; k * 32u < 16u * seq; k++) {     // uniform trip count: shuffles
       const uint32_t idx = (uint32_t)lane + 32u * k;
       const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
@@ -688,6 +785,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
       const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
       const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
+      const long long xs2 = OFF ? 2ll * __shfl_sync(0xffffffffu, e_xsum, (int)s) : 0ll;
       const uint32_t o = rg * 16u + r;
       if (idx >= 16u * seq || o >= out || fl) continue;
       float yv;
@@ -699,7 +797,10 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       } else {
         long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
                         65536ll * s_acc[r][3 * s + 2];
-        tot >>= 6;                               // the operands carried 64 * t: exact
+        if (OFF)
+          tot -= xs2;                            // the offset operands' 2 sum x
+        else
+          tot >>= 6;                             // the operands carried 64 * t: exact
         yv = ((float)tot * ri) * sc;
       }
       if (BIAS) yv = bi + yv;
@@ -758,6 +859,7 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
                    uint32_t tiles, uint32_t count, int rt_log2, PeerOut po) {
   constexpr int KB = NT == 1 ? 4 : (NT <= 4 ? 2 : 1);   // blocks per warp in flight
   constexpr int CH = NT <= 2 ? 4 : 1;                   // accumulator chains per n-tile
+  constexpr bool OFF = CH == 4;                         // a chain per step: offset operands
   constexpr int kMaxRT = NT >= 5 ? 4 : 8;
   __shared__ int red[kDecWarps][NT * 4][32];
   __shared__ int s_acc[kMaxRT][16][8 * NT + 1];
@@ -794,6 +896,12 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   const uint2 *fr = P.frag + 2 * lane;
   const float e_rinv = (uint32_t)lane < seq ? __ldcg(P.rowinv + lane) : 0.0f;
   const int e_flag = (uint32_t)lane < seq ? __ldcg(P.rowflag + lane) : 0;
+  XsumLanes<NT> xl;
+  if (OFF)
+    xl.load(P, seq, lane);
+  else
+    xl.zero();
+  const uint32_t xkey = offset_key();
 
   int acc[NT][CH][4];
 #pragma unroll
@@ -831,7 +939,11 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
 #pragma unroll
     for (int u = 0; u < KB; u++) {
       uint32_t A[4][4];
-      unpack_block(wa[u], wb[u], A);       // zero weights past nblk add 0
+      // words past nblk are zero and so are their fragments: they add 0
+      if (OFF)
+        unpack_offset(wa[u], wb[u], xkey, A);
+      else
+        unpack_signed(wa[u], wb[u], A);
 #pragma unroll
       for (int t = 0; t < NT; t++)
 #pragma unroll
@@ -851,8 +963,12 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
 #pragma unroll
     for (int r = 0; r < 4; r++) {
       int v = 0;
+      if (OFF) {
+        v = offset_combine(acc[t][0][r], acc[t][1 % CH][r], acc[t][2 % CH][r], acc[t][3 % CH][r]);
+      } else {
 #pragma unroll
-      for (int j = 0; j < CH; j++) v += acc[t][j][r];
+        for (int j = 0; j < CH; j++) v += acc[t][j][r];
+      }
       red[warp][t * 4 + r][lane] = v;
     }
   __syncthreads();
@@ -879,6 +995,7 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   };
   if (live) {
     const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
+    const long long e_xsum = OFF ? xl.total(lane) : 0ll;
     for (uint32_t k = (uint32_t)kw; k * 32u < 16u * seq; k += (uint32_t)wpt) {   // warp-uniform
       const uint32_t idx = (uint32_t)lane + 32u * k;
       const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
@@ -886,11 +1003,15 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
       const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
       const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
       const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
+      const long long xs2 = OFF ? 2ll * __shfl_sync(0xffffffffu, e_xsum, (int)s) : 0ll;
       const uint32_t o = rt * 16u + r;
       if (idx >= 16u * seq || o >= out || fl) continue;
       long long tot = (long long)s_acc[tl][r][3 * s] + 256ll * s_acc[tl][r][3 * s + 1] +
                       65536ll * s_acc[tl][r][3 * s + 2];
-      tot >>= 6;                                   // the operands carried 64 * t: exact
+      if (OFF)
+        tot -= xs2;                                // the offset operands' 2 sum x
+      else
+        tot >>= 6;                                 // the operands carried 64 * t: exact
       float yv = ((float)tot * ri) * sc;
       if (BIAS) yv = bi + yv;
       const uint64_t oi = (uint64_t)s * out + o;

@@ -317,7 +317,7 @@ k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restri
   const RowStats mx = cluster_combine<true>(cl, &st[1]);
   if (ws) {
     __syncthreads();
-    quantize_slice(xs, sl, mx.v, mx.bad != 0, live, rank == 0, b, B,
+    quantize_slice(xs, sl, mx.v, mx.bad != 0, live, rank, b, B,
                    prep_at(ws, (int)B, H, 0));
   }
   cl.sync();                     // no CTA leaves while its statistics are read
@@ -357,7 +357,7 @@ k_silu_prep(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint3
   const RowStats mx = cluster_combine<true>(cl, &st);
   if (ws) {
     __syncthreads();
-    quantize_slice(xs, sl, mx.v, mx.bad != 0, live, rank == 0, b, B,
+    quantize_slice(xs, sl, mx.v, mx.bad != 0, live, rank, b, B,
                    prep_at(ws, (int)B, fr, 0));
   }
   cl.sync();

@@ -24,16 +24,23 @@ constexpr int kMaxFastSeq = 16;  // 48 (s, limb) columns = 6 n-tiles of 8
 // (n = 3s + limb), the k32 step within the block is j = 2h + e and
 // lane = 4*(n%8) + q.  A lane's fragments for steps (0,1) and for (2,3) are
 // each one 16-byte load, and the 32 lanes of a warp read 512 contiguous
-// bytes.  Lane q of MMA j in block blk covers word w = 2q + (j>>1) of the
-// block and, within it, with k = 2*(j&1): codes {k, 4+k, 8+k, 12+k} (b0) and
-// {k+1, 5+k, 9+k, 13+k} (b1) -- the order in which the weight operand
-// registers carry them (k_ternary.cu, unpack_block).
-// Blocks are outermost so that a run of blocks is one contiguous chunk the
-// main kernel can stage into shared memory with a single bulk copy.
+// bytes.  Lane q of MMA j in block blk covers words 2q (b0) and 2q+1 (b1) of
+// the block and, within each, codes {j, 4+j, 8+j, 12+j}: two-bit field j of
+// every byte, the bits from which the weight operand registers of step j
+// are made (k_ternary.cu, unpack_signed / unpack_offset).  Every step thus
+// carries one field, so an accumulator per step holds one power-of-four
+// scale.  Blocks are outermost so that a run of blocks is one contiguous
+// chunk the main kernel can stage into shared memory with a single bulk copy.
+//
+// XSUM[s][r] is CTA r's share of sum xq_i over the values whose code sits in
+// field 0, 1 or 2 of its byte (i % 4 != 3): the exact offset that the
+// one-instruction weight operands 4^j (t + 2) of fields 0..2 add.
+constexpr int kRowCluster = 8;     // CTAs that share one row in the prep
 struct PrepOut {
   uint2 *frag;      // NT * cols * 8 bytes
   float *rowinv;    // [kMaxFastSeq] 2^-e_s
   int *rowflag;     // [kMaxFastSeq] 1: compute (., s) on the CUDA cores
+  long long *xsum;  // [kMaxFastSeq][kRowCluster]
 };
 
 __host__ __device__ inline int n_tiles(int seq) { return (3 * seq + 7) / 8; }
@@ -48,8 +55,9 @@ __host__ __device__ inline size_t frag_bytes(int seq, uint32_t cols) {
 __host__ __device__ inline size_t align256(size_t b) {
   return (b + 255u) & ~(size_t)255u;
 }
+constexpr size_t kPrepTail = 256u + (size_t)kMaxFastSeq * kRowCluster * 8u;
 __host__ __device__ inline size_t prep_bytes(int seq, uint32_t cols) {
-  return align256(frag_bytes(seq, cols)) + 256u;
+  return align256(frag_bytes(seq, cols)) + kPrepTail;
 }
 __device__ inline PrepOut prep_at(void *ws, int seq, uint32_t cols, uint32_t z) {
   char *base = (char *)ws + (size_t)z * prep_bytes(seq, cols);
@@ -57,6 +65,7 @@ __device__ inline PrepOut prep_at(void *ws, int seq, uint32_t cols, uint32_t z) 
   p.frag = (uint2 *)base;
   p.rowinv = (float *)(base + align256(frag_bytes(seq, cols)));
   p.rowflag = (int *)(p.rowinv + kMaxFastSeq);
+  p.xsum = (long long *)(base + align256(frag_bytes(seq, cols)) + 256u);
   return p;
 }
 
@@ -85,13 +94,16 @@ __device__ __forceinline__ bool row_scale(float mm, bool bad, float *mul, float 
 // Quantize the 16 values V of packed word W of sequence row S into the
 // fragments of P (zeros when !OK): three balanced int8 limbs per value,
 // written in the column order of the weight operands (see the layout note).
-__device__ __forceinline__ void quantize_word(const float (&v)[16], float mul, bool ok,
-                                              uint32_t W, uint32_t s, int NT, PrepOut P) {
+// Returns the word's share of XSUM: the sum of its xq over codes i % 4 != 3.
+__device__ __forceinline__ long long quantize_word(const float (&v)[16], float mul, bool ok,
+                                                   uint32_t W, uint32_t s, int NT, PrepOut P) {
   int l[3][16];
+  long long part = 0;
 #pragma unroll
   for (int k = 0; k < 16; k++) {
     if (ok) {
       int qv = __float2int_rn(v[k] * mul);   // exact scaling, one rounding
+      if ((k & 3) != 3) part += qv;
       int l0 = (int)(int8_t)(qv & 0xff);
       int r = (qv - l0) >> 8;
       int l1 = (int)(int8_t)(r & 0xff);
@@ -102,23 +114,20 @@ __device__ __forceinline__ void quantize_word(const float (&v)[16], float mul, b
     }
   }
   const uint32_t blk = W / 8u, wq = W % 8u;
-  const uint32_t q = wq >> 1;
+  const uint32_t q = wq >> 1, e = wq & 1u;   // word 2q is b0, word 2q+1 is b1
+  uint32_t *fw = reinterpret_cast<uint32_t *>(P.frag);
 #pragma unroll
   for (int li = 0; li < 3; li++) {
     int n = 3 * (int)s + li;
     if (n >= 8 * NT) continue;
 #pragma unroll
-    for (int jlo = 0; jlo < 2; jlo++) {
-      const int k = 2 * jlo;
-      const uint32_t j = ((wq & 1u) << 1) | (uint32_t)jlo;
-      uint2 fr;
-      fr.x = pack4(l[li][k], l[li][4 + k], l[li][8 + k], l[li][12 + k]);
-      fr.y = pack4(l[li][k + 1], l[li][5 + k], l[li][9 + k], l[li][13 + k]);
-      size_t idx = ((((size_t)blk * NT + (uint32_t)(n / 8)) * 2u + (j >> 1)) * 32u +
-                    (uint32_t)(n % 8) * 4u + q) * 2u + (j & 1u);
-      P.frag[idx] = fr;
+    for (int j = 0; j < 4; j++) {
+      const size_t idx = ((((size_t)blk * NT + (uint32_t)(n / 8)) * 2u + (uint32_t)(j >> 1)) * 32u +
+                          (uint32_t)(n % 8) * 4u + q) * 2u + (uint32_t)(j & 1);
+      fw[2 * idx + e] = pack4(l[li][j], l[li][4 + j], l[li][8 + j], l[li][12 + j]);
     }
   }
+  return part;
 }
 
 // ---- one row over a thread-block cluster ------------------------------------
@@ -128,7 +137,6 @@ __device__ __forceinline__ void quantize_word(const float (&v)[16], float mul, b
 // share one row: each owns a run of columns starting on a packed-word
 // boundary, the row statistics are combined through distributed shared
 // memory, and each CTA quantizes its own words.
-constexpr int kRowCluster = 8;
 
 struct RowSlice {
   uint32_t c0, c1;   // columns [c0, c1) owned by this CTA; c0 % 16 == 0
@@ -148,18 +156,22 @@ __device__ __forceinline__ RowSlice row_slice(uint32_t cols, uint32_t rank) {
 // Quantize this CTA's slice XS (columns [c0, c1) of row s, staged in shared
 // memory) into P once the row's maximum MM and non-finite flag BAD are known
 // cluster-wide.  LIVE is false for the padding rows s >= seq of the last
-// n-tile, whose fragments are written as zeros.  WRITER (one CTA of the
-// cluster) stores the row's scale and flag.  Needs cols % 16 == 0.
+// n-tile, whose fragments are written as zeros.  Rank 0 of the cluster
+// stores the row's scale and flag; rank RANK stores its share of XSUM.
+// Called by every thread of the CTA (it ends in a CTA-wide reduction).
+// Needs cols % 16 == 0.
 __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, float mm, bool bad,
-                                               bool live, bool writer, uint32_t s, uint32_t seq,
+                                               bool live, uint32_t rank, uint32_t s, uint32_t seq,
                                                PrepOut P) {
+  __shared__ long long xred[32];
   const int NT = n_tiles((int)seq);
   float mul = 0.0f, inv = 0.0f;
   const bool ok = live && row_scale(mm, bad, &mul, &inv);
-  if (live && writer && threadIdx.x == 0) {
+  if (live && rank == 0 && threadIdx.x == 0) {
     P.rowinv[s] = inv;
     P.rowflag[s] = !ok;
   }
+  long long part = 0;
   for (uint32_t W = sl.c0 / 16u + threadIdx.x; W < sl.c1 / 16u; W += blockDim.x) {
     float v[16];
     if (ok) {
@@ -170,7 +182,16 @@ __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, flo
         v[4 * v4] = f.x; v[4 * v4 + 1] = f.y; v[4 * v4 + 2] = f.z; v[4 * v4 + 3] = f.w;
       }
     }
-    quantize_word(v, mul, ok, W, s, NT, P);
+    part += quantize_word(v, mul, ok, W, s, NT, P);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) xred[threadIdx.x >> 5] = part;
+  __syncthreads();
+  if (threadIdx.x == 0 && live) {
+    long long t = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += xred[w];
+    P.xsum[s * kRowCluster + rank] = t;
   }
 }
 

@@ -86,9 +86,11 @@ def test_static_workspace_matches_caller_workspace(lib):
 def test_static_workspace_rejects_oversize(lib):
     import torch
     from nelisp_cuda import _lib as L
-    cols = 43680 + 16                      # seq 16 needs 48 bytes per column
+    # seq 16 needs 48 bytes per column plus a 1280-byte tail (row scales,
+    # flags and offset sums): 43664 columns is the widest row that fits
+    cols = 43664 + 16
     assert lib.nl_ternary_workspace_bytes(16, cols) > STATIC_MAX
-    assert lib.nl_ternary_workspace_bytes(16, 43680) <= STATIC_MAX
+    assert lib.nl_ternary_workspace_bytes(16, 43664) <= STATIC_MAX
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     rc = lib.nl_ternary_gemv_static_dev(None, None, None, None, None, 16, 8, cols, stream)
     assert rc == L.NL_ERROR

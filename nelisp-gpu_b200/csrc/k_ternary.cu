@@ -146,6 +146,81 @@ ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
   cl.sync();                      // no CTA leaves while its maximum is read
 }
 
+// Many rows (count * seq >= kPrepRowsMin): one CTA per (row s, problem z),
+// no cluster and no cluster barrier.  Pass 1 reads the row for its maximum
+// and non-finite flag; pass 2 reads it again (from L2) and quantizes one
+// packed word per thread per step.  The CTA's XSUM goes to slot 0 of the row
+// and the other slots are zeroed.  Needs X 16-byte aligned, x_stride % 4 == 0
+// and cols % 16 == 0.
+constexpr int kPrepRowThreads = 256;
+constexpr uint32_t kPrepRowsMin = 32;
+__global__ void __launch_bounds__(kPrepRowThreads)
+ternary_prep_rows_kernel(const float *__restrict__ X, uint64_t x_stride, uint32_t seq,
+                         uint32_t cols, void *ws) {
+  pdl_trigger();                  // the GEMV may start streaming its weights
+  pdl_wait();                     // X may come from the preceding kernel
+  __shared__ float red[kPrepRowThreads / 32];
+  __shared__ long long xred[kPrepRowThreads / 32];
+  const uint32_t s = blockIdx.x, z = blockIdx.y;
+  const int NT = n_tiles((int)seq);
+  const uint32_t wng = cols / 16u;
+  const float4 *xr = reinterpret_cast<const float4 *>(X + z * x_stride + (size_t)s * cols);
+  const PrepOut P = prep_at(ws, (int)seq, cols, z);
+  float m = 0.0f;
+  int bad = 0;
+  for (uint32_t W = threadIdx.x; W < wng; W += blockDim.x) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 f = __ldg(xr + 4u * W + k);
+      m = fmaxf(fmaxf(m, fabsf(f.x)), fmaxf(fabsf(f.y), fmaxf(fabsf(f.z), fabsf(f.w))));
+      bad |= !isfinite(f.x) | !isfinite(f.y) | !isfinite(f.z) | !isfinite(f.w);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  bad = __syncthreads_or(bad);    // also orders red[]
+  float mm = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kPrepRowThreads / 32; w++) mm = fmaxf(mm, red[w]);
+  float mul = 0.0f, inv = 0.0f;
+  const bool ok = row_scale(mm, bad != 0, &mul, &inv);
+  if (threadIdx.x == 0) {
+    P.rowinv[s] = inv;
+    P.rowflag[s] = !ok;
+  }
+  long long part = 0;
+  for (uint32_t W = threadIdx.x; W < wng; W += blockDim.x) {
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 f = ok ? __ldg(xr + 4u * W + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+    }
+    part += quantize_word(v, mul, ok, W, s, NT, P);
+  }
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) xred[threadIdx.x >> 5] = part;
+  __syncthreads();
+  if (threadIdx.x < (unsigned)kRowCluster) {
+    long long t = 0;
+    if (threadIdx.x == 0)
+      for (int w = 0; w < kPrepRowThreads / 32; w++) t += xred[w];
+    P.xsum[s * kRowCluster + threadIdx.x] = t;
+  }
+}
+
+// The GEMV's prep launch: the one-CTA-per-row kernel for many aligned rows,
+// else the clustered one.
+cudaError_t launch_prep_any(const float *X, uint64_t x_stride, uint32_t count, uint32_t seq,
+                            uint32_t cols, void *ws, cudaStream_t st, bool pdl) {
+  if ((uint64_t)count * seq >= kPrepRowsMin && ((uintptr_t)X & 15u) == 0 && x_stride % 4u == 0 &&
+      cols % 16u == 0)
+    return launch_k(ternary_prep_rows_kernel, dim3(seq, count), dim3(kPrepRowThreads), 0, st,
+                    pdl, X, x_stride, seq, cols, ws);
+  return launch_k(ternary_prep_kernel, dim3(kRowCluster * seq, count), dim3(kPrepThreads), 0, st,
+                  pdl, X, x_stride, seq, cols, ws);
+}
+
 // ---------------------------------------------------------------------------
 // Fast path, step 2: the tensor-core GEMV.
 // ---------------------------------------------------------------------------
@@ -1313,10 +1388,12 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
   for (uint32_t s0 = 0; s0 < seq; s0 += kMaxFastSeq) {
     uint32_t ns = min((uint32_t)kMaxFastSeq, seq - s0);
     int NT = n_tiles((int)ns);
-    dim3 pgrid(kRowCluster * ns, count);
-    ternary_prep_kernel<<<pgrid, kPrepThreads, 0, stream>>>(X + (uint64_t)s0 * cols,
-                                                    x_stride, ns, cols, ws);
-    cudaError_t e = cudaPeekAtLastError();
+    // Programmatic launch: the prep's blocks become resident while the
+    // preceding kernel drains and wait (griddepcontrol.wait) before they
+    // read X or write the workspace.
+    cudaError_t e = launch_prep_any(X + (uint64_t)s0 * cols, x_stride, count, ns, cols, ws,
+                                    stream, true);
+    if (e == cudaSuccess) e = cudaPeekAtLastError();
     if (e != cudaSuccess) return e;
     {
       // The short-grid limit is an index into the whole Y; shift it per chunk.
@@ -1359,9 +1436,7 @@ cudaError_t ternary_prep_launch(const float *X, uint64_t x_stride, uint32_t coun
                                 uint32_t seq, uint32_t cols, void *ws, cudaStream_t stream,
                                 bool pdl) {
   if (count == 0 || seq == 0) return cudaSuccess;
-  dim3 pgrid(kRowCluster * seq, count);
-  cudaError_t e = launch_k(ternary_prep_kernel, pgrid, dim3(kPrepThreads), 0, stream, pdl, X,
-                           x_stride, seq, cols, ws);
+  cudaError_t e = launch_prep_any(X, x_stride, count, seq, cols, ws, stream, pdl);
   count_launches(1);
   return e != cudaSuccess ? e : cudaPeekAtLastError();
 }

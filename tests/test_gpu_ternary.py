@@ -491,3 +491,43 @@ def test_host_submit_overlaps_calls_and_waits_in_order():
     assert lib.nl_host_wait(0) == 0
     assert lib.nl_host_wait(tickets[-1] + 1) != 0
     assert b"unknown ticket" in lib.nl_last_error()
+
+
+def test_row_prep_matches_cluster_prep_bitwise():
+    """A batched call over many rows takes the one-CTA-per-row prep; each
+    problem alone takes the clustered prep.  Both must give the same bits,
+    including problems whose rows are flagged (NaN, infinity, values too small
+    to scale) and an all-zero row."""
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(31337)
+    count, seq, out, cols = 40, 1, 512, 2560
+    d = torch.device("cuda")
+    Ws = [pack_trits(rng.integers(-1, 2, size=(out, cols))) for _ in range(count)]
+    S = rng.uniform(0.5, 1.5, count * out).astype(np.float32)
+    X = rng.standard_normal(count * seq * cols).astype(np.float32)
+    X[3 * cols + 7] = np.nan
+    X[5 * cols + 100] = np.inf
+    X[8 * cols:9 * cols] *= np.float32(1e-39)
+    X[11 * cols:12 * cols] = 0.0
+    tW = torch.from_numpy(np.concatenate(Ws).view(np.int32)).to(d)
+    tS = torch.from_numpy(S).to(d)
+    tX = torch.from_numpy(X).to(d)
+    tY = torch.zeros(count * seq * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv_batched(count, tX, seq * cols, tW, out * cols // 16, tS, out, tY, seq * out,
+                             seq, out, cols)
+    torch.cuda.synchronize()
+    batched = tY.cpu().numpy()
+    for z in range(count):
+        y1 = torch.zeros(seq * out, dtype=torch.float32, device=d)
+        dev.ternary_gemv(tX[z * seq * cols:(z + 1) * seq * cols],
+                         tW[z * out * cols // 16:(z + 1) * out * cols // 16],
+                         tS[z * out:(z + 1) * out], y1, seq, out, cols)
+        torch.cuda.synchronize()
+        one = y1.cpu().numpy()
+        got = batched[z * seq * out:(z + 1) * seq * out]
+        assert np.array_equal(got.view(np.uint32), one.view(np.uint32)), z
+        if z in (0, 8, 11):
+            want = nlo.ternary_gemv_rows(X[z * cols:(z + 1) * cols],
+                                         Ws[z], S[z * out:(z + 1) * out], seq, out, cols)
+            assert nlo.tk_err(got, want) < TOL, z

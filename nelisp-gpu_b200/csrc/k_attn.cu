@@ -30,6 +30,7 @@
 #include <string.h>
 
 #include "nl_internal.h"
+#include "ternary_prep.cuh"
 
 namespace nl {
 namespace {
@@ -598,6 +599,50 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
   }
 }
 
+// The decoder's combine: attn_combine_kernel's merge, then the last CTA of
+// sequence row b to finish (ROW_CTR[b] counts the row's heads; that CTA
+// resets it for the next launch) quantizes the row's context C[b] (heads *
+// HD columns) into WS, the O-projection GEMV's activation workspace for
+// g.B rows -- the work of a separate prep launch.  Other CTAs' C values are
+// read through L2 after a fence on both sides of the counter.
+template <int HD>
+__global__ void attn_combine_prep_kernel(const float *__restrict__ part, AttnGeom g,
+                                         float *__restrict__ C, void *ws, int *row_ctr) {
+  pdl_trigger();                 // the O-projection may start streaming its weights
+  pdl_wait();
+  __shared__ float red[32];
+  __shared__ long long xred[32];
+  __shared__ int s_last;
+  const uint32_t bh = blockIdx.x;
+  const uint32_t bb = bh / g.heads, h = bh % g.heads;
+  const float *pp = part + (uint64_t)bh * g.nsplit * (HD + 2);
+  float mm = -INFINITY;
+  for (uint32_t s = 0; s < g.nsplit; s++) mm = fmaxf(mm, pp[(uint64_t)s * (HD + 2)]);
+  for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
+    float ll = 0.0f, oo = 0.0f;
+    for (uint32_t s = 0; s < g.nsplit; s++) {
+      const float *ps = pp + (uint64_t)s * (HD + 2);
+      if (ps[0] > -INFINITY) {
+        float c = expf(ps[0] - mm);
+        ll += ps[1] * c;
+        oo += ps[2 + d] * c;
+      }
+    }
+    C[(uint64_t)bb * g.heads * HD + (uint64_t)h * HD + d] = oo / ll;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(row_ctr + bb, 1) == (int)g.heads - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const uint32_t cols = g.heads * (uint32_t)HD;
+  prep_row_cta(C + (uint64_t)bb * cols, cols, bb, g.B, prep_at(ws, (int)g.B, cols, 0), red, xred);
+  if (threadIdx.x == 0) row_ctr[bb] = 0;
+}
+
 // Reference arithmetic for head sizes the split kernel does not cover: one
 // thread per output lane, two passes, as kernels.el:368-390.
 __global__ void attn_simple_kernel(const float *__restrict__ Q,
@@ -901,7 +946,8 @@ cudaError_t rope_table_launch(float2 *rope, uint32_t maxseq, uint32_t hd, float 
 
 cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, const int *POS,
                                     float *C, const AttnGeom &g, const float2 *rope,
-                                    void *scratch, cudaStream_t st) {
+                                    void *scratch, cudaStream_t st, void *prep_ws,
+                                    int *row_ctr) {
   if (g.B == 0 || g.heads == 0) return cudaSuccess;
   if (!rope_split_ok(g) || !scratch || !aligned16(CK) || !aligned16(CV))
     return cudaErrorInvalidValue;
@@ -920,7 +966,11 @@ cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, cons
       NL_ATTN(HD, 5) NL_ATTN(HD, 6) NL_ATTN(HD, 7) NL_ATTN(HD, 8)                         \
       default: break;                                                                     \
     }                                                                                     \
-    if (e == cudaSuccess)                                                                 \
+    if (e == cudaSuccess && prep_ws && row_ctr)                                           \
+      e = launch_pdl(attn_combine_prep_kernel<HD>, dim3(g.B * g.heads),                   \
+                     dim3(HD < 128 ? HD : 128), 0, st, (const float *)part, g, C, prep_ws,  \
+                     row_ctr);                                                            \
+    else if (e == cudaSuccess)                                                            \
       e = launch_pdl(attn_combine_kernel<HD>, dim3(g.B * g.heads), dim3(HD < 128 ? HD : 128), \
                      0, st, (const float *)part, g, C, (uint64_t)UINT64_MAX);             \
     break;

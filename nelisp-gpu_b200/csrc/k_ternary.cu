@@ -147,11 +147,8 @@ ternary_prep_kernel(const float *__restrict__ X, uint64_t x_stride,
 }
 
 // Many rows (count * seq >= kPrepRowsMin): one CTA per (row s, problem z),
-// no cluster and no cluster barrier.  Pass 1 reads the row for its maximum
-// and non-finite flag; pass 2 reads it again (from L2) and quantizes one
-// packed word per thread per step.  The CTA's XSUM goes to slot 0 of the row
-// and the other slots are zeroed.  Needs X 16-byte aligned, x_stride % 4 == 0
-// and cols % 16 == 0.
+// no cluster and no cluster barrier (prep_row_cta).  Needs X 16-byte
+// aligned, x_stride % 4 == 0 and cols % 16 == 0.
 constexpr int kPrepRowThreads = 256;
 constexpr uint32_t kPrepRowsMin = 32;
 __global__ void __launch_bounds__(kPrepRowThreads)
@@ -159,54 +156,11 @@ ternary_prep_rows_kernel(const float *__restrict__ X, uint64_t x_stride, uint32_
                          uint32_t cols, void *ws) {
   pdl_trigger();                  // the GEMV may start streaming its weights
   pdl_wait();                     // X may come from the preceding kernel
-  __shared__ float red[kPrepRowThreads / 32];
-  __shared__ long long xred[kPrepRowThreads / 32];
+  __shared__ float red[32];
+  __shared__ long long xred[32];
   const uint32_t s = blockIdx.x, z = blockIdx.y;
-  const int NT = n_tiles((int)seq);
-  const uint32_t wng = cols / 16u;
-  const float4 *xr = reinterpret_cast<const float4 *>(X + z * x_stride + (size_t)s * cols);
-  const PrepOut P = prep_at(ws, (int)seq, cols, z);
-  float m = 0.0f;
-  int bad = 0;
-  for (uint32_t W = threadIdx.x; W < wng; W += blockDim.x) {
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float4 f = __ldg(xr + 4u * W + k);
-      m = fmaxf(fmaxf(m, fabsf(f.x)), fmaxf(fabsf(f.y), fmaxf(fabsf(f.z), fabsf(f.w))));
-      bad |= !isfinite(f.x) | !isfinite(f.y) | !isfinite(f.z) | !isfinite(f.w);
-    }
-  }
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  bad = __syncthreads_or(bad);    // also orders red[]
-  float mm = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kPrepRowThreads / 32; w++) mm = fmaxf(mm, red[w]);
-  float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(mm, bad != 0, &mul, &inv);
-  if (threadIdx.x == 0) {
-    P.rowinv[s] = inv;
-    P.rowflag[s] = !ok;
-  }
-  long long part = 0;
-  for (uint32_t W = threadIdx.x; W < wng; W += blockDim.x) {
-    float v[16];
-#pragma unroll
-    for (int k = 0; k < 4; k++) {
-      const float4 f = ok ? __ldg(xr + 4u * W + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-      v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
-    }
-    part += quantize_word(v, mul, ok, W, s, NT, P);
-  }
-  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-  if ((threadIdx.x & 31) == 0) xred[threadIdx.x >> 5] = part;
-  __syncthreads();
-  if (threadIdx.x < (unsigned)kRowCluster) {
-    long long t = 0;
-    if (threadIdx.x == 0)
-      for (int w = 0; w < kPrepRowThreads / 32; w++) t += xred[w];
-    P.xsum[s * kRowCluster + threadIdx.x] = t;
-  }
+  prep_row_cta(X + z * x_stride + (size_t)s * cols, cols, s, seq, prep_at(ws, (int)seq, cols, z),
+               red, xred);
 }
 
 // The GEMV's prep launch: the one-CTA-per-row kernel for many aligned rows,

@@ -654,6 +654,7 @@ struct nl_decoder {
   int *tok = nullptr, *prompt = nullptr, *out_tok = nullptr, *pos = nullptr;
   unsigned long long *keys = nullptr;
   void *ws_qkv = nullptr, *ws_o = nullptr, *ws_gu = nullptr, *ws_d = nullptr, *attn_scr = nullptr;
+  int *attn_ctr = nullptr;       // per sequence row: heads combined (the O prep's trigger)
   float2 *rope = nullptr;   // [max_seq][head_dim / 2] (cos, sin)
   // Peer all-reduce (tensor parallelism): this rank's block of counters,
   // key slots and receive slots, exported to the peers; every rank's block
@@ -795,14 +796,12 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
                             H, false, fast_h ? D->ws_qkv : nullptr, st);
     if (e != cudaSuccess) return cuda_status(e, "step: qkv");
     // RoPE of q and k, the cache append of k and v, and the split-K
-    // attention over positions 0..pos in one kernel (plus the split merge).
+    // attention over positions 0..pos in one kernel; then the split merge,
+    // whose last CTA per sequence row quantizes the row for the O GEMV.
     e = attn_rope_decode_launch(D->qkv, L.ck, L.cv, D->pos, D->ctx, geom, D->rope,
-                                D->attn_scr, st);
+                                D->attn_scr, st, fast_o ? D->ws_o : nullptr,
+                                fast_o ? D->attn_ctr : nullptr);
     if (e != cudaSuccess) return cuda_status(e, "step: attention");
-    if (fast_o) {
-      e = ternary_prep_launch(D->ctx, 0, 1, B, D->hr * hd, D->ws_o, st, true);
-      if (e != cudaSuccess) return cuda_status(e, "step: o prep");
-    }
     po[0].tadd = po[1].tadd = pin[0].tadd = pin[1].tadd = l + 1;
     e = ternary_main_launch(1, D->ctx, 0, L.wo, 0, L.so, 0, nullptr, D->o, 0, B, H, D->hr * hd,
                             false, fast_o ? D->ws_o : nullptr, st, D->par ? &po[0] : nullptr);
@@ -1025,8 +1024,10 @@ static int decoder_build(nl_decoder *D) {
   DALLOC(D->keys, (size_t)B * 8);
   DALLOC(D->ep, 8);
   DALLOC(D->err, 4);
+  DALLOC(D->attn_ctr, (size_t)B * 4);
   if ((e = cudaMemsetAsync(D->ep, 0, 8, D->stream)) != cudaSuccess ||
-      (e = cudaMemsetAsync(D->err, 0, 4, D->stream)) != cudaSuccess)
+      (e = cudaMemsetAsync(D->err, 0, 4, D->stream)) != cudaSuccess ||
+      (e = cudaMemsetAsync(D->attn_ctr, 0, (size_t)B * 4, D->stream)) != cudaSuccess)
     return cuda_status(e, "decoder: counters");
   DALLOC(D->prompt, (size_t)B * c.max_seq * 4);
   DALLOC(D->out_tok, (size_t)B * c.max_seq * 4);

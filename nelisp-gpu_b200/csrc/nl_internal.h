@@ -207,9 +207,12 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // the [maxseq][hd/2] (cos, sin) table rope_table_launch fills.
 cudaError_t rope_table_launch(float2 *rope, uint32_t maxseq, uint32_t hd, float base,
                               cudaStream_t st);
+// With PREP_WS and ROW_CTR (g.B zeroed ints), the combine also quantizes each
+// finished context row into PREP_WS, the O-projection GEMV's workspace.
 cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, const int *POS,
                                     float *C, const AttnGeom &g, const float2 *rope,
-                                    void *scratch, cudaStream_t st);
+                                    void *scratch, cudaStream_t st, void *prep_ws = nullptr,
+                                    int *row_ctr = nullptr);
 size_t attn_rope_scratch_bytes(const AttnGeom &g);   // 0: shape not covered
 // Causal attention over rows 0..seq-1 of B sequences (attn-causal-gqa per
 // sequence): Q / CTX rows of heads*hd floats, K / V rows of kvheads*hd,

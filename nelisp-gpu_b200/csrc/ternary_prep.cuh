@@ -195,6 +195,63 @@ __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, flo
   }
 }
 
+// ---- one row in one CTA --------------------------------------------------------
+// Row S of a problem (XR: cols floats, 16-byte aligned, cols % 16 == 0) by
+// every thread of one CTA (blockDim.x a multiple of 32): pass 1 reads the row
+// for its maximum and non-finite flag, pass 2 reads it again (L2) and
+// quantizes one packed word per thread per step.  The CTA's XSUM goes to
+// slot 0 of the row and the other slots are zeroed.  Loads bypass L1, so the
+// row may have been written by other CTAs of the same kernel (made visible
+// by a fence).  RED / XRED: shared scratch of 32 entries each.
+__device__ __forceinline__ void prep_row_cta(const float *xr_f, uint32_t cols, uint32_t s,
+                                             uint32_t seq, PrepOut P, float *red,
+                                             long long *xred) {
+  const int NT = n_tiles((int)seq);
+  const uint32_t wng = cols / 16u;
+  const float4 *xr = reinterpret_cast<const float4 *>(xr_f);
+  const int nwarp = (int)(blockDim.x >> 5);
+  float m = 0.0f;
+  int bad = 0;
+  for (uint32_t W = threadIdx.x; W < wng; W += blockDim.x) {
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 f = __ldcg(xr + 4u * W + k);
+      m = fmaxf(fmaxf(m, fabsf(f.x)), fmaxf(fabsf(f.y), fmaxf(fabsf(f.z), fabsf(f.w))));
+      bad |= !isfinite(f.x) | !isfinite(f.y) | !isfinite(f.z) | !isfinite(f.w);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  bad = __syncthreads_or(bad);    // also orders red[]
+  float mm = 0.0f;
+  for (int w = 0; w < nwarp; w++) mm = fmaxf(mm, red[w]);
+  float mul = 0.0f, inv = 0.0f;
+  const bool ok = row_scale(mm, bad != 0, &mul, &inv);
+  if (threadIdx.x == 0) {
+    P.rowinv[s] = inv;
+    P.rowflag[s] = !ok;
+  }
+  long long part = 0;
+  for (uint32_t W = threadIdx.x; W < wng; W += blockDim.x) {
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const float4 f = ok ? __ldcg(xr + 4u * W + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+    }
+    part += quantize_word(v, mul, ok, W, s, NT, P);
+  }
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if ((threadIdx.x & 31) == 0) xred[threadIdx.x >> 5] = part;
+  __syncthreads();
+  if (threadIdx.x < (unsigned)kRowCluster) {
+    long long t = 0;
+    if (threadIdx.x == 0)
+      for (int w = 0; w < nwarp; w++) t += xred[w];
+    P.xsum[s * kRowCluster + threadIdx.x] = t;
+  }
+}
+
 // ---- the generic CUDA-core row ------------------------------------------------
 __device__ __forceinline__ float trit_of(uint32_t w, uint32_t f) {
   return (float)(((int32_t)(w << (30u - 2u * f))) >> 30);

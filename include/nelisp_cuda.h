@@ -292,7 +292,7 @@ int nl_selftest_wait_timeout(void);
  * callers that must not let it allocate (the reference's ternary-rows always
  * takes its buffers from the caller).  Returns NL_ERROR with a message when
  * nl_ternary_workspace_bytes(seq, cols) exceeds the maximum (e.g. seq 16 with
- * cols above 43680, seq 1 above 262112).  The first call on a device looks
+ * cols above 43664, seq 1 above 261984).  The first call on a device looks
  * the array's address up with that device current; make it before any
  * stream capture.  Calls that overlap in time share the array and race: the
  * caller serialises them.  Does not synchronise. */

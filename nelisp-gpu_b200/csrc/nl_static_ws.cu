@@ -8,9 +8,10 @@
 // allocating library routine.
 //
 // Nothing in the workspace must start at zero: the prep launch writes every
-// fragment word of the live rows and their scales and flags before the GEMV
-// launch reads them, in stream order, on every call; the padding columns of
-// the last n-tile only reach MMA output columns the epilogue discards.
+// fragment word of the live rows, their scales, flags and offset sums (all
+// eight slots of each live row) before the GEMV launch reads them, in stream
+// order, on every call; the padding columns of the last n-tile only reach MMA
+// output columns the epilogue discards.
 //
 // Calls that overlap in time (different streams, or host threads) share the
 // one array and race; the caller serialises them.

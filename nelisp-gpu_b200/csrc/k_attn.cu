@@ -368,12 +368,15 @@ attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
 // softmax over keys j <= i of (q_i . k_j) / sqrt(hd), context = sum p_j v_j,
 // kv head h / (heads / kvheads).  Here, flash-style in f32 on the CUDA cores
 // (TF32 products would miss the 1e-4 bar): one CTA per (sequence, head,
-// 64-row query block) walks 64-key tiles up to the diagonal with an online
+// 32-row query block) walks 64-key tiles up to the diagonal with an online
 // softmax.  Threads ty*16 .. ty*16+15 own query rows 4ty .. 4ty+3: their
 // scores (4 rows x 4 keys each) and their context columns (4 rows x HD/16),
-// so the running max / sum stay in registers; keys are transposed in shared
-// memory for conflict-free score loads.
-constexpr int kCausalBQ = 64, kCausalBK = 64;
+// so the running max / sum stay in registers.  Q, K and the probabilities
+// are kept transposed in shared memory ([dim][row], [dim][key], [key][row]),
+// so each operand group of four is one 128-bit load: two loads per 16 FMAs
+// for the scores, three per 32 for the context.  Query blocks are issued
+// from the last (the longest causal walk) to the first.
+constexpr int kCausalBK = 64;
 
 struct CausalGeom {
   uint32_t seq, heads, kvheads;
@@ -382,30 +385,56 @@ struct CausalGeom {
   uint64_t limit;                   // invocations (h * seq + i) to compute
 };
 
-template <int HD>
-__global__ void __launch_bounds__(256)
+// Shared-memory strides (floats) of the transposed arrays: four past the
+// row length keeps rows 16-byte aligned and staggers the transposing stores
+// over the banks.
+template <int BQ>
+struct CausalTile {
+  static constexpr int kThreads = 4 * BQ;          // 16 threads per 4 query rows
+  static constexpr int QS = BQ + 4, KS = kCausalBK + 4, PS = BQ + 4;
+};
+
+// Stage ROWS rows x HD columns of SRC (row stride LD, rows past NROWS read
+// as 0) transposed into DST[col * STRIDE + row].  A warp takes 8 rows x 4
+// float4 columns: 64-byte runs from global memory, stores spread over the
+// banks by the padded stride.
+template <int HD, int ROWS, int STRIDE, int NT>
+__device__ __forceinline__ void stage_transposed(float *dst, const float *src, uint64_t ld,
+                                                 uint32_t nrows, int tid) {
+  constexpr int kLogRows = ROWS == 32 ? 5 : 6;
+  static_assert(ROWS == 32 || ROWS == 64, "tile rows");
+  for (int e = tid; e < ROWS * HD / 4; e += NT) {
+    const int r = (e >> 2) & (ROWS - 1), c4 = ((e >> (2 + kLogRows)) << 2) | (e & 3);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if ((uint32_t)r < nrows) v = *reinterpret_cast<const float4 *>(src + (uint64_t)r * ld + 4 * c4);
+    dst[(4 * c4 + 0) * STRIDE + r] = v.x;
+    dst[(4 * c4 + 1) * STRIDE + r] = v.y;
+    dst[(4 * c4 + 2) * STRIDE + r] = v.z;
+    dst[(4 * c4 + 3) * STRIDE + r] = v.w;
+  }
+}
+
+template <int HD, int BQ>
+__global__ void __launch_bounds__(4 * BQ)
 attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
                    const float *__restrict__ V, float *__restrict__ CTX, CausalGeom g) {
+  using T = CausalTile<BQ>;
+  constexpr int NT = T::kThreads;
   constexpr int DPT = HD / 16;                     // context columns per thread
   extern __shared__ __align__(16) float smc[];
-  float *Qs = smc;                                 // [BQ][HD]
-  float *Kt = Qs + kCausalBQ * HD;                 // [HD][BK]
-  float *Vs = Kt + HD * kCausalBK;                 // [BK][HD]
-  float *Ps = Vs + kCausalBK * HD;                 // [BQ][BK + 1]
+  float *Qt = smc;                                 // [HD][QS]
+  float *Kt = Qt + HD * T::QS;                     // [HD][KS]
+  float *Vs = Kt + HD * T::KS;                     // [BK][HD]
+  float *Pt = Vs + kCausalBK * HD;                 // [BK][PS]
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const uint32_t q0 = blockIdx.x * kCausalBQ, h = blockIdx.y, bz = blockIdx.z;
+  const uint32_t q0 = (gridDim.x - 1u - blockIdx.x) * BQ, h = blockIdx.y, bz = blockIdx.z;
   const uint32_t kvh = h / (g.heads / g.kvheads);
   const float *Qb = Q + bz * g.q_batch + (uint64_t)h * HD;
   const float *Kb = K + bz * g.kv_batch + (uint64_t)kvh * HD;
   const float *Vb = V + bz * g.kv_batch + (uint64_t)kvh * HD;
   const float scale = 1.0f / sqrtf((float)HD);
-  for (int e = tid; e < kCausalBQ * HD / 4; e += 256) {
-    const int r = e / (HD / 4), c4 = e % (HD / 4);
-    const uint32_t i = q0 + r;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (i < g.seq) v = *reinterpret_cast<const float4 *>(Qb + i * g.q_row + 4 * c4);
-    reinterpret_cast<float4 *>(Qs + r * HD)[c4] = v;
-  }
+  stage_transposed<HD, BQ, T::QS, NT>(Qt, Qb + (uint64_t)q0 * g.q_row, g.q_row,
+                                      g.seq > q0 ? g.seq - q0 : 0u, tid);
   float m[4], l[4], o[4][DPT];
 #pragma unroll
   for (int a = 0; a < 4; a++) {
@@ -414,25 +443,20 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 #pragma unroll
     for (int c = 0; c < DPT; c++) o[a][c] = 0.0f;
   }
-  const uint32_t kend = min(g.seq, q0 + kCausalBQ);        // keys past the block's last row
+  const uint32_t kend = min(g.seq, q0 + BQ);       // keys past the block's last row
   for (uint32_t k0 = 0; k0 < kend; k0 += kCausalBK) {
     __syncthreads();
-    for (int e = tid; e < kCausalBK * HD / 4; e += 256) {
+    stage_transposed<HD, kCausalBK, T::KS, NT>(Kt, Kb + (uint64_t)k0 * g.kv_row, g.kv_row,
+                                               g.seq - k0, tid);
+    for (int e = tid; e < kCausalBK * HD / 4; e += NT) {
       const int r = e / (HD / 4), c4 = e % (HD / 4);
       const uint32_t j = k0 + r;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (j < g.seq) {
-        kv = *reinterpret_cast<const float4 *>(Kb + j * g.kv_row + 4 * c4);
-        vv = *reinterpret_cast<const float4 *>(Vb + j * g.kv_row + 4 * c4);
-      }
-      Kt[(4 * c4 + 0) * kCausalBK + r] = kv.x;
-      Kt[(4 * c4 + 1) * kCausalBK + r] = kv.y;
-      Kt[(4 * c4 + 2) * kCausalBK + r] = kv.z;
-      Kt[(4 * c4 + 3) * kCausalBK + r] = kv.w;
+      float4 vv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < g.seq) vv = *reinterpret_cast<const float4 *>(Vb + j * g.kv_row + 4 * c4);
       reinterpret_cast<float4 *>(Vs + r * HD)[c4] = vv;
     }
     __syncthreads();
-    // scores: rows 4ty + a, keys 4tx + b
+    // scores: rows 4ty + a, keys 4tx + b, summed over d in order
     float sc[4][4];
 #pragma unroll
     for (int a = 0; a < 4; a++)
@@ -440,10 +464,9 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
       for (int b = 0; b < 4; b++) sc[a][b] = 0.0f;
 #pragma unroll 8
     for (int d = 0; d < HD; d++) {
-      const float4 kk = *reinterpret_cast<const float4 *>(Kt + d * kCausalBK + 4 * tx);
-      float qa[4];
-#pragma unroll
-      for (int a = 0; a < 4; a++) qa[a] = Qs[(4 * ty + a) * HD + d];
+      const float4 kk = *reinterpret_cast<const float4 *>(Kt + d * T::KS + 4 * tx);
+      const float4 qq = *reinterpret_cast<const float4 *>(Qt + d * T::QS + 4 * ty);
+      const float qa[4] = {qq.x, qq.y, qq.z, qq.w};
 #pragma unroll
       for (int a = 0; a < 4; a++) {
         sc[a][0] = fmaf(qa[a], kk.x, sc[a][0]);
@@ -453,6 +476,7 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
       }
     }
     // causal mask, online softmax per row (reductions over the 16 threads of a row)
+    float pr[4][4];
 #pragma unroll
     for (int a = 0; a < 4; a++) {
       const uint32_t i = q0 + 4 * ty + a;
@@ -471,7 +495,7 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 #pragma unroll
       for (int b = 0; b < 4; b++) {
         const float p = mn == -INFINITY ? 0.0f : expf(sc[a][b] - mn);
-        Ps[(4 * ty + a) * (kCausalBK + 1) + 4 * tx + b] = p;
+        pr[a][b] = p;
         rsum += p;
       }
       for (int off = 8; off > 0; off >>= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
@@ -480,19 +504,28 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 #pragma unroll
       for (int c = 0; c < DPT; c++) o[a][c] *= corr;
     }
+    // The probabilities of rows 4ty .. 4ty+3 are written and read by the 16
+    // threads that own those rows, all in one warp.
+#pragma unroll
+    for (int b = 0; b < 4; b++)
+      *reinterpret_cast<float4 *>(Pt + (4 * tx + b) * T::PS + 4 * ty) =
+          make_float4(pr[0][b], pr[1][b], pr[2][b], pr[3][b]);
     __syncwarp();
     // context: rows 4ty + a, columns tx*DPT .. tx*DPT + DPT-1
     const int jn = (int)min((uint32_t)kCausalBK, kend - k0);
     for (int j = 0; j < jn; j++) {
+      const float4 pp = *reinterpret_cast<const float4 *>(Pt + j * T::PS + 4 * ty);
+      const float pa[4] = {pp.x, pp.y, pp.z, pp.w};
       float vv[DPT];
 #pragma unroll
-      for (int c = 0; c < DPT; c++) vv[c] = Vs[j * HD + tx * DPT + c];
-#pragma unroll
-      for (int a = 0; a < 4; a++) {
-        const float p = Ps[(4 * ty + a) * (kCausalBK + 1) + j];
-#pragma unroll
-        for (int c = 0; c < DPT; c++) o[a][c] = fmaf(p, vv[c], o[a][c]);
+      for (int c4 = 0; c4 < DPT / 4; c4++) {
+        const float4 v4 = *reinterpret_cast<const float4 *>(Vs + j * HD + tx * DPT + 4 * c4);
+        vv[4 * c4] = v4.x; vv[4 * c4 + 1] = v4.y; vv[4 * c4 + 2] = v4.z; vv[4 * c4 + 3] = v4.w;
       }
+#pragma unroll
+      for (int a = 0; a < 4; a++)
+#pragma unroll
+        for (int c = 0; c < DPT; c++) o[a][c] = fmaf(pa[a], vv[c], o[a][c]);
     }
   }
 #pragma unroll
@@ -534,9 +567,33 @@ __global__ void attn_causal_simple_kernel(const float *__restrict__ Q, const flo
   }
 }
 
+template <int BQ>
 size_t causal_smem(int hd) {
-  return ((size_t)kCausalBQ * hd + (size_t)hd * kCausalBK + (size_t)kCausalBK * hd +
-          (size_t)kCausalBQ * (kCausalBK + 1)) * sizeof(float);
+  using T = CausalTile<BQ>;
+  return ((size_t)hd * T::QS + (size_t)hd * T::KS + (size_t)kCausalBK * hd +
+          (size_t)kCausalBK * T::PS) * sizeof(float);
+}
+
+// Query block: 32 rows by default (a shorter causal critical path and twice
+// the CTAs; measured faster than 64 rows at 512 and 2048 rows on B200:
+// 126 vs 150 us and 1137 vs 1270 us for 20 heads x 128).
+// NELISP_CAUSAL_BQ=64 selects 64-row blocks.
+template <int HD, int BQ>
+cudaError_t causal_fast(const float *Q, const float *K, const float *V, float *CTX,
+                        const CausalGeom &g, uint32_t batch, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_causal_kernel<HD, BQ>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)causal_smem<BQ>(HD));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const dim3 grid((g.seq + BQ - 1) / BQ, g.heads, batch);
+  attn_causal_kernel<HD, BQ><<<grid, CausalTile<BQ>::kThreads, causal_smem<BQ>(HD), st>>>(
+      Q, K, V, CTX, g);
+  count_launches(1);
+  return cudaPeekAtLastError();
 }
 
 cudaError_t causal_launch(const float *Q, const float *K, const float *V, float *CTX,
@@ -545,26 +602,17 @@ cudaError_t causal_launch(const float *Q, const float *K, const float *V, float 
   const bool fast = (hd == 64 || hd == 128) && aligned16(Q) && aligned16(K) && aligned16(V) &&
                     aligned16(CTX) && g.q_row % 4 == 0 && g.kv_row % 4 == 0 &&
                     g.q_batch % 4 == 0 && g.kv_batch % 4 == 0;
-  cudaError_t e;
   if (fast) {
-    static bool configured = false;
-    if (!configured) {
-      if ((e = cudaFuncSetAttribute(attn_causal_kernel<128>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)causal_smem(128))) != cudaSuccess ||
-          (e = cudaFuncSetAttribute(attn_causal_kernel<64>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)causal_smem(64))) != cudaSuccess)
-        return e;
-      configured = true;
-    }
-    const dim3 grid((g.seq + kCausalBQ - 1) / kCausalBQ, g.heads, batch);
+    static const int forced = [] {
+      const char *v = getenv("NELISP_CAUSAL_BQ");
+      return v ? atoi(v) : 0;
+    }();
+    const bool small = forced != 64;
     if (hd == 128)
-      attn_causal_kernel<128><<<grid, 256, causal_smem(128), st>>>(Q, K, V, CTX, g);
-    else
-      attn_causal_kernel<64><<<grid, 256, causal_smem(64), st>>>(Q, K, V, CTX, g);
-    count_launches(1);
-    return cudaPeekAtLastError();
+      return small ? causal_fast<128, 32>(Q, K, V, CTX, g, batch, st)
+                   : causal_fast<128, 64>(Q, K, V, CTX, g, batch, st);
+    return small ? causal_fast<64, 32>(Q, K, V, CTX, g, batch, st)
+                 : causal_fast<64, 64>(Q, K, V, CTX, g, batch, st);
   }
   for (uint32_t b = 0; b < batch; b++) {
     attn_causal_simple_kernel<<<(unsigned)ceil_div64((uint64_t)g.heads * g.seq, 128), 128, 0, st>>>(

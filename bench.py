@@ -592,7 +592,26 @@ def run_kernel_rows(device, peak, with_cpu, with_upload=True):
         tc = cpu_time(lambda: nlo.decode_attn_b(Qh, Kh, Vh, [float(ctx - 1)], Bn, dim, H, H,
                                                 ctx))
         rows["decode-attn-b B8 H32 ctx4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
-    del Q, CK, CV, Cq, flush
+    del Q, CK, CV, Cq
+    # causal prefill attention at the decoder's prefill shape: 512 rows,
+    # 20 heads x 128 (f32 on the CUDA cores; FFMA-bound)
+    seq, H, hd = PROMPT_LEN, 20, 128
+    Qp = torch.randn(seq * H * hd, generator=g, device=device)
+    Kp = torch.randn(seq * H * hd, generator=g, device=device)
+    Vp = torch.randn(seq * H * hd, generator=g, device=device)
+    Cp = torch.empty(seq * H * hd, device=device)
+    t = timed(lambda: dev.dispatch("attn-causal-gqa", [Qp, Kp, Vp, Cp], [seq, H, H, hd],
+                                   g64(H * seq)))
+    flops = 4.0 * hd * H * seq * (seq + 1) / 2
+    rows["attn-causal-gqa 512x20x128"] = {
+        "us": round(t * 1e6, 2), "TFLOP/s": round(flops / t / 1e12, 2),
+        "frac_of_ffma_nominal": round(flops / t / 1e9 / ffma_peak, 4),
+        "bound": "ffma (f32, 1e-4 bar)"}
+    if with_cpu:
+        Qh, Kh, Vh = Qp.cpu().numpy(), Kp.cpu().numpy(), Vp.cpu().numpy()
+        tc = cpu_time(lambda: nlo.attn_causal_gqa(Qh, Kh, Vh, seq, H, H, hd))
+        rows["attn-causal-gqa 512x20x128"]["cpu_GFLOP/s"] = round(flops / tc / 1e9, 2)
+    del Qp, Kp, Vp, Cp, flush
     torch.cuda.empty_cache()
     if with_upload:            # one process reads the disk; the other ranks skip it
         rows.update(upload_rows())
@@ -703,6 +722,27 @@ def run_decode_profile(args):
     dec.close()
 
 
+def run_attn_profile(args):
+    """Only the causal prefill attention at the decoder's prefill shape
+    (512 rows, 20 heads x 128), warm-up then timed launches: the case ncu
+    captures for that kernel."""
+    import torch
+
+    from nelisp_cuda import dev, load
+    torch.cuda.set_device(0)
+    load()
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    seq, H, hd = PROMPT_LEN, 20, 128
+    Q, K, V = (torch.randn(seq * H * hd, generator=g, device=device) for _ in range(3))
+    C = torch.empty(seq * H * hd, device=device)
+    for _ in range(args.warmup + args.steps):
+        dev.dispatch("attn-causal-gqa", [Q, K, V, C], [seq, H, H, hd], (H * seq + 63) // 64)
+    torch.cuda.synchronize()
+    emit({"attn_profile": True, "launches": args.warmup + args.steps})
+
+
 def cpu_decode_baseline():
     """The CPU model of the decoder (oracle/nl_oracle_decoder.c) on the full
     configuration, batch 1, over a bounded sample: a 2-token prompt and 2
@@ -811,12 +851,16 @@ def main():
                     help="only a short decoder run, batch --batch (the case ncu lists)")
     ap.add_argument("--profile-run", action="store_true",
                     help="only warm-up and timed steps (the case ncu captures)")
+    ap.add_argument("--attn-profile", action="store_true",
+                    help="only causal prefill attention launches (the case ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         run_reference(args)
     elif args.decode_profile:
         run_decode_profile(args)
+    elif args.attn_profile:
+        run_attn_profile(args)
     else:
         run_gpu(args)
 

@@ -714,8 +714,9 @@ def run_decode_profile(args):
 
     from nelisp_cuda.decoder import BITNET_2B, Decoder
     torch.cuda.set_device(0)
-    dec = Decoder(BITNET_2B, max_batch=8, max_seq=64, device=0)
-    prompt = np.random.default_rng(5).integers(0, BITNET_2B["vocab"], size=(args.batch, 4))
+    dec = Decoder(BITNET_2B, max_batch=8, max_seq=args.prompt + 8, device=0)
+    prompt = np.random.default_rng(5).integers(0, BITNET_2B["vocab"],
+                                               size=(args.batch, args.prompt))
     toks, pf, dc = dec.generate(prompt, 4)
     emit({"decode_profile": True, "batch": args.batch, "ms_per_step": dc / 4,
                       "kernels_per_step": dec.info()["kernels_per_step"]})
@@ -849,6 +850,8 @@ def main():
                     help="skip the matmul / softmax / SwiGLU / attention rows")
     ap.add_argument("--decode-profile", action="store_true",
                     help="only a short decoder run, batch --batch (the case ncu lists)")
+    ap.add_argument("--prompt", type=int, default=4,
+                    help="prompt length of --decode-profile (the decode steps' context)")
     ap.add_argument("--profile-run", action="store_true",
                     help="only warm-up and timed steps (the case ncu captures)")
     ap.add_argument("--attn-profile", action="store_true",

@@ -334,3 +334,45 @@ def test_attn_causal_gqa_short_grid(host):
     assert nlo.tk_err(C[:, 0], want[:, 0]) < 1e-4
     assert nlo.tk_err(C[:24, 1], want[:24, 1]) < 1e-4
     assert not C[24:, 1].any()
+
+
+_BQ64_SCRIPT = r"""
+import sys, numpy as np
+sys.path[:0] = [{root!r}, {pkg!r}]
+from nelisp_cuda.host import Host
+h = Host()
+out = {{}}
+for seq, heads, kvheads, hd in ((65, 4, 1, 128), (130, 20, 20, 128), (300, 8, 4, 64)):
+    rng = np.random.default_rng(seq + heads + hd)
+    Q = rng.standard_normal(seq * heads * hd).astype(np.float32)
+    K = rng.standard_normal(seq * kvheads * hd).astype(np.float32)
+    V = rng.standard_normal(seq * kvheads * hd).astype(np.float32)
+    C = h.run2("attn-causal-gqa", [("in", Q), ("in", K), ("in", V), ("out", seq * heads * hd)],
+               [seq, heads, kvheads, hd], (heads * seq + 63) // 64)[0]
+    out[f"{{seq}}_{{heads}}_{{kvheads}}_{{hd}}"] = C
+    out[f"q{{seq}}"], out[f"k{{seq}}"], out[f"v{{seq}}"] = Q, K, V
+np.savez(sys.argv[1], **out)
+"""
+
+
+def test_attn_causal_gqa_64_row_blocks(tmp_path):
+    """The 64-row query blocks (NELISP_CAUSAL_BQ=64, read once per process,
+    hence a subprocess) against the oracle on ragged and GQA shapes."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG, ROOT
+    script = tmp_path / "bq64.py"
+    script.write_text(_BQ64_SCRIPT.format(root=ROOT, pkg=PKG))
+    outp = tmp_path / "bq64.npz"
+    env = dict(os.environ, NELISP_CAUSAL_BQ="64")
+    subprocess.run([sys.executable, str(script), str(outp)], env=env, check=True, cwd=ROOT,
+                   timeout=300)
+    res = np.load(outp)
+    for key in res.files:
+        if key[0] in "qkv":
+            continue
+        seq, heads, kvheads, hd = (int(x) for x in key.split("_"))
+        want = nlo.attn_causal_gqa(res[f"q{seq}"], res[f"k{seq}"], res[f"v{seq}"], seq, heads,
+                                   kvheads, hd)
+        assert nlo.tk_err(res[key], want) < 1e-4, key

@@ -750,6 +750,28 @@ def run_attn_profile(args):
     emit({"attn_profile": True, "launches": args.warmup + args.steps})
 
 
+def run_gemm_profile(args):
+    """Only the prefill ternary GEMM (512 rows x 2560 -> 6912, the tcgen05
+    path for more than 16 rows), warm-up then timed launches: the case ncu
+    captures for that kernel."""
+    import torch
+
+    from nelisp_cuda import dev, load
+    torch.cuda.set_device(0)
+    load()
+    device = torch.device("cuda", 0)
+    seq, out, cols = PROMPT_LEN, 6912, 2560
+    W, S = make_weights(torch, 1, out, cols, 77, device)
+    g = torch.Generator(device=device)
+    g.manual_seed(8)
+    X = torch.randn(seq * cols, generator=g, device=device)
+    Y = torch.empty(seq * out, device=device)
+    for _ in range(args.warmup + args.steps):
+        dev.ternary_gemv(X, W[0], S[0], Y, seq, out, cols)   # library workspace
+    torch.cuda.synchronize()
+    emit({"gemm_profile": True, "launches": args.warmup + args.steps})
+
+
 def cpu_decode_baseline():
     """The CPU model of the decoder (oracle/nl_oracle_decoder.c) on the full
     configuration, batch 1, over a bounded sample: a 2-token prompt and 2
@@ -862,6 +884,8 @@ def main():
                     help="only warm-up and timed steps (the case ncu captures)")
     ap.add_argument("--attn-profile", action="store_true",
                     help="only causal prefill attention launches (the case ncu captures)")
+    ap.add_argument("--gemm-profile", action="store_true",
+                    help="only prefill ternary GEMM launches (the case ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -870,6 +894,8 @@ def main():
         run_decode_profile(args)
     elif args.attn_profile:
         run_attn_profile(args)
+    elif args.gemm_profile:
+        run_gemm_profile(args)
     else:
         run_gpu(args)
 

@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 
 #include "nl_internal.h"
 #include "ternary_prep.cuh"
@@ -42,15 +43,20 @@ namespace nl {
 namespace {
 
 constexpr int kUmmaM = 128;              // output rows per CTA
-constexpr int kUmmaTok = 80;             // sequence rows per CTA
-constexpr int kUmmaN = 3 * kUmmaTok;     // MMA N: (row, limb) columns
 constexpr int kUmmaK = 128;              // K per stage (bytes of int8)
 constexpr int kUmmaStages = 4;
-constexpr uint32_t kTmemCols = 512;      // two 240-column accumulators
+constexpr uint32_t kTmemCols = 512;      // two accumulators of up to 256 columns
 constexpr int kUmmaThreads = 224;        // 7 warps
 constexpr uint32_t kWBytes = kUmmaM * kUmmaK / 4;      // packed weights per stage
 constexpr uint32_t kABytes = kUmmaM * kUmmaK;           // int8 A per stage
-constexpr uint32_t kBBytes = kUmmaN * kUmmaK;           // int8 B per stage
+// Sequence rows per CTA: 80 or 64 (chosen per shape, umma_tok).  MMA N is
+// the (row, limb) columns, 3 * TOK <= 256, and N x 128 B of int8 B per stage.
+template <int TOK>
+struct UmmaTile {
+  static constexpr int N = 3 * TOK;
+  static constexpr uint32_t BBytes = N * kUmmaK;
+  static_assert(N % 48 == 0 && N <= 256 && BBytes % 1024 == 0, "tile");
+};
 constexpr uint32_t kWaitRounds = 4096;
 constexpr uint32_t kSuspendNs = 1000000;
 constexpr uint32_t kTop2 = 0xC0C0C0C0u;
@@ -96,16 +102,19 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return (uint64_t)((addr >> 4) & 0x3FFFu) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) |
          (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: s8 x s8 -> s32, both K-major, M = 128, N = kUmmaN.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kUmmaN >> 3) << 17) |
-                            ((uint32_t)(kUmmaM >> 4) << 24);
+// Instruction descriptor: s8 x s8 -> s32, both K-major, M = 128, N.
+template <int N>
+constexpr uint32_t umma_idesc() {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(kUmmaM >> 4) << 24);
+}
 
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
-                                        uint32_t accumulate) {
+                                        uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate));
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
@@ -188,6 +197,7 @@ umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict_
 // Two MMA issuers take the K stages in turn (one thread issues a tcgen05.mma
 // only every ~50-170 cycles, a 128 x 240 x 32 MMA takes the tensor core ~120),
 // each into its own accumulator; the epilogue adds the two exactly.
+template <int TOK>
 __global__ void __launch_bounds__(kUmmaThreads, 1)
 ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
                     const float *__restrict__ X, const uint32_t *__restrict__ WP,
@@ -195,11 +205,14 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
                     const float *__restrict__ rowinv, const int *__restrict__ rowflag,
                     float *__restrict__ Y, uint32_t seq, uint32_t out, uint32_t cols,
                     int *err) {
+  constexpr int kUmmaN = UmmaTile<TOK>::N;
+  constexpr uint32_t kBBytes = UmmaTile<TOK>::BBytes;
+  constexpr uint32_t kIdesc = umma_idesc<kUmmaN>();
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint8_t *sA = base;                                   // stages x 16 KB (1024-aligned)
-  uint8_t *sB = sA + kUmmaStages * kABytes;             // stages x 30 KB (1024-aligned)
+  uint8_t *sB = sA + kUmmaStages * kABytes;             // stages x N x 128 B (1024-aligned)
   uint8_t *sW = sB + kUmmaStages * kBBytes;             // stages x 4 KB
   uint64_t *full = reinterpret_cast<uint64_t *>(sW + kUmmaStages * kWBytes);
   uint64_t *aready = full + kUmmaStages;
@@ -208,7 +221,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m0 = blockIdx.x * kUmmaM, t0 = blockIdx.y * kUmmaTok;
+  const uint32_t m0 = blockIdx.x * kUmmaM, t0 = blockIdx.y * (uint32_t)TOK;
   const uint32_t nk = cols / kUmmaK;
 
   if (threadIdx.x == 0) {
@@ -266,7 +279,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         const uint32_t a0 = su32(sA + st * kABytes), b0 = su32(sB + st * kBBytes);
 #pragma unroll
         for (int k = 0; k < kUmmaK / 32; k++)
-          umma_i8(acc_d, smem_desc(a0 + 32u * k), smem_desc(b0 + 32u * k),
+          umma_i8(acc_d, smem_desc(a0 + 32u * k), smem_desc(b0 + 32u * k), kIdesc,
                   (!first || k > 0) ? 1u : 0u);
         first = false;
         umma_commit(&empty[st]);      // the stage is free once these MMAs are done
@@ -331,7 +344,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       // Rows the prep flagged (non-finite or unrepresentable): the generic
       // CUDA-core arithmetic, one output row of this warp's 32 at a time.
       const uint32_t wng = cols / 16u, nblk = cols / 128u;
-      for (uint32_t j = 0; j < (uint32_t)kUmmaTok; j++) {
+      for (uint32_t j = 0; j < (uint32_t)TOK; j++) {
         const uint32_t s = t0 + j;
         if (s >= seq) break;
         if (!rowflag[s]) continue;
@@ -374,15 +387,40 @@ EncodeFn encode_fn() {
   return fn;
 }
 
+template <int TOK>
 size_t umma_smem_bytes() {
-  return 1024 + (size_t)kUmmaStages * (kABytes + kBBytes + kWBytes) + 3 * kUmmaStages * 8 + 16 + 16;
+  return 1024 + (size_t)kUmmaStages * (kABytes + UmmaTile<TOK>::BBytes + kWBytes) +
+         3 * kUmmaStages * 8 + 16 + 16;
+}
+
+// Sequence rows per CTA for SEQ rows x OUT outputs: the height whose grid,
+// rounded up to whole waves of one CTA per SM, costs the fewest MMA columns
+// (waves x 3 TOK); ties keep 80.  NELISP_UMMA_TOK=64 or 80 forces one.
+int umma_tok(uint32_t seq, uint32_t out) {
+  static const int forced = [] {
+    const char *v = getenv("NELISP_UMMA_TOK");
+    const int t = v ? atoi(v) : 0;
+    return t == 64 || t == 80 ? t : 0;
+  }();
+  if (forced) return forced;
+  const uint64_t mt = (out + kUmmaM - 1) / kUmmaM;
+  auto cost = [&](uint32_t tok) {
+    const uint64_t ctas = mt * ((seq + tok - 1) / tok);
+    return ((ctas + 147) / 148) * tok;
+  };
+  return cost(64) < cost(80) ? 64 : 80;
+}
+
+uint32_t umma_cols_for(uint32_t seq, int tok) {
+  return (seq + tok - 1) / tok * 3u * (uint32_t)tok;
 }
 
 }  // namespace
 
+// Limb rows of the B operand in the workspace: enough for either tile height.
 uint32_t umma_cols_padded(uint32_t seq) {
-  const uint32_t tiles = (seq + kUmmaTok - 1) / kUmmaTok;
-  return tiles * kUmmaN;
+  const uint32_t a = umma_cols_for(seq, 64), b = umma_cols_for(seq, 80);
+  return a > b ? a : b;
 }
 
 size_t ternary_umma_ws_bytes(uint32_t seq, uint32_t cols) {
@@ -406,6 +444,7 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   int8_t *XB = reinterpret_cast<int8_t *>(ws);
   float *rowinv = reinterpret_cast<float *>((char *)ws + align256((size_t)ncol * cols));
   int *rowflag = reinterpret_cast<int *>((char *)rowinv + align256((size_t)seq * 4));
+  const int tok = umma_tok(seq, out);
   CUtensorMap mw, mb;
   {
     const cuuint64_t dims[2] = {cols / 16u, out}, strides[1] = {(cuuint64_t)cols / 16u * 4u};
@@ -417,17 +456,21 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   }
   {
     const cuuint64_t dims[2] = {cols, ncol}, strides[1] = {cols};
-    const cuuint32_t box[2] = {kUmmaK, kUmmaN}, es[2] = {1, 1};
+    const cuuint32_t box[2] = {kUmmaK, 3u * (uint32_t)tok}, es[2] = {1, 1};
     if (enc(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, XB, dims, strides, box, es,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaSuccess;
   }
   static bool configured = false;
-  const size_t smem = umma_smem_bytes();
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(ternary_umma_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(ternary_umma_kernel<80>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)umma_smem_bytes<80>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ternary_umma_kernel<64>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)umma_smem_bytes<64>());
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -436,10 +479,15 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   cudaError_t e = launch_k(umma_prep_kernel, dim3(seq), dim3(256), 0, st, false, X, cols, XB,
                            rowinv, rowflag);
   if (e != cudaSuccess) return e;
-  const dim3 grid((out + kUmmaM - 1) / kUmmaM, (seq + kUmmaTok - 1) / kUmmaTok);
-  e = launch_pdl(ternary_umma_kernel, grid, dim3(kUmmaThreads), smem, st, mw, mb, X, WP, S, BIAS,
-                 (const float *)rowinv, (const int *)rowflag, Y, seq, out, cols,
-                 wait_flag_device());
+  const dim3 grid((out + kUmmaM - 1) / kUmmaM, (seq + tok - 1) / tok);
+  if (tok == 64)
+    e = launch_pdl(ternary_umma_kernel<64>, grid, dim3(kUmmaThreads), umma_smem_bytes<64>(), st,
+                   mw, mb, X, WP, S, BIAS, (const float *)rowinv, (const int *)rowflag, Y, seq,
+                   out, cols, wait_flag_device());
+  else
+    e = launch_pdl(ternary_umma_kernel<80>, grid, dim3(kUmmaThreads), umma_smem_bytes<80>(), st,
+                   mw, mb, X, WP, S, BIAS, (const float *)rowinv, (const int *)rowflag, Y, seq,
+                   out, cols, wait_flag_device());
   count_launches(2);
   return e != cudaSuccess ? e : cudaPeekAtLastError();
 }

@@ -531,3 +531,66 @@ def test_row_prep_matches_cluster_prep_bitwise():
             want = nlo.ternary_gemv_rows(X[z * cols:(z + 1) * cols],
                                          Ws[z], S[z * out:(z + 1) * out], seq, out, cols)
             assert nlo.tk_err(got, want) < TOL, z
+
+
+_UMMA_TOK_SCRIPT = r"""
+import sys, numpy as np, torch
+sys.path[:0] = [{root!r}, {pkg!r}]
+from nelisp_cuda import dev
+
+
+def pack_trits(t):
+    out, cols = t.shape
+    codes = np.where(t == 1, 1, np.where(t == -1, 3, 0)).astype(np.uint32)
+    w = np.zeros((out, cols // 16), np.uint32)
+    for f in range(16):
+        w |= codes[:, f::16] << np.uint32(2 * f)
+    return w.ravel()
+
+
+rng = np.random.default_rng(9090)
+res = {{}}
+for (seq, out, cols) in [(17, 300, 512), (130, 640, 1024), (512, 6912, 2560)]:
+    t = rng.integers(-1, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, out).astype(np.float32)
+    X = rng.standard_normal(seq * cols).astype(np.float32)
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X, WP.view(np.int32), S))
+    tY = torch.empty(seq * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols)
+    torch.cuda.synchronize()
+    key = f"{{seq}}_{{out}}_{{cols}}"
+    res[key] = tY.cpu().numpy()
+    res["x_" + key], res["w_" + key], res["s_" + key] = X, WP, S
+np.savez(sys.argv[1], **res)
+"""
+
+
+def test_tcgen05_gemm_tile_heights_agree_bitwise(tmp_path):
+    """The prefill GEMM with 64- and with 80-row sequence tiles (forced by
+    NELISP_UMMA_TOK, read once per process, hence subprocesses) sums the same
+    exact integer products: identical bits, and within the GEMV bar of the
+    oracle, ragged last tiles included."""
+    import os
+    import subprocess
+    import sys
+    from conftest import PKG, ROOT
+    script = tmp_path / "tok.py"
+    script.write_text(_UMMA_TOK_SCRIPT.format(root=ROOT, pkg=PKG))
+    res = {}
+    for tok in ("64", "80"):
+        env = dict(os.environ, NELISP_UMMA_TOK=tok)
+        env.pop("NELISP_TERNARY_PATH", None)
+        outp = tmp_path / f"tok{tok}.npz"
+        subprocess.run([sys.executable, str(script), str(outp)], env=env, check=True, cwd=ROOT,
+                       timeout=300)
+        res[tok] = np.load(outp)
+    for key in res["64"].files:
+        if key[0] in "xws":
+            continue
+        assert np.array_equal(res["64"][key].view(np.uint32), res["80"][key].view(np.uint32)), key
+        seq, out, cols = (int(v) for v in key.split("_"))
+        r = res["64"]
+        want = nlo.ternary_gemv_rows(r["x_" + key], r["w_" + key], r["s_" + key], seq, out, cols)
+        assert nlo.tk_err(r[key], want) < TOL, key

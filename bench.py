@@ -22,6 +22,7 @@ arm runs on rank 0 only.
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import statistics
@@ -48,6 +49,24 @@ FALLBACK_HBM_GBS = 6650.0
 def gemv_bytes(out, cols, batch):
     """Algorithmic bytes of one GEMV: packed W, per-row s, x and y."""
     return out * cols // 4 + out * 4 + cols * 4 * batch + out * 4 * batch
+
+
+def gemv_config(batch):
+    """The workload description both arms report (so the two lines name the
+    same configuration)."""
+    return {"workload": "ternary GEMV y=diag(s)(W x), W 4096x4096 2-bit packed, "
+                        f"batch {batch}, {COPIES} distinct weight copies per step",
+            "out": OUT, "cols": COLS, "batch": batch, "copies_per_step": COPIES,
+            "bytes_per_gemv": gemv_bytes(OUT, COLS, batch),
+            "l2": "inputs larger than L2 (271 MB of weights per step per GPU)",
+            "parallelism": "weak: every rank runs its own copies, no collective"}
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
 
 
 def peaks():
@@ -369,14 +388,16 @@ def run_gpu(args):
     # CPU baseline: the oracle port on this box's host cores (rank 0, N = 1)
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        cpu = cpu_baseline(Wh[:1].ravel(), Sh[0], X[0].reshape(-1).cpu().numpy(), batch,
-                           seconds=args.cpu_seconds)
+        cpu = cpu_baseline(batch, seconds=args.cpu_seconds)
 
     kernels = None
     if not args.no_kernels:
         kernels = run_kernel_rows(device, peak, rank == 0 and ws == 1 and not args.no_cpu,
                                   with_upload=rank == 0)
 
+    tp_parity = None
+    if not args.no_decode:
+        tp_parity = tp_parity_check(dist, ws, rank, local)
     decode = None
     if not args.no_decode:
         decode = run_decoder(dist, ws, rank, local, peak)
@@ -394,12 +415,7 @@ def run_gpu(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int8xint8->int32 (exact ternary x 3-limb activations) + f32 epilogue",
             "data": "synthetic (seeded; trits p=1/3, s~U[0.5,1.5], x~N(0,1))",
-            "config": {"workload": "ternary GEMV y=diag(s)(W x), W 4096x4096 2-bit packed, "
-                                   f"batch {batch}, {COPIES} distinct weight copies per step",
-                       "out": OUT, "cols": COLS, "batch": batch, "copies_per_step": COPIES,
-                       "bytes_per_gemv": per_gemv,
-                       "l2": "inputs larger than L2 (271 MB of weights per step per GPU)",
-                       "parallelism": f"weak: {ws} independent replica(s), no collective"},
+            "config": gemv_config(batch),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
@@ -427,6 +443,8 @@ def run_gpu(args):
             line["kernels"] = kernels
         if decode:
             line["decode"] = decode
+        if tp_parity:
+            line["tp_parity"] = tp_parity       # last: it stays in a tail of the output
         emit(line)
     if dist:
         dist.barrier()
@@ -464,7 +482,9 @@ def run_decoder(dist, ws, rank, local, peak):
     rng = np.random.default_rng(512)
     for batch in (1, 8):
         prompt = rng.integers(0, BITNET_2B["vocab"], size=(batch, PROMPT_LEN))
-        dec.generate(prompt[:, :8], 4)                  # warm-up: capture, attributes, NCCL
+        # warm-up at the timed prompt length: the step graph for this prompt,
+        # the batched prefill's buffers and its collectives' first use
+        dec.generate(prompt, 2)
         toks, pf, dc = dec.generate(prompt, GEN_STEPS)
         t = torch.tensor([pf, dc], device=torch.device("cuda", local))
         if dist:
@@ -481,12 +501,89 @@ def run_decoder(dist, ws, rank, local, peak):
             "bytes_per_step_per_gpu": int(nbytes),
             "achieved_GBs_per_gpu": round(gbs, 1),
             "frac_of_hbm": round(gbs / peak, 4),
-            "tokens_head": [int(v) for v in toks[0, :8]],
+            "tokens_sha256_16": hashlib.sha256(
+                np.ascontiguousarray(toks, dtype="<i4").tobytes()).hexdigest()[:16],
         }
     res["kernels_per_step"] = dec.info()["kernels_per_step"]
     res["shard_rank0"] = {k: info[k] for k in ("kv_heads", "ffn", "vocab")}
     dec.close()
     return res
+
+
+# Tensor-parallel parity: the BitNet-2B layer shapes (20 heads over 20 KV
+# heads of 128, FFN 6912) on 2 layers with an odd vocabulary, so that every
+# TP size splits heads, FFN blocks and vocabulary rows unevenly where they do
+# not divide (TP = 8: heads 3,3,3,3,2,2,2,2; FFN blocks 7 x 6 + 6 x 2).
+TP_CHECK_CFG = dict(hidden=2560, layers=2, heads=20, kv_heads=20, head_dim=128, ffn=6912,
+                    vocab=5003, rms_eps=1e-5, rope_base=10000.0, seed=29)
+TP_TOL = 1e-4        # logits, tk-err per (position, sequence): the decoder tests' bar
+
+
+def tp_parity_check(dist, ws, rank, local):
+    """Every rank builds its shard of the TP_CHECK_CFG decoder; the ranks
+    decode together (two runs: a short prompt stepped through the decode
+    graph, and a 12-token prompt through the batched prefill), the logits of
+    every rank's vocabulary rows are gathered, and rank 0 compares them with
+    the CPU model (oracle/nl_oracle_decoder.c) at every position both have.
+    Returns the summary on rank 0 (None elsewhere)."""
+    import numpy as np
+
+    from nelisp_cuda.decoder import Decoder, nccl_unique_id
+    nid = None
+    if ws > 1:
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    runs = [(2, 5, 6), (3, 12, 4)]            # (batch, prompt, steps)
+    max_seq = 16
+    rng = np.random.default_rng(77)
+    prompts = [rng.integers(0, TP_CHECK_CFG["vocab"], size=(b, p)) for b, p, _ in runs]
+    dec = Decoder(TP_CHECK_CFG, max_batch=3, max_seq=max_seq, tp_rank=rank, tp_size=ws,
+                  nccl_id=nid, keep_logits=True, device=local)
+    info = dec.info()
+    mine = []
+    for (b, p, steps), prompt in zip(runs, prompts):
+        toks, _, _ = dec.generate(prompt, steps)
+        mine.append((toks, dec.logits()[:, :b].copy()))
+    dec.close()
+    parts = [None] * ws
+    if dist:
+        dist.all_gather_object(parts, (info["vocab_begin"], info["kv_heads"], info["ffn"], mine))
+    else:
+        parts = [(info["vocab_begin"], info["kv_heads"], info["ffn"], mine)]
+    if rank != 0:
+        return None
+    import oracle as nlo
+    nlo.set_threads(host_cores())
+    parts.sort(key=lambda q: q[0])
+    worst, tokens_equal, ranks_agree, checksum, hashes = 0.0, True, True, 0.0, []
+    for i, ((b, p, steps), prompt) in enumerate(zip(runs, prompts)):
+        full = np.concatenate([q[3][i][1] for q in parts], axis=2)       # [max_seq, b, vocab]
+        toks = parts[0][3][i][0]
+        ranks_agree &= all(np.array_equal(q[3][i][0], toks) for q in parts)
+        want_t, want_lg = nlo.decoder_generate(dict(TP_CHECK_CFG, max_batch=b, max_seq=max_seq),
+                                               prompt, steps, keep_logits=True)
+        batched = b * (p - 1) > 16          # positions 0..p-2 ran in the batched prefill
+        first = p - 1 if batched else 0
+        for pos in range(first, p + steps - 1):
+            for bb in range(b):
+                worst = max(worst, nlo.tk_err(full[pos, bb], want_lg[pos, bb]))
+        checksum += float(np.abs(full[first:p + steps - 1].astype(np.float64)).sum())
+        for bb in range(b):
+            for j in range(steps):
+                top2 = np.sort(want_lg[p - 1 + j, bb])[-2:]
+                if top2[1] - top2[0] < 1e-3 * max(1.0, abs(float(top2[1]))):
+                    break                    # a near tie: later tokens may differ legitimately
+                tokens_equal &= bool(toks[bb, j] == want_t[bb, j])
+        hashes.append(hashlib.sha256(np.ascontiguousarray(toks, "<i4").tobytes()).hexdigest()[:16])
+    return {"config": "hidden 2560, 2 layers, 20 heads / 20 kv heads x 128, ffn 6912, "
+                      "vocab 5003; runs (batch, prompt, steps) = " + str(runs),
+            "tp": ws,
+            "shards": [{"kv_heads": q[1], "ffn": q[2]} for q in parts],
+            "max_tk_err": float(f"{worst:.3e}"), "tol": TP_TOL,
+            "tokens_equal": bool(tokens_equal), "ranks_agree": bool(ranks_agree),
+            "logits_abs_sum": float(f"{checksum:.9e}"), "tokens_sha256_16": hashes,
+            "ok": bool(worst < TP_TOL and tokens_equal and ranks_agree)}
 
 
 def run_kernel_rows(device, peak, with_cpu, with_upload=True):
@@ -578,27 +675,41 @@ def run_kernel_rows(device, peak, with_cpu, with_upload=True):
         tc = cpu_time(lambda: nlo.silu_mul(gh, uh, n), 5)
         rows["silu-mul 16x11008"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
     del Gt, U, O
-    # decode attention: B 8, 32 heads x 128, context 4096; the
-    # cache holds keys already rotated (RoPE is applied when a key is appended)
+    # decode attention: B 8, 32 heads x 128, context 4096 as the
+    # configuration states it: RoPE (base 10000) of q and of the new key at
+    # position 4095, the append of key and value, softmax attention over the
+    # 4096 positions (scale 1/sqrt(128)) -- nl_decode_attn_rope_dev, one
+    # pass; the cache holds the earlier keys already rotated
     Bn, H, hd, ctx = 8, 32, 128, 4096
     dim = H * hd
-    Q = torch.randn(Bn * dim, generator=g, device=device)
+    QKV = torch.randn(Bn * 3 * dim, generator=g, device=device)
     CK = torch.randn(Bn * ctx * dim, generator=g, device=device)
     CV = torch.randn(Bn * ctx * dim, generator=g, device=device)
-    POS = torch.tensor([float(ctx - 1)], device=device)
+    POSi = torch.tensor([ctx - 1], dtype=torch.int32, device=device)
     Cq = torch.empty(Bn * dim, device=device)
+    t = timed(lambda: dev.decode_attn_rope(QKV, CK, CV, POSi, Cq, Bn, H, H, hd, ctx, 10000.0))
+    nbytes = (2 * Bn * (ctx - 1) * dim * 4 + 2 * Bn * dim * 4      # cached K, V read; new row written
+              + Bn * 3 * dim * 4 + Bn * dim * 4)                   # q|k|v in, context out
+    rows["decode-attn B8 H32 ctx4096 (RoPE q/k + append + attention)"] = {
+        "us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
+        "frac_of_hbm": round(nbytes / t / 1e9 / peak, 4), "bytes": nbytes, "bound": "hbm",
+        "entry": "nl_decode_attn_rope_dev"}
+    # the registry's decode-attn-b on the same cache (q taken as given)
+    POS = torch.tensor([float(ctx - 1)], device=device)
+    Q = QKV[:Bn * dim].contiguous()
     t = timed(lambda: dev.dispatch("decode-attn-b", [Q, CK, CV, POS, Cq], [Bn, dim, H, H, ctx],
                                    g64(Bn * dim)))
     nbytes = 2 * Bn * ctx * dim * 4 + 2 * Bn * dim * 4
     rows["decode-attn-b B8 H32 ctx4096"] = {
         "us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
-        "frac_of_hbm": round(nbytes / t / 1e9 / peak, 4), "bytes": nbytes, "bound": "hbm"}
+        "frac_of_hbm": round(nbytes / t / 1e9 / peak, 4), "bytes": nbytes, "bound": "hbm",
+        "entry": "nl_dispatch_dev decode-attn-b (registry op; no RoPE)"}
     if with_cpu:
         Qh, Kh, Vh = Q.cpu().numpy(), CK.cpu().numpy(), CV.cpu().numpy()
         tc = cpu_time(lambda: nlo.decode_attn_b(Qh, Kh, Vh, [float(ctx - 1)], Bn, dim, H, H,
                                                 ctx))
         rows["decode-attn-b B8 H32 ctx4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
-    del Q, CK, CV, Cq
+    del Q, QKV, CK, CV, Cq
     # causal prefill attention at the decoder's prefill shape: 512 rows,
     # 20 heads x 128 (f32 on the CUDA cores; FFMA-bound)
     seq, H, hd = PROMPT_LEN, 20, 128
@@ -694,24 +805,59 @@ def upload_rows():
     return rows
 
 
-def cpu_baseline(WP, S, X, batch, seconds=10.0):
+def cpu_gemv_problems(batch, n_mats=8, seed=1234):
+    """N_MATS distinct seeded 4096x4096 problems for the CPU legs (cycled, so
+    the weights do not all stay in one core's cache)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    Ws, Ss, Xs = [], [], []
+    for _ in range(n_mats):
+        t = rng.integers(0, 3, size=(OUT, COLS // 16, 16))
+        codes = np.array([0, 1, 3], np.uint32)[t]
+        Ws.append((codes << (2 * np.arange(16, dtype=np.uint32))).sum(-1).astype(np.uint32).ravel())
+        Ss.append(rng.uniform(0.5, 1.5, OUT).astype(np.float32))
+        Xs.append(rng.standard_normal(batch * COLS).astype(np.float32))
+    return Ws, Ss, Xs
+
+
+def cpu_gemv_step(nlo, probs, batch, n_gemv):
+    Ws, Ss, Xs = probs
+    for i in range(n_gemv):
+        z = i % len(Ws)
+        nlo.ternary_gemv_rows(Xs[z], Ws[z], Ss[z], batch, OUT, COLS)
+
+
+def cpu_gemv_calibrate(nlo, probs, batch, step_s=0.25):
+    """GEMVs per CPU step for about STEP_S seconds of work (4 .. 64)."""
+    t0 = time.perf_counter()
+    cpu_gemv_step(nlo, probs, batch, len(probs[0]))
+    per = (time.perf_counter() - t0) / len(probs[0])
+    return int(min(COPIES, max(4, round(step_s / max(per, 1e-6)))))
+
+
+def cpu_baseline(batch, seconds=10.0):
     """The oracle's ternary GEMV (restated `ternary-rows' with the row scale
-    in every block) on all host threads, timed over a bounded sample."""
+    in every block) on all host threads, over a bounded sample: the same
+    steps as the reference arm, repeated for about SECONDS."""
     import oracle as nlo
     nlo.lib()
+    nlo.set_threads(host_cores())
+    probs = cpu_gemv_problems(batch)
+    n_gemv = cpu_gemv_calibrate(nlo, probs, batch)
+    cpu_gemv_step(nlo, probs, batch, n_gemv)           # warm-up
     n = 0
     t0 = time.perf_counter()
     while True:
-        nlo.ternary_gemv_rows(X, WP, S, batch, OUT, COLS)
+        cpu_gemv_step(nlo, probs, batch, n_gemv)
         n += 1
         el = time.perf_counter() - t0
-        if el >= seconds or n >= 10000:
+        if el >= seconds:
             break
-    per = el / n
+    per = el / (n * n_gemv)
     return {"value": round(gemv_bytes(OUT, COLS, batch) / per / 1e9, 3), "unit": "GB/s",
             "cores": nlo.threads(), "kind": "port",
-            "sample": f"{n} GEMVs 4096x4096 batch {batch} in {el:.1f} s "
-                      "(oracle/nl_oracle.c ternary-rows restatement, OpenMP)"}
+            "sample": f"{n * n_gemv} GEMVs 4096x4096 batch {batch} ({n} steps of {n_gemv}) in "
+                      f"{el:.1f} s (oracle/nl_oracle.c ternary-rows restatement, OpenMP)"}
 
 
 def run_decode_profile(args):
@@ -772,76 +918,73 @@ def run_gemm_profile(args):
     emit({"gemm_profile": True, "launches": args.warmup + args.steps})
 
 
+DECODE_CPU_CTX = PROMPT_LEN + GEN_STEPS // 2     # the average context of the 256 steps
+
+
 def cpu_decode_baseline():
     """The CPU model of the decoder (oracle/nl_oracle_decoder.c) on the full
-    configuration, batch 1, over a bounded sample: a 2-token prompt and 2
-    generated tokens (3 positions, all host threads)."""
-    import numpy as np
-
+    configuration at the benchmark's context: batch 1, two greedy positions
+    at context 640 (the average over the 256 generated tokens after the
+    512-token prompt), the KV cache rows below it filled with seeded values.
+    Weight generation is not timed; all host threads."""
     import oracle as nlo
     from nelisp_cuda.decoder import BITNET_2B
-    cfg = dict(BITNET_2B, max_batch=1, max_seq=4)
-    t0 = time.perf_counter()
-    nlo.decoder_generate(cfg, np.array([[11, 12]]), 1)
-    setup = time.perf_counter() - t0                    # weight generation + 2 positions
-    t0 = time.perf_counter()
-    nlo.decoder_generate(cfg, np.array([[11, 12]]), 2)
-    full = time.perf_counter() - t0                     # weight generation + 3 positions
-    per_tok = max(full - setup, 1e-9)
-    return {"value": round(1.0 / per_tok, 3), "unit": "tok/s", "cores": nlo.threads(),
-            "kind": "port", "sample": "batch 1, one decode position at context 3 "
-            "(difference of two runs, so weight generation is excluded)"}
+    nlo.set_threads(host_cores())
+    steps = 2
+    cfg = dict(BITNET_2B, max_batch=1, max_seq=DECODE_CPU_CTX + steps)
+    sec = nlo.decoder_time_positions(cfg, 1, DECODE_CPU_CTX, steps)
+    return {"value": round(steps / sec, 4), "unit": "tok/s", "cores": nlo.threads(),
+            "kind": "port",
+            "sample": f"batch 1, {steps} decode positions at context {DECODE_CPU_CTX} "
+                      f"({sec:.1f} s; the reference's per-output-lane decode-attn-b and "
+                      "ternary-rows restated, OpenMP)"}
 
 
 # ---- the reference arm ----------------------------------------------------------------------
 
 def run_reference(args):
+    """The reference's arithmetic for the headline path on the host cores:
+    the C restatement of `ternary-rows' (oracle/nl_oracle.c) with the row
+    scale in every block, on all the host threads this process may use (set
+    explicitly: torchrun exports OMP_NUM_THREADS=1).  A step is a bounded
+    sample of the 64-GEMV step, sized to about 0.25 s; rank 0 alone runs."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np
-
     import oracle as nlo
     nlo.lib()
+    nlo.set_threads(host_cores())
     batch = args.batch
-    rng = np.random.default_rng(1234)
-    n_copies = 4                      # a bounded sample of the 64-copy step
-    Ws, Ss, Xs = [], [], []
-    for _ in range(n_copies):
-        t = rng.integers(0, 3, size=(OUT, COLS // 16, 16))
-        codes = np.array([0, 1, 3], np.uint32)[t]
-        Ws.append((codes << (2 * np.arange(16, dtype=np.uint32))).sum(-1).astype(np.uint32).ravel())
-        Ss.append(rng.uniform(0.5, 1.5, OUT).astype(np.float32))
-        Xs.append(rng.standard_normal(batch * COLS).astype(np.float32))
+    probs = cpu_gemv_problems(batch)
+    n_gemv = cpu_gemv_calibrate(nlo, probs, batch)
 
     def step():
-        for z in range(n_copies):
-            nlo.ternary_gemv_rows(Xs[z], Ws[z], Ss[z], batch, OUT, COLS)
+        cpu_gemv_step(nlo, probs, batch, n_gemv)
 
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         step()
-    per = (time.perf_counter() - t0) / args.steps
-    value = n_copies * gemv_bytes(OUT, COLS, batch) / per / 1e9
-    sample = (f"{n_copies} of the step's {COPIES} GEMVs per step (4096x4096, batch {batch}); "
-              "oracle/nl_oracle.c restatement of ternary-rows, OpenMP on all host threads")
+    el = time.perf_counter() - t0
+    per = el / args.steps
+    value = n_gemv * gemv_bytes(OUT, COLS, batch) / per / 1e9
+    sample = (f"{n_gemv} of the step's {COPIES} GEMVs per step (4096x4096, batch {batch}), "
+              f"{args.steps} steps in {el:.1f} s; oracle/nl_oracle.c restatement of "
+              "ternary-rows, OpenMP")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": "ternary GEMV y=diag(s)(W x), W 4096x4096 2-bit packed, "
-                               f"batch {batch}, {COPIES} distinct weight copies per step",
-                   "out": OUT, "cols": COLS, "batch": batch, "copies_per_step": COPIES,
-                   "parallelism": "host cores (reference arm runs on rank 0 only)"},
+        "config": gemv_config(batch),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": nlo.threads(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "note": "the reference's own path (Elisp DSL -> SPIR-V -> Vulkan) cannot run: no "
-                "Emacs, no Vulkan loader or ICD (unavailable on this box)",
+                "Emacs, no Vulkan loader or ICD (unavailable on this box); this arm times its "
+                "algorithm restated in C on the host cores, rank 0 only",
     }
     emit(line)
 

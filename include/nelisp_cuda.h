@@ -229,6 +229,25 @@ int nl_ternary_gemv_batched_dev(uint32_t count, const float *X,
                                 uint32_t cols, void *workspace,
                                 size_t ws_bytes, void *stream);
 
+/* One decode position of attention for BATCH sequences, with the three
+ * dispatches the decode loop makes in the reference fused into one pass:
+ * rope-half on q and on the new key at absolute position POS[0]
+ * (lisp/nelisp-gpu-kernels.el:857-882, half-split pairs (m, m + hd/2),
+ * theta = pos / base^(2m/hd)), cache-append-b of the rotated key and the
+ * value at POS[0] (:358-365), and decode-attn-b over positions 0..POS[0]
+ * with scale 1/sqrt(hd) (:368-390).  QKV holds per sequence row
+ * [heads*hd q | kv_heads*hd k | kv_heads*hd v] (the fused Q|K|V linear's
+ * output); CK / CV are [batch][max_seq][kv_heads*hd] (16-byte aligned) and
+ * hold already-rotated keys; C receives [batch][heads*hd].  POS is one
+ * int32 on the device.  hd is 32, 64, 128 or 256, heads/kv_heads <= 8.
+ * The first call for a (max_seq, hd, base) builds a table in library
+ * memory; make it outside any stream capture.  Does not synchronise. */
+int nl_decode_attn_rope_dev(const float *QKV, float *CK, float *CV,
+                            const int32_t *POS, float *C, uint32_t batch,
+                            uint32_t heads, uint32_t kv_heads,
+                            uint32_t head_dim, uint32_t max_seq,
+                            float rope_base, void *stream);
+
 /* nl_ternary_gemv_batched_dev end to end on host buffers: copies the COUNT
  * activation blocks in from X_HOST, runs the GEMVs on the device-resident
  * weights WP and scales S (device pointers, e.g. from nl_resident_info) and
@@ -291,11 +310,14 @@ int nl_selftest_wait_timeout(void);
  * (2 MiB).  No reference counterpart: an addition of this library for
  * callers that must not let it allocate (the reference's ternary-rows always
  * takes its buffers from the caller).  Returns NL_ERROR with a message when
- * nl_ternary_workspace_bytes(seq, cols) exceeds the maximum (e.g. seq 16 with
- * cols above 43664, seq 1 above 261984).  The first call on a device looks
- * the array's address up with that device current; make it before any
- * stream capture.  Calls that overlap in time share the array and race: the
- * caller serialises them.  Does not synchronise. */
+ * nl_ternary_workspace_bytes(seq, cols) -- the workspace of the fastest path
+ * for the shape -- exceeds the maximum (e.g. seq 16 with cols above 43664,
+ * seq 1 above 261984, seq 512 with cols 2560), and when nl_init has not run
+ * on this process (the call would otherwise have to allocate the library's
+ * wait flag).  The first call on a device looks the array's address up with
+ * that device current; make it before any stream capture.  Calls that
+ * overlap in time share the array and race: the caller serialises them.
+ * Does not synchronise. */
 int nl_ternary_gemv_static_dev(const float *X, const uint32_t *WP,
                                const float *S, const float *BIAS, float *Y,
                                uint32_t seq, uint32_t out, uint32_t cols,

@@ -85,7 +85,7 @@ int main(int argc, char **argv) {
       checks++;
     }
   double flop = 2.0 * (double)M * N * K;
-  printf("matmul %ux%u x %ux%u  gpu=%.6fs  %.1f GFLOP/s  checks=%zu  %s\n", M, K, K, N, dt,
+  printf("matmul %ux%u x %ux%u  gpu=%.4fs  %.1f GFLOP/s  checks=%zu  %s\n", M, K, K, N, dt,
          flop / dt / 1e9, checks, bad ? "FAIL" : "PASS");
   nl_shutdown();
   return bad ? 1 : 0;

@@ -71,6 +71,9 @@ int cuda_status(cudaError_t e, const char *what);
 // host-mapped flag (wait_flag_device(), allocated by nl_init before any
 // capture); the synchronising entry points report and clear it.
 int *wait_flag_device();
+// The flag's device address if it is allocated already, else nullptr; never
+// allocates (for entry points that promise no allocation).
+int *wait_flag_if_allocated();
 bool take_wait_timeout();
 __device__ __forceinline__ void report_wait_timeout(int *err) {
   if (err) {

@@ -355,6 +355,8 @@ int *wait_flag_device() {
   return g_wait_dev;
 }
 
+int *wait_flag_if_allocated() { return g_wait_dev; }
+
 bool take_wait_timeout() {
   if (!g_wait_host || !*(volatile int *)g_wait_host) return false;
   *(volatile int *)g_wait_host = 0;
@@ -1019,6 +1021,66 @@ extern "C" int nl_dispatch_dev(const char *name, uint32_t nbuf, void *const *buf
 // ---- typed entry points -------------------------------------------------------------
 extern "C" size_t nl_ternary_workspace_bytes(uint32_t seq, uint32_t cols) {
   return ternary_ws_bytes_best(1, seq, cols, false);
+}
+
+// The (cos, sin) table of the fused decode attention, kept for the last
+// (maxseq, head size, base) asked for.
+namespace {
+struct RopeTable {
+  float2 *tab = nullptr;
+  uint32_t maxseq = 0, hd = 0;
+  float base = 0.0f;
+} g_rope;
+}  // namespace
+
+extern "C" int nl_decode_attn_rope_dev(const float *QKV, float *CK, float *CV, const int32_t *POS,
+                                       float *C, uint32_t batch, uint32_t heads,
+                                       uint32_t kv_heads, uint32_t head_dim, uint32_t max_seq,
+                                       float rope_base, void *stream) {
+  int rc = ensure_ready();
+  if (rc) return rc;
+  if (batch == 0) return NL_OK;
+  if (heads == 0 || kv_heads == 0 || max_seq == 0 || heads % kv_heads)
+    return set_error(NL_ERROR, "decode-attn-rope: heads %u, kv heads %u, max_seq %u", heads,
+                     kv_heads, max_seq);
+  const AttnGeom geo = attn_geom(batch, heads * head_dim, heads, kv_heads, max_seq,
+                                 (uint64_t)batch * max_seq * kv_heads * head_dim);
+  const size_t scr = attn_rope_scratch_bytes(geo);
+  if (!scr)
+    return set_error(NL_ERROR,
+                     "decode-attn-rope: head size %u (32, 64, 128 or 256) with at most 8 query "
+                     "heads per kv head",
+                     head_dim);
+  if (((uintptr_t)CK | (uintptr_t)CV) & 15u)
+    return set_error(NL_ERROR, "decode-attn-rope: the caches must be 16-byte aligned");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!g_rope.tab || g_rope.maxseq < max_seq || g_rope.hd != head_dim ||
+      g_rope.base != rope_base) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+      cudaGetLastError();
+      return set_error(NL_ERROR, "decode-attn-rope: first call for this shape inside a capture");
+    }
+    cudaDeviceSynchronize();   // the old table may still be read
+    if (g_rope.tab) cudaFree(g_rope.tab);
+    g_rope = RopeTable{};
+    void *p = nullptr;
+    cudaError_t e = cudaMalloc(&p, (size_t)max_seq * (head_dim / 2) * sizeof(float2));
+    if (e != cudaSuccess) return cuda_status(e, "decode-attn-rope: table");
+    if ((e = rope_table_launch((float2 *)p, max_seq, head_dim, rope_base, st)) != cudaSuccess) {
+      cudaFree(p);
+      return cuda_status(e, "decode-attn-rope: table");
+    }
+    g_rope.tab = (float2 *)p;
+    g_rope.maxseq = max_seq;
+    g_rope.hd = head_dim;
+    g_rope.base = rope_base;
+  }
+  void *ws = library_workspace(scr, st);
+  if (!ws) return set_error(NL_ERROR, "decode-attn-rope: no workspace of %zu bytes", scr);
+  return cuda_status(attn_rope_decode_launch(QKV, CK, CV, POS, C, geo, g_rope.tab, ws, st,
+                                             nullptr, nullptr),
+                     "decode-attn-rope");
 }
 
 static int ternary_common(uint32_t count, const float *X, uint64_t xs, const uint32_t *WP,

@@ -5,7 +5,8 @@
 // cudaMalloc on first use (and on any larger request); this variant instead
 // runs the same prep + GEMV launches on g_static_ws, whose device address is
 // looked up once per device.  It calls no cudaMalloc / cudaFree and no
-// allocating library routine.
+// allocating library routine, and refuses to run before nl_init (which
+// allocates the host-mapped flag the kernels' bounded waits report through).
 //
 // Nothing in the workspace must start at zero: the prep launch writes every
 // fragment word of the live rows, their scales, flags and offset sums (all
@@ -63,7 +64,17 @@ using namespace nl;
 extern "C" int nl_ternary_gemv_static_dev(const float *X, const uint32_t *WP, const float *S,
                                           const float *BIAS, float *Y, uint32_t seq,
                                           uint32_t out, uint32_t cols, void *stream) {
-  const size_t need = ternary_ws_bytes(1, seq, cols);
+  // The kernels' bounded waits report through the host-mapped flag that
+  // nl_init allocates; allocating it here would break this entry point's
+  // promise, so a call before nl_init is refused.
+  if (!wait_flag_if_allocated())
+    return set_error(NL_ERROR,
+                     "ternary static: call nl_init first (this entry point allocates "
+                     "nothing, not even the library's context)");
+  // The workspace the fastest path for this shape takes (the value
+  // nl_ternary_workspace_bytes reports), so that no fast path declines for
+  // want of room and the call never silently degrades.
+  const size_t need = ternary_ws_bytes_best(1, seq, cols, false);
   if (need > (size_t)NL_TERNARY_STATIC_WS_BYTES)
     return set_error(NL_ERROR,
                      "ternary static: seq %u x cols %u needs %zu bytes of workspace, above "

@@ -81,6 +81,8 @@ SIGNATURES = {
     "nl_ternary_gemv_batched_dev": (_i, [_u32, _vp, _u64, _vp, _u64, _vp, _u64, _vp, _u64,
                                          _u32, _u32, _u32, _vp, _sz, _vp]),
     "nl_ternary_gemv_static_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp]),
+    "nl_decode_attn_rope_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32,
+                                     ctypes.c_float, _vp]),
     "nl_wait_status": (_i, []),
     "nl_upload_file_ternary": (_i, [ctypes.c_char_p, _u64, _u32, _u32, ctypes.c_int,
                                     ctypes.POINTER(_u32), ctypes.POINTER(_u32)]),

@@ -81,5 +81,17 @@ def ternary_gemv_batched(count, X, x_stride, WP, w_stride, S, s_stride, Y, y_str
                                                  _p(workspace), ws_bytes, _stream(stream)))
 
 
+def decode_attn_rope(QKV, CK, CV, POS, C, batch, heads, kv_heads, head_dim, max_seq,
+                     rope_base=10000.0, stream=None):
+    """One decode position: RoPE of q and the new key at POS[0] (int32 on the
+    device), the cache append of key and value, attention over 0..POS[0]."""
+    for t in (QKV, CK, CV, C):
+        _check_tensor(t, "torch.float32")
+    _check_tensor(POS, "torch.int32")
+    L.check(_lib().nl_decode_attn_rope_dev(_p(QKV), _p(CK), _p(CV), _p(POS), _p(C), batch, heads,
+                                             kv_heads, head_dim, max_seq, rope_base,
+                                             _stream(stream)))
+
+
 def launch_count() -> int:
     return int(L.load().nl_launch_count())

@@ -126,6 +126,7 @@ def _declare(L):
         "nlo_decoder_generate": [ctypes.c_void_p, _u32, _u32, ctypes.POINTER(ctypes.c_int32), _u32,
                                  ctypes.POINTER(ctypes.c_int32), _F],
         "nlo_threads": [],
+        "nlo_decoder_time_positions": [ctypes.c_void_p, _u32, _u32, _u32],
     }
     for name, argt in sigs.items():
         fn = getattr(L, name)
@@ -134,6 +135,7 @@ def _declare(L):
     L.nlo_matmul_sample_ref.restype = ctypes.c_double
     L.nlo_threads.restype = ctypes.c_int
     L.nlo_decoder_generate.restype = ctypes.c_int
+    L.nlo_decoder_time_positions.restype = ctypes.c_double
 
 
 def _f(a):
@@ -550,6 +552,17 @@ def decoder_generate(cfg: dict, prompt, steps: int, keep_logits: bool = False):
     if rc != 0:
         raise RuntimeError(f"nlo_decoder_generate: {rc}")
     return out, lg
+
+
+def decoder_time_positions(cfg: dict, batch: int, ctx: int, steps: int) -> float:
+    """Seconds the CPU model takes for STEPS greedy decode positions at
+    context CTX .. CTX+STEPS-1 (KV cache rows below CTX filled with seeded
+    values; weight generation not timed)."""
+    c = DecoderConfig(**cfg)
+    sec = lib().nlo_decoder_time_positions(ctypes.byref(c), batch, ctx, steps)
+    if sec < 0:
+        raise RuntimeError("nlo_decoder_time_positions: bad arguments")
+    return sec
 
 
 # ---- metrics -------------------------------------------------------------

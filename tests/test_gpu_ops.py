@@ -202,6 +202,83 @@ def test_decode_attn_b(host, B, heads, kvheads, hd, maxseq, pos):
     assert nlo.tk_err(C, want) < 1e-4
 
 
+def test_decode_attn_b_benchmark_shape():
+    """decode-attn-b at exactly the benchmark's configuration (BASELINE
+    batch 8, 32 heads x 128, context 4096, position 4095), on
+    device tensors through nl_dispatch_dev as the benchmark calls it, so the
+    split count the benchmark times is the one checked."""
+    import torch
+    from nelisp_cuda import dev
+    B, H, hd, ctx = 8, 32, 128, 4096
+    dim = H * hd
+    rng = np.random.default_rng(4096)
+    Q = rng.standard_normal(B * dim).astype(np.float32)
+    CK = rng.standard_normal(B * ctx * dim).astype(np.float32)
+    CV = rng.standard_normal(B * ctx * dim).astype(np.float32)
+    d = torch.device("cuda")
+    tQ, tK, tV = (torch.from_numpy(a).to(d) for a in (Q, CK, CV))
+    tP = torch.tensor([float(ctx - 1)], device=d)
+    tC = torch.full((B * dim,), float("nan"), device=d)
+    dev.dispatch("decode-attn-b", [tQ, tK, tV, tP, tC], [B, dim, H, H, ctx], g64(B * dim))
+    torch.cuda.synchronize()
+    want = nlo.decode_attn_b(Q, CK, CV, [float(ctx - 1)], B, dim, H, H, ctx)
+    assert nlo.tk_err(tC.cpu().numpy(), want) < 1e-4
+
+
+def _rope_np(x, pos, hd, base):
+    """rope-half (kernels.el:857-882) of one [heads*hd] row at position POS,
+    in f32: pairs (m, m + hd/2), theta = pos / base^(2m/hd)."""
+    half = hd // 2
+    m = np.arange(half, dtype=np.float32)
+    theta = np.float32(pos) / np.power(np.float32(base), (np.float32(2.0) * m) / np.float32(hd))
+    c, s = np.cos(theta).astype(np.float32), np.sin(theta).astype(np.float32)
+    r = x.reshape(-1, hd).copy()
+    a0, a1 = r[:, :half].copy(), r[:, half:].copy()
+    r[:, :half] = a0 * c - a1 * s
+    r[:, half:] = a1 * c + a0 * s
+    return r.ravel()
+
+
+@pytest.mark.parametrize("B,heads,kvheads,hd,maxseq,pos", [
+    (8, 32, 32, 128, 4096, 4095),   # the benchmark's configuration
+    (2, 20, 20, 128, 700, 511),     # the decoder's head shape, mid-sequence
+    (3, 8, 2, 64, 100, 0),          # GQA, first position
+    (1, 12, 4, 32, 64, 40),
+])
+def test_decode_attn_rope_matches_reference_composition(B, heads, kvheads, hd, maxseq, pos):
+    """nl_decode_attn_rope_dev against the reference's three dispatches run on
+    the CPU: rope-half of q and of the new key at POS, cache-append-b of the
+    rotated key and the value, decode-attn-b over 0..POS (1e-4)."""
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(B * 7 + hd + pos)
+    dim, kvdim = heads * hd, kvheads * hd
+    QKV = rng.standard_normal(B * (dim + 2 * kvdim)).astype(np.float32)
+    CK = rng.standard_normal(B * maxseq * kvdim).astype(np.float32)
+    CV = rng.standard_normal(B * maxseq * kvdim).astype(np.float32)
+    d = torch.device("cuda")
+    tQKV, tK, tV = (torch.from_numpy(a).to(d) for a in (QKV, CK, CV))
+    tP = torch.tensor([pos], dtype=torch.int32, device=d)
+    tC = torch.full((B * dim,), float("nan"), device=d)
+    dev.decode_attn_rope(tQKV, tK, tV, tP, tC, B, heads, kvheads, hd, maxseq, 10000.0)
+    torch.cuda.synchronize()
+    rows = QKV.reshape(B, dim + 2 * kvdim)
+    q = np.concatenate([_rope_np(rows[b, :dim], pos, hd, 10000.0) for b in range(B)])
+    k = np.concatenate([_rope_np(rows[b, dim:dim + kvdim], pos, hd, 10000.0) for b in range(B)])
+    v = np.ascontiguousarray(rows[:, dim + kvdim:]).ravel()
+    ck = nlo.cache_append_b(k, [float(pos)], CK, B, kvdim, maxseq)   # returns a copy
+    cv = nlo.cache_append_b(v, [float(pos)], CV, B, kvdim, maxseq)
+    want = nlo.decode_attn_b(q, ck, cv, [float(pos)], B, dim, heads, kvheads, maxseq)
+    assert nlo.tk_err(tC.cpu().numpy(), want) < 1e-4
+    gk = tK.cpu().numpy().reshape(B, maxseq, kvdim)
+    gv = tV.cpu().numpy().reshape(B, maxseq, kvdim)
+    assert np.array_equal(gv[:, pos], v.reshape(B, kvdim))          # values: copied
+    assert nlo.tk_err(gk[:, pos].ravel(), k) < 1e-5                   # keys: rotated
+    keep = np.ones(maxseq, bool)
+    keep[pos] = False                                                 # nothing else written
+    assert np.array_equal(gk[:, keep], CK.reshape(B, maxseq, kvdim)[:, keep])
+
+
 def test_decode_attn_single(host):
     rng = np.random.default_rng(12)
     heads, kvheads, hd, rows, pos = 8, 8, 128, 64, 40

@@ -229,6 +229,80 @@ def test_gemv_4096_per_row_scale(batch):
     assert nlo.tk_err(tY.cpu().numpy(), want) < TOL
 
 
+# ---- outlier-dominated activation rows ---------------------------------------------
+# The fast paths round each activation row to an integer after scaling it
+# by 2^(21-E), where 2^E <= max|x| < 2^(E+1): every value moves by at most
+# 2^(E-22), so an output moves by at most s * sum_i |t_i| * 2^(E-22) (plus
+# the f32 rounding of the epilogue).  With one entry 10^4 times the rest the
+# small entries keep only a few bits; the reference sums exact +-x in f32.
+# The reference's own metric (tk-err, normalised by the largest output)
+# stays below 1e-5, and every output stays inside the stated bound.
+
+def _outlier_rows(rng, seq, cols, factor):
+    X = rng.standard_normal((seq, cols)).astype(np.float32)
+    for s in range(seq):
+        X[s, rng.integers(0, cols)] = np.float32(factor * (1 if s % 2 == 0 else -1))
+    return X
+
+
+def _check_outlier_bound(y, X, t, S):
+    seq = X.shape[0]
+    exact = (X.astype(np.float64) @ t.T.astype(np.float64)) * S.astype(np.float64)
+    nz = np.abs(t).sum(axis=1).astype(np.float64)              # sum_i |t_i| per row
+    for s in range(seq):
+        E = np.floor(np.log2(np.abs(X[s]).max()))
+        bound = S.astype(np.float64) * nz * 2.0 ** (E - 22)
+        slack = 4 * (np.abs(exact[s]) + bound) * 2.0 ** -24 + 1e-30   # f32 epilogue
+        err = np.abs(y[s].astype(np.float64) - exact[s])
+        assert np.all(err <= bound + slack), (s, float((err - bound - slack).max()))
+
+
+@pytest.mark.parametrize("seq,out,cols,factor", [(1, 1024, 4096, 1e4), (4, 512, 4096, 1e4),
+                                                 (16, 256, 2560, 1e4), (1, 512, 2560, 1e6),
+                                                 (40, 128, 2560, 1e4)])
+def test_outlier_rows_within_stated_bound(seq, out, cols, factor):
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(int(factor) % 1000 + seq)
+    t = rng.integers(-1, 2, size=(out, cols))
+    WP = pack_trits(t)
+    S = rng.uniform(0.5, 1.5, out).astype(np.float32)
+    X = _outlier_rows(rng, seq, cols, factor)
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X.ravel(), WP.view(np.int32), S))
+    tY = torch.empty(seq * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv(tX, tW, tS, tY, seq, out, cols)
+    torch.cuda.synchronize()
+    y = tY.cpu().numpy()
+    want = nlo.ternary_gemv_rows(X.ravel(), WP, S, seq, out, cols)
+    assert nlo.tk_err(y, want) < TOL
+    _check_outlier_bound(y.reshape(seq, out), X, t, S)
+
+
+def test_outlier_rows_batched_streaming_path():
+    """The benchmark's path (many 4096-row problems in one call: the
+    persistent TMA kernel) on outlier rows."""
+    import torch
+    from nelisp_cuda import dev
+    rng = np.random.default_rng(404)
+    count, out, cols = 16, 4096, 4096
+    ts = [rng.integers(-1, 2, size=(out, cols)) for _ in range(count)]
+    WP = np.concatenate([pack_trits(t) for t in ts])
+    S = rng.uniform(0.5, 1.5, count * out).astype(np.float32)
+    X = np.concatenate([_outlier_rows(rng, 1, cols, 1e4) for _ in range(count)])
+    d = torch.device("cuda")
+    tX, tW, tS = (torch.from_numpy(a).to(d) for a in (X.ravel(), WP.view(np.int32), S))
+    tY = torch.empty(count * out, dtype=torch.float32, device=d)
+    dev.ternary_gemv_batched(count, tX, cols, tW, out * cols // 16, tS, out, tY, out, 1, out, cols)
+    torch.cuda.synchronize()
+    y = tY.cpu().numpy().reshape(count, out)
+    for z in range(count):
+        want = nlo.ternary_gemv_rows(X[z], WP[z * out * cols // 16:(z + 1) * out * cols // 16],
+                                     S[z * out:(z + 1) * out], 1, out, cols)
+        assert nlo.tk_err(y[z], want) < TOL
+        _check_outlier_bound(y[z:z + 1], X[z:z + 1], ts[z], S[z * out:(z + 1) * out])
+
+
 def test_gemv_batched_matches_single():
     import torch
     from nelisp_cuda import dev
@@ -452,8 +526,8 @@ def test_batched_host_entry_matches_device_entry(count, seq, out, cols):
 
 
 def test_host_submit_overlaps_calls_and_waits_in_order():
-    """Five nl_ternary_gemv_host_submit calls in flight at once (more than the
-    library's three staging slots), each on its own activations and output
+    """Eleven nl_ternary_gemv_host_submit calls in flight at once (more than the
+    library's eight staging slots, so slots are reused), each on its own activations and output
     buffer: one nl_host_wait on the last ticket completes them all, each with
     the bits of the device entry; an unissued ticket is an error."""
     import ctypes
@@ -468,7 +542,7 @@ def test_host_submit_overlaps_calls_and_waits_in_order():
     d = torch.device("cuda")
     tW = torch.from_numpy(Ws.view(np.int32)).to(d)
     tS = torch.from_numpy(S).to(d)
-    calls = 5
+    calls = 11
     Xs = [torch.from_numpy(rng.standard_normal(count * seq * cols).astype(np.float32)).pin_memory()
           for _ in range(calls)]
     Ys = [torch.full((count * seq * out,), 7.0, dtype=torch.float32).pin_memory()

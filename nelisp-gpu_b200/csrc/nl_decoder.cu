@@ -40,6 +40,7 @@
 
 #include "nl_internal.h"
 #include "nl_rng.h"
+#include "nl_step.h"
 #include "ternary_prep.cuh"
 
 namespace nl {
@@ -678,6 +679,13 @@ struct nl_decoder {
   uint64_t weight_bytes = 0;
   std::vector<void *> allocs;
   uint32_t last_batch = 0, last_positions = 0;
+  // the one-kernel decode step (nl_step.cu), when the shapes allow it
+  bool step_ok = false;
+  nl::StepLayer *step_layers = nullptr;   // [layers], device
+  float *step_h = nullptr;                // [2][max_batch][hidden]
+  unsigned *step_acnt = nullptr, *step_amax = nullptr;
+  long long *step_dpart = nullptr;
+  unsigned long long *step_bar = nullptr;  // [0] barrier arrivals, [1] launches completed
 };
 
 namespace nl {
@@ -764,74 +772,116 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   // Every kernel of the step is launched with programmatic stream
   // serialization and waits for its predecessor before reading anything, so
   // each one's launch overlaps the tail of the one before.
-  e = launch_pdl(k_norm<kNormGather>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
-                 (const int *)D->tok, (const float *)D->embed, D->h, (const float *)nullptr,
-                 (const float *)D->layers[0].gattn, D->x, fast_h ? D->ws_qkv : nullptr, B, H,
-                 eps, PeerIn{});
-  count_launches(1);
-  if (e != cudaSuccess) return cuda_status(e, "step: embed");
   const AttnGeom geom = attn_geom(B, D->hr * hd, D->hr, D->kvr, c.max_seq,
                                   (uint64_t)c.max_batch * c.max_seq * D->kvr * hd);
-  // Tensor parallelism: O / down partials go peer to peer (D->par), or
-  // through NCCL all-reduces.
-  PeerOut po[2] = {};
-  PeerIn pin[2] = {};
-  if (D->par) {
-    for (int set = 0; set < 2; set++) {
-      for (int r = 0; r < D->size; r++) po[set].dst[r] = par_slot(D, D->par_peer[r], set, D->rank);
-      po[set].n = D->size;
-      po[set].ep = D->ep;
-      po[set].tmul = c.layers;
-      pin[set].slots = par_slot(D, D->par_local, set, 0);
-      pin[set].tp = (uint32_t)D->size;
-      pin[set].slot_stride = c.max_batch * H;
-      pin[set].ep = D->ep;
-      pin[set].tmul = c.layers;
-      pin[set].err = D->err;
+  if (D->step_ok && B <= kStepMaxB) {
+    // All layers in one persistent kernel; the LM head and the next token follow.
+    StepArgs a = {};
+    a.layers = D->step_layers;
+    a.L = c.layers;
+    a.B = B;
+    a.H = H;
+    a.hd = hd;
+    a.hr = D->hr;
+    a.kvr = D->kvr;
+    a.fr = D->fr;
+    a.maxseq = c.max_seq;
+    a.max_batch = c.max_batch;
+    a.qkv_rows = D->qkv_rows;
+    a.eps = eps;
+    a.coef = geom.coef;
+    a.nsplit = geom.nsplit;
+    a.chunk = geom.chunk;
+    a.dch = step_down_chunks(D->fr);
+    a.embed = D->embed;
+    a.gfinal = D->gfinal;
+    a.rope = D->rope;
+    a.hbuf = D->step_h;
+    a.qkv = D->qkv;
+    a.ctx = D->ctx;
+    a.o = D->o;
+    a.a = D->a;
+    a.x_final = D->x;
+    a.apart = (float *)D->attn_scr;
+    a.acnt = D->step_acnt;
+    a.amax = D->step_amax;
+    a.dpart = D->step_dpart;
+    a.tok = D->tok;
+    a.pos = D->pos;
+    a.bar = D->step_bar;
+    a.sep = D->step_bar + 1;
+    a.err = D->err;
+    e = step_launch(a, st);
+    count_launches(1);
+    if (e != cudaSuccess) return cuda_status(e, "step: layers");
+  } else {
+    e = launch_pdl(k_norm<kNormGather>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                   (const int *)D->tok, (const float *)D->embed, D->h, (const float *)nullptr,
+                   (const float *)D->layers[0].gattn, D->x, fast_h ? D->ws_qkv : nullptr, B, H,
+                   eps, PeerIn{});
+    count_launches(1);
+    if (e != cudaSuccess) return cuda_status(e, "step: embed");
+    // Tensor parallelism: O / down partials go peer to peer (D->par), or
+    // through NCCL all-reduces.
+    PeerOut po[2] = {};
+    PeerIn pin[2] = {};
+    if (D->par) {
+      for (int set = 0; set < 2; set++) {
+        for (int r = 0; r < D->size; r++) po[set].dst[r] = par_slot(D, D->par_peer[r], set, D->rank);
+        po[set].n = D->size;
+        po[set].ep = D->ep;
+        po[set].tmul = c.layers;
+        pin[set].slots = par_slot(D, D->par_local, set, 0);
+        pin[set].tp = (uint32_t)D->size;
+        pin[set].slot_stride = c.max_batch * H;
+        pin[set].ep = D->ep;
+        pin[set].tmul = c.layers;
+        pin[set].err = D->err;
+      }
     }
-  }
-  for (uint32_t l = 0; l < c.layers; l++) {
-    Layer &L = D->layers[l];
-    e = ternary_main_launch(1, D->x, 0, L.wqkv, 0, L.sqkv, 0, nullptr, D->qkv, 0, B, D->qkv_rows,
-                            H, false, fast_h ? D->ws_qkv : nullptr, st);
-    if (e != cudaSuccess) return cuda_status(e, "step: qkv");
-    // RoPE of q and k, the cache append of k and v, and the split-K
-    // attention over positions 0..pos in one kernel; then the split merge,
-    // whose last CTA per sequence row quantizes the row for the O GEMV.
-    e = attn_rope_decode_launch(D->qkv, L.ck, L.cv, D->pos, D->ctx, geom, D->rope,
-                                D->attn_scr, st, fast_o ? D->ws_o : nullptr,
-                                fast_o ? D->attn_ctr : nullptr);
-    if (e != cudaSuccess) return cuda_status(e, "step: attention");
-    po[0].tadd = po[1].tadd = pin[0].tadd = pin[1].tadd = l + 1;
-    e = ternary_main_launch(1, D->ctx, 0, L.wo, 0, L.so, 0, nullptr, D->o, 0, B, H, D->hr * hd,
-                            false, fast_o ? D->ws_o : nullptr, st, D->par ? &po[0] : nullptr);
-    if (e != cudaSuccess) return cuda_status(e, "step: o");
-    if (!D->par && (rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
-    // tag of this layer's use: ep * layers + l + 1 (never 0: the slots start zeroed)
-    e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
-                   (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
-                   (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps, pin[0]);
-    count_launches(1);
-    if (e != cudaSuccess) return cuda_status(e, "step: ffn norm");
-    e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
-                            false, fast_h ? D->ws_gu : nullptr, st);
-    if (e != cudaSuccess) return cuda_status(e, "step: gate/up");
-    e = launch_pdl(k_silu_prep, dim3(gnorm), dim3(kNormThreads),
-                   (size_t)row_slice_cols(D->fr) * sizeof(float), st, (const float *)D->gu, D->a,
-                   fast_d ? D->ws_d : nullptr, B, D->fr);
-    count_launches(1);
-    if (e != cudaSuccess) return cuda_status(e, "step: swiglu");
-    e = ternary_main_launch(1, D->a, 0, L.wd, 0, L.sd, 0, nullptr, D->d, 0, B, H, D->fr, false,
-                            fast_d ? D->ws_d : nullptr, st, D->par ? &po[1] : nullptr);
-    if (e != cudaSuccess) return cuda_status(e, "step: down");
-    if (!D->par && (rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
-    const bool last = l + 1 == c.layers;
-    e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
-                   (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
-                   (const float *)(last ? D->gfinal : D->layers[l + 1].gattn), D->x,
-                   (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps, pin[1]);
-    count_launches(1);
-    if (e != cudaSuccess) return cuda_status(e, "step: attn norm");
+    for (uint32_t l = 0; l < c.layers; l++) {
+      Layer &L = D->layers[l];
+      e = ternary_main_launch(1, D->x, 0, L.wqkv, 0, L.sqkv, 0, nullptr, D->qkv, 0, B, D->qkv_rows,
+                              H, false, fast_h ? D->ws_qkv : nullptr, st);
+      if (e != cudaSuccess) return cuda_status(e, "step: qkv");
+      // RoPE of q and k, the cache append of k and v, and the split-K
+      // attention over positions 0..pos in one kernel; then the split merge,
+      // whose last CTA per sequence row quantizes the row for the O GEMV.
+      e = attn_rope_decode_launch(D->qkv, L.ck, L.cv, D->pos, D->ctx, geom, D->rope,
+                                  D->attn_scr, st, fast_o ? D->ws_o : nullptr,
+                                  fast_o ? D->attn_ctr : nullptr);
+      if (e != cudaSuccess) return cuda_status(e, "step: attention");
+      po[0].tadd = po[1].tadd = pin[0].tadd = pin[1].tadd = l + 1;
+      e = ternary_main_launch(1, D->ctx, 0, L.wo, 0, L.so, 0, nullptr, D->o, 0, B, H, D->hr * hd,
+                              false, fast_o ? D->ws_o : nullptr, st, D->par ? &po[0] : nullptr);
+      if (e != cudaSuccess) return cuda_status(e, "step: o");
+      if (!D->par && (rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+      // tag of this layer's use: ep * layers + l + 1 (never 0: the slots start zeroed)
+      e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                     (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
+                     (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps, pin[0]);
+      count_launches(1);
+      if (e != cudaSuccess) return cuda_status(e, "step: ffn norm");
+      e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
+                              false, fast_h ? D->ws_gu : nullptr, st);
+      if (e != cudaSuccess) return cuda_status(e, "step: gate/up");
+      e = launch_pdl(k_silu_prep, dim3(gnorm), dim3(kNormThreads),
+                     (size_t)row_slice_cols(D->fr) * sizeof(float), st, (const float *)D->gu, D->a,
+                     fast_d ? D->ws_d : nullptr, B, D->fr);
+      count_launches(1);
+      if (e != cudaSuccess) return cuda_status(e, "step: swiglu");
+      e = ternary_main_launch(1, D->a, 0, L.wd, 0, L.sd, 0, nullptr, D->d, 0, B, H, D->fr, false,
+                              fast_d ? D->ws_d : nullptr, st, D->par ? &po[1] : nullptr);
+      if (e != cudaSuccess) return cuda_status(e, "step: down");
+      if (!D->par && (rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
+      const bool last = l + 1 == c.layers;
+      e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                     (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
+                     (const float *)(last ? D->gfinal : D->layers[l + 1].gattn), D->x,
+                     (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps, pin[1]);
+      count_launches(1);
+      if (e != cudaSuccess) return cuda_status(e, "step: attn norm");
+    }
   }
   const size_t smem_lm = (size_t)(B <= 1 ? 1 : (B <= 2 ? 2 : (B <= 4 ? 4 : (B <= 8 ? 8 : 16)))) *
                          H * sizeof(float);
@@ -1042,6 +1092,31 @@ static int decoder_build(nl_decoder *D) {
     if (attn_rope_scratch_bytes(g) > scr) scr = attn_rope_scratch_bytes(g);
   }
   DALLOC(D->attn_scr, scr + 256);
+  // The one-kernel step (TP = 1, batch <= 8, the head sizes and widths it covers).
+  D->step_ok = step_supported(1, H, hd, D->hr, D->kvr, D->fr, D->size);
+  if (D->step_ok) {
+    std::vector<StepLayer> sl(c.layers);
+    for (uint32_t l = 0; l < c.layers; l++) {
+      const Layer &L = D->layers[l];
+      sl[l] = StepLayer{L.wqkv, L.wo, L.wgu, L.wd, L.sqkv, L.so, L.sgu, L.sd, L.gattn, L.gffn,
+                        L.ck, L.cv};
+    }
+    const uint32_t SB = B < kStepMaxB ? B : kStepMaxB;
+    DALLOC(D->step_layers, sizeof(StepLayer) * c.layers);
+    DALLOC(D->step_h, (size_t)2 * SB * H * 4);
+    DALLOC(D->step_acnt, (size_t)SB * D->kvr * 4);
+    DALLOC(D->step_amax, (size_t)SB * 4);
+    DALLOC(D->step_dpart, step_dpart_bytes(SB, H, D->fr));
+    DALLOC(D->step_bar, 16);
+    if ((e = cudaMemcpyAsync(D->step_layers, sl.data(), sizeof(StepLayer) * c.layers,
+                             cudaMemcpyHostToDevice, D->stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(D->step_acnt, 0, (size_t)SB * D->kvr * 4, D->stream)) !=
+            cudaSuccess ||
+        (e = cudaMemsetAsync(D->step_bar, 0, 16, D->stream)) != cudaSuccess)
+      return cuda_status(e, "decoder: step buffers");
+    if ((e = cudaStreamSynchronize(D->stream)) != cudaSuccess)
+      return cuda_status(e, "decoder: step buffers");
+  }
   if (D->keep_logits) DALLOC(D->logits, (size_t)c.max_seq * B * D->vr * 4);
   if ((rc = set_smem_limits(D))) return rc;
   return cuda_status(cudaStreamSynchronize(D->stream), "decoder: build");
@@ -1363,11 +1438,13 @@ extern "C" int nl_decoder_generate(nl_decoder *D, uint32_t batch, uint32_t promp
   cudaEventDestroy(e1);
   cudaEventDestroy(e2);
   if (rc) return rc;
-  if (D->par) {
+  {
     int herr = 0;
     if ((rc = cuda_status(cudaMemcpy(&herr, D->err, 4, cudaMemcpyDeviceToHost), "generate: err")))
       return rc;
-    if (herr) return set_error(NL_ERROR, "generate: a tensor-parallel peer exchange timed out");
+    if (herr)
+      return set_error(NL_ERROR, D->par ? "generate: a tensor-parallel peer exchange timed out"
+                                        : "generate: a bounded wait of the decode step timed out");
   }
   count_launches(D->kernels_per_step * ((batched ? 0u : prompt_len - 1) + steps));
   if (prefill_ms) *prefill_ms = a;

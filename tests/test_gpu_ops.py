@@ -273,7 +273,10 @@ def test_decode_attn_rope_matches_reference_composition(B, heads, kvheads, hd, m
     gk = tK.cpu().numpy().reshape(B, maxseq, kvdim)
     gv = tV.cpu().numpy().reshape(B, maxseq, kvdim)
     assert np.array_equal(gv[:, pos], v.reshape(B, kvdim))          # values: copied
-    assert nlo.tk_err(gk[:, pos].ravel(), k) < 1e-5                   # keys: rotated
+    # keys: rotated.  At position 4095 one f32 ulp of the angle is 2.4e-4 rad,
+    # so the library's powf / cosf and the host's round it differently: the
+    # attention bar, not the GEMV one
+    assert nlo.tk_err(gk[:, pos].ravel(), k) < 1e-4
     keep = np.ones(maxseq, bool)
     keep[pos] = False                                                 # nothing else written
     assert np.array_equal(gk[:, keep], CK.reshape(B, maxseq, kvdim)[:, keep])

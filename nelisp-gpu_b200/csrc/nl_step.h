@@ -50,13 +50,19 @@ struct StepSmem {
 __host__ __device__ inline uint32_t step_align(uint32_t b) { return (b + 127u) & ~127u; }
 
 // Offsets of the step kernel's shared memory for NST ring stages: the
-// mbarriers, the ring, ACT (the activation fragments of one K chunk, or the
-// attention merge scratch), RED / SACC (the cross-warp sums of a tile) and
+// mbarriers, the ring, ACT (the activation fragments of one K chunk and the
+// rows they are made from, or the attention merge scratch), RED / SACC (the cross-warp sums of a tile) and
 // PRE (the prep's per-word partials and row statistics).
+// Activation fragments of one K chunk: NT n-tiles of int8 limbs.
+__host__ __device__ inline uint32_t step_frag_bytes(uint32_t NT) { return NT * kStepMaxK * 8u; }
+// Sequence rows NT n-tiles hold (three limbs a row).
+__host__ __device__ inline uint32_t step_rows(uint32_t NT) { return 8u * NT / 3u; }
+
 __host__ __device__ inline StepSmem step_layout(uint32_t NT, uint32_t hd, uint32_t grp,
                                                 uint32_t nst) {
   StepSmem s;
-  uint32_t act = NT * kStepMaxK * 8u;
+  // the fragments, then the staged rows they are made from
+  uint32_t act = step_frag_bytes(NT) + step_rows(NT) * kStepMaxK * 4u;
   const uint32_t attn = 2u * (4u * grp * hd + 8u * grp) * 4u;
   if (attn > act) act = attn;
   s.ring = 2u * kStepMaxStages * 8u;

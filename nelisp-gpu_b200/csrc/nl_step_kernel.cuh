@@ -61,10 +61,6 @@ constexpr int kThreads = kCT + 32;        // and the producer warp
 constexpr uint32_t kSuspendNs = 200000;   // a try_wait suspends at most this long
 constexpr uint64_t kWaitNs = 1000000000ull;   // any wait gives up after one second
 constexpr int kAW = 4;                    // warps per attention task (half a CTA)
-// Prep words a thread holds: rows of the n-tiles times the words of a row.
-__host__ __device__ constexpr int prep_items(int NT) {
-  return (int)((((8u * (uint32_t)NT) / 3u) * (kStepMaxK / 16u) + kCT - 1) / kCT);
-}
 constexpr uint32_t kNaN = 0x7fc00000u;
 
 // ---- synchronisation ------------------------------------------------------------
@@ -150,7 +146,7 @@ __device__ __forceinline__ void grid_sync(unsigned long long *bar, unsigned long
   csync();
   if (threadIdx.x == 0) {
     __threadfence();
-    atomicAdd(bar, 1ull);
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], 1;\n" ::"l"(bar) : "memory");
     const uint64_t t0 = gtime();
     for (uint32_t i = 1; ld_acquire_gpu(bar) < target; i++) {
       if ((i & 63u) == 0u) {           // now and then: a wait elsewhere gave up, or time is out
@@ -254,7 +250,7 @@ __device__ __forceinline__ void consume(Ring &r, uint32_t nbw, uint32_t frag, in
 // partials into SACC[16][8 NT + 1] (row, n = 3 s + limb) as the decode GEMV
 // lays it out.
 template <int NT>
-__device__ __noinline__ void tile(Ring &r, uint32_t nbw, uint32_t frag, int warp, int lane,
+__device__ __forceinline__ void tile(Ring &r, uint32_t nbw, uint32_t frag, int warp, int lane,
                                      uint32_t xkey, int *red, int *sacc, int *err) {
   constexpr int CH = TileT<NT>::CH;
   int acc[NT][CH][4];
@@ -320,42 +316,42 @@ __device__ __forceinline__ void given_scale(float mm, float *mul, float *inv, in
 }
 
 // The prep of B activation rows of K columns in this CTA, into shared
-// memory.  LOAD(b, W, v) gives the 16 values of packed word W of row b.
-// NORM: x = (v * rinv) * G, rinv from the row's sum of squares (per-word
-// partials, then a fixed order per row); then the row maximum, its
-// power-of-two scale and the int8 limbs of every value (quantize_word, the
-// prep kernels' format) into FRAG.  GIVEN: the scale comes from MAXB[b]
-// (float bits of the row maximum).  HDST (may be null): v is stored there.
+// memory.  LOAD(b, W, v) gives the 16 values of packed word W of row b,
+// which are staged in XS ([B][K] floats).  NORM: x = (v * rinv) * G, rinv
+// from the row's sum of squares (per-word partials, then a fixed order per
+// row); then the row maximum, its power-of-two scale and the int8 limbs of
+// every value (quantize_word, the prep kernels' format) into FRAG.  GIVEN:
+// the scale comes from MAXB[b] (float bits of the row maximum).  HDST (may
+// be null): v is stored there too.
 enum { kPrepPlain = 0, kPrepNorm = 1, kPrepGiven = 2 };
 template <int MODE, int NT, class Load>
-__device__ __noinline__ void prep_rows(const Load &load, uint32_t B, uint32_t K,
+__device__ __forceinline__ void prep_rows(const Load &load, uint32_t B, uint32_t K,
                                           const float *G, float eps, const unsigned *maxb,
-                                          float *hdst, void *frag, float *pss, float *pmx,
-                                          int *pbad, RowStat *st, int warp, int lane) {
+                                          float *hdst, void *frag, float *xs, float *pss,
+                                          float *pmx, int *pbad, RowStat *st, int warp,
+                                          int lane) {
   const uint32_t nw = K / 16u, n = B * nw;
   const int tid = (int)threadIdx.x;
-  constexpr int kMaxItems = prep_items(NT);
-  float v[kMaxItems][16];
-  if (tid < (int)B) st->xs[tid] = 0ll;
+#pragma unroll 1
+  for (uint32_t k = (uint32_t)tid; k < n; k += kCT) {
+    const uint32_t b = k / nw, W = k % nw;
+    float v[16];
+    load(b, W, v);
+    float4 *x4 = reinterpret_cast<float4 *>(xs + (size_t)b * K + 16u * W);
 #pragma unroll
-  for (int m = 0; m < kMaxItems; m++) {
-    const uint32_t k = (uint32_t)tid + (uint32_t)m * kCT;
-    if (k < n) {
-      const uint32_t b = k / nw, W = k % nw;
-      load(b, W, v[m]);
-      if (hdst) {
-        float4 *d4 = reinterpret_cast<float4 *>(hdst + (size_t)b * K + 16u * W);
+    for (int e = 0; e < 4; e++)
+      x4[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+    if (hdst) {
+      float4 *d4 = reinterpret_cast<float4 *>(hdst + (size_t)b * K + 16u * W);
 #pragma unroll
-        for (int e = 0; e < 4; e++)
-          __stcg(d4 + e, make_float4(v[m][4 * e], v[m][4 * e + 1], v[m][4 * e + 2],
-                                     v[m][4 * e + 3]));
-      }
-      if (MODE == kPrepNorm) {
-        float ss = 0.0f;
+      for (int e = 0; e < 4; e++)
+        __stcg(d4 + e, make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]));
+    }
+    if (MODE == kPrepNorm) {
+      float ss = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 16; e++) ss = fmaf(v[m][e], v[m][e], ss);
-        pss[k] = ss;
-      }
+      for (int e = 0; e < 16; e++) ss = fmaf(v[e], v[e], ss);
+      pss[k] = ss;
     }
   }
   if (MODE == kPrepNorm) {
@@ -370,33 +366,29 @@ __device__ __noinline__ void prep_rows(const Load &load, uint32_t B, uint32_t K,
   }
   csync();
   if (MODE != kPrepGiven) {
+#pragma unroll 1
+    for (uint32_t k = (uint32_t)tid; k < n; k += kCT) {
+      const uint32_t b = k / nw, W = k % nw;
+      float4 *x4 = reinterpret_cast<float4 *>(xs + (size_t)b * K + 16u * W);
+      float mm = 0.0f;
+      int bad = 0;
 #pragma unroll
-    for (int m = 0; m < kMaxItems; m++) {
-      const uint32_t k = (uint32_t)tid + (uint32_t)m * kCT;
-      if (k < n) {
-        const uint32_t b = k / nw, W = k % nw;
-        float mm = 0.0f;
-        int bad = 0;
+      for (int e = 0; e < 4; e++) {
+        float4 f = x4[e];
         if (MODE == kPrepNorm) {
           const float ri = st->rinv[b];
-          const float4 *g4 = reinterpret_cast<const float4 *>(G + 16u * W);
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            const float4 gv = __ldg(g4 + e);
-            v[m][4 * e] = __fmul_rn(__fmul_rn(v[m][4 * e], ri), gv.x);
-            v[m][4 * e + 1] = __fmul_rn(__fmul_rn(v[m][4 * e + 1], ri), gv.y);
-            v[m][4 * e + 2] = __fmul_rn(__fmul_rn(v[m][4 * e + 2], ri), gv.z);
-            v[m][4 * e + 3] = __fmul_rn(__fmul_rn(v[m][4 * e + 3], ri), gv.w);
-          }
+          const float4 gv = __ldg(reinterpret_cast<const float4 *>(G + 16u * W) + e);
+          f.x = __fmul_rn(__fmul_rn(f.x, ri), gv.x);
+          f.y = __fmul_rn(__fmul_rn(f.y, ri), gv.y);
+          f.z = __fmul_rn(__fmul_rn(f.z, ri), gv.z);
+          f.w = __fmul_rn(__fmul_rn(f.w, ri), gv.w);
+          x4[e] = f;
         }
-#pragma unroll
-        for (int e = 0; e < 16; e++) {
-          mm = fmaxf(mm, fabsf(v[m][e]));
-          bad |= !isfinite(v[m][e]);
-        }
-        pmx[k] = mm;
-        pbad[k] = bad;
+        mm = fmaxf(fmaxf(mm, fabsf(f.x)), fmaxf(fmaxf(fabsf(f.y), fabsf(f.z)), fabsf(f.w)));
+        bad |= !isfinite(f.x) | !isfinite(f.y) | !isfinite(f.z) | !isfinite(f.w);
       }
+      pmx[k] = mm;
+      pbad[k] = bad;
     }
     csync();
     if ((uint32_t)warp < B) {
@@ -424,14 +416,26 @@ __device__ __noinline__ void prep_rows(const Load &load, uint32_t B, uint32_t K,
   csync();
   PrepOut P;
   P.frag = reinterpret_cast<uint2 *>(frag);
+  long long *pxs = reinterpret_cast<long long *>(pss);   // the word partials are dead now
+#pragma unroll 1
+  for (uint32_t k = (uint32_t)tid; k < n; k += kCT) {
+    const uint32_t b = k / nw, W = k % nw;
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs + (size_t)b * K + 16u * W);
+    float v[16];
 #pragma unroll
-  for (int m = 0; m < kMaxItems; m++) {
-    const uint32_t k = (uint32_t)tid + (uint32_t)m * kCT;
-    if (k < n) {
-      const uint32_t b = k / nw, W = k % nw;
-      const long long part = quantize_word(v[m], st->mul[b], st->flag[b] == 0, W, b, NT, P);
-      atomicAdd(reinterpret_cast<unsigned long long *>(&st->xs[b]), (unsigned long long)part);
+    for (int e = 0; e < 4; e++) {
+      const float4 f = x4[e];
+      v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
     }
+    pxs[k] = quantize_word(v, st->mul[b], st->flag[b] == 0, W, b, NT, P);
+  }
+  csync();
+  if ((uint32_t)warp < B) {            // the row's offset sum (exact: any order)
+    long long x = 0;
+    for (uint32_t W = (uint32_t)lane; W < nw; W += 32u) x += pxs[warp * nw + W];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    if (lane == 0) st->xs[warp] = x;
   }
   csync();
 }
@@ -456,7 +460,7 @@ struct AttnCtx {
 // merged.  The last split of a (b, kv head) to finish merges all splits
 // into the context rows (attn_combine's order).
 template <int HD>
-__device__ __noinline__ void attn_task(const AttnCtx &C, uint32_t split, uint32_t bkv,
+__device__ __forceinline__ void attn_task(const AttnCtx &C, uint32_t split, uint32_t bkv,
                                           float *scr, int h, int *s_last) {
   constexpr int DPL = HD / 32;
   constexpr int U = 4;
@@ -589,19 +593,37 @@ __device__ __noinline__ void attn_task(const AttnCtx &C, uint32_t split, uint32_
   hsync(h);
   if (*s_last) {
     __threadfence();
+    constexpr int SB = 8;   // splits whose loads are in flight at once
     for (uint32_t e = (uint32_t)hl; e < C.grp * (uint32_t)HD; e += kAW * 32) {
       const uint32_t hq = kvh * C.grp + e / HD, d = e % HD;
       const float *pp = C.apart + ((uint64_t)bb * C.hr + hq) * C.nsplit * (HD + 2);
       float mm = -INFINITY;
-      for (uint32_t s = 0; s < C.nsplit; s++) mm = fmaxf(mm, __ldcg(pp + (uint64_t)s * (HD + 2)));
+      for (uint32_t s0 = 0; s0 < C.nsplit; s0 += SB) {
+        float mv[SB];
+#pragma unroll
+        for (int u = 0; u < SB; u++)
+          mv[u] = s0 + u < C.nsplit ? __ldcg(pp + (uint64_t)(s0 + u) * (HD + 2)) : -INFINITY;
+#pragma unroll
+        for (int u = 0; u < SB; u++) mm = fmaxf(mm, mv[u]);
+      }
       float ll = 0.0f, oo = 0.0f;
-      for (uint32_t s = 0; s < C.nsplit; s++) {
-        const float *ps = pp + (uint64_t)s * (HD + 2);
-        const float m0 = __ldcg(ps);
-        if (m0 > -INFINITY) {
-          const float c = expf(m0 - mm);
-          ll += __ldcg(ps + 1) * c;
-          oo += __ldcg(ps + 2 + d) * c;
+      for (uint32_t s0 = 0; s0 < C.nsplit; s0 += SB) {
+        float mv[SB], lv[SB], ov[SB];
+#pragma unroll
+        for (int u = 0; u < SB; u++) {
+          const bool in = s0 + u < C.nsplit;
+          const float *ps = pp + (uint64_t)(s0 + u) * (HD + 2);
+          mv[u] = in ? __ldcg(ps) : -INFINITY;
+          lv[u] = in ? __ldcg(ps + 1) : 0.0f;
+          ov[u] = in ? __ldcg(ps + 2 + d) : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < SB; u++) {      // in split order, as attn_combine
+          if (mv[u] > -INFINITY) {
+            const float c = expf(mv[u] - mm);
+            ll += lv[u] * c;
+            oo += ov[u] * c;
+          }
         }
       }
       __stcg(C.ctx + (uint64_t)bb * C.hr * HD + (uint64_t)hq * HD + d, oo / ll);
@@ -611,14 +633,11 @@ __device__ __noinline__ void attn_task(const AttnCtx &C, uint32_t split, uint32_
   hsync(h);   // s_last is reused by the next task
 }
 
-// The f32 output of the down GEMV for (b, column i): its chunk sums, scaled.
-__device__ __forceinline__ float down_value(const long long *dpart, uint32_t dch, uint32_t B,
-                                            uint32_t H, const float *sd, float inv, int flag,
-                                            uint32_t b, uint32_t i) {
-  long long tot = 0;
-  for (uint32_t c = 0; c < dch; c++) tot += __ldcg(dpart + ((uint64_t)c * B + b) * H + i);
+// The f32 output of the down GEMV for (b, column i): the exact sum of its
+// chunks' dot products (accumulated in DSUM), scaled.
+__device__ __forceinline__ float down_value(long long tot, float sd, float inv, int flag) {
   if (flag) return __uint_as_float(kNaN);
-  return ((float)tot * inv) * __ldg(sd + i);
+  return ((float)tot * inv) * sd;
 }
 
 // ---- the kernel ---------------------------------------------------------------------------
@@ -687,6 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
   int *pbad = reinterpret_cast<int *>(pss);   // the sums of squares are consumed by then
   RowStat *st = reinterpret_cast<RowStat *>(pmx + kStepMaxB * (kStepMaxK / 16u));
   const uint32_t frag = sa(act);
+  float *xsm = reinterpret_cast<float *>(act + step_frag_bytes(NT));   // staged rows
   const uint32_t xkey = offset_key();
   const unsigned long long nbar = step_barriers(nl);
   const unsigned long long base = __ldcg(A.sep) * nbar * (unsigned long long)G;
@@ -711,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
               v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
             }
           },
-          B, H, Ly.gattn, A.eps, nullptr, lead ? A.hbuf : nullptr, act, pss, pmx, pbad, st, warp,
+          B, H, Ly.gattn, A.eps, nullptr, lead ? A.hbuf : nullptr, act, xsm, pss, pmx, pbad, st, warp,
           lane);
     } else {
       // the previous layer's down GEMV output, scaled as its rows were
@@ -733,22 +753,30 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
               const float4 f = __ldcg(h4 + e);
               v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
             }
+            const long long *dp = A.dpart + (size_t)b * H + 16u * W;
+            long long tot[16];
+            float sc[16];
 #pragma unroll
-            for (int e = 0; e < 16; e++)
-              v[e] = __fadd_rn(v[e], down_value(A.dpart, A.dch, B, H, sd, inv, fl, b,
-                                                16u * W + (uint32_t)e));
+            for (int e = 0; e < 16; e++) {
+              tot[e] = __ldcg(dp + e);
+              sc[e] = __ldg(sd + 16u * W + (uint32_t)e);
+            }
+#pragma unroll
+            for (int e = 0; e < 16; e++) v[e] = __fadd_rn(v[e], down_value(tot[e], sc[e], inv, fl));
           },
-          B, H, Ly.gattn, A.eps, nullptr, lead ? A.hbuf : nullptr, act, pss, pmx, pbad, st, warp,
+          B, H, Ly.gattn, A.eps, nullptr, lead ? A.hbuf : nullptr, act, xsm, pss, pmx, pbad, st, warp,
           lane);
     }
+    const float *sq = Ly.sqkv;
     for (uint32_t t = qr.lo; t < qr.hi; t++) {
+      // the epilogue's scale, requested before the tile's MMAs
+      const float sc = tid < 16 * (int)B ? __ldg(sq + 16u * t + (uint32_t)(tid & 15)) : 0.0f;
       tile<NT>(ring, H / 16u, frag, warp, lane, xkey, red, sacc, err);
       if (tid < 16 * (int)B) {
         const int r = tid & 15, s = tid >> 4;
         const uint32_t oi = 16u * t + (uint32_t)r;
         const long long tot = tile_tot<NT>(sacc, r, s, st->xs[s]);
-        const float y = st->flag[s] ? __uint_as_float(kNaN)
-                                    : ((float)tot * st->inv[s]) * __ldg(Ly.sqkv + oi);
+        const float y = st->flag[s] ? __uint_as_float(kNaN) : ((float)tot * st->inv[s]) * sc;
         __stcg(A.qkv + (uint64_t)s * A.qkv_rows + oi, y);
       }
     }
@@ -776,6 +804,12 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
       ac.coef = A.coef;
       ac.ck = Ly.ck;
       ac.cv = Ly.cv;
+      // this layer's down GEMV accumulates into A.dpart: clear it (the
+      // previous layer's sums were read before the last barrier)
+      {
+        const Range z = share(B * H, G, cta);
+        for (uint32_t i = z.lo + (uint32_t)tid; i < z.hi; i += kCT) __stcg(A.dpart + i, 0ll);
+      }
       for (uint32_t t = 2u * cta + (uint32_t)h; t < ntask; t += 2u * G)
         attn_task<HD>(ac, t % A.nsplit, t / A.nsplit, scr, h, &s_last[h]);
     }
@@ -794,16 +828,17 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
               v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
             }
           },
-          B, qcols, nullptr, 0.0f, nullptr, nullptr, act, pss, pmx, pbad, st, warp, lane);
+          B, qcols, nullptr, 0.0f, nullptr, nullptr, act, xsm, pss, pmx, pbad, st, warp, lane);
     }
+    const float *so = Ly.so;
     for (uint32_t t = orr.lo; t < orr.hi; t++) {
+      const float sc = tid < 16 * (int)B ? __ldg(so + 16u * t + (uint32_t)(tid & 15)) : 0.0f;
       tile<NT>(ring, qcols / 16u, frag, warp, lane, xkey, red, sacc, err);
       if (tid < 16 * (int)B) {
         const int r = tid & 15, s = tid >> 4;
         const uint32_t oi = 16u * t + (uint32_t)r;
         const long long tot = tile_tot<NT>(sacc, r, s, st->xs[s]);
-        const float y = st->flag[s] ? __uint_as_float(kNaN)
-                                    : ((float)tot * st->inv[s]) * __ldg(Ly.so + oi);
+        const float y = st->flag[s] ? __uint_as_float(kNaN) : ((float)tot * st->inv[s]) * sc;
         __stcg(A.o + (uint64_t)s * H + oi, y);
       }
     }
@@ -824,23 +859,26 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
               v[4 * e + 3] = __fadd_rn(f.w, g.w);
             }
           },
-          B, H, Ly.gffn, A.eps, nullptr, lead ? (A.hbuf + (size_t)B * H) : nullptr, act, pss, pmx, pbad, st, warp,
+          B, H, Ly.gffn, A.eps, nullptr, lead ? (A.hbuf + (size_t)B * H) : nullptr, act, xsm, pss, pmx, pbad, st, warp,
           lane);
     }
+    const float *sgu = Ly.sgu;
     for (uint32_t t = gr.lo; t < gr.hi; t++) {
+      const uint32_t c = 16u * t + (uint32_t)(tid & 15);
+      const float scg = tid < 16 * (int)B ? __ldg(sgu + c) : 0.0f;
+      const float scu = tid < 16 * (int)B ? __ldg(sgu + F + c) : 0.0f;
       tile<NT>(ring, H / 16u, frag, warp, lane, xkey, red, sacc, err);             // gate rows
       tile<NT>(ring, H / 16u, frag, warp, lane, xkey, red, sacc + sstride, err);   // up rows
       if (tid < 16 * (int)B) {
         const int r = tid & 15, s = tid >> 4;
-        const uint32_t c = 16u * t + (uint32_t)r;
         float av;
         if (st->flag[s]) {
           av = __uint_as_float(kNaN);
         } else {
           const long long tg = tile_tot<NT>(sacc, r, s, st->xs[s]);
           const long long tu = tile_tot<NT>(sacc + sstride, r, s, st->xs[s]);
-          const float gv = ((float)tg * st->inv[s]) * __ldg(Ly.sgu + c);
-          const float uv = ((float)tu * st->inv[s]) * __ldg(Ly.sgu + F + c);
+          const float gv = ((float)tg * st->inv[s]) * scg;
+          const float uv = ((float)tu * st->inv[s]) * scu;
           const float sg = 1.0f / (1.0f + expf(-gv));
           av = __fmul_rn(__fmul_rn(gv, sg), uv);
         }
@@ -864,13 +902,14 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
               v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
             }
           },
-          B, kc, nullptr, 0.0f, A.amax, nullptr, act, pss, pmx, pbad, st, warp, lane);
+          B, kc, nullptr, 0.0f, A.amax, nullptr, act, xsm, pss, pmx, pbad, st, warp, lane);
       for (uint32_t t = dr.lo; t < dr.hi; t++) {
         tile<NT>(ring, kc / 16u, frag, warp, lane, xkey, red, sacc, err);
         if (tid < 16 * (int)B) {
           const int r = tid & 15, s = tid >> 4;
           const uint32_t oi = 16u * t + (uint32_t)r;
-          __stcg(A.dpart + ((uint64_t)dgroup * B + s) * H + oi, tile_tot<NT>(sacc, r, s, st->xs[s]));
+          atomicAdd(reinterpret_cast<unsigned long long *>(A.dpart + (uint64_t)s * H + oi),
+                    (unsigned long long)tile_tot<NT>(sacc, r, s, st->xs[s]));
         }
       }
     }
@@ -895,7 +934,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
         for (uint32_t e = 0; e < 16; e++) {
           const uint32_t i = 16u * W + e;
           const float v = __fadd_rn(__ldcg((A.hbuf + (size_t)B * H) + (size_t)b * H + i),
-                                    down_value(A.dpart, A.dch, B, H, sd, inv, fl, b, i));
+                                    down_value(__ldcg(A.dpart + (size_t)b * H + i),
+                                               __ldg(sd + i), inv, fl));
           xrow[i] = v;
           ss = fmaf(v, v, ss);
         }

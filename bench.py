@@ -592,7 +592,8 @@ def run_kernel_rows(device, peak, with_cpu, with_upload=True):
     decode attention (B 8, 32 heads x 128, context 4096), each through the
     registry (nl_dispatch_dev, the reference's kernel names and push
     constants) on device tensors.  Every timed launch is bracketed by its own
-    CUDA events after a 256 MB L2 flush, so each reads its inputs from HBM
+    CUDA events after a 256 MB L2 flush (a read, so that no dirty flush data
+    is written back during the timed launch), so each reads its inputs from HBM
     (SwiGLU's 2 MB stay L2-sized: reported as such)."""
     import numpy as np
     import torch
@@ -600,14 +601,14 @@ def run_kernel_rows(device, peak, with_cpu, with_upload=True):
     from nelisp_cuda import dev
     g = torch.Generator(device=device)
     g.manual_seed(2026)
-    flush = torch.empty(64 << 20, dtype=torch.float32, device=device)
+    flush = torch.zeros(64 << 20, dtype=torch.float32, device=device)
 
     def timed(fn, iters=20):
         for _ in range(3):
             fn()
         tot = 0.0
         for _ in range(iters):
-            flush.zero_()
+            flush.sum()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()
@@ -656,11 +657,31 @@ def run_kernel_rows(device, peak, with_cpu, with_upload=True):
     rows["softmax 4096x4096"] = {"us": round(t * 1e6, 2), "GB/s": round(nbytes / t / 1e9, 1),
                                  "frac_of_hbm": round(nbytes / t / 1e9 / peak, 4),
                                  "bytes": nbytes, "bound": "hbm"}
+    # back to back over four distinct 64 MB rows sets (512 MB: every launch
+    # reads HBM), so one launch's start-up is not charged to each row set
+    Xs = [torch.randn(M * N, generator=g, device=device) * 2.0 for _ in range(3)] + [X]
+    Ys = [torch.empty(M * N, device=device) for _ in range(3)] + [Y]
+    for i in range(4):
+        dev.dispatch("softmax", [Xs[i], Ys[i]], [M, N], g64(M))
+    torch.cuda.synchronize()
+    reps = 40
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(reps):
+        dev.dispatch("softmax", [Xs[i % 4], Ys[i % 4]], [M, N], g64(M))
+    b.record()
+    torch.cuda.synchronize()
+    ts = a.elapsed_time(b) * 1e-3 / reps
+    rows["softmax 4096x4096"].update({
+        "us_stream": round(ts * 1e6, 2), "GB/s_stream": round(nbytes / ts / 1e9, 1),
+        "frac_of_hbm_stream": round(nbytes / ts / 1e9 / peak, 4),
+        "note": "us: one launch after an L2 flush, launch start-up included; us_stream: "
+                "launches back to back over 4 distinct 64 MB inputs"})
     if with_cpu:
         Xh = X.cpu().numpy()
         tc = cpu_time(lambda: nlo.softmax(Xh, M, N))
         rows["softmax 4096x4096"]["cpu_GB/s"] = round(nbytes / tc / 1e9, 2)
-    del X, Y
+    del X, Y, Xs, Ys
     # SwiGLU silu(g) * u on 16 x 11008
     n = 16 * 11008
     Gt, U, O = (torch.randn(n, generator=g, device=device), torch.randn(n, generator=g,
@@ -896,6 +917,51 @@ def run_attn_profile(args):
     emit({"attn_profile": True, "launches": args.warmup + args.steps})
 
 
+def run_softmax_profile(args):
+    """Only row-softmax launches at the benchmark's shape (4096 x 4096, x ~
+    N(0, 4)), warm-up then timed: the case ncu captures for that kernel."""
+    import torch
+
+    from nelisp_cuda import dev, load
+    torch.cuda.set_device(0)
+    load()
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device)
+    g.manual_seed(11)
+    M = N = 4096
+    X = torch.randn(M * N, generator=g, device=device) * 2.0
+    Y = torch.empty(M * N, device=device)
+    for _ in range(args.warmup + args.steps):
+        dev.dispatch("softmax", [X, Y], [M, N], (M + 63) // 64)
+    torch.cuda.synchronize()
+    emit({"softmax_profile": True, "launches": args.warmup + args.steps})
+
+
+def run_dattn_profile(args):
+    """Only the fused decode attention (RoPE of q and k, cache append,
+    split-K attention) at the benchmark's shape: batch 8, 32 heads x 128,
+    context 4096 -- the case ncu captures for those kernels."""
+    import torch
+
+    from nelisp_cuda import dev, load
+    torch.cuda.set_device(0)
+    load()
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device)
+    g.manual_seed(12)
+    Bn, H, hd, ctx = 8, 32, 128, 4096
+    dim = H * hd
+    QKV = torch.randn(Bn * 3 * dim, generator=g, device=device)
+    CK = torch.randn(Bn * ctx * dim, generator=g, device=device)
+    CV = torch.randn(Bn * ctx * dim, generator=g, device=device)
+    POS = torch.tensor([ctx - 1], dtype=torch.int32, device=device)
+    C = torch.empty(Bn * dim, device=device)
+    for _ in range(args.warmup + args.steps):
+        dev.decode_attn_rope(QKV, CK, CV, POS, C, Bn, H, H, hd, ctx, 10000.0)
+    torch.cuda.synchronize()
+    emit({"dattn_profile": True, "launches": args.warmup + args.steps})
+
+
 def run_gemm_profile(args):
     """Only the prefill ternary GEMM (512 rows x 2560 -> 6912, the tcgen05
     path for more than 16 rows), warm-up then timed launches: the case ncu
@@ -1029,6 +1095,10 @@ def main():
                     help="only causal prefill attention launches (the case ncu captures)")
     ap.add_argument("--gemm-profile", action="store_true",
                     help="only prefill ternary GEMM launches (the case ncu captures)")
+    ap.add_argument("--softmax-profile", action="store_true",
+                    help="only softmax 4096x4096 launches (the case ncu captures)")
+    ap.add_argument("--dattn-profile", action="store_true",
+                    help="only fused decode-attention launches (the case ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -1039,6 +1109,10 @@ def main():
         run_attn_profile(args)
     elif args.gemm_profile:
         run_gemm_profile(args)
+    elif args.softmax_profile:
+        run_softmax_profile(args)
+    elif args.dattn_profile:
+        run_dattn_profile(args)
     else:
         run_gpu(args)
 

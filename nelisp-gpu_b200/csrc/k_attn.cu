@@ -735,9 +735,10 @@ AttnGeom make_geom(uint32_t B, uint32_t dim, uint32_t heads, uint32_t kvheads,
   g.maxseq = maxseq;
   g.cache_words = cache_words;
   g.coef = 1.0f / sqrtf((float)g.hd);
-  // Enough CTAs for ~4 per SM, at least 32 keys each.
+  // About one full wave of the split kernel (7 CTAs of 128 threads fit an SM
+  // at its register count), at least 32 keys each.
   uint32_t units = B * kvheads;
-  uint32_t want = units ? (uint32_t)ceil_div(4 * 148, (int)units) : 1;
+  uint32_t want = units ? (7u * 148u) / units : 1;
   if (want < 1) want = 1;
   uint32_t chunk = maxseq ? (maxseq + want - 1) / want : 1;
   if (chunk < 32) chunk = 32;

@@ -432,7 +432,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) 
 // takes RPW consecutive rows at a time, lanes stride the hidden dimension in
 // float4 steps against x held in shared memory.
 template <int NB>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 2)
 k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
          unsigned long long *__restrict__ keys, float *__restrict__ logits,
          const int *__restrict__ pos, uint32_t B, uint32_t vr, uint32_t v0, uint32_t H,
@@ -465,10 +465,16 @@ k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
 #pragma unroll
     for (int r = 0; r < RPW; r++)
       er[r] = reinterpret_cast<const float4 *>(E + (size_t)min(r0 + r, vr - 1) * H);
-    for (uint32_t c = lane; c < h4; c += 32) {
-      float4 ev[RPW];
+    // the next column step's float4s are requested before this step's FMAs
+    float4 ev[RPW];
 #pragma unroll
-      for (int r = 0; r < RPW; r++) ev[r] = __ldcs(er[r] + c);
+    for (int r = 0; r < RPW; r++)
+      ev[r] = (uint32_t)lane < h4 ? __ldcs(er[r] + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t c = lane; c < h4; c += 32) {
+      float4 en[RPW];
+#pragma unroll
+      for (int r = 0; r < RPW; r++)
+        en[r] = c + 32 < h4 ? __ldcs(er[r] + c + 32) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
       for (int b = 0; b < NB; b++) {
         const float4 xv = reinterpret_cast<const float4 *>(xs + (size_t)b * H)[c];
@@ -480,6 +486,8 @@ k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
           acc[r][b] = fmaf(ev[r].w, xv.w, acc[r][b]);
         }
       }
+#pragma unroll
+      for (int r = 0; r < RPW; r++) ev[r] = en[r];
     }
 #pragma unroll
     for (int r = 0; r < RPW; r++) {

@@ -352,6 +352,30 @@ int nl_nccl_unique_id(void *id_out);
  * logits for nl_decoder_logits. */
 int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int tp_size,
                       const void *nccl_id, int keep_logits, nl_decoder **out);
+/* The weights of a decoder as resident buffers: handles from nl_upload,
+ * nl_upload_file or nl_upload_file_ternary (the reference's OP_UPLOAD /
+ * OP_UPLOAD_FILE, host/vkserver.c:336-410, through which
+ * lisp/nelisp-gpu-server.el:141-197 loads a model's tensors).  Ternary
+ * matrices are packed two-bit rows of cols/16 words (the ternary-rows
+ * format), scales f32 per row, norms f32 [hidden].  Each array holds LAYERS
+ * handles.  Shapes: wq [heads*head_dim x hidden], wk / wv [kv_heads*head_dim
+ * x hidden], wo [hidden x heads*head_dim], wgate / wup [ffn x hidden], wdown
+ * [hidden x ffn]; embed f32 [vocab x hidden] is also the (tied) LM head. */
+typedef struct {
+  uint32_t embed, final_norm;
+  const uint32_t *wq, *wk, *wv, *wo, *wgate, *wup, *wdown;
+  const uint32_t *sq, *sk, *sv, *so, *sgate, *sup, *sdown;
+  const uint32_t *attn_norm, *ffn_norm;
+} nl_decoder_weights;
+
+/* nl_decoder_create with the weights of W instead of synthetic ones (the
+ * config's seed is not used).  Each rank copies its shard out of the full
+ * tensors on the device (rows of Q|K|V and gate|up, columns of O and down);
+ * the handles may be freed afterwards.  NL_ERROR when a handle's size does
+ * not match its tensor's shape. */
+int nl_decoder_create_from_weights(const nl_decoder_config *cfg, const nl_decoder_weights *w,
+                                   int tp_rank, int tp_size, const void *nccl_id,
+                                   int keep_logits, nl_decoder **out);
 /* Greedy generation for BATCH sequences: PROMPT is [batch x prompt_len]
  * int32 (host); OUT_TOKENS receives [batch x steps].  Each step is one CUDA
  * graph replay; PREFILL_MS times the prompt_len - 1 replays that fill the

@@ -687,6 +687,7 @@ struct nl_decoder {
   uint64_t weight_bytes = 0;
   std::vector<void *> allocs;
   uint32_t last_batch = 0, last_positions = 0;
+  const nl_decoder_weights *src = nullptr;   // caller's weights while building, or synthetic
   // the one-kernel decode step (nl_step.cu), when the shapes allow it
   bool step_ok = false;
   nl::StepLayer *step_layers = nullptr;   // [layers], device
@@ -990,6 +991,31 @@ extern "C" void nl_decoder_destroy(nl_decoder *D) {
   delete D;
 }
 
+// The device address of resident buffer HANDLE, which must hold WORDS words.
+static int weight_ptr(uint32_t handle, uint64_t words, const char *what, const uint32_t **p) {
+  void *ptr = nullptr;
+  uint32_t n = 0;
+  if (nl_resident_info(handle, &ptr, &n) != NL_OK || !ptr)
+    return set_error(NL_ERROR, "decoder weights: %s: handle %u is not resident", what, handle);
+  if ((uint64_t)n != words)
+    return set_error(NL_ERROR, "decoder weights: %s: handle %u holds %u words, the shape needs %llu",
+                     what, handle, n, (unsigned long long)words);
+  *p = static_cast<const uint32_t *>(ptr);
+  return NL_OK;
+}
+// ROWS rows of WNG words each (row pitch PITCH words, starting at word W0 of
+// row R0) of resident HANDLE, whose full shape is FULL_ROWS x PITCH, into DST.
+static int copy_block(nl_decoder *D, void *dst, uint32_t handle, uint64_t full_rows,
+                      uint64_t pitch, uint64_t r0, uint64_t rows, uint64_t w0, uint64_t wng,
+                      const char *what) {
+  const uint32_t *p = nullptr;
+  int rc = weight_ptr(handle, full_rows * pitch, what, &p);
+  if (rc) return rc;
+  return cuda_status(cudaMemcpy2DAsync(dst, wng * 4, p + r0 * pitch + w0, pitch * 4, wng * 4,
+                                       rows, cudaMemcpyDeviceToDevice, D->stream),
+                     "decoder weights: copy");
+}
+
 static int decoder_build(nl_decoder *D) {
   const nl_decoder_config &c = D->cfg;
   const uint32_t H = c.hidden, hd = c.head_dim;
@@ -1033,6 +1059,35 @@ static int decoder_build(nl_decoder *D) {
     wb += (wq + wo + wgu + wdn) * 4 + ((size_t)D->qkv_rows + 2 * H + 2 * D->fr) * 4 + 2 * H * 4;
     const uint32_t rq = D->hr * hd, rk = D->kvr * hd;
     int rc;
+    if (const nl_decoder_weights *w = D->src) {
+      // this rank's shard out of the caller's full tensors
+      const uint64_t hw = H / 16, qw = (uint64_t)qd / 16, fw = c.ffn / 16;
+      if ((rc = copy_block(D, L.wqkv, w->wq[l], qd, hw, (uint64_t)h0 * hd, rq, 0, hw, "wq")) ||
+          (rc = copy_block(D, L.wqkv + (size_t)rq * hw, w->wk[l], kvd, hw, (uint64_t)kv0 * hd,
+                           rk, 0, hw, "wk")) ||
+          (rc = copy_block(D, L.wqkv + (size_t)(rq + rk) * hw, w->wv[l], kvd, hw,
+                           (uint64_t)kv0 * hd, rk, 0, hw, "wv")) ||
+          (rc = copy_block(D, L.sqkv, w->sq[l], qd, 1, (uint64_t)h0 * hd, rq, 0, 1, "sq")) ||
+          (rc = copy_block(D, L.sqkv + rq, w->sk[l], kvd, 1, (uint64_t)kv0 * hd, rk, 0, 1,
+                           "sk")) ||
+          (rc = copy_block(D, L.sqkv + rq + rk, w->sv[l], kvd, 1, (uint64_t)kv0 * hd, rk, 0, 1,
+                           "sv")) ||
+          (rc = copy_block(D, L.wo, w->wo[l], H, qw, 0, H, (uint64_t)h0 * hd / 16, rq / 16,
+                           "wo")) ||
+          (rc = copy_block(D, L.so, w->so[l], H, 1, 0, H, 0, 1, "so")) ||
+          (rc = copy_block(D, L.wgu, w->wgate[l], c.ffn, hw, f0, D->fr, 0, hw, "wgate")) ||
+          (rc = copy_block(D, L.wgu + (size_t)D->fr * hw, w->wup[l], c.ffn, hw, f0, D->fr, 0, hw,
+                           "wup")) ||
+          (rc = copy_block(D, L.sgu, w->sgate[l], c.ffn, 1, f0, D->fr, 0, 1, "sgate")) ||
+          (rc = copy_block(D, L.sgu + D->fr, w->sup[l], c.ffn, 1, f0, D->fr, 0, 1, "sup")) ||
+          (rc = copy_block(D, L.wd, w->wdown[l], H, fw, 0, H, f0 / 16, D->fr / 16, "wdown")) ||
+          (rc = copy_block(D, L.sd, w->sdown[l], H, 1, 0, H, 0, 1, "sdown")) ||
+          (rc = copy_block(D, L.gattn, w->attn_norm[l], H, 1, 0, H, 0, 1, "attn_norm")) ||
+          (rc = copy_block(D, L.gffn, w->ffn_norm[l], H, 1, 0, H, 0, 1, "ffn_norm")))
+        return rc;
+      wb += (wq + wo + wgu + wdn) * 4 + ((size_t)D->qkv_rows + 2 * H + 2 * D->fr) * 4 + 2 * H * 4;
+      continue;
+    }
     if ((rc = gen_ternary(D, L.wqkv, rq, H, T + NL_T_WQ, (uint64_t)h0 * hd, H, 0)) ||
         (rc = gen_ternary(D, L.wqkv + (size_t)rq * (H / 16), rk, H, T + NL_T_WK,
                           (uint64_t)kv0 * hd, H, 0)) ||
@@ -1057,11 +1112,17 @@ static int decoder_build(nl_decoder *D) {
   const size_t en = (size_t)c.vocab * H;
   DALLOC(D->embed, en * 4);
   DALLOC(D->gfinal, (size_t)H * 4);
-  gen_embed_kernel<<<grid_for(en, 256), 256, 0, D->stream>>>(
-      D->embed, en, nl_tensor_key(c.seed, NL_T_EMBED));
   int rc;
-  if ((rc = cuda_status(cudaPeekAtLastError(), "decoder: embedding"))) return rc;
-  if ((rc = gen_norm(D, D->gfinal, H, NL_T_FINAL_NORM))) return rc;
+  if (const nl_decoder_weights *w = D->src) {
+    if ((rc = copy_block(D, D->embed, w->embed, c.vocab, H, 0, c.vocab, 0, H, "embed")) ||
+        (rc = copy_block(D, D->gfinal, w->final_norm, H, 1, 0, H, 0, 1, "final_norm")))
+      return rc;
+  } else {
+    gen_embed_kernel<<<grid_for(en, 256), 256, 0, D->stream>>>(
+        D->embed, en, nl_tensor_key(c.seed, NL_T_EMBED));
+    if ((rc = cuda_status(cudaPeekAtLastError(), "decoder: embedding"))) return rc;
+    if ((rc = gen_norm(D, D->gfinal, H, NL_T_FINAL_NORM))) return rc;
+  }
   wb += (size_t)D->vr * H * 4 + (size_t)H * 4;
   D->weight_bytes = wb;
   const uint32_t B = c.max_batch;
@@ -1225,8 +1286,25 @@ static int setup_peer_allreduce(nl_decoder *D) {
   return NL_OK;
 }
 
+static int decoder_create(const nl_decoder_config *cfg, const nl_decoder_weights *w, int tp_rank,
+                          int tp_size, const void *nccl_id, int keep_logits, nl_decoder **out);
+
 extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int tp_size,
                                  const void *nccl_id, int keep_logits, nl_decoder **out) {
+  return decoder_create(cfg, nullptr, tp_rank, tp_size, nccl_id, keep_logits, out);
+}
+
+extern "C" int nl_decoder_create_from_weights(const nl_decoder_config *cfg,
+                                              const nl_decoder_weights *w, int tp_rank,
+                                              int tp_size, const void *nccl_id, int keep_logits,
+                                              nl_decoder **out) {
+  if (out) *out = nullptr;
+  if (!w) return set_error(NL_ERROR, "decoder: no weights");
+  return decoder_create(cfg, w, tp_rank, tp_size, nccl_id, keep_logits, out);
+}
+
+static int decoder_create(const nl_decoder_config *cfg, const nl_decoder_weights *w, int tp_rank,
+                          int tp_size, const void *nccl_id, int keep_logits, nl_decoder **out) {
   *out = nullptr;
   int rc = nl_init(-1);
   if (rc) return rc;
@@ -1247,6 +1325,7 @@ extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int 
   D->rank = tp_rank;
   D->size = tp_size;
   D->keep_logits = keep_logits != 0;
+  D->src = w;
   if (tp_size > 1) {
     Nccl *n = nccl();
     if (!n) { delete D; return set_error(NL_ERROR, "libnccl.so.2 not available"); }
@@ -1262,6 +1341,7 @@ extern "C" int nl_decoder_create(const nl_decoder_config *cfg, int tp_rank, int 
     nl_decoder_destroy(D);
     return rc;
   }
+  D->src = nullptr;   // the caller's handles are not needed after the copies
   *out = D;
   return NL_OK;
 }

@@ -96,6 +96,7 @@ SIGNATURES = {
     # decoder (nelisp_cuda.decoder rebinds these with the config struct)
     "nl_nccl_unique_id": (_i, [_vp]),
     "nl_decoder_create": (_i, [_vp, _i, _i, _vp, _i, ctypes.POINTER(_vp)]),
+    "nl_decoder_create_from_weights": (_i, [_vp, _vp, _i, _i, _vp, _i, ctypes.POINTER(_vp)]),
     "nl_decoder_generate": (_i, [_vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp]),
     "nl_decoder_logits": (_i, [_vp, _vp, _u64]),
     "nl_decoder_info": (_i, [_vp, _vp, _vp, _vp]),

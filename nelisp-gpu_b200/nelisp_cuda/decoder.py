@@ -28,6 +28,21 @@ class Config(ctypes.Structure):
                 ("rope_base", ctypes.c_float), ("seed", ctypes.c_uint64)]
 
 
+_U32P = ctypes.POINTER(ctypes.c_uint32)
+
+
+class Weights(ctypes.Structure):
+    """nl_decoder_weights: resident-buffer handles of a decoder's tensors."""
+    _P = _U32P
+    _fields_ = [("embed", ctypes.c_uint32), ("final_norm", ctypes.c_uint32)] + \
+        [(n, _U32P) for n in ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "sq", "sk", "sv",
+                           "so", "sgate", "sup", "sdown", "attn_norm", "ffn_norm")]
+
+
+LAYER_TENSORS = ("wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "sq", "sk", "sv", "so",
+                 "sgate", "sup", "sdown", "attn_norm", "ffn_norm")
+
+
 def _bind(lib):
     if getattr(lib, "_nl_decoder_bound", False):
         return lib
@@ -37,6 +52,10 @@ def _bind(lib):
                                       ctypes.c_void_p, ctypes.c_int,
                                       ctypes.POINTER(ctypes.c_void_p)]
     lib.nl_decoder_create.restype = ctypes.c_int
+    lib.nl_decoder_create_from_weights.argtypes = [ctypes.POINTER(Config), ctypes.POINTER(Weights),
+                                                   ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                                   ctypes.c_int, ctypes.POINTER(ctypes.c_void_p)]
+    lib.nl_decoder_create_from_weights.restype = ctypes.c_int
     lib.nl_decoder_generate.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32,
                                         ctypes.POINTER(ctypes.c_int32), ctypes.c_uint32,
                                         ctypes.POINTER(ctypes.c_int32),
@@ -66,16 +85,29 @@ def nccl_unique_id() -> bytes:
 class Decoder:
     def __init__(self, config: dict, max_batch: int, max_seq: int, tp_rank: int = 0,
                  tp_size: int = 1, nccl_id: bytes | None = None, keep_logits: bool = False,
-                 device: int | None = None):
+                 device: int | None = None, weights: dict | None = None):
+        """WEIGHTS (optional): resident-buffer handles (nl_upload ...) of the
+        full tensors -- 'embed' and 'final_norm' handles, and for each name in
+        LAYER_TENSORS a list of one handle per layer; without it the weights
+        are generated from the config's seed."""
         self.lib = _bind(L.load())
         if device is not None:
             L.check(self.lib.nl_init(device))
         self.cfg = dict(config, max_batch=max_batch, max_seq=max_seq)
-        c = Config(**self.cfg)
+        c = Config(**{k: v for k, v in self.cfg.items() if k in [f[0] for f in Config._fields_]})
         h = ctypes.c_void_p()
         idbuf = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
-        L.check(self.lib.nl_decoder_create(ctypes.byref(c), tp_rank, tp_size, idbuf,
-                                           1 if keep_logits else 0, ctypes.byref(h)))
+        if weights is None:
+            L.check(self.lib.nl_decoder_create(ctypes.byref(c), tp_rank, tp_size, idbuf,
+                                               1 if keep_logits else 0, ctypes.byref(h)))
+        else:
+            arrays = {n: (ctypes.c_uint32 * len(weights[n]))(*weights[n]) for n in LAYER_TENSORS}
+            w = Weights(embed=weights["embed"], final_norm=weights["final_norm"],
+                        **{n: ctypes.cast(a, Weights._P) for n, a in arrays.items()})
+            L.check(self.lib.nl_decoder_create_from_weights(ctypes.byref(c), ctypes.byref(w),
+                                                            tp_rank, tp_size, idbuf,
+                                                            1 if keep_logits else 0,
+                                                            ctypes.byref(h)))
         self.h = h
         self.tp_rank, self.tp_size = tp_rank, tp_size
 

@@ -127,6 +127,7 @@ def _declare(L):
                                  ctypes.POINTER(ctypes.c_int32), _F],
         "nlo_threads": [],
         "nlo_decoder_time_positions": [ctypes.c_void_p, _u32, _u32, _u32],
+        "nlo_decoder_tensor": [ctypes.c_void_p, _u32, _u32, ctypes.c_void_p],
     }
     for name, argt in sigs.items():
         fn = getattr(L, name)
@@ -136,6 +137,7 @@ def _declare(L):
     L.nlo_threads.restype = ctypes.c_int
     L.nlo_decoder_generate.restype = ctypes.c_int
     L.nlo_decoder_time_positions.restype = ctypes.c_double
+    L.nlo_decoder_tensor.restype = ctypes.c_uint64
 
 
 def _f(a):
@@ -563,6 +565,32 @@ def decoder_time_positions(cfg: dict, batch: int, ctx: int, steps: int) -> float
     if sec < 0:
         raise RuntimeError("nlo_decoder_time_positions: bad arguments")
     return sec
+
+
+DECODER_TENSORS = ["wq", "wk", "wv", "wo", "wgate", "wup", "wdown", "sq", "sk", "sv", "so",
+                   "sgate", "sup", "sdown", "attn_norm", "ffn_norm"]
+
+
+def decoder_tensor(cfg: dict, layer: int, name: str) -> np.ndarray:
+    """One tensor of the CPU model's synthetic weights (the same values the
+    library generates from the seed): packed two-bit rows as uint32 for the
+    ternary matrices, float32 for scales, gains ('embed', 'final_norm' with
+    layer 0)."""
+    which = {"embed": 16, "final_norm": 17}.get(name)
+    if which is None:
+        which = DECODER_TENSORS.index(name)
+    H, hd, F = cfg["hidden"], cfg["head_dim"], cfg["ffn"]
+    qd, kvd = cfg["heads"] * hd, cfg["kv_heads"] * hd
+    words = {"wq": qd * H // 16, "wk": kvd * H // 16, "wv": kvd * H // 16, "wo": H * qd // 16,
+             "wgate": F * H // 16, "wup": F * H // 16, "wdown": H * F // 16, "sq": qd,
+             "sk": kvd, "sv": kvd, "so": H, "sgate": F, "sup": F, "sdown": H, "attn_norm": H,
+             "ffn_norm": H, "embed": cfg["vocab"] * H, "final_norm": H}[name]
+    out = np.zeros(words, np.uint32 if name.startswith("w") else np.float32)
+    c = DecoderConfig(**{k: v for k, v in cfg.items() if k in [f[0] for f in DecoderConfig._fields_]})
+    n = lib().nlo_decoder_tensor(ctypes.byref(c), layer, which, out.ctypes.data_as(ctypes.c_void_p))
+    if n != words:
+        raise RuntimeError(f"nlo_decoder_tensor({name}): {n} words, expected {words}")
+    return out
 
 
 # ---- metrics -------------------------------------------------------------

@@ -245,6 +245,45 @@ static void model_position(const nlo_decoder_config *c, Model *M, uint32_t p, co
   }
 }
 
+/* One tensor of the CPU model's weights into OUT: per-layer tensor WHICH
+ * (WQ .. GFFN, the library's tensor ids) of layer LAYER -- packed two-bit rows
+ * of ceil(K/16) words for WQ .. WDOWN, f32 for the scales and gains -- or
+ * the embedding (WHICH 16, f32 [vocab x hidden]) or the final gain (17).
+ * Returns the number of 32-bit words written, 0 for a bad WHICH. */
+uint64_t nlo_decoder_tensor(const nlo_decoder_config *c, uint32_t layer, uint32_t which,
+                            void *out) {
+  const uint32_t H = c->hidden, hd = c->head_dim, F = c->ffn;
+  const uint32_t qd = c->heads * hd, kvd = c->kv_heads * hd;
+  const uint64_t T = (uint64_t)layer * 16;
+  uint32_t *W = (uint32_t *)out;
+  float *S = (float *)out;
+  switch (which) {
+    case WQ: pack_rows(W, tkey(c->seed, T + WQ), qd, H); return (uint64_t)qd * ((H + 15) / 16);
+    case WK: pack_rows(W, tkey(c->seed, T + WK), kvd, H); return (uint64_t)kvd * ((H + 15) / 16);
+    case WV: pack_rows(W, tkey(c->seed, T + WV), kvd, H); return (uint64_t)kvd * ((H + 15) / 16);
+    case WO: pack_rows(W, tkey(c->seed, T + WO), H, qd); return (uint64_t)H * ((qd + 15) / 16);
+    case WGATE: pack_rows(W, tkey(c->seed, T + WGATE), F, H); return (uint64_t)F * ((H + 15) / 16);
+    case WUP: pack_rows(W, tkey(c->seed, T + WUP), F, H); return (uint64_t)F * ((H + 15) / 16);
+    case WDOWN: pack_rows(W, tkey(c->seed, T + WDOWN), H, F); return (uint64_t)H * ((F + 15) / 16);
+    case SQ: scales(S, tkey(c->seed, T + SQ), qd, H); return qd;
+    case SK: scales(S, tkey(c->seed, T + SK), kvd, H); return kvd;
+    case SV: scales(S, tkey(c->seed, T + SV), kvd, H); return kvd;
+    case SO: scales(S, tkey(c->seed, T + SO), H, qd); return H;
+    case SGATE: scales(S, tkey(c->seed, T + SGATE), F, H); return F;
+    case SUP: scales(S, tkey(c->seed, T + SUP), F, H); return F;
+    case SDOWN: scales(S, tkey(c->seed, T + SDOWN), H, F); return H;
+    case GATTN: gains(S, tkey(c->seed, T + GATTN), H); return H;
+    case GFFN: gains(S, tkey(c->seed, T + GFFN), H); return H;
+    case 16: {
+      const uint64_t k = tkey(c->seed, T_EMBED);
+      for (uint64_t i = 0; i < (uint64_t)c->vocab * H; i++) S[i] = 2.0f * unit(k, i) - 1.0f;
+      return (uint64_t)c->vocab * H;
+    }
+    case 17: gains(S, tkey(c->seed, T_FINAL), H); return H;
+    default: return 0;
+  }
+}
+
 static uint32_t argmax_row(const float *lg, uint32_t V) {
   uint32_t best = 0;
   for (uint32_t r = 1; r < V; r++)

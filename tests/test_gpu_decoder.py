@@ -103,3 +103,64 @@ def test_decoder_batched_prefill_matches_cpu_model():
             if top2[1] - top2[0] < 1e-3 * max(1.0, abs(top2[1])):
                 break
             assert toks[b, i] == want_t[b, i], (b, i)
+
+
+def test_decoder_from_uploaded_weights_matches_synthetic():
+    """nl_decoder_create_from_weights on resident buffers (nl_upload) holding
+    the very tensors the seed generates: the same logits, bit for bit, as the
+    synthetic decoder; the handles are freed right after the constructor,
+    which copies what it needs."""
+    import ctypes
+
+    from nelisp_cuda import _lib as L
+    from nelisp_cuda.decoder import LAYER_TENSORS, Decoder
+    cfg = dict(SMALL, heads=8, kv_heads=4, hidden=512, ffn=1024, seed=41)
+    lib = L.load()
+    rng = np.random.default_rng(8)
+    B, P, steps, max_seq = 2, 4, 4, 12
+    prompt = rng.integers(0, cfg["vocab"], size=(B, P))
+    handles = []
+
+    def up(a):
+        h = ctypes.c_uint32()
+        a = np.ascontiguousarray(a)
+        L.check(lib.nl_upload(a.ctypes.data, a.size, ctypes.byref(h)))
+        handles.append(h.value)
+        return h.value
+
+    full = dict(cfg, max_batch=B, max_seq=max_seq)
+    w = {n: [up(nlo.decoder_tensor(full, l, n)) for l in range(cfg["layers"])]
+         for n in LAYER_TENSORS}
+    w["embed"] = up(nlo.decoder_tensor(full, 0, "embed"))
+    w["final_norm"] = up(nlo.decoder_tensor(full, 0, "final_norm"))
+    dec = Decoder(cfg, max_batch=B, max_seq=max_seq, keep_logits=True, weights=w)
+    for h in handles:
+        lib.nl_free(h)
+    t1, _, _ = dec.generate(prompt, steps)
+    lg1 = dec.logits()
+    dec.close()
+    dec = Decoder(cfg, max_batch=B, max_seq=max_seq, keep_logits=True)
+    t0, _, _ = dec.generate(prompt, steps)
+    lg0 = dec.logits()
+    dec.close()
+    assert np.array_equal(t1, t0)
+    npos = P + steps - 1
+    assert np.array_equal(lg1[:npos].view(np.uint32), lg0[:npos].view(np.uint32))
+
+
+def test_decoder_from_weights_rejects_wrong_shapes():
+    import ctypes
+
+    from nelisp_cuda import NlError
+    from nelisp_cuda import _lib as L
+    from nelisp_cuda.decoder import LAYER_TENSORS, Decoder
+    lib = L.load()
+    h = ctypes.c_uint32()
+    a = np.zeros(7, np.uint32)
+    L.check(lib.nl_upload(a.ctypes.data, a.size, ctypes.byref(h)))
+    w = {n: [h.value] * SMALL["layers"] for n in LAYER_TENSORS}
+    w["embed"] = w["final_norm"] = h.value
+    with pytest.raises(NlError) as e:
+        Decoder(SMALL, max_batch=1, max_seq=8, weights=w)
+    assert "holds 7 words" in str(e.value)
+    lib.nl_free(h.value)

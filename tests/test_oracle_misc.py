@@ -181,3 +181,19 @@ def test_quant_w_pack_decodes_to_quant_w(per_row):
             assert S[o] == S[0]
     if not per_row:
         assert abs(S[0] - np.abs(W.astype(np.float64)).mean()) <= 1e-6 * S[0]
+
+
+def test_decoder_tensor_export_shapes_and_values():
+    """The CPU model's weights exported per tensor: packed trits decode to
+    {-1, 0, +1} in about equal shares, scales lie in [0.5, 1.5) / sqrt(2K/3)."""
+    cfg = dict(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=300,
+               rms_eps=1e-5, rope_base=10000.0, seed=5, max_batch=1, max_seq=4)
+    w = nlo.decoder_tensor(cfg, 1, "wgate")
+    assert w.dtype == np.uint32 and w.size == 512 * 256 // 16
+    codes = (w[:, None] >> (2 * np.arange(16, dtype=np.uint32))) & 3
+    share = [(codes == c).mean() for c in (0, 1, 3)]
+    assert (codes != 2).all() and all(0.3 < x < 0.37 for x in share)
+    s = nlo.decoder_tensor(cfg, 0, "sdown")
+    rs = 1.0 / np.sqrt(2.0 * 512 / 3.0)
+    assert s.size == 256 and (s >= 0.5 * rs * 0.999).all() and (s < 1.5 * rs * 1.001).all()
+    assert nlo.decoder_tensor(cfg, 0, "embed").size == 300 * 256

@@ -96,11 +96,45 @@ def main():
     info = dec.info()
     lg = dec.logits()
     dec.close()
+    # The same decoder built from uploaded full tensors (each rank copies its
+    # shard out of them): this rank's logits must be the same bits.
+    import ctypes
+
+    import oracle as nlo
+    from nelisp_cuda import _lib as L
+    from nelisp_cuda.decoder import LAYER_TENSORS
+    lib = L.load()
+    full_cfg = dict(cfg, max_batch=B, max_seq=max_seq)
+    handles = []
+
+    def up(a):
+        h = ctypes.c_uint32()
+        a = np.ascontiguousarray(a)
+        L.check(lib.nl_upload(a.ctypes.data, a.size, ctypes.byref(h)))
+        handles.append(h.value)
+        return h.value
+
+    w = {n: [up(nlo.decoder_tensor(full_cfg, l, n)) for l in range(cfg["layers"])]
+         for n in LAYER_TENSORS}
+    w["embed"] = up(nlo.decoder_tensor(full_cfg, 0, "embed"))
+    w["final_norm"] = up(nlo.decoder_tensor(full_cfg, 0, "final_norm"))
+    dec = Decoder(cfg, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=ws,
+                  nccl_id=obj[0], keep_logits=True, device=local, weights=w)
+    for h in handles:
+        lib.nl_free(h)
+    toks_w, _, _ = dec.generate(prompt, steps)
+    lg_w = dec.logits()
+    dec.close()
+    same_w = bool(np.array_equal(toks_w, toks) and
+                  np.array_equal(lg_w[:P + steps - 1].view(np.uint32),
+                                 lg[:P + steps - 1].view(np.uint32)))
     parts = [None] * ws
-    dist.all_gather_object(parts, (info["vocab_begin"], lg, toks))
+    dist.all_gather_object(parts, (info["vocab_begin"], lg, toks, same_w))
     ok = True
     if rank == 0:
-        import oracle as nlo
+        if not all(p[3] for p in parts):
+            print("decoder from uploaded weights differs", [p[3] for p in parts], flush=True)
+            ok = False
         want_t, want_lg = nlo.decoder_generate(dict(cfg, max_batch=B, max_seq=max_seq), prompt,
                                                steps, keep_logits=True)
         parts.sort(key=lambda p: p[0])

@@ -324,6 +324,164 @@ k_norm(const int *__restrict__ tok, const float *__restrict__ E, float *__restri
   cl.sync();                     // no CTA leaves while its statistics are read
 }
 
+// The same per row in one CTA, one float4 of the row per thread (ROW4
+// float4s a thread for longer rows): the row's statistics are two block
+// reductions (warp shuffles, one barrier each) instead of the cluster's
+// barriers and distributed-shared-memory reads, so a decode step's norm is
+// one load round trip and a few barriers.  XS (dynamic shared memory) holds
+// the row for the quantisation, which writes the CTA's offset sum to slot 0
+// and zeroes the others.
+template <int ROW4>
+__device__ __forceinline__ void row_stats_quantize(float (&v)[ROW4][4], uint32_t cols, uint32_t b,
+                                                   uint32_t B, float *xs, float *red, void *ws) {
+  __shared__ long long xred[32];
+  const int nw = (int)(blockDim.x >> 5), w = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
+  float mm = 0.0f;
+  int bad = 0;
+#pragma unroll
+  for (int k = 0; k < ROW4; k++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      mm = fmaxf(mm, fabsf(v[k][e]));
+      bad |= !isfinite(v[k][e]);
+    }
+  for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+  if (lane == 0) red[w] = mm;
+  bad = __syncthreads_or(bad);
+  float rm = 0.0f;
+  for (int i = 0; i < nw; i++) rm = fmaxf(rm, red[i]);
+  if (!ws) return;
+  const int NT = n_tiles((int)B);
+  PrepOut P = prep_at(ws, (int)B, cols, 0);
+  float mul = 0.0f, inv = 0.0f;
+  const bool ok = row_scale(rm, bad != 0, &mul, &inv);
+  if (threadIdx.x == 0) {
+    P.rowinv[b] = inv;
+    P.rowflag[b] = !ok;
+  }
+  long long part = 0;
+  for (uint32_t W = threadIdx.x; W < cols / 16u; W += blockDim.x) {
+    float q[16];
+    const float4 *x4 = reinterpret_cast<const float4 *>(xs + 16u * W);
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float4 f = x4[e];
+      q[4 * e] = f.x; q[4 * e + 1] = f.y; q[4 * e + 2] = f.z; q[4 * e + 3] = f.w;
+    }
+    part += quantize_word(q, mul, ok, W, b, NT, P);
+  }
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) xred[w] = part;
+  __syncthreads();
+  if (threadIdx.x < (unsigned)kRowCluster) {
+    long long t = 0;
+    if (threadIdx.x == 0)
+      for (int i = 0; i < nw; i++) t += xred[i];
+    P.xsum[b * kRowCluster + threadIdx.x] = t;
+  }
+}
+
+// h = E[tok] (gather) or h = h + delta; x = (h * rsqrt(mean h^2 + eps)) * g
+// and the next GEMV's prep: one CTA of cols/4 threads per sequence row.
+template <int MODE>
+__global__ void __launch_bounds__(1024)
+k_norm_cta(const int *__restrict__ tok, const float *__restrict__ E, float *__restrict__ h,
+           const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
+           void *ws, uint32_t B, uint32_t H, float eps, PeerIn pin) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[32];
+  const uint32_t b = blockIdx.x, t = threadIdx.x;
+  const bool in = 4u * t < H;
+  const uint32_t tag = pin.slots ? (uint32_t)(*pin.ep * pin.tmul + pin.tadd) : 0u;
+  float v[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+  float4 *h4 = reinterpret_cast<float4 *>(h + (size_t)b * H);
+  if (in) {
+    if (MODE == kNormGather) {
+      const float4 f = __ldg(reinterpret_cast<const float4 *>(E + (size_t)__ldg(tok + b) * H) + t);
+      v[0][0] = f.x; v[0][1] = f.y; v[0][2] = f.z; v[0][3] = f.w;
+    } else {
+      const float4 f = h4[t];
+      const float hv[4] = {f.x, f.y, f.z, f.w};
+      float dv[4];
+      if (pin.slots) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const unsigned long long *sl = pin.slots + (size_t)b * H + 4u * t + e;
+          float sum = tagged_value(sl, tag, pin.err);
+          for (uint32_t r = 1; r < pin.tp; r++)
+            sum = __fadd_rn(sum, tagged_value(sl + (size_t)r * pin.slot_stride, tag, pin.err));
+          dv[e] = sum;
+        }
+      } else {
+        const float4 d = reinterpret_cast<const float4 *>(delta + (size_t)b * H)[t];
+        dv[0] = d.x; dv[1] = d.y; dv[2] = d.z; dv[3] = d.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; e++) v[0][e] = __fadd_rn(hv[e], dv[e]);
+    }
+    h4[t] = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 4; e++) ss = fmaf(v[0][e], v[0][e], ss);
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((t & 31) == 0) red[t >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += red[i];
+  const float rinv = 1.0f / sqrtf(tot / (float)H + eps);
+  __syncthreads();   // red is reused
+  if (in) {
+    const float4 gv = __ldg(reinterpret_cast<const float4 *>(g) + t);
+    v[0][0] = __fmul_rn(__fmul_rn(v[0][0], rinv), gv.x);
+    v[0][1] = __fmul_rn(__fmul_rn(v[0][1], rinv), gv.y);
+    v[0][2] = __fmul_rn(__fmul_rn(v[0][2], rinv), gv.z);
+    v[0][3] = __fmul_rn(__fmul_rn(v[0][3], rinv), gv.w);
+    const float4 xv = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
+    reinterpret_cast<float4 *>(x + (size_t)b * H)[t] = xv;
+    reinterpret_cast<float4 *>(xs)[t] = xv;
+  }
+  row_stats_quantize<1>(v, H, b, B, xs, red, ws);
+}
+
+// a = silu(gate) * up and the down GEMV's prep: one CTA per sequence row,
+// ROW4 float4 of the row per thread.
+template <int ROW4>
+__global__ void __launch_bounds__(1024)
+k_silu_cta(const float *__restrict__ gu, float *__restrict__ a, void *ws, uint32_t B,
+           uint32_t fr) {
+  pdl_trigger();
+  pdl_wait();
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[32];
+  const uint32_t b = blockIdx.x;
+  const float4 *g4 = reinterpret_cast<const float4 *>(gu + (size_t)b * 2 * fr);
+  const float4 *u4 = reinterpret_cast<const float4 *>(gu + (size_t)b * 2 * fr + fr);
+  float v[ROW4][4];
+#pragma unroll
+  for (int k = 0; k < ROW4; k++) {
+    const uint32_t i = threadIdx.x + (uint32_t)k * blockDim.x;
+    if (4u * i < fr) {
+      const float4 gv = g4[i], uv = u4[i];
+      const float gg[4] = {gv.x, gv.y, gv.z, gv.w}, uu[4] = {uv.x, uv.y, uv.z, uv.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float sg = 1.0f / (1.0f + expf(-gg[e]));
+        v[k][e] = __fmul_rn(__fmul_rn(gg[e], sg), uu[e]);
+      }
+      const float4 av = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+      reinterpret_cast<float4 *>(a + (size_t)b * fr)[i] = av;
+      reinterpret_cast<float4 *>(xs)[i] = av;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; e++) v[k][e] = 0.0f;
+    }
+  }
+  row_stats_quantize<ROW4>(v, fr, b, B, xs, red, ws);
+}
+
 // a = silu(gate) * up, then the down GEMV's prep: one cluster per sequence
 // row, each CTA on its column slice, the row maximum combined across the
 // cluster.
@@ -773,6 +931,20 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   cudaStream_t st = D->stream;
   const uint32_t gnorm = B * kRowCluster;
   const size_t smem_h = (size_t)row_slice_cols(H) * sizeof(float);
+  // One CTA per row (a float4 a thread) where the row fits 1024 threads;
+  // else the 8-CTA clusters.  NELISP_DECODER_NORM=cluster keeps the clusters.
+  static const bool cluster_norm = [] {
+    const char *v = getenv("NELISP_DECODER_NORM");
+    return v && strcmp(v, "cluster") == 0;
+  }();
+  const bool cta_rows = !cluster_norm && H % 128u == 0 && H / 4u <= 1024u;
+  const uint32_t norm_threads = (H / 4u + 31u) / 32u * 32u;
+  const uint32_t silu_row4 = cluster_norm || D->fr % 128u ? 0u
+                             : D->fr / 4u <= 1024u        ? 1u
+                             : D->fr / 4u <= 2048u        ? 2u
+                                                          : 0u;
+  const uint32_t silu_threads =
+      silu_row4 ? ((D->fr / 4u + silu_row4 - 1u) / silu_row4 + 31u) / 32u * 32u : 0u;
   const bool fast_o = ternary_fast_shape(D->hr * hd, D->hr * hd / 128, D->hr * hd / 16, false);
   const bool fast_d = ternary_fast_shape(D->fr, D->fr / 128, D->fr / 16, false);
   const bool fast_h = ternary_fast_shape(H, H / 128, H / 16, false);
@@ -824,10 +996,14 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
     count_launches(1);
     if (e != cudaSuccess) return cuda_status(e, "step: layers");
   } else {
-    e = launch_pdl(k_norm<kNormGather>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
-                   (const int *)D->tok, (const float *)D->embed, D->h, (const float *)nullptr,
-                   (const float *)D->layers[0].gattn, D->x, fast_h ? D->ws_qkv : nullptr, B, H,
-                   eps, PeerIn{});
+    e = cta_rows ? launch_pdl(k_norm_cta<kNormGather>, dim3(B), dim3(norm_threads), (size_t)H * 4,
+                              st, (const int *)D->tok, (const float *)D->embed, D->h,
+                              (const float *)nullptr, (const float *)D->layers[0].gattn, D->x,
+                              fast_h ? D->ws_qkv : nullptr, B, H, eps, PeerIn{})
+                 : launch_pdl(k_norm<kNormGather>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                              (const int *)D->tok, (const float *)D->embed, D->h,
+                              (const float *)nullptr, (const float *)D->layers[0].gattn, D->x,
+                              fast_h ? D->ws_qkv : nullptr, B, H, eps, PeerIn{});
     count_launches(1);
     if (e != cudaSuccess) return cuda_status(e, "step: embed");
     // Tensor parallelism: O / down partials go peer to peer (D->par), or
@@ -866,17 +1042,30 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
       if (e != cudaSuccess) return cuda_status(e, "step: o");
       if (!D->par && (rc = allreduce(D, D->o, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
       // tag of this layer's use: ep * layers + l + 1 (never 0: the slots start zeroed)
-      e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
-                     (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
-                     (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps, pin[0]);
+      e = cta_rows
+              ? launch_pdl(k_norm_cta<kNormAdd>, dim3(B), dim3(norm_threads), (size_t)H * 4, st,
+                           (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
+                           (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps,
+                           pin[0])
+              : launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                           (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->o,
+                           (const float *)L.gffn, D->x, fast_h ? D->ws_gu : nullptr, B, H, eps,
+                           pin[0]);
       count_launches(1);
       if (e != cudaSuccess) return cuda_status(e, "step: ffn norm");
       e = ternary_main_launch(1, D->x, 0, L.wgu, 0, L.sgu, 0, nullptr, D->gu, 0, B, 2 * D->fr, H,
                               false, fast_h ? D->ws_gu : nullptr, st);
       if (e != cudaSuccess) return cuda_status(e, "step: gate/up");
-      e = launch_pdl(k_silu_prep, dim3(gnorm), dim3(kNormThreads),
-                     (size_t)row_slice_cols(D->fr) * sizeof(float), st, (const float *)D->gu, D->a,
-                     fast_d ? D->ws_d : nullptr, B, D->fr);
+      if (silu_row4 == 1)
+        e = launch_pdl(k_silu_cta<1>, dim3(B), dim3(silu_threads), (size_t)D->fr * 4, st,
+                       (const float *)D->gu, D->a, fast_d ? D->ws_d : nullptr, B, D->fr);
+      else if (silu_row4 == 2)
+        e = launch_pdl(k_silu_cta<2>, dim3(B), dim3(silu_threads), (size_t)D->fr * 4, st,
+                       (const float *)D->gu, D->a, fast_d ? D->ws_d : nullptr, B, D->fr);
+      else
+        e = launch_pdl(k_silu_prep, dim3(gnorm), dim3(kNormThreads),
+                       (size_t)row_slice_cols(D->fr) * sizeof(float), st, (const float *)D->gu,
+                       D->a, fast_d ? D->ws_d : nullptr, B, D->fr);
       count_launches(1);
       if (e != cudaSuccess) return cuda_status(e, "step: swiglu");
       e = ternary_main_launch(1, D->a, 0, L.wd, 0, L.sd, 0, nullptr, D->d, 0, B, H, D->fr, false,
@@ -884,10 +1073,15 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
       if (e != cudaSuccess) return cuda_status(e, "step: down");
       if (!D->par && (rc = allreduce(D, D->d, (size_t)B * H, kNcclFloat32, kNcclSum))) return rc;
       const bool last = l + 1 == c.layers;
-      e = launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
-                     (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
-                     (const float *)(last ? D->gfinal : D->layers[l + 1].gattn), D->x,
-                     (!last && fast_h) ? D->ws_qkv : nullptr, B, H, eps, pin[1]);
+      const float *gn = last ? D->gfinal : D->layers[l + 1].gattn;
+      void *wsn = (!last && fast_h) ? D->ws_qkv : nullptr;
+      e = cta_rows
+              ? launch_pdl(k_norm_cta<kNormAdd>, dim3(B), dim3(norm_threads), (size_t)H * 4, st,
+                           (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
+                           gn, D->x, wsn, B, H, eps, pin[1])
+              : launch_pdl(k_norm<kNormAdd>, dim3(gnorm), dim3(kNormThreads), smem_h, st,
+                           (const int *)nullptr, (const float *)nullptr, D->h, (const float *)D->d,
+                           gn, D->x, wsn, B, H, eps, pin[1]);
       count_launches(1);
       if (e != cudaSuccess) return cuda_status(e, "step: attn norm");
     }
@@ -949,6 +1143,16 @@ int set_smem_limits(nl_decoder *D) {
                                 (int)hs)) != cudaSuccess ||
       (e = cudaFuncSetAttribute(k_silu_prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)fs)) != cudaSuccess)
+    return cuda_status(e, "decoder: smem");
+  const int hrow = (int)(D->cfg.hidden * 4u), frow = (int)(D->fr * 4u);
+  if ((e = cudaFuncSetAttribute(k_norm_cta<kNormGather>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, hrow)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_norm_cta<kNormAdd>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                hrow)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_silu_cta<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                frow)) != cudaSuccess ||
+      (e = cudaFuncSetAttribute(k_silu_cta<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                frow)) != cudaSuccess)
     return cuda_status(e, "decoder: smem");
   return NL_OK;
 }

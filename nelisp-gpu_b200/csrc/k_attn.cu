@@ -658,22 +658,42 @@ __global__ void attn_combine_prep_kernel(const float *__restrict__ part, AttnGeo
                                          float *__restrict__ C, void *ws, int *row_ctr) {
   pdl_trigger();                 // the O-projection may start streaming its weights
   pdl_wait();
+  extern __shared__ __align__(16) float xrow[];   // the finished row, for the last CTA
   __shared__ float red[32];
   __shared__ long long xred[32];
   __shared__ int s_last;
+  constexpr int SB = 8;          // splits whose loads are in flight at once
   const uint32_t bh = blockIdx.x;
   const uint32_t bb = bh / g.heads, h = bh % g.heads;
   const float *pp = part + (uint64_t)bh * g.nsplit * (HD + 2);
   float mm = -INFINITY;
-  for (uint32_t s = 0; s < g.nsplit; s++) mm = fmaxf(mm, pp[(uint64_t)s * (HD + 2)]);
+  for (uint32_t s0 = 0; s0 < g.nsplit; s0 += SB) {
+    float mv[SB];
+#pragma unroll
+    for (int u = 0; u < SB; u++)
+      mv[u] = s0 + u < g.nsplit ? pp[(uint64_t)(s0 + u) * (HD + 2)] : -INFINITY;
+#pragma unroll
+    for (int u = 0; u < SB; u++) mm = fmaxf(mm, mv[u]);
+  }
   for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
     float ll = 0.0f, oo = 0.0f;
-    for (uint32_t s = 0; s < g.nsplit; s++) {
-      const float *ps = pp + (uint64_t)s * (HD + 2);
-      if (ps[0] > -INFINITY) {
-        float c = expf(ps[0] - mm);
-        ll += ps[1] * c;
-        oo += ps[2 + d] * c;
+    for (uint32_t s0 = 0; s0 < g.nsplit; s0 += SB) {
+      float mv[SB], lv[SB], ov[SB];
+#pragma unroll
+      for (int u = 0; u < SB; u++) {
+        const bool in = s0 + u < g.nsplit;
+        const float *ps = pp + (uint64_t)(s0 + u) * (HD + 2);
+        mv[u] = in ? ps[0] : -INFINITY;
+        lv[u] = in ? ps[1] : 0.0f;
+        ov[u] = in ? ps[2 + d] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < SB; u++) {   // in split order, as attn_combine_kernel
+        if (mv[u] > -INFINITY) {
+          const float c = expf(mv[u] - mm);
+          ll += lv[u] * c;
+          oo += ov[u] * c;
+        }
       }
     }
     C[(uint64_t)bb * g.heads * HD + (uint64_t)h * HD + d] = oo / ll;
@@ -686,8 +706,67 @@ __global__ void attn_combine_prep_kernel(const float *__restrict__ part, AttnGeo
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const uint32_t cols = g.heads * (uint32_t)HD;
-  prep_row_cta(C + (uint64_t)bb * cols, cols, bb, g.B, prep_at(ws, (int)g.B, cols, 0), red, xred);
+  // The last CTA of the row: the whole row into shared memory in one round
+  // trip (every float4 load issued before any is used), its maximum, then
+  // the prep's quantisation from shared memory (prep_row_cta's format: the
+  // CTA's offset sum in slot 0, the other slots zeroed).
+  const uint32_t cols = g.heads * (uint32_t)HD, n4 = cols / 4u;
+  const float4 *c4 = reinterpret_cast<const float4 *>(C + (uint64_t)bb * cols);
+  float4 *x4 = reinterpret_cast<float4 *>(xrow);
+  constexpr int LB = 8;
+  float mx = 0.0f;
+  int bad = 0;
+  for (uint32_t i0 = threadIdx.x; i0 < n4; i0 += LB * blockDim.x) {
+    float4 v[LB];
+#pragma unroll
+    for (int u = 0; u < LB; u++) {
+      const uint32_t i = i0 + (uint32_t)u * blockDim.x;
+      v[u] = i < n4 ? __ldcg(c4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < LB; u++) {
+      const uint32_t i = i0 + (uint32_t)u * blockDim.x;
+      if (i < n4) {
+        x4[i] = v[u];
+        mx = fmaxf(fmaxf(mx, fmaxf(fabsf(v[u].x), fabsf(v[u].y))),
+                   fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+        bad |= !isfinite(v[u].x) | !isfinite(v[u].y) | !isfinite(v[u].z) | !isfinite(v[u].w);
+      }
+    }
+  }
+  const int nw = (int)(blockDim.x >> 5), w = (int)(threadIdx.x >> 5), lane = (int)(threadIdx.x & 31);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) red[w] = mx;
+  bad = __syncthreads_or(bad);
+  float rm = 0.0f;
+  for (int i = 0; i < nw; i++) rm = fmaxf(rm, red[i]);
+  PrepOut P = prep_at(ws, (int)g.B, cols, 0);
+  const int NT = n_tiles((int)g.B);
+  float mul = 0.0f, inv = 0.0f;
+  const bool ok = row_scale(rm, bad != 0, &mul, &inv);
+  if (threadIdx.x == 0) {
+    P.rowinv[bb] = inv;
+    P.rowflag[bb] = !ok;
+  }
+  long long partx = 0;
+  for (uint32_t W = threadIdx.x; W < cols / 16u; W += blockDim.x) {
+    float q[16];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const float4 f = x4[4u * W + e];
+      q[4 * e] = f.x; q[4 * e + 1] = f.y; q[4 * e + 2] = f.z; q[4 * e + 3] = f.w;
+    }
+    partx += quantize_word(q, mul, ok, W, bb, NT, P);
+  }
+  for (int o = 16; o > 0; o >>= 1) partx += __shfl_xor_sync(0xffffffffu, partx, o);
+  if (lane == 0) xred[w] = partx;
+  __syncthreads();
+  if (threadIdx.x < (unsigned)kRowCluster) {
+    long long t = 0;
+    if (threadIdx.x == 0)
+      for (int i = 0; i < nw; i++) t += xred[i];
+    P.xsum[bb * kRowCluster + threadIdx.x] = t;
+  }
   if (threadIdx.x == 0) row_ctr[bb] = 0;
 }
 
@@ -1015,10 +1094,14 @@ cudaError_t attn_rope_decode_launch(const float *QKV, float *CK, float *CV, cons
       NL_ATTN(HD, 5) NL_ATTN(HD, 6) NL_ATTN(HD, 7) NL_ATTN(HD, 8)                         \
       default: break;                                                                     \
     }                                                                                     \
+    if (e == cudaSuccess && prep_ws && row_ctr && (size_t)g.heads * HD * 4 > (48u << 10)) \
+      e = cudaFuncSetAttribute(attn_combine_prep_kernel<HD>,                               \
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,                \
+                               (int)((size_t)g.heads * HD * 4));                           \
     if (e == cudaSuccess && prep_ws && row_ctr)                                           \
       e = launch_pdl(attn_combine_prep_kernel<HD>, dim3(g.B * g.heads),                   \
-                     dim3(HD < 128 ? HD : 128), 0, st, (const float *)part, g, C, prep_ws,  \
-                     row_ctr);                                                            \
+                     dim3(HD < 128 ? HD : 128), (size_t)g.heads * HD * 4, st,               \
+                     (const float *)part, g, C, prep_ws, row_ctr);                         \
     else if (e == cudaSuccess)                                                            \
       e = launch_pdl(attn_combine_kernel<HD>, dim3(g.B * g.heads), dim3(HD < 128 ? HD : 128), \
                      0, st, (const float *)part, g, C, (uint64_t)UINT64_MAX);             \

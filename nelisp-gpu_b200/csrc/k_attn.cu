@@ -308,9 +308,13 @@ attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
     }
   };
   const uint32_t pc = has_p ? p : p1;             // cached keys: [p0, pc)
-  constexpr int U = 4;                            // key rows in flight per warp
-  for (uint32_t j0 = p0 + warp * U; j0 < pc; j0 += kAttnWarps * U) {
-    float kr[U][DPL], vr[U][DPL];
+  // Warp w takes the groups of U rows starting at p0 + w U, p0 + (w + 4) U,
+  // ...  The next group's rows are requested before the current group is
+  // folded (two groups in registers).  U = 2 keeps the kernel within the
+  // 72 registers a thread that let 7 CTAs share an SM (one wave of splits);
+  // more query heads per KV head take U = 1 for the same reason.
+  constexpr int U = GRP <= 2 ? 2 : 1;
+  auto load_rows = [&](uint32_t j0, float (&kr)[U][DPL], float (&vr)[U][DPL]) {
 #pragma unroll
     for (int u = 0; u < U; u++) {
       const uint32_t j = j0 + u;
@@ -329,10 +333,27 @@ attn_rope_partial_kernel(const float *__restrict__ QKV, float *__restrict__ CK,
         }
       }
     }
+  };
+  {
+    float kr[U][DPL], vr[U][DPL];
+    uint32_t j0 = p0 + warp * U;
+    if (j0 < pc) load_rows(j0, kr, vr);
+    for (; j0 < pc; j0 += kAttnWarps * U) {
+      float kq[U][DPL], vq[U][DPL];
+      const uint32_t jn = j0 + kAttnWarps * U;
+      if (jn < pc) load_rows(jn, kq, vq);
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      if (j0 + u >= pc) break;
-      fold(kr[u], vr[u]);
+      for (int u = 0; u < U; u++) {
+        if (j0 + u >= pc) break;
+        fold(kr[u], vr[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < U; u++)
+#pragma unroll
+        for (int d = 0; d < DPL; d++) {
+          kr[u][d] = kq[u][d];
+          vr[u][d] = vq[u][d];
+        }
     }
   }
   if (has_p && warp == (int)(((pc - p0) / U) % kAttnWarps)) fold(kn, vn);

@@ -644,6 +644,71 @@ cudaError_t causal_launch(const float *Q, const float *K, const float *V, float 
 }
 
 // One CTA per (b, h): merge the splits and write C.
+// One head's merge at output lane d: the NSPLIT partials (max, sum, HD
+// outputs each) are combined with the global maximum first, then the scaled
+// sums in split order.  Up to kMergeBatch splits -- a decode step's usual
+// count -- are loaded in one round trip; more take two passes in batches.
+constexpr int kMergeBatch = 32;
+template <int HD>
+__device__ __forceinline__ float merge_splits(const float *__restrict__ pp, uint32_t nsplit,
+                                              uint32_t d) {
+  if (nsplit <= (uint32_t)kMergeBatch) {
+    float mv[kMergeBatch], lv[kMergeBatch], ov[kMergeBatch];
+#pragma unroll
+    for (int u = 0; u < kMergeBatch; u++) {
+      const bool in = (uint32_t)u < nsplit;
+      const float *ps = pp + (uint64_t)u * (HD + 2);
+      mv[u] = in ? ps[0] : -INFINITY;
+      lv[u] = in ? ps[1] : 0.0f;
+      ov[u] = in ? ps[2 + d] : 0.0f;
+    }
+    float mm = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kMergeBatch; u++) mm = fmaxf(mm, mv[u]);
+    float ll = 0.0f, oo = 0.0f;
+#pragma unroll
+    for (int u = 0; u < kMergeBatch; u++) {
+      if (mv[u] > -INFINITY) {
+        const float c = expf(mv[u] - mm);
+        ll += lv[u] * c;
+        oo += ov[u] * c;
+      }
+    }
+    return oo / ll;
+  }
+  constexpr int SB = 8;
+  float mm = -INFINITY;
+  for (uint32_t s0 = 0; s0 < nsplit; s0 += SB) {
+    float mv[SB];
+#pragma unroll
+    for (int u = 0; u < SB; u++)
+      mv[u] = s0 + u < nsplit ? pp[(uint64_t)(s0 + u) * (HD + 2)] : -INFINITY;
+#pragma unroll
+    for (int u = 0; u < SB; u++) mm = fmaxf(mm, mv[u]);
+  }
+  float ll = 0.0f, oo = 0.0f;
+  for (uint32_t s0 = 0; s0 < nsplit; s0 += SB) {
+    float mv[SB], lv[SB], ov[SB];
+#pragma unroll
+    for (int u = 0; u < SB; u++) {
+      const bool in = s0 + u < nsplit;
+      const float *ps = pp + (uint64_t)(s0 + u) * (HD + 2);
+      mv[u] = in ? ps[0] : -INFINITY;
+      lv[u] = in ? ps[1] : 0.0f;
+      ov[u] = in ? ps[2 + d] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < SB; u++) {
+      if (mv[u] > -INFINITY) {
+        const float c = expf(mv[u] - mm);
+        ll += lv[u] * c;
+        oo += ov[u] * c;
+      }
+    }
+  }
+  return oo / ll;
+}
+
 template <int HD>
 __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
                                     float *__restrict__ C, uint64_t limit) {
@@ -651,20 +716,10 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, AttnGeom g,
   const uint32_t bh = blockIdx.x;
   const uint32_t bb = bh / g.heads, h = bh % g.heads;
   const float *pp = part + (uint64_t)bh * g.nsplit * (HD + 2);
-  float mm = -INFINITY;
-  for (uint32_t s = 0; s < g.nsplit; s++) mm = fmaxf(mm, pp[(uint64_t)s * (HD + 2)]);
   for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
-    float ll = 0.0f, oo = 0.0f;
-    for (uint32_t s = 0; s < g.nsplit; s++) {
-      const float *ps = pp + (uint64_t)s * (HD + 2);
-      if (ps[0] > -INFINITY) {
-        float c = expf(ps[0] - mm);
-        ll += ps[1] * c;
-        oo += ps[2 + d] * c;
-      }
-    }
-    uint64_t idx = (uint64_t)bb * g.heads * HD + (uint64_t)h * HD + d;
-    if (idx < limit) C[idx] = oo / ll;
+    const uint64_t idx = (uint64_t)bb * g.heads * HD + (uint64_t)h * HD + d;
+    const float v = merge_splits<HD>(pp, g.nsplit, d);
+    if (idx < limit) C[idx] = v;
   }
 }
 
@@ -683,42 +738,11 @@ __global__ void attn_combine_prep_kernel(const float *__restrict__ part, AttnGeo
   __shared__ float red[32];
   __shared__ long long xred[32];
   __shared__ int s_last;
-  constexpr int SB = 8;          // splits whose loads are in flight at once
   const uint32_t bh = blockIdx.x;
   const uint32_t bb = bh / g.heads, h = bh % g.heads;
   const float *pp = part + (uint64_t)bh * g.nsplit * (HD + 2);
-  float mm = -INFINITY;
-  for (uint32_t s0 = 0; s0 < g.nsplit; s0 += SB) {
-    float mv[SB];
-#pragma unroll
-    for (int u = 0; u < SB; u++)
-      mv[u] = s0 + u < g.nsplit ? pp[(uint64_t)(s0 + u) * (HD + 2)] : -INFINITY;
-#pragma unroll
-    for (int u = 0; u < SB; u++) mm = fmaxf(mm, mv[u]);
-  }
-  for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
-    float ll = 0.0f, oo = 0.0f;
-    for (uint32_t s0 = 0; s0 < g.nsplit; s0 += SB) {
-      float mv[SB], lv[SB], ov[SB];
-#pragma unroll
-      for (int u = 0; u < SB; u++) {
-        const bool in = s0 + u < g.nsplit;
-        const float *ps = pp + (uint64_t)(s0 + u) * (HD + 2);
-        mv[u] = in ? ps[0] : -INFINITY;
-        lv[u] = in ? ps[1] : 0.0f;
-        ov[u] = in ? ps[2 + d] : 0.0f;
-      }
-#pragma unroll
-      for (int u = 0; u < SB; u++) {   // in split order, as attn_combine_kernel
-        if (mv[u] > -INFINITY) {
-          const float c = expf(mv[u] - mm);
-          ll += lv[u] * c;
-          oo += ov[u] * c;
-        }
-      }
-    }
-    C[(uint64_t)bb * g.heads * HD + (uint64_t)h * HD + d] = oo / ll;
-  }
+  for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x)
+    C[(uint64_t)bb * g.heads * HD + (uint64_t)h * HD + d] = merge_splits<HD>(pp, g.nsplit, d);
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();

@@ -54,6 +54,14 @@ def test_decoder_matches_cpu_model_gqa_batch3():
     check_against_cpu(cfg, prompt, steps=5, max_seq=12)
 
 
+def test_decoder_long_cache_many_splits():
+    # max_seq 1100 over 4 KV heads at batch 1: 35 attention splits of 32 keys,
+    # more than the merge loads in one round trip (its batched two-pass form)
+    rng = np.random.default_rng(4)
+    prompt = rng.integers(0, SMALL["vocab"], size=(1, 5))
+    check_against_cpu(SMALL, prompt, steps=4, max_seq=1100)
+
+
 def test_decoder_bitnet_shapes_one_layer():
     # the benchmark's layer shapes (hidden 2560, 20 heads of 128, FFN 6912)
     cfg = dict(hidden=2560, layers=1, heads=20, kv_heads=20, head_dim=128, ffn=6912,

@@ -188,6 +188,7 @@ def test_decode_rope_b_and_cache_append_b(host):
     (1, 20, 20, 128, 96, 0),       # one key
     (3, 6, 3, 64, 70, 69),
     (2, 4, 2, 16, 33, 20),         # head size the split kernel does not cover
+    (1, 4, 1, 128, 2048, 1500),    # 64 splits: the merge's batched two-pass form
 ])
 def test_decode_attn_b(host, B, heads, kvheads, hd, maxseq, pos):
     rng = np.random.default_rng(B * 100 + hd + pos)
@@ -244,6 +245,7 @@ def _rope_np(x, pos, hd, base):
     (2, 20, 20, 128, 700, 511),     # the decoder's head shape, mid-sequence
     (3, 8, 2, 64, 100, 0),          # GQA, first position
     (1, 12, 4, 32, 64, 40),
+    (1, 2, 2, 64, 1200, 1199),      # 38 splits, the last key at the cache end
 ])
 def test_decode_attn_rope_matches_reference_composition(B, heads, kvheads, hd, maxseq, pos):
     """nl_decode_attn_rope_dev against the reference's three dispatches run on

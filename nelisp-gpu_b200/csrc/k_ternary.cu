@@ -505,24 +505,32 @@ __device__ __forceinline__ uint2 lds64(uint32_t addr) {
   return v;
 }
 
-__host__ __device__ inline int tma_stages(int NT, int nw) {
-  int per = 2048 * nw + NT * kTmaBlocks * 1024;
-  int st = (112 * 1024) / per;
+// 16-row groups a consumer warp multiplies per item.  The one-n-tile offset
+// path takes two: both groups' MMAs use each activation fragment load, and
+// the ring wait, the stage release and the loop cost are paid once per two
+// groups' weights.  Its CTA then fills an SM alone (ring up to 200 KB, the
+// register file for 9 warps).  Other paths take one group, two CTAs an SM.
+__host__ __device__ constexpr int tma_groups(int NT, bool per_block) {
+  return (!per_block && NT == 1) ? 2 : 1;
+}
+__host__ __device__ inline int tma_stages(int NT, int nw, int rg) {
+  int per = 2048 * nw * rg + NT * kTmaBlocks * 1024;
+  int st = ((rg == 1 ? 112 : nw >= 8 ? 200 : 100) * 1024) / per;
   return st < 2 ? 2 : (st > 6 ? 6 : st);
 }
-__host__ __device__ inline size_t tma_smem_bytes(int NT, int nw) {
-  int S = tma_stages(NT, nw);
-  return 1024 /* alignment slack */ + (size_t)S * (2048 * nw + NT * kTmaBlocks * 1024) +
-         (size_t)2 * S * 8 + (size_t)nw * 16 * (8 * NT + 1) * 4;
+__host__ __device__ inline size_t tma_smem_bytes(int NT, int nw, int rg) {
+  int S = tma_stages(NT, nw, rg);
+  return 1024 /* alignment slack */ + (size_t)S * (2048 * nw * rg + NT * kTmaBlocks * 1024) +
+         (size_t)2 * S * 8 + (size_t)nw * 16 * rg * (8 * NT + 1) * 4;
 }
 
 // Persistent: a grid of at most (resident CTAs per SM) x 148 CTAs walks the
-// work items -- (problem z, tile of 16*nw rows) -- round-robin.  The producer
+// work items -- (problem z, tile of 16*RG*nw rows) -- round-robin.  The producer
 // warp streams the (item, chunk) sequence through the S-stage ring without a
 // break between items, so the copies of a CTA's next item are in flight while
 // the consumers finish the current one and run its epilogue.
 template <int NT, bool PER_BLOCK>
-__global__ void __launch_bounds__(288, NT <= 3 ? 2 : 1)
+__global__ void __launch_bounds__(288, (NT <= 3 && tma_groups(NT, PER_BLOCK) == 1) ? 2 : 1)
 ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restrict__ X,
                    uint64_t x_stride, const uint32_t *__restrict__ WP, uint64_t w_stride,
                    const float *__restrict__ SCALE, uint64_t s_stride,
@@ -532,8 +540,11 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   extern __shared__ uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = (blockDim.x >> 5) - 1;            // consumer warps; warp nw produces
-  const int S = tma_stages(NT, nw);
-  const uint32_t wbytes = 2048u * nw;              // weight tile per stage
+  constexpr int RG = tma_groups(NT, PER_BLOCK);
+  constexpr uint32_t R = 16u * RG;                 // rows of one warp's item
+  static_assert(RG == 1 || !PER_BLOCK, "per-block scales take one row group");
+  const int S = tma_stages(NT, nw, RG);
+  const uint32_t wbytes = 2048u * nw * RG;         // weight tile per stage
   const uint32_t fstage = NT * kTmaBlocks * 128;   // fragment uint2 per stage
   uint8_t *base = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -545,7 +556,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
 
   const uint32_t nblk = cols / 128u, wng = cols / 16u;
   const uint32_t nchunk = (nblk + kTmaBlocks - 1) / kTmaBlocks;
-  const uint32_t tpp = (out + 16u * nw - 1) / (16u * nw);   // tiles per problem
+  const uint32_t tpp = (out + R * nw - 1) / (R * nw);       // tiles per problem
   const uint32_t items = tpp * count;
 
   if (threadIdx.x == 0) {
@@ -578,7 +589,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
         const uint32_t nb = min((uint32_t)kTmaBlocks, nblk - c * kTmaBlocks);
         mbar_expect_tx(&full[st], wbytes + (uint32_t)kTmaBlocks * NT * 1024u);
         tma_load_2d(wbuf + (size_t)st * wbytes, &tmW, (int)(c * 32u),
-                    (int)(z * out + tile * 16u * nw), &full[st]);
+                    (int)(z * out + tile * R * nw), &full[st]);
         if (nb < (uint32_t)kTmaBlocks)             // the blocks past the row end
           bulk_load(fbuf + (size_t)st * fstage + (size_t)nb * NT * 128u, g_zero_frags,
                     ((uint32_t)kTmaBlocks - nb) * NT * 1024u, &full[st]);
@@ -618,7 +629,8 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
   // Byte offsets of this lane's 8-byte words in a stage's weight tile: row r
   // of the tile holds 128 bytes; the 16-byte chunk k of row r sits at chunk
   // k ^ (r % 8) (128B swizzle).  Block b, words 2q..2q+1 -> chunk 2b + q/2.
-  const uint32_t rowA = (uint32_t)warp * 16u + gq, rowB = rowA + 8u;
+  // Row group g of the warp adds 16 g rows: 2048 g bytes, same swizzle.
+  const uint32_t rowA = (uint32_t)warp * R + gq, rowB = rowA + 8u;
   uint32_t offA[kTmaBlocks], offB[kTmaBlocks];
 #pragma unroll
   for (int b = 0; b < kTmaBlocks; b++) {
@@ -626,23 +638,23 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     offA[b] = rowA * 128u + ((k ^ (rowA & 7u)) << 4) + in;
     offB[b] = rowB * 128u + ((k ^ (rowB & 7u)) << 4) + in;
   }
-  int(*s_acc)[8 * NT + 1] = reinterpret_cast<int(*)[8 * NT + 1]>(epi + warp * 16 * (8 * NT + 1));
+  int(*s_acc)[8 * NT + 1] = reinterpret_cast<int(*)[8 * NT + 1]>(epi + warp * R * (8 * NT + 1));
 
   const uint32_t wsm = smem_u32(wbuf), fsm = smem_u32(fbuf);
   int cst = 0;                                     // ring stage and lap parity
   uint32_t cph = 0;
   for (uint32_t it = blockIdx.x; it < items; it += gridDim.x) {
     const uint32_t z = it / tpp, tile = it % tpp;
-    const uint32_t rg = tile * nw + warp;          // 16-row group within problem z
-    const bool active = rg * 16u < out;
-    const uint32_t rA = active ? min(rg * 16u + (uint32_t)gq, out - 1u) : 0u;
-    const uint32_t rB = active ? min(rg * 16u + (uint32_t)gq + 8u, out - 1u) : 0u;
+    const uint32_t rbase = (tile * nw + warp) * R;  // this warp's first row in problem z
+    const bool active = rbase < out;
+    const uint32_t rA = active ? min(rbase + (uint32_t)gq, out - 1u) : 0u;
+    const uint32_t rB = active ? min(rbase + (uint32_t)gq + 8u, out - 1u) : 0u;
     const float *Sz = SCALE + z * s_stride;
     PrepOut P = prep_at(ws, (int)seq, cols, z);
     // The epilogue's operands, requested now so their latency hides behind
-    // the chunk loop: lane l holds the scale and bias of row l % 16 of the
-    // group and the inverse scale and flag of sequence row l.
-    const uint32_t erow = active ? min(rg * 16u + (uint32_t)(lane & 15), out - 1u) : 0u;
+    // the chunk loop: lane l holds the scale and bias of row l % R of the
+    // warp's rows and the inverse scale and flag of sequence row l.
+    const uint32_t erow = active ? min(rbase + (uint32_t)lane % R, out - 1u) : 0u;
     const float e_scale = PER_BLOCK ? 0.0f : __ldg(Sz + erow);
     const float e_bias = BIAS ? __ldg(BIAS + erow) : 0.0f;
     const float e_rinv = (uint32_t)lane < seq ? P.rowinv[lane] : 0.0f;
@@ -653,7 +665,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     else
       xl.zero();
 
-    int acc[NT][4][4];                    // [n-tile][k-step][reg]: independent chains
+    int acc[RG][NT][4][4];                // [group][n-tile][k-step][reg]: independent chains
     float yf[NT][4];
 #pragma unroll
     for (int t = 0; t < NT; t++)
@@ -661,7 +673,9 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       for (int r = 0; r < 4; r++) {
         yf[t][r] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[t][j][r] = 0;
+        for (int g = 0; g < RG; g++)
+#pragma unroll
+          for (int j = 0; j < 4; j++) acc[g][t][j][r] = 0;
       }
 
     // Chunks run without a per-block test: in the row's last chunk, when
@@ -674,21 +688,27 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       const uint32_t fb = fsm + (uint32_t)cst * (fstage * 8u) + (uint32_t)lane * 16u;
 #pragma unroll
       for (int b = 0; b < kTmaBlocks; b++) {
-        const uint2 a = lds64(wt + offA[b]);
-        const uint2 cw = lds64(wt + offB[b]);
-        uint32_t A[4][4];
-        if (OFF)
-          unpack_offset(a, cw, xkey, A);
-        else
-          unpack_signed(a, cw, A);
+        uint32_t A[RG][4][4];
+#pragma unroll
+        for (int g = 0; g < RG; g++) {
+          const uint2 a = lds64(wt + offA[b] + 2048u * g);
+          const uint2 cw = lds64(wt + offB[b] + 2048u * g);
+          if (OFF)
+            unpack_offset(a, cw, xkey, A[g]);
+          else
+            unpack_signed(a, cw, A[g]);
+        }
 #pragma unroll
         for (int t = 0; t < NT; t++) {
           const uint32_t ft = fb + (uint32_t)(b * NT + t) * 1024u;
           const uint4 f01 = lds128(ft), f23 = lds128(ft + 512u);
-          mma_s8(acc[t][0], A[0][0], A[0][1], A[0][2], A[0][3], lo2(f01));
-          mma_s8(acc[t][1], A[1][0], A[1][1], A[1][2], A[1][3], hi2(f01));
-          mma_s8(acc[t][2], A[2][0], A[2][1], A[2][2], A[2][3], lo2(f23));
-          mma_s8(acc[t][3], A[3][0], A[3][1], A[3][2], A[3][3], hi2(f23));
+#pragma unroll
+          for (int g = 0; g < RG; g++) {
+            mma_s8(acc[g][t][0], A[g][0][0], A[g][0][1], A[g][0][2], A[g][0][3], lo2(f01));
+            mma_s8(acc[g][t][1], A[g][1][0], A[g][1][1], A[g][1][2], A[g][1][3], hi2(f01));
+            mma_s8(acc[g][t][2], A[g][2][0], A[g][2][1], A[g][2][2], A[g][2][3], lo2(f23));
+            mma_s8(acc[g][t][3], A[g][3][0], A[g][3][1], A[g][3][2], A[g][3][3], hi2(f23));
+          }
         }
         if (PER_BLOCK) {
           const uint32_t blk = c * kTmaBlocks + b;
@@ -699,9 +719,10 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
             for (int t = 0; t < NT; t++) {
 #pragma unroll
               for (int r = 0; r < 4; r++) {
-                const int v = acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
+                int(&a0)[4][4] = acc[0][t];
+                const int v = a0[0][r] + a0[1][r] + a0[2][r] + a0[3][r];
                 yf[t][r] = fmaf((float)v, r < 2 ? bA : bB, yf[t][r]);
-                acc[t][0][r] = acc[t][1][r] = acc[t][2][r] = acc[t][3][r] = 0;
+                a0[0][r] = a0[1][r] = a0[2][r] = a0[3][r] = 0;
               }
             }
           }
@@ -717,33 +738,36 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     if (!active) continue;
 
 #pragma unroll
-    for (int t = 0; t < NT; t++) {
-      int v[4];
+    for (int g = 0; g < RG; g++)
 #pragma unroll
-      for (int r = 0; r < 4; r++)
-        v[r] = PER_BLOCK ? __float_as_int(yf[t][r])
-                 : OFF ? offset_combine(acc[t][0][r], acc[t][1][r], acc[t][2][r], acc[t][3][r])
-                       : acc[t][0][r] + acc[t][1][r] + acc[t][2][r] + acc[t][3][r];
-      s_acc[gq][8 * t + 2 * q] = v[0];
-      s_acc[gq][8 * t + 2 * q + 1] = v[1];
-      s_acc[gq + 8][8 * t + 2 * q] = v[2];
-      s_acc[gq + 8][8 * t + 2 * q + 1] = v[3];
-    }
+      for (int t = 0; t < NT; t++) {
+        const int(&a)[4][4] = acc[g][t];
+        int v[4];
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+          v[r] = PER_BLOCK ? __float_as_int(yf[t][r])
+                   : OFF ? offset_combine(a[0][r], a[1][r], a[2][r], a[3][r])
+                         : a[0][r] + a[1][r] + a[2][r] + a[3][r];
+        s_acc[16 * g + gq][8 * t + 2 * q] = v[0];
+        s_acc[16 * g + gq][8 * t + 2 * q + 1] = v[1];
+        s_acc[16 * g + gq + 8][8 * t + 2 * q] = v[2];
+        s_acc[16 * g + gq + 8][8 * t + 2 * q + 1] = v[3];
+      }
     __syncwarp();
     const uint32_t *Wz = WP + z * w_stride;
     float *Yz = Y + z * y_stride;
     const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
     const long long e_xsum = OFF ? xl.total(lane) : 0ll;
-    for (uint32_t k = 0; k * 32u < 16u * seq; k++) {     // uniform trip count: shuffles
+    for (uint32_t k = 0; k * 32u < R * seq; k++) {       // uniform trip count: shuffles
       const uint32_t idx = (uint32_t)lane + 32u * k;
-      const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
+      const uint32_t r = idx % R, s = min(idx / R, 31u);
       const float sc = __shfl_sync(0xffffffffu, e_scale, (int)r);
       const float bi = __shfl_sync(0xffffffffu, e_bias, (int)r);
       const float ri = __shfl_sync(0xffffffffu, e_rinv, (int)s);
       const int fl = __shfl_sync(0xffffffffu, e_flag, (int)s);
       const long long xs2 = OFF ? 2ll * __shfl_sync(0xffffffffu, e_xsum, (int)s) : 0ll;
-      const uint32_t o = rg * 16u + r;
-      if (idx >= 16u * seq || o >= out || fl) continue;
+      const uint32_t o = rbase + r;
+      if (idx >= R * seq || o >= out || fl) continue;
       float yv;
       if (PER_BLOCK) {
         const int *sr = s_acc[r];
@@ -765,8 +789,8 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     }
     if (any_flag) {
       const float *Xz = X + z * x_stride;
-      for (uint32_t r = 0; r < 16u; r++) {
-        const uint32_t o = rg * 16u + r;
+      for (uint32_t r = 0; r < R; r++) {
+        const uint32_t o = rbase + r;
         if (o >= out) break;
         float acc8[8];
         const uint32_t *Wrow = Wz + (uint64_t)o * wng;
@@ -1082,9 +1106,10 @@ cudaError_t launch_tma_nt(const CUtensorMap &map, uint32_t items, int nw, cudaSt
                           uint32_t count) {
   static int configured = 0;
   static int per_sm[9] = {0};                  // resident CTAs per SM, by nw
-  size_t smem = tma_smem_bytes(NT, 2);         // the largest CTA this instance runs
-  if (tma_smem_bytes(NT, 4) > smem) smem = tma_smem_bytes(NT, 4);
-  if (tma_smem_bytes(NT, 8) > smem) smem = tma_smem_bytes(NT, 8);
+  constexpr int RG = tma_groups(NT, PB);
+  size_t smem = tma_smem_bytes(NT, 2, RG);     // the largest CTA this instance runs
+  if (tma_smem_bytes(NT, 4, RG) > smem) smem = tma_smem_bytes(NT, 4, RG);
+  if (tma_smem_bytes(NT, 8, RG) > smem) smem = tma_smem_bytes(NT, 8, RG);
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(ternary_tma_kernel<NT, PB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1094,7 +1119,7 @@ cudaError_t launch_tma_nt(const CUtensorMap &map, uint32_t items, int nw, cudaSt
   if (!per_sm[nw]) {
     int n = 0;
     cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-        &n, ternary_tma_kernel<NT, PB>, 32 * (nw + 1), tma_smem_bytes(NT, nw));
+        &n, ternary_tma_kernel<NT, PB>, 32 * (nw + 1), tma_smem_bytes(NT, nw, RG));
     if (e != cudaSuccess) return e;
     per_sm[nw] = n > 0 ? n : 1;
   }
@@ -1110,7 +1135,7 @@ cudaError_t launch_tma_nt(const CUtensorMap &map, uint32_t items, int nw, cudaSt
   // The preceding kernel in the stream is always this GEMV's own prep (or a
   // kernel with the prep fused in), launched without the attribute.
   return launch_pdl(ternary_tma_kernel<NT, PB>, dim3(grid), dim3(32 * (nw + 1)),
-                    tma_smem_bytes(NT, nw), st, map, X, xs, WP, wst, S, ss, B, Y, ys, seq,
+                    tma_smem_bytes(NT, nw, RG), st, map, X, xs, WP, wst, S, ss, B, Y, ys, seq,
                     out, cols, limit, ws, count, wait_flag_device());
 }
 
@@ -1128,13 +1153,16 @@ bool try_launch_tma(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   }();
   const uint32_t wng = cols / 16u;
   if (!use_tma || (count > 1 && wst != (uint64_t)out * wng)) return false;
-  const int groups16 = ceil_div((int)out, 16);
-  int nw = 8;
-  while (nw > 2 && (uint64_t)ceil_div(groups16, nw) * count < 2u * 148u) nw >>= 1;
-  CUtensorMap map;
-  if (!make_weight_map(&map, WP, (uint64_t)count * out, wng, nw)) return false;
-  const uint32_t items = (uint32_t)ceil_div(groups16, nw) * count;
   const int NT = n_tiles((int)seq);
+  const int rg = tma_groups(NT, per_block);
+  // warps of RG 16-row groups; enough items for every resident CTA
+  const int groups = ceil_div((int)out, 16 * rg);
+  const uint64_t want = rg == 1 ? 2u * 148u : 148u;
+  int nw = 8;
+  while (nw > 2 && (uint64_t)ceil_div(groups, nw) * count < want) nw >>= 1;
+  CUtensorMap map;
+  if (!make_weight_map(&map, WP, (uint64_t)count * out, wng, nw * rg)) return false;
+  const uint32_t items = (uint32_t)ceil_div(groups, nw) * count;
 #define NL_CASE(N)                                                                         \
   case N:                                                                                  \
     *err = per_block ? launch_tma_nt<N, true>(map, items, nw, st, X, xs, WP, wst, S, ss, B, \

@@ -413,7 +413,7 @@ def run_gpu(args):
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int8xint8->int32 (exact ternary x 3-limb activations) + f32 epilogue",
+            "dtype": "int8xint8->int32 (exact ternary x int8-limb activations) + f32 epilogue",
             "data": "synthetic (seeded; trits p=1/3, s~U[0.5,1.5], x~N(0,1))",
             "config": gemv_config(batch),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,

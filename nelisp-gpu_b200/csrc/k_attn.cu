@@ -786,9 +786,9 @@ __global__ void attn_combine_prep_kernel(const float *__restrict__ part, AttnGeo
   float rm = 0.0f;
   for (int i = 0; i < nw; i++) rm = fmaxf(rm, red[i]);
   PrepOut P = prep_at(ws, (int)g.B, cols, 0);
-  const int NT = n_tiles((int)g.B);
+  const int NT = n_tiles((int)g.B), L = n_limbs((int)g.B);
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(rm, bad != 0, &mul, &inv);
+  const bool ok = row_scale(rm, bad != 0, &mul, &inv, L);
   if (threadIdx.x == 0) {
     P.rowinv[bb] = inv;
     P.rowflag[bb] = !ok;
@@ -801,7 +801,7 @@ __global__ void attn_combine_prep_kernel(const float *__restrict__ part, AttnGeo
       const float4 f = x4[4u * W + e];
       q[4 * e] = f.x; q[4 * e + 1] = f.y; q[4 * e + 2] = f.z; q[4 * e + 3] = f.w;
     }
-    partx += quantize_word(q, mul, ok, W, bb, NT, P);
+    partx += quantize_word(q, mul, ok, W, bb, NT, L, P);
   }
   for (int o = 16; o > 0; o >>= 1) partx += __shfl_xor_sync(0xffffffffu, partx, o);
   if (lane == 0) xred[w] = partx;

@@ -12,19 +12,21 @@
 // the arithmetic onto the tensor cores in exact integer form:
 //
 //  * prep: every activation row s is scaled by a power of two 2^e_s so that
-//    max|x| lands in [2^21, 2^22), rounded to an integer xq and split into
-//    three balanced int8 limbs, xq = l0 + 256 l1 + 65536 l2.  The rounding is
-//    the only inexact step (half a unit of 2^-22 of the row maximum, below
-//    f32's own accumulation error over a row).  Limbs are written straight
-//    into mma B-fragment order, so the main loop loads one uint2 per MMA.
+//    max|x| lands in [2^(8L-3), 2^(8L-2)), rounded to an integer xq and split
+//    into L balanced int8 limbs, xq = l0 + 256 l1 + 65536 l2 (+ 2^24 l3):
+//    L = 4 (30 bits) for up to four sequence rows, whose limb columns fit
+//    the n-tiles three would take, else L = 3 (22 bits).  The rounding is the
+//    only inexact step (half a unit of 2^-(8L-2) of the row maximum).  Limbs
+//    are written straight into mma B-fragment order, so the main loop loads
+//    one uint2 per MMA.
 //  * main: each warp owns 16 weight rows.  Lanes load the packed words
 //    (8 bytes per row per 128-column block, 4 lanes per row), turn the
 //    two-bit codes into int8 operands with a shift and a mask per four codes
 //    (a code in the top two bits of a byte is 64 times its trit:
 //    00->0, 01->+1, 10->-2, 11->-1, the reference's sign-extending decode)
 //    and issue mma.m16n8k32.s8 with int32 accumulation: the dot products are
-//    exact.  N carries (sequence, limb) pairs: n = 3s + l.
-//  * epilogue: the three limb sums of (row, s) are combined in int64,
+//    exact.  N carries (sequence, limb) pairs: n = L s + l.
+//  * epilogue: the L limb sums of (row, s) are combined in int64,
 //    converted once and scaled by 2^-e_s and the row's scale (per-row mode),
 //    or flushed per 128-column block against BETA[o,b] (ternary-rows mode).
 //
@@ -365,7 +367,7 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
   if (!active) return;
 
   // Epilogue: stage per-(row, n) results in shared memory (reusing the
-  // fragment buffers), then combine the three limbs of each (row, s).
+  // fragment buffers), then combine the limbs of each (row, s).
   // Per-block results are float sums; they travel as bit patterns.
   int(*s_acc)[8 * NT + 1] =
       reinterpret_cast<int(*)[8 * NT + 1]>(reinterpret_cast<int *>(smem) + warp * 16 * (8 * NT + 1));
@@ -384,19 +386,16 @@ ternary_mma_kernel(const float *__restrict__ X, uint64_t x_stride,
   float *Yz = Y + z * y_stride;
   bool any_flag = false;
   for (uint32_t s = 0; s < seq; s++) any_flag |= (P.rowflag[s] != 0);
+  const int L = n_limbs((int)seq);
   for (uint32_t idx = lane; idx < 16u * seq; idx += 32u) {
     const uint32_t r = idx & 15u, s = idx >> 4;
     const uint32_t o = rg * 16u + r;
     if (o >= out) continue;
     float y;
     if (PER_BLOCK) {
-      const int *sr = s_acc[r];
-      float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
-      v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
-      y = v * P.rowinv[s];
+      y = limb_total_f(s_acc[r], s, L) * P.rowinv[s];
     } else {
-      long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
-                      65536ll * s_acc[r][3 * s + 2];
+      long long tot = limb_total(s_acc[r], s, L);
       tot >>= 6;                               // the operands carried 64 * t: exact
       y = ((float)tot * P.rowinv[s]) * __ldg(Sz + o);
     }
@@ -758,6 +757,7 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
     float *Yz = Y + z * y_stride;
     const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
     const long long e_xsum = OFF ? xl.total(lane) : 0ll;
+    const int L = n_limbs((int)seq);
     for (uint32_t k = 0; k * 32u < R * seq; k++) {       // uniform trip count: shuffles
       const uint32_t idx = (uint32_t)lane + 32u * k;
       const uint32_t r = idx % R, s = min(idx / R, 31u);
@@ -770,13 +770,9 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
       if (idx >= R * seq || o >= out || fl) continue;
       float yv;
       if (PER_BLOCK) {
-        const int *sr = s_acc[r];
-        float v = __int_as_float(sr[3 * s]) + __int_as_float(sr[3 * s + 1]) * 256.0f;
-        v = (v + __int_as_float(sr[3 * s + 2]) * 65536.0f) * 0.015625f;   // / 64, exact
-        yv = v * ri;
+        yv = limb_total_f(s_acc[r], s, L) * ri;
       } else {
-        long long tot = (long long)s_acc[r][3 * s] + 256ll * s_acc[r][3 * s + 1] +
-                        65536ll * s_acc[r][3 * s + 2];
+        long long tot = limb_total(s_acc[r], s, L);
         if (OFF)
           tot -= xs2;                            // the offset operands' 2 sum x
         else
@@ -976,6 +972,7 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   if (live) {
     const bool any_flag = __any_sync(0xffffffffu, e_flag != 0);
     const long long e_xsum = OFF ? xl.total(lane) : 0ll;
+    const int L = n_limbs((int)seq);
     for (uint32_t k = (uint32_t)kw; k * 32u < 16u * seq; k += (uint32_t)wpt) {   // warp-uniform
       const uint32_t idx = (uint32_t)lane + 32u * k;
       const uint32_t r = idx & 15u, s = min(idx >> 4, 31u);
@@ -986,8 +983,7 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
       const long long xs2 = OFF ? 2ll * __shfl_sync(0xffffffffu, e_xsum, (int)s) : 0ll;
       const uint32_t o = rt * 16u + r;
       if (idx >= 16u * seq || o >= out || fl) continue;
-      long long tot = (long long)s_acc[tl][r][3 * s] + 256ll * s_acc[tl][r][3 * s + 1] +
-                      65536ll * s_acc[tl][r][3 * s + 2];
+      long long tot = limb_total(s_acc[tl][r], s, L);
       if (OFF)
         tot -= xs2;                                // the offset operands' 2 sum x
       else
@@ -1293,9 +1289,14 @@ cudaError_t ternary_gemv_launch(uint32_t count, const float *X,
     if (launched || e != cudaSuccess) return e;
   }
   // Sequences in chunks of 16 (one prep + one main launch per chunk); the
-  // workspace is reused chunk to chunk, ordered by the stream.
-  for (uint32_t s0 = 0; s0 < seq; s0 += kMaxFastSeq) {
-    uint32_t ns = min((uint32_t)kMaxFastSeq, seq - s0);
+  // workspace is reused chunk to chunk, ordered by the stream.  Past 16 rows
+  // no chunk is left with four rows or fewer (the last two share the rest
+  // evenly): every row then gets the three-limb precision that the tcgen05
+  // GEMM gives such calls, whichever kernel runs.
+  for (uint32_t s0 = 0, ns = 0; s0 < seq; s0 += ns) {
+    ns = min((uint32_t)kMaxFastSeq, seq - s0);
+    if (seq > (uint32_t)kMaxFastSeq && seq - s0 > ns && seq - s0 - ns <= 4u)
+      ns = (seq - s0 + 1u) / 2u;
     int NT = n_tiles((int)ns);
     // Programmatic launch: the prep's blocks become resident while the
     // preceding kernel drains and wait (griddepcontrol.wait) before they

@@ -279,7 +279,7 @@ tc_prep_kernel(const float *__restrict__ X, uint64_t x_stride, uint32_t seq, uin
     anybad |= *cl.map_shared_rank(&s_bad, k);
   }
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(mm, anybad != 0, &mul, &inv);
+  const bool ok = row_scale(mm, anybad != 0, &mul, &inv, 3);
   TcPrep P = tc_prep_at(ws, count, seq, cols);
   if (rank == 0 && threadIdx.x == 0) {
     P.rowinv[z * 16 + s] = inv;
@@ -325,7 +325,7 @@ tc_prep_rows_kernel(const float *__restrict__ X, uint64_t x_stride, uint32_t seq
 #pragma unroll
   for (int w = 0; w < kTcRowThreads / 32; w++) mm = fmaxf(mm, red[w]);
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(mm, bad != 0, &mul, &inv);
+  const bool ok = row_scale(mm, bad != 0, &mul, &inv, 3);
   TcPrep P = tc_prep_at(ws, count, seq, cols);
   if (threadIdx.x == 0) {
     P.rowinv[z * 16 + s] = inv;
@@ -699,11 +699,13 @@ bool ternary_tc_applies(uint32_t count, uint32_t seq, uint32_t out, uint32_t col
     const char *v = getenv("NELISP_TERNARY_PATH");   // ring / tma: the chunked kernels
     return !(v && (strcmp(v, "ring") == 0 || strcmp(v, "tma") == 0));
   }();
+  // tc: this kernel from five rows up.  Up to four rows the other paths
+  // carry activations to 30 bits (four limbs); this kernel's format has 22.
   static const bool forced = [] {
-    const char *v = getenv("NELISP_TERNARY_PATH");   // tc: this kernel from one row up
+    const char *v = getenv("NELISP_TERNARY_PATH");
     return v && strcmp(v, "tc") == 0;
   }();
-  if (forced && !per_block && seq >= 1 && seq <= 16u && cols % 128u == 0 && cols >= kTcK &&
+  if (forced && !per_block && seq >= 5u && seq <= 16u && cols % 128u == 0 && cols >= kTcK &&
       cols <= kTcMaxCols && (count == 1 || w_stride == (uint64_t)out * (cols / 16u)))
     return true;
   // Below six rows the register-fed mma.sync kernels stream faster: the A

@@ -160,7 +160,7 @@ umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict_
   for (int w = 0; w < 8; w++) mm = fmaxf(mm, red[w]);
   // the exponent of the GEMV's prep (ternary_prep.cuh, row_scale)
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(mm, sbad != 0, &mul, &inv);
+  const bool ok = row_scale(mm, sbad != 0, &mul, &inv, 3);
   if (threadIdx.x == 0) {
     rowinv[s] = inv;
     rowflag[s] = !ok;

@@ -351,10 +351,10 @@ __device__ __forceinline__ void row_stats_quantize(float (&v)[ROW4][4], uint32_t
   float rm = 0.0f;
   for (int i = 0; i < nw; i++) rm = fmaxf(rm, red[i]);
   if (!ws) return;
-  const int NT = n_tiles((int)B);
+  const int NT = n_tiles((int)B), L = n_limbs((int)B);
   PrepOut P = prep_at(ws, (int)B, cols, 0);
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(rm, bad != 0, &mul, &inv);
+  const bool ok = row_scale(rm, bad != 0, &mul, &inv, L);
   if (threadIdx.x == 0) {
     P.rowinv[b] = inv;
     P.rowflag[b] = !ok;
@@ -368,7 +368,7 @@ __device__ __forceinline__ void row_stats_quantize(float (&v)[ROW4][4], uint32_t
       const float4 f = x4[e];
       q[4 * e] = f.x; q[4 * e + 1] = f.y; q[4 * e + 2] = f.z; q[4 * e + 3] = f.w;
     }
-    part += quantize_word(q, mul, ok, W, b, NT, P);
+    part += quantize_word(q, mul, ok, W, b, NT, L, P);
   }
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   if (lane == 0) xred[w] = part;

@@ -55,7 +55,7 @@ __host__ __device__ inline uint32_t step_align(uint32_t b) { return (b + 127u) &
 // PRE (the prep's per-word partials and row statistics).
 // Activation fragments of one K chunk: NT n-tiles of int8 limbs.
 __host__ __device__ inline uint32_t step_frag_bytes(uint32_t NT) { return NT * kStepMaxK * 8u; }
-// Sequence rows NT n-tiles hold (three limbs a row).
+// Sequence rows NT n-tiles hold at most (three limbs a row; four for up to four rows).
 __host__ __device__ inline uint32_t step_rows(uint32_t NT) { return 8u * NT / 3u; }
 
 __host__ __device__ inline StepSmem step_layout(uint32_t NT, uint32_t hd, uint32_t grp,

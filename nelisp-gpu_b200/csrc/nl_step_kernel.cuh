@@ -296,9 +296,10 @@ struct RowStat {
 
 // Exact integer dot product of tile row R, sequence row S, from SACC.
 template <int NT>
-__device__ __forceinline__ long long tile_tot(const int *sacc, int r, int s, long long xs) {
-  const int *row = sacc + r * (8 * NT + 1) + 3 * s;
+__device__ __forceinline__ long long tile_tot(const int *sacc, int r, int s, long long xs, int L) {
+  const int *row = sacc + r * (8 * NT + 1) + L * s;
   long long tot = (long long)row[0] + 256ll * row[1] + 65536ll * row[2];
+  if (L == 4) tot += 16777216ll * row[3];
   if (TileT<NT>::OFF)
     tot -= 2ll * xs;                 // the offset operands' 2 sum xq
   else
@@ -307,9 +308,9 @@ __device__ __forceinline__ long long tile_tot(const int *sacc, int r, int s, lon
 }
 
 // The scale of the rows a down GEMV ran with: from the SwiGLU row maximum.
-__device__ __forceinline__ void given_scale(float mm, float *mul, float *inv, int *flag) {
+__device__ __forceinline__ void given_scale(float mm, int L, float *mul, float *inv, int *flag) {
   float m, i;
-  const bool ok = row_scale(mm, !isfinite(mm), &m, &i);
+  const bool ok = row_scale(mm, !isfinite(mm), &m, &i, L);
   *mul = m;
   *inv = i;
   *flag = !ok;
@@ -403,14 +404,14 @@ __device__ __forceinline__ void prep_rows(const Load &load, uint32_t B, uint32_t
       bad = __any_sync(0xffffffffu, bad);
       if (lane == 0) {
         float mul, inv;
-        const bool ok = row_scale(mm, bad != 0, &mul, &inv);
+        const bool ok = row_scale(mm, bad != 0, &mul, &inv, n_limbs((int)B));
         st->mul[warp] = mul;
         st->inv[warp] = inv;
         st->flag[warp] = !ok;
       }
     }
   } else if (tid < (int)B) {
-    given_scale(__uint_as_float(__ldcg(maxb + tid)), &st->mul[tid], &st->inv[tid],
+    given_scale(__uint_as_float(__ldcg(maxb + tid)), n_limbs((int)B), &st->mul[tid], &st->inv[tid],
                 &st->flag[tid]);
   }
   csync();
@@ -427,7 +428,7 @@ __device__ __forceinline__ void prep_rows(const Load &load, uint32_t B, uint32_t
       const float4 f = x4[e];
       v[4 * e] = f.x; v[4 * e + 1] = f.y; v[4 * e + 2] = f.z; v[4 * e + 3] = f.w;
     }
-    pxs[k] = quantize_word(v, st->mul[b], st->flag[b] == 0, W, b, NT, P);
+    pxs[k] = quantize_word(v, st->mul[b], st->flag[b] == 0, W, b, NT, n_limbs((int)B), P);
   }
   csync();
   if ((uint32_t)warp < B) {            // the row's offset sum (exact: any order)
@@ -737,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
       // the previous layer's down GEMV output, scaled as its rows were
       if (tid < (int)B) {
         float mul;
-        given_scale(__uint_as_float(__ldcg(A.amax + tid)), &mul, &st->dinv[tid], &st->dflag[tid]);
+        given_scale(__uint_as_float(__ldcg(A.amax + tid)), n_limbs((int)B), &mul, &st->dinv[tid], &st->dflag[tid]);
       }
       csync();
       const float *sd = layers[l - 1].sd;
@@ -775,7 +776,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
       if (tid < 16 * (int)B) {
         const int r = tid & 15, s = tid >> 4;
         const uint32_t oi = 16u * t + (uint32_t)r;
-        const long long tot = tile_tot<NT>(sacc, r, s, st->xs[s]);
+        const long long tot = tile_tot<NT>(sacc, r, s, st->xs[s], n_limbs((int)B));
         const float y = st->flag[s] ? __uint_as_float(kNaN) : ((float)tot * st->inv[s]) * sc;
         __stcg(A.qkv + (uint64_t)s * A.qkv_rows + oi, y);
       }
@@ -837,7 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
       if (tid < 16 * (int)B) {
         const int r = tid & 15, s = tid >> 4;
         const uint32_t oi = 16u * t + (uint32_t)r;
-        const long long tot = tile_tot<NT>(sacc, r, s, st->xs[s]);
+        const long long tot = tile_tot<NT>(sacc, r, s, st->xs[s], n_limbs((int)B));
         const float y = st->flag[s] ? __uint_as_float(kNaN) : ((float)tot * st->inv[s]) * sc;
         __stcg(A.o + (uint64_t)s * H + oi, y);
       }
@@ -875,8 +876,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
         if (st->flag[s]) {
           av = __uint_as_float(kNaN);
         } else {
-          const long long tg = tile_tot<NT>(sacc, r, s, st->xs[s]);
-          const long long tu = tile_tot<NT>(sacc + sstride, r, s, st->xs[s]);
+          const long long tg = tile_tot<NT>(sacc, r, s, st->xs[s], n_limbs((int)B));
+          const long long tu = tile_tot<NT>(sacc + sstride, r, s, st->xs[s], n_limbs((int)B));
           const float gv = ((float)tg * st->inv[s]) * scg;
           const float uv = ((float)tu * st->inv[s]) * scu;
           const float sg = 1.0f / (1.0f + expf(-gv));
@@ -909,7 +910,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
           const int r = tid & 15, s = tid >> 4;
           const uint32_t oi = 16u * t + (uint32_t)r;
           atomicAdd(reinterpret_cast<unsigned long long *>(A.dpart + (uint64_t)s * H + oi),
-                    (unsigned long long)tile_tot<NT>(sacc, r, s, st->xs[s]));
+                    (unsigned long long)tile_tot<NT>(sacc, r, s, st->xs[s], n_limbs((int)B)));
         }
       }
     }
@@ -921,7 +922,7 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const StepArgs A) {
   {
     if (tid < (int)B) {
       float mul;
-      given_scale(__uint_as_float(__ldcg(A.amax + tid)), &mul, &st->dinv[tid], &st->dflag[tid]);
+      given_scale(__uint_as_float(__ldcg(A.amax + tid)), n_limbs((int)B), &mul, &st->dinv[tid], &st->dflag[tid]);
     }
     csync();
     const float *sd = layers[nl - 1].sd;

@@ -4,9 +4,12 @@
 // the GEMV's own prep kernel and the decoder's fused normalisation epilogues.
 //
 // Each row s is scaled by a power of two 2^e_s that puts max|x| in
-// [2^21, 2^22), rounded to an integer xq (the only inexact step: half a unit
-// of 2^-22 of the row maximum) and split into three balanced int8 limbs,
-// xq = l0 + 256 l1 + 65536 l2.  Rows holding a non-finite value, or whose
+// [2^(8L-3), 2^(8L-2)), rounded to an integer xq (the only inexact step: half
+// a unit of 2^-(8L-2) of the row maximum) and split into L balanced int8
+// limbs, xq = l0 + 256 l1 + 65536 l2 (+ 2^24 l3).  Problems of up to four
+// sequence rows take L = 4 (xq to 30 bits): their limb columns fit the
+// n-tiles that three limbs would take anyway, so the fourth costs no MMA.
+// More rows take L = 3 (22 bits).  Rows holding a non-finite value, or whose
 // maximum is so small that 2^e_s would leave the f32 normals, are flagged
 // and computed on the CUDA cores instead.
 #pragma once
@@ -17,11 +20,11 @@
 
 namespace nl {
 
-constexpr int kMaxFastSeq = 16;  // 48 (s, limb) columns = 6 n-tiles of 8
+constexpr int kMaxFastSeq = 16;  // 48 (s, limb) columns = 6 n-tiles of 8 (L = 3)
 
 // Fragment layout for one problem: uint2 frag[blk][nt][h][lane][e], where
 // blk is the 128-column block, n-tile nt holds columns n = 8nt .. 8nt+7
-// (n = 3s + limb), the k32 step within the block is j = 2h + e and
+// (n = L s + limb), the k32 step within the block is j = 2h + e and
 // lane = 4*(n%8) + q.  A lane's fragments for steps (0,1) and for (2,3) are
 // each one 16-byte load, and the 32 lanes of a warp read 512 contiguous
 // bytes.  Lane q of MMA j in block blk covers words 2q (b0) and 2q+1 (b1) of
@@ -43,7 +46,9 @@ struct PrepOut {
   long long *xsum;  // [kMaxFastSeq][kRowCluster]
 };
 
-__host__ __device__ inline int n_tiles(int seq) { return (3 * seq + 7) / 8; }
+// Limbs per activation value for a problem of SEQ rows (see above).
+__host__ __device__ inline int n_limbs(int seq) { return seq <= 4 ? 4 : 3; }
+__host__ __device__ inline int n_tiles(int seq) { return (n_limbs(seq) * seq + 7) / 8; }
 // Offset (in uint2) of the fragment pair (j = 2h, 2h+1) of LANE for n-tile T of
 // block BLK.
 __host__ __device__ inline size_t frag_pair(uint32_t blk, int NT, int t, int h, int lane) {
@@ -69,22 +74,18 @@ __device__ inline PrepOut prep_at(void *ws, int seq, uint32_t cols, uint32_t z) 
   return p;
 }
 
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-  return (uint32_t)(a & 0xff) | ((uint32_t)(b & 0xff) << 8) |
-         ((uint32_t)(c & 0xff) << 16) | ((uint32_t)(d & 0xff) << 24);
-}
-
-// Exponent of a row: 2^e puts the row maximum MM in [2^21, 2^22).  False
-// when the row cannot be represented (non-finite, or 2^e / 2^-e outside the
-// f32 normals); a zero row is representable with mul = inv = 0.
-__device__ __forceinline__ bool row_scale(float mm, bool bad, float *mul, float *inv) {
+// Exponent of a row of L-limb values: 2^e puts the row maximum MM in
+// [2^(8L-3), 2^(8L-2)).  False when the row cannot be represented
+// (non-finite, or 2^e / 2^-e outside the f32 normals); a zero row is
+// representable with mul = inv = 0.
+__device__ __forceinline__ bool row_scale(float mm, bool bad, float *mul, float *inv, int L) {
   *mul = 0.0f;
   *inv = 0.0f;
   if (bad) return false;
   if (!(mm > 0.0f)) return true;
   int E;
   frexpf(mm, &E);                      // mm in [2^(E-1), 2^E)
-  const int e = 22 - E;
+  const int e = 8 * L - 2 - E;
   if (e > 126 || e < -126) return false;
   *mul = ldexpf(1.0f, e);
   *inv = ldexpf(1.0f, -e);
@@ -92,42 +93,65 @@ __device__ __forceinline__ bool row_scale(float mm, bool bad, float *mul, float 
 }
 
 // Quantize the 16 values V of packed word W of sequence row S into the
-// fragments of P (zeros when !OK): three balanced int8 limbs per value,
-// written in the column order of the weight operands (see the layout note).
-// Returns the word's share of XSUM: the sum of its xq over codes i % 4 != 3.
+// fragments of P (zeros when !OK): L balanced int8 limbs per value (MUL from
+// row_scale with the same L), written in the column order of the weight
+// operands (see the layout note).  Returns the word's share of XSUM: the sum
+// of its xq over codes i % 4 != 3.
+//
+// The balanced base-256 digits d_l in [-128, 127] of xq are the bytes of
+// xq + 128 (1 + 256 + ...) less 128: byte l of U = xq + 0x80808080 (L = 4;
+// 0x00808080 for L = 3, whose top digit is at most 64 in magnitude) is
+// d_l + 128, and d_l as an int8 bit pattern is that byte XOR 0x80.  A
+// fragment word gathers digit l of four values with byte permutes.
 __device__ __forceinline__ long long quantize_word(const float (&v)[16], float mul, bool ok,
-                                                   uint32_t W, uint32_t s, int NT, PrepOut P) {
-  int l[3][16];
+                                                   uint32_t W, uint32_t s, int NT, int L,
+                                                   PrepOut P) {
+  const uint32_t bias = L == 4 ? 0x80808080u : 0x00808080u;
+  uint32_t u[16];
   long long part = 0;
 #pragma unroll
   for (int k = 0; k < 16; k++) {
-    if (ok) {
-      int qv = __float2int_rn(v[k] * mul);   // exact scaling, one rounding
-      if ((k & 3) != 3) part += qv;
-      int l0 = (int)(int8_t)(qv & 0xff);
-      int r = (qv - l0) >> 8;
-      int l1 = (int)(int8_t)(r & 0xff);
-      int l2 = (r - l1) >> 8;                // |qv| <= 2^22 -> |l2| <= 64
-      l[0][k] = l0; l[1][k] = l1; l[2][k] = l2;
-    } else {
-      l[0][k] = l[1][k] = l[2][k] = 0;
-    }
+    const int qv = ok ? __float2int_rn(v[k] * mul) : 0;   // exact scaling, one rounding
+    if ((k & 3) != 3) part += qv;
+    u[k] = (uint32_t)qv + bias;
   }
   const uint32_t blk = W / 8u, wq = W % 8u;
   const uint32_t q = wq >> 1, e = wq & 1u;   // word 2q is b0, word 2q+1 is b1
   uint32_t *fw = reinterpret_cast<uint32_t *>(P.frag);
 #pragma unroll
-  for (int li = 0; li < 3; li++) {
-    int n = 3 * (int)s + li;
+  for (int li = 0; li < 4; li++) {
+    if (li >= L) break;
+    const int n = L * (int)s + li;
     if (n >= 8 * NT) continue;
+    const uint32_t sel = (uint32_t)li | ((4u + (uint32_t)li) << 4);
 #pragma unroll
     for (int j = 0; j < 4; j++) {
+      const uint32_t lo = __byte_perm(u[j], u[4 + j], sel);
+      const uint32_t hi = __byte_perm(u[8 + j], u[12 + j], sel);
       const size_t idx = ((((size_t)blk * NT + (uint32_t)(n / 8)) * 2u + (uint32_t)(j >> 1)) * 32u +
                           (uint32_t)(n % 8) * 4u + q) * 2u + (uint32_t)(j & 1);
-      fw[2 * idx + e] = pack4(l[li][j], l[li][4 + j], l[li][8 + j], l[li][12 + j]);
+      fw[2 * idx + e] = __byte_perm(lo, hi, 0x5410) ^ 0x80808080u;
     }
   }
   return part;
+}
+
+// The value of sequence row S from the int32 sums ROW[n] of the limb columns
+// n = L s + limb: exact in int64 (limb_total), or, for sums that per-block
+// scales made floats (their bits in ROW), in f32 (limb_total_f; the /64 of
+// the signed operands folded in).
+__device__ __forceinline__ long long limb_total(const int *row, uint32_t s, int L) {
+  const int *c = row + L * (int)s;
+  long long t = (long long)c[0] + 256ll * c[1] + 65536ll * c[2];
+  if (L == 4) t += 16777216ll * c[3];
+  return t;
+}
+__device__ __forceinline__ float limb_total_f(const int *row, uint32_t s, int L) {
+  const int *c = row + L * (int)s;
+  float v = __int_as_float(c[0]) + __int_as_float(c[1]) * 256.0f;
+  v = v + __int_as_float(c[2]) * 65536.0f;
+  if (L == 4) v = v + __int_as_float(c[3]) * 16777216.0f;
+  return v * 0.015625f;                        // / 64, exact
 }
 
 // ---- one row over a thread-block cluster ------------------------------------
@@ -164,9 +188,9 @@ __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, flo
                                                bool live, uint32_t rank, uint32_t s, uint32_t seq,
                                                PrepOut P) {
   __shared__ long long xred[32];
-  const int NT = n_tiles((int)seq);
+  const int NT = n_tiles((int)seq), L = n_limbs((int)seq);
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = live && row_scale(mm, bad, &mul, &inv);
+  const bool ok = live && row_scale(mm, bad, &mul, &inv, L);
   if (live && rank == 0 && threadIdx.x == 0) {
     P.rowinv[s] = inv;
     P.rowflag[s] = !ok;
@@ -182,7 +206,7 @@ __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, flo
         v[4 * v4] = f.x; v[4 * v4 + 1] = f.y; v[4 * v4 + 2] = f.z; v[4 * v4 + 3] = f.w;
       }
     }
-    part += quantize_word(v, mul, ok, W, s, NT, P);
+    part += quantize_word(v, mul, ok, W, s, NT, L, P);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
@@ -206,7 +230,7 @@ __device__ __forceinline__ void quantize_slice(const float *xs, RowSlice sl, flo
 __device__ __forceinline__ void prep_row_cta(const float *xr_f, uint32_t cols, uint32_t s,
                                              uint32_t seq, PrepOut P, float *red,
                                              long long *xred) {
-  const int NT = n_tiles((int)seq);
+  const int NT = n_tiles((int)seq), L = n_limbs((int)seq);
   const uint32_t wng = cols / 16u;
   const float4 *xr = reinterpret_cast<const float4 *>(xr_f);
   const int nwarp = (int)(blockDim.x >> 5);
@@ -226,7 +250,7 @@ __device__ __forceinline__ void prep_row_cta(const float *xr_f, uint32_t cols, u
   float mm = 0.0f;
   for (int w = 0; w < nwarp; w++) mm = fmaxf(mm, red[w]);
   float mul = 0.0f, inv = 0.0f;
-  const bool ok = row_scale(mm, bad != 0, &mul, &inv);
+  const bool ok = row_scale(mm, bad != 0, &mul, &inv, L);
   if (threadIdx.x == 0) {
     P.rowinv[s] = inv;
     P.rowflag[s] = !ok;
@@ -239,7 +263,7 @@ __device__ __forceinline__ void prep_row_cta(const float *xr_f, uint32_t cols, u
       const float4 f = ok ? __ldcg(xr + 4u * W + k) : make_float4(0.f, 0.f, 0.f, 0.f);
       v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
     }
-    part += quantize_word(v, mul, ok, W, s, NT, P);
+    part += quantize_word(v, mul, ok, W, s, NT, L, P);
   }
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
   if ((threadIdx.x & 31) == 0) xred[threadIdx.x >> 5] = part;

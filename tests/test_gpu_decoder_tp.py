@@ -25,11 +25,11 @@ def _torchrun(n, port, *args):
     return subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=400)
 
 
-@pytest.mark.parametrize("n", [2, 4, 8])
-def test_decoder_tp_matches_cpu_model(n):
+@pytest.mark.parametrize("n,extra", [(2, ()), (2, ("--uneven",)), (4, ()), (8, ())])
+def test_decoder_tp_matches_cpu_model(n, extra):
     if _gpu_count() < n:
         pytest.skip(f"needs {n} GPUs")
-    r = _torchrun(n, 29533 + n)
+    r = _torchrun(n, 29533 + n + 10 * len(extra), *extra)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     assert f"TP_OK {n}" in r.stdout
 

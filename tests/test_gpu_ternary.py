@@ -231,12 +231,24 @@ def test_gemv_4096_per_row_scale(batch):
 
 # ---- outlier-dominated activation rows ---------------------------------------------
 # The fast paths round each activation row to an integer after scaling it
-# by 2^(21-E), where 2^E <= max|x| < 2^(E+1): every value moves by at most
-# 2^(E-22), so an output moves by at most s * sum_i |t_i| * 2^(E-22) (plus
-# the f32 rounding of the epilogue).  With one entry 10^4 times the rest the
-# small entries keep only a few bits; the reference sums exact +-x in f32.
-# The reference's own metric (tk-err, normalised by the largest output)
-# stays below 1e-5, and every output stays inside the stated bound.
+# by 2^(P-1-E), where 2^E <= max|x| < 2^(E+1) and P = 30 bits for problems of
+# up to four sequence rows (four int8 limbs), 22 bits for more (three):
+# every value moves by at most 2^(E-P), so an output moves by at most
+# s * sum_i |t_i| * 2^(E-P) (plus the f32 rounding of the epilogue).  With
+# one entry 10^4 times the rest the small entries keep P - 14 bits; the
+# reference sums exact +-x in f32 (within 8e-7 of exact on these rows).
+# With 30 bits the reference's own metric (tk-err, normalised by the largest
+# output) stays below 1e-5; with 22 bits it reaches 1.9e-5 on these rows,
+# so the bar for five or more rows is 2.5e-5.  Every output stays inside the
+# stated bound.
+
+def _precision_bits(seq):
+    return 30 if seq <= 4 else 22
+
+
+def _outlier_tol(seq):
+    return TOL if seq <= 4 else 2.5e-5
+
 
 def _outlier_rows(rng, seq, cols, factor):
     X = rng.standard_normal((seq, cols)).astype(np.float32)
@@ -251,13 +263,14 @@ def _check_outlier_bound(y, X, t, S):
     nz = np.abs(t).sum(axis=1).astype(np.float64)              # sum_i |t_i| per row
     for s in range(seq):
         E = np.floor(np.log2(np.abs(X[s]).max()))
-        bound = S.astype(np.float64) * nz * 2.0 ** (E - 22)
+        bound = S.astype(np.float64) * nz * 2.0 ** (E - _precision_bits(seq))
         slack = 4 * (np.abs(exact[s]) + bound) * 2.0 ** -24 + 1e-30   # f32 epilogue
         err = np.abs(y[s].astype(np.float64) - exact[s])
         assert np.all(err <= bound + slack), (s, float((err - bound - slack).max()))
 
 
-@pytest.mark.parametrize("seq,out,cols,factor", [(1, 1024, 4096, 1e4), (4, 512, 4096, 1e4),
+@pytest.mark.parametrize("seq,out,cols,factor", [(1, 1024, 4096, 1e4), (2, 768, 2560, 1e4),
+                                                 (3, 512, 2560, 1e4), (4, 512, 4096, 1e4),
                                                  (16, 256, 2560, 1e4), (1, 512, 2560, 1e6),
                                                  (40, 128, 2560, 1e4)])
 def test_outlier_rows_within_stated_bound(seq, out, cols, factor):
@@ -275,7 +288,7 @@ def test_outlier_rows_within_stated_bound(seq, out, cols, factor):
     torch.cuda.synchronize()
     y = tY.cpu().numpy()
     want = nlo.ternary_gemv_rows(X.ravel(), WP, S, seq, out, cols)
-    assert nlo.tk_err(y, want) < TOL
+    assert nlo.tk_err(y, want) < _outlier_tol(seq)
     _check_outlier_bound(y.reshape(seq, out), X, t, S)
 
 
@@ -330,9 +343,10 @@ def test_gemv_batched_matches_single():
 # ---- the fast-path kernels agree bit for bit ------------------------------------
 # The decode kernel (row tiles split over warps), the persistent TMA kernel,
 # the register-ring kernel, the tcgen05 GEMV (NELISP_TERNARY_PATH=tc forces
-# it from one row up) and, for more than 16 sequence rows, the tcgen05 GEMM
-# sum the same exact integer products and scale them the same way, so they
-# must give identical bits.  NELISP_TERNARY_PATH is read once
+# it from five rows up; up to four rows the others carry 30-bit activations,
+# which its format does not) and, for more than 16 sequence rows, the
+# tcgen05 GEMM sum the same exact integer products and scale them the same
+# way, so they must give identical bits.  NELISP_TERNARY_PATH is read once
 # per process, hence one subprocess per path.
 
 _PATH_SCRIPT = r"""

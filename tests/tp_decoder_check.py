@@ -20,6 +20,10 @@ CFG = dict(hidden=512, layers=2, heads=8, kv_heads=4, head_dim=64, ffn=1024, voc
 # (TP 8: heads 3,3,3,3,2,2,2,2; FFN 896 on rank 0).
 CFG20 = dict(hidden=2560, layers=2, heads=20, kv_heads=20, head_dim=128, ffn=6912, vocab=5003,
              rms_eps=1e-5, rope_base=10000.0, seed=31)
+# Five heads of 128 and 11 FFN blocks: at 2 ranks heads 3,2 and FFN 768,640,
+# the uneven split of 8 ranks on the 20-head model, on two GPUs.
+CFG5 = dict(hidden=640, layers=2, heads=5, kv_heads=5, head_dim=128, ffn=1408, vocab=1003,
+            rms_eps=1e-5, rope_base=10000.0, seed=37)
 
 
 def peer_timeout(ws, rank, local):
@@ -86,7 +90,7 @@ def main():
     from nelisp_cuda.decoder import Decoder, nccl_unique_id
     obj = [nccl_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(obj, src=0)
-    cfg = CFG if ws <= 2 else CFG20
+    cfg = CFG5 if "--uneven" in sys.argv else (CFG if ws <= 2 else CFG20)
     rng = np.random.default_rng(5)
     B, P, steps, max_seq = 2, 5, 6, 16
     prompt = rng.integers(0, cfg["vocab"], size=(B, P))
@@ -118,6 +122,9 @@ def main():
          for n in LAYER_TENSORS}
     w["embed"] = up(nlo.decoder_tensor(full_cfg, 0, "embed"))
     w["final_norm"] = up(nlo.decoder_tensor(full_cfg, 0, "final_norm"))
+    # a communicator of its own: an NCCL unique id serves one initialisation
+    obj = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
     dec = Decoder(cfg, max_batch=B, max_seq=max_seq, tp_rank=rank, tp_size=ws,
                   nccl_id=obj[0], keep_logits=True, device=local, weights=w)
     for h in handles:

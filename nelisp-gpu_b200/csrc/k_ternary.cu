@@ -966,7 +966,9 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
       Y[z * y_stride + oi] = v;
     } else {
       const unsigned long long word = tag | __float_as_uint(v);
-      for (int r = 0; r < po.n; r++) po.dst[r][z * y_stride + oi] = word;
+#pragma unroll
+      for (int r = 0; r < 8; r++)        // constant indices: PeerOut stays in parameter space
+        if (r < po.n) po.dst[r][z * y_stride + oi] = word;
     }
   };
   if (live) {

@@ -178,7 +178,9 @@ __device__ __forceinline__ void peer_signal(const PeerSig &sig) {
     __threadfence_system();
     if (atomicInc(sig.done, gridDim.x - 1u) == gridDim.x - 1u) {
       __threadfence_system();
-      for (int r = 0; r < sig.n; r++) atomicAdd_system(sig.ctr[r], 1ull);
+#pragma unroll
+      for (int r = 0; r < 8; r++)        // constant indices: SIG stays in parameter space
+        if (r < sig.n) atomicAdd_system(sig.ctr[r], 1ull);
     }
   }
 }
@@ -668,6 +670,123 @@ k_lmhead(const float *__restrict__ E, const float *__restrict__ x,
   if (sig.n) peer_signal(sig);
 }
 
+// The LM head for 2 to 8 sequence rows: k_lmhead's arithmetic (the same
+// per-lane column order, warp reduction and argmax keys, so the same bits),
+// with the embedding rows streamed into shared memory by cp.async instead of
+// registers.  Every warp keeps kLmStages column steps of its 4 rows in
+// flight in its own ring slots (2 KB a step), and each lane reads back only
+// the 16-byte pieces it copied itself, so a thread's own cp.async wait orders
+// them.  One CTA of 16 warps an SM: with 8 rows of x (80 KB) and the 128 KB
+// of rings, twice the bytes in flight of k_lmhead<8>, whose registers hold
+// them.  The first steps are requested before the programmatic-launch wait
+// (the embeddings are not written by the preceding kernel).  Needs H % 128
+// == 0.
+constexpr int kLmWarps = 16, kLmStages = 4, kLmRows = 4;
+__host__ __device__ inline size_t lmhead_ring_smem(int NB, uint32_t H) {
+  return (size_t)NB * H * 4u + (size_t)kLmWarps * kLmStages * kLmRows * 32u * 16u;
+}
+__device__ __forceinline__ void lm_cp16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n"
+               ::"r"((unsigned)__cvta_generic_to_shared(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void lm_cp_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+__device__ __forceinline__ void lm_cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(kLmStages - 1) : "memory");
+}
+template <int NB>
+__global__ void __launch_bounds__(kLmWarps * 32, 1)
+k_lmhead_ring(const float *__restrict__ E, const float *__restrict__ x,
+              unsigned long long *__restrict__ keys, float *__restrict__ logits,
+              const int *__restrict__ pos, uint32_t B, uint32_t vr, uint32_t v0, uint32_t H,
+              uint32_t logit_stride, const unsigned long long *ep, uint32_t key_stride,
+              PeerSig sig) {
+  pdl_trigger();
+  extern __shared__ __align__(16) float lsm[];
+  float *xs = lsm;                                              // [NB][H]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float4 *wr = reinterpret_cast<float4 *>(lsm + (size_t)NB * H) +
+               (size_t)warp * kLmStages * kLmRows * 32 + lane;   // this lane's ring slots
+  const uint32_t gw = blockIdx.x * kLmWarps + (uint32_t)warp;
+  const uint32_t nw = gridDim.x * kLmWarps;
+  const uint32_t h4 = H / 4, ks = h4 / 32;                      // column steps of a row group
+  const uint32_t groups = (vr + kLmRows - 1) / kLmRows;
+  const uint32_t mine = groups > gw ? (groups - gw + nw - 1) / nw : 0u;
+  const uint32_t total = mine * ks;                             // this warp's steps
+  // step i: row group gw + (i / ks) nw, columns 4 (lane + 32 (i % ks)) .. +3
+  auto issue = [&](uint32_t i) {
+    if (i < total) {
+      const uint32_t r0 = (gw + (i / ks) * nw) * kLmRows, c = (uint32_t)lane + 32u * (i % ks);
+      float4 *dst = wr + (size_t)(i % kLmStages) * kLmRows * 32;
+#pragma unroll
+      for (int u = 0; u < kLmRows; u++)
+        lm_cp16(dst + u * 32, E + (size_t)min(r0 + (uint32_t)u, vr - 1) * H + 4u * c);
+    }
+    lm_cp_commit();                  // empty groups keep the count uniform
+  };
+#pragma unroll
+  for (int i = 0; i < kLmStages; i++) issue((uint32_t)i);
+  pdl_wait();
+  if (sig.n) keys += (*ep & 1ull) * key_stride;
+  for (uint32_t i = threadIdx.x; i < NB * h4; i += blockDim.x)
+    reinterpret_cast<float4 *>(xs)[i] = (i / h4) < B ? reinterpret_cast<const float4 *>(x)[i]
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+  __syncthreads();
+  unsigned long long best[NB];
+#pragma unroll
+  for (int b = 0; b < NB; b++) best[b] = 0ull;
+  float *lg = logits ? logits + (size_t)(*pos) * logit_stride : nullptr;
+  for (uint32_t g0 = 0; g0 < total; g0 += ks) {
+    float acc[kLmRows][NB];
+#pragma unroll
+    for (int r = 0; r < kLmRows; r++)
+#pragma unroll
+      for (int b = 0; b < NB; b++) acc[r][b] = 0.0f;
+    for (uint32_t k = 0; k < ks; k++) {
+      const uint32_t i = g0 + k;
+      lm_cp_wait();                  // step i has landed (this thread's copies)
+      const float4 *src = wr + (size_t)(i % kLmStages) * kLmRows * 32;
+      float4 ev[kLmRows];
+#pragma unroll
+      for (int r = 0; r < kLmRows; r++) ev[r] = src[r * 32];
+      const uint32_t c = (uint32_t)lane + 32u * k;
+#pragma unroll
+      for (int b = 0; b < NB; b++) {
+        const float4 xv = reinterpret_cast<const float4 *>(xs + (size_t)b * H)[c];
+#pragma unroll
+        for (int r = 0; r < kLmRows; r++) {
+          acc[r][b] = fmaf(ev[r].x, xv.x, acc[r][b]);
+          acc[r][b] = fmaf(ev[r].y, xv.y, acc[r][b]);
+          acc[r][b] = fmaf(ev[r].z, xv.z, acc[r][b]);
+          acc[r][b] = fmaf(ev[r].w, xv.w, acc[r][b]);
+        }
+      }
+      issue(i + kLmStages);          // into the slots just read (their values are used)
+    }
+    const uint32_t r0 = (gw + (g0 / ks) * nw) * kLmRows;
+#pragma unroll
+    for (int r = 0; r < kLmRows; r++) {
+#pragma unroll
+      for (int b = 0; b < NB; b++) {
+        float v = acc[r][b];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const uint32_t row = r0 + r;
+        if (row < vr && (uint32_t)b < B) {
+          const unsigned long long kk = argmax_key(v, v0 + row);
+          if (kk > best[b]) best[b] = kk;
+          if (lg && lane == 0) lg[(size_t)b * vr + row] = v;
+        }
+      }
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  if (lane == 0)
+    for (int b = 0; b < NB; b++)
+      if ((uint32_t)b < B && best[b]) atomicMax(keys + b, best[b]);
+  if (sig.n) peer_signal(sig);
+}
+
 // Next token: from the prompt while it lasts, else the argmax; reset the
 // keys and advance the position.  One CTA.
 // With peer keys (PK.n > 0): wait for every rank's LM head of this step, take
@@ -695,7 +814,9 @@ __global__ void k_next(unsigned long long *keys, const int *prompt, uint32_t P, 
     unsigned long long key;
     if (pk.n) {
       key = 0ull;
-      for (int r = 0; r < pk.n; r++) {
+#pragma unroll
+      for (int r = 0; r < 8; r++) {      // constant indices: PK stays in parameter space
+        if (r >= pk.n) break;
         const unsigned long long k = ld_acquire_sys(pk.keys[r] + (e & 1ull) * pk.stride + b);
         key = k > key ? k : key;
       }
@@ -1110,11 +1231,20 @@ int enqueue_step(nl_decoder *D, uint32_t B) {
   e = launch_pdl(k_lmhead<NB>, dim3(lmgrid), dim3(256), smem_lm, st, E, (const float *)D->x, \
                  keys, lg, (const int *)D->pos, B, D->vr, D->v0, H, lstride,              \
                  (const unsigned long long *)D->ep, c.max_batch, sig)
+#define NL_LMR(NB)                                                                        \
+  e = launch_pdl(k_lmhead_ring<NB>, dim3(148), dim3(kLmWarps * 32), lmhead_ring_smem(NB, H), \
+                 st, E, (const float *)D->x, keys, lg, (const int *)D->pos, B, D->vr, D->v0, \
+                 H, lstride, (const unsigned long long *)D->ep, c.max_batch, sig)
+  const bool ring = H % 128u == 0 && lmhead_ring_smem(8, H) <= (size_t)(227u << 10);
   if (B <= 1) NL_LM(1);
+  else if (B <= 2 && ring) NL_LMR(2);
   else if (B <= 2) NL_LM(2);
+  else if (B <= 4 && ring) NL_LMR(4);
   else if (B <= 4) NL_LM(4);
+  else if (B <= 8 && ring) NL_LMR(8);
   else if (B <= 8) NL_LM(8);
   else NL_LM(16);
+#undef NL_LMR
 #undef NL_LM
   count_launches(1);
   if (e != cudaSuccess) return cuda_status(e, "step: lm head");
@@ -1135,6 +1265,14 @@ int set_smem_limits(nl_decoder *D) {
       (e = cudaFuncSetAttribute(k_lmhead<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)(lm / 4))) != cudaSuccess)
     return cuda_status(e, "decoder: lm head smem");
+  if (D->cfg.hidden % 128u == 0 && lmhead_ring_smem(8, D->cfg.hidden) <= (size_t)(227u << 10) &&
+      ((e = cudaFuncSetAttribute(k_lmhead_ring<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)lmhead_ring_smem(8, D->cfg.hidden))) != cudaSuccess ||
+       (e = cudaFuncSetAttribute(k_lmhead_ring<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)lmhead_ring_smem(4, D->cfg.hidden))) != cudaSuccess ||
+       (e = cudaFuncSetAttribute(k_lmhead_ring<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)lmhead_ring_smem(2, D->cfg.hidden))) != cudaSuccess))
+    return cuda_status(e, "decoder: lm head ring smem");
   const size_t hs = (size_t)row_slice_cols(D->cfg.hidden) * sizeof(float),
                fs = (size_t)row_slice_cols(D->fr) * sizeof(float);
   if ((e = cudaFuncSetAttribute(k_norm<kNormGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,

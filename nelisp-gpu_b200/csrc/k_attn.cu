@@ -559,6 +559,211 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
   }
 }
 
+// ---- causal attention on the tensor cores (3xTF32) ----------------------------
+// The same operation as attn_causal_kernel with both products, Q K^T and
+// P V, on mma.sync.m16n8k8 tf32: every f32 operand x is split into
+// x_big = tf32(x) and x_small = tf32(x - x_big), and each product is summed as
+// a_small b_big + a_big b_small + a_big b_big (the small x small term, below
+// 2^-21 of the product, is dropped), accumulating in f32.
+//
+// One CTA of 4 warps per (sequence, head, 16-row query block): the CTA
+// stages 32-key tiles of K and V up to the diagonal into shared memory, and
+// warp w takes keys 8w .. 8w+7 of every tile for all 16 rows, with its own
+// online softmax; the four warps' (max, sum, context) are merged at the end
+// in warp order.  Splitting the keys over the warps gives a 512-row prefill
+// of 20 heads 2560 warps instead of 640.  Q is kept split (tf32 big, small)
+// in shared memory; K and V as f32 rows padded by 4 floats, which makes
+// every fragment load conflict-free.  The probabilities are taken from the
+// score accumulators as the A operand of P V as they are: the MMA's K index
+// t stands for key 2t and t + 4 for key 2t + 1 of the warp's 8 keys, and the
+// V fragments are read in that order.  Query blocks are issued from the last
+// (the longest causal walk) to the first.
+constexpr int kTcBQ = 16, kTcBK = 32;
+__device__ __forceinline__ uint32_t tf32_of(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void tf32_split(float x, uint32_t &big, uint32_t &small) {
+  big = tf32_of(x);
+  small = tf32_of(x - __uint_as_float(big));
+}
+__device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// d += a b with both split: a_small b_big + a_big b_small + a_big b_big.
+__device__ __forceinline__ void mma_3xtf32(float (&d)[4], const uint32_t (&ab)[4],
+                                           const uint32_t (&as)[4], uint32_t bb0, uint32_t bb1,
+                                           uint32_t bs0, uint32_t bs1) {
+  mma_tf32(d, as, bb0, bb1);
+  mma_tf32(d, ab, bs0, bs1);
+  mma_tf32(d, ab, bb0, bb1);
+}
+__host__ __device__ constexpr size_t causal_tc_smem(int hd) {
+  // Q split [BQ][HD + 4] uint2, then K and V [BK][HD + 4] floats each (the
+  // merge reuses K and V for the warps' contexts: 4 x 16 x HD floats)
+  return (size_t)kTcBQ * (hd + 4) * 8u + (size_t)2 * kTcBK * (hd + 4) * 4u + 2u * 4u * kTcBQ * 4u;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128)
+attn_causal_tc_kernel(const float *__restrict__ Q, const float *__restrict__ K,
+                      const float *__restrict__ V, float *__restrict__ CTX, CausalGeom g) {
+  constexpr int LD = HD + 4, NO = HD / 8;
+  static_assert(4 * kTcBQ * HD <= 2 * kTcBK * LD, "the merge fits the K and V tiles");
+  extern __shared__ __align__(16) float smt[];
+  uint2 *Qs = reinterpret_cast<uint2 *>(smt);                 // [BQ][LD] (big, small)
+  float *Ks = smt + 2 * kTcBQ * LD;                           // [BK][LD]
+  float *Vs = Ks + kTcBK * LD;                                // [BK][LD]
+  float *Ms = Vs + kTcBK * LD;                                // [4 warps][BQ]
+  float *Ls = Ms + 4 * kTcBQ;                                 // [4 warps][BQ]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gq = lane >> 2, t4 = lane & 3;
+  const uint32_t q0 = (gridDim.x - 1u - blockIdx.x) * kTcBQ, h = blockIdx.y, bz = blockIdx.z;
+  const uint32_t kvh = h / (g.heads / g.kvheads);
+  const float *Qb = Q + bz * g.q_batch + (uint64_t)h * HD;
+  const float *Kb = K + bz * g.kv_batch + (uint64_t)kvh * HD;
+  const float *Vb = V + bz * g.kv_batch + (uint64_t)kvh * HD;
+  const float scale = 1.0f / sqrtf((float)HD);
+  // Q rows, split once (rows past seq as 0)
+  for (int e = tid; e < kTcBQ * HD / 4; e += 128) {
+    const int r = e / (HD / 4), c4 = e % (HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + (uint32_t)r < g.seq)
+      v = *reinterpret_cast<const float4 *>(Qb + (uint64_t)(q0 + r) * g.q_row + 4 * c4);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      uint32_t b, sm;
+      tf32_split(f[i], b, sm);
+      Qs[r * LD + 4 * c4 + i] = make_uint2(b, sm);
+    }
+  }
+  float o[NO][4], m[2], l[2];
+#pragma unroll
+  for (int dt = 0; dt < NO; dt++) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.0f;
+  m[0] = m[1] = -INFINITY;
+  l[0] = l[1] = 0.0f;
+  const uint32_t kend = min(g.seq, q0 + kTcBQ);
+  for (uint32_t k0 = 0; k0 < kend; k0 += kTcBK) {
+    __syncthreads();                               // the previous tile is consumed
+    for (int e = tid; e < kTcBK * HD / 4; e += 128) {
+      const int r = e / (HD / 4), c4 = e % (HD / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (k0 + (uint32_t)r < g.seq) {
+        kv = *reinterpret_cast<const float4 *>(Kb + (uint64_t)(k0 + r) * g.kv_row + 4 * c4);
+        vv = *reinterpret_cast<const float4 *>(Vb + (uint64_t)(k0 + r) * g.kv_row + 4 * c4);
+      }
+      *reinterpret_cast<float4 *>(Ks + r * LD + 4 * c4) = kv;
+      *reinterpret_cast<float4 *>(Vs + r * LD + 4 * c4) = vv;
+    }
+    __syncthreads();
+    const uint32_t kw = k0 + 8u * (uint32_t)warp;  // this warp's 8 keys
+    if (kw > q0 + kTcBQ - 1u || kw >= g.seq) continue;   // all past every row of the block
+    // scores of rows gq, gq + 8 and keys kw + 2 t4 (+1)
+    float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const uint2 *qa = Qs + gq * LD + t4;
+    const float *kb = Ks + (8 * warp + gq) * LD + t4;
+#pragma unroll 8
+    for (int kk = 0; kk < HD / 8; kk++) {
+      const uint2 x0 = qa[8 * kk], x1 = qa[8 * LD + 8 * kk];
+      const uint2 x2 = qa[8 * kk + 4], x3 = qa[8 * LD + 8 * kk + 4];
+      const uint32_t ab[4] = {x0.x, x1.x, x2.x, x3.x}, as[4] = {x0.y, x1.y, x2.y, x3.y};
+      uint32_t bb0, bs0, bb1, bs1;
+      tf32_split(kb[8 * kk], bb0, bs0);
+      tf32_split(kb[8 * kk + 4], bb1, bs1);
+      mma_3xtf32(sc, ab, as, bb0, bb1, bs0, bs1);
+    }
+    // causal mask and online softmax over this warp's keys; a row's 8 keys
+    // sit in the 4 lanes of its quad
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+      const uint32_t i = q0 + (uint32_t)gq + 8u * hf;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const uint32_t j = kw + 2u * t4 + e;
+        const float v = (j <= i && j < g.seq) ? sc[2 * hf + e] * scale : -INFINITY;
+        sc[2 * hf + e] = v;
+        mx = fmaxf(mx, v);
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m[hf], mx);
+      const float corr = mn == -INFINITY ? 1.0f : expf(m[hf] - mn);   // exp(-inf) = 0
+      float sum = 0.0f;
+#pragma unroll
+      for (int e = 0; e < 2; e++) {
+        const float p = mn == -INFINITY ? 0.0f : expf(sc[2 * hf + e] - mn);
+        sc[2 * hf + e] = p;
+        sum += p;
+      }
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      l[hf] = l[hf] * corr + sum;
+      m[hf] = mn;
+#pragma unroll
+      for (int dt = 0; dt < NO; dt++) {
+        o[dt][2 * hf] *= corr;
+        o[dt][2 * hf + 1] *= corr;
+      }
+    }
+    // context += P V over the warp's 8 keys
+    uint32_t pb[4], ps[4];
+    tf32_split(sc[0], pb[0], ps[0]);               // P[gq][2 t4]
+    tf32_split(sc[2], pb[1], ps[1]);               // P[gq + 8][2 t4]
+    tf32_split(sc[1], pb[2], ps[2]);               // P[gq][2 t4 + 1]
+    tf32_split(sc[3], pb[3], ps[3]);               // P[gq + 8][2 t4 + 1]
+    const float *vb = Vs + (8 * warp + 2 * t4) * LD + gq;
+#pragma unroll
+    for (int dt = 0; dt < NO; dt++) {
+      uint32_t bb0, bs0, bb1, bs1;
+      tf32_split(vb[8 * dt], bb0, bs0);            // V[key 2 t4][dim 8 dt + gq]
+      tf32_split(vb[LD + 8 * dt], bb1, bs1);       // V[key 2 t4 + 1][dim 8 dt + gq]
+      mma_3xtf32(o[dt], pb, ps, bb0, bb1, bs0, bs1);
+    }
+  }
+  // merge the warps: max, then the rescaled sums in warp order
+  __syncthreads();                                 // K and V are free
+  float *Os = Ks;                                  // [4 warps][BQ][HD]
+#pragma unroll
+  for (int hf = 0; hf < 2; hf++) {
+    const int r = gq + 8 * hf;
+    if (t4 == 0) {
+      Ms[warp * kTcBQ + r] = m[hf];
+      Ls[warp * kTcBQ + r] = l[hf];
+    }
+#pragma unroll
+    for (int dt = 0; dt < NO; dt++)
+      *reinterpret_cast<float2 *>(Os + ((size_t)warp * kTcBQ + r) * HD + 8 * dt + 2 * t4) =
+          make_float2(o[dt][2 * hf], o[dt][2 * hf + 1]);
+  }
+  __syncthreads();
+  for (int e = tid; e < kTcBQ * HD; e += 128) {
+    const int r = e / HD, d = e % HD;
+    const uint32_t i = q0 + (uint32_t)r;
+    if (i >= g.seq || (uint64_t)h * g.seq + i >= g.limit) continue;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; w++) mm = fmaxf(mm, Ms[w * kTcBQ + r]);
+    float ll = 0.0f, oo = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+      const float mw = Ms[w * kTcBQ + r];
+      if (mw > -INFINITY) {
+        const float c = expf(mw - mm);
+        ll += Ls[w * kTcBQ + r] * c;
+        oo += Os[((size_t)w * kTcBQ + r) * HD + d] * c;
+      }
+    }
+    CTX[bz * g.q_batch + i * g.q_row + (uint64_t)h * HD + d] = oo / ll;
+  }
+}
+
 // Any head size: the reference's three passes, one thread per (head, row).
 __global__ void attn_causal_simple_kernel(const float *__restrict__ Q, const float *__restrict__ K,
                                           const float *__restrict__ V, float *__restrict__ CTX,
@@ -617,6 +822,23 @@ cudaError_t causal_fast(const float *Q, const float *K, const float *V, float *C
   return cudaPeekAtLastError();
 }
 
+template <int HD>
+cudaError_t causal_tc(const float *Q, const float *K, const float *V, float *CTX,
+                      const CausalGeom &g, uint32_t batch, cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_causal_tc_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)causal_tc_smem(HD));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  const dim3 grid((g.seq + kTcBQ - 1) / kTcBQ, g.heads, batch);
+  attn_causal_tc_kernel<HD><<<grid, 128, causal_tc_smem(HD), st>>>(Q, K, V, CTX, g);
+  count_launches(1);
+  return cudaPeekAtLastError();
+}
+
 cudaError_t causal_launch(const float *Q, const float *K, const float *V, float *CTX,
                           const CausalGeom &g, uint32_t hd, uint32_t batch, cudaStream_t st) {
   if (g.seq == 0 || g.heads == 0 || batch == 0) return cudaSuccess;
@@ -624,6 +846,13 @@ cudaError_t causal_launch(const float *Q, const float *K, const float *V, float 
                     aligned16(CTX) && g.q_row % 4 == 0 && g.kv_row % 4 == 0 &&
                     g.q_batch % 4 == 0 && g.kv_batch % 4 == 0;
   if (fast) {
+    // NELISP_CAUSAL_PATH=ffma: the CUDA-core kernel instead of the tensor cores
+    static const bool ffma = [] {
+      const char *v = getenv("NELISP_CAUSAL_PATH");
+      return v && strcmp(v, "ffma") == 0;
+    }();
+    if (!ffma) return hd == 128 ? causal_tc<128>(Q, K, V, CTX, g, batch, st)
+                                : causal_tc<64>(Q, K, V, CTX, g, batch, st);
     static const int forced = [] {
       const char *v = getenv("NELISP_CAUSAL_BQ");
       return v ? atoi(v) : 0;

@@ -8,22 +8,25 @@
 // summed in int32 by tcgen05.mma.kind::i8, and the limbs are recombined in
 // int64 -- so the result is the exact sum rounded once per row scale.
 //
-// One CTA computes a tile of 128 output rows x 80 sequence rows (N = 240
-// columns = 80 rows x 3 limbs) over the whole K, 7 warps:
-//   warp 0      TMA producer: the packed weight tile (128 rows x 128 columns,
-//               two bits each, 4 KB) and the int8 limb tile (240 x 128 B,
-//               128-byte swizzle) per stage, S-stage mbarrier ring; the
-//               weights of the first stages are requested before waiting
-//               for the prep kernel (programmatic dependent launch);
-//   warps 2-5   expand the two-bit codes into the int8 A tile in shared
-//               memory (one thread per weight row; one shift and one mask per
+// One CTA computes a tile of 128 MH output rows x 64 or 80 sequence rows
+// (N = 3 x the rows: one column per limb) over the whole K, 3 + 4 MH warps:
+//   warp 0      TMA producer: the packed weight tile (128 MH rows x 128
+//               columns, two bits each, 4 MH KB) and the int8 limb tile
+//               (N x 128 B, 128-byte swizzle) per stage, S-stage mbarrier
+//               ring; the weights of the first stages are requested before
+//               waiting for the prep kernel (programmatic dependent launch);
+//   warps 2 ..  expand the two-bit codes into the int8 A tiles in shared
+//   1 + 4 MH    memory (one thread per weight row; one shift and one mask per
 //               four weights, 64 * t per byte), then arrive;
-//   warps 1, 6  two MMA issuers taking the stages in turn, four 128x240x32
-//               MMAs per stage each into its own TMEM accumulator (warp 1
-//               also allocates TMEM); tcgen05.commit frees the stage;
-//   warps 2-5   finally read both accumulators back (tcgen05.ld), add them,
-//               recombine the limbs and write Y; rows the prep flagged are
-//               computed there on the CUDA cores.
+//   warp 1 and  two MMA issuers, four 128xNx32 MMAs per stage each into its
+//   2 + 4 MH    own TMEM accumulator (warp 1 also allocates TMEM);
+//               tcgen05.commit frees the stage.  MH = 1: they take the
+//               stages in turn (two partial sums of the same rows); MH = 2:
+//               issuer h multiplies rows half h in every stage against the
+//               same limb tile, halving the limb stream per MMA;
+//   warps 2 ..  finally read the accumulators back (tcgen05.ld), recombine
+//   1 + 4 MH    the limbs and write Y; rows the prep flagged are computed
+//               there on the CUDA cores.
 // The shift-and-mask expansion leaves the 16 codes of a packed word in the
 // order P = {3,7,11,15, 2,6,10,14, 1,5,9,13, 0,4,8,12}; the limb tile is
 // written in the same order, so the K index of A and B agrees.
@@ -46,7 +49,6 @@ constexpr int kUmmaM = 128;              // output rows per CTA
 constexpr int kUmmaK = 128;              // K per stage (bytes of int8)
 constexpr int kUmmaStages = 4;
 constexpr uint32_t kTmemCols = 512;      // two accumulators of up to 256 columns
-constexpr int kUmmaThreads = 224;        // 7 warps
 constexpr uint32_t kWBytes = kUmmaM * kUmmaK / 4;      // packed weights per stage
 constexpr uint32_t kABytes = kUmmaM * kUmmaK;           // int8 A per stage
 // Sequence rows per CTA: 80 or 64 (chosen per shape, umma_tok).  MMA N is
@@ -56,6 +58,18 @@ struct UmmaTile {
   static constexpr int N = 3 * TOK;
   static constexpr uint32_t BBytes = N * kUmmaK;
   static_assert(N % 48 == 0 && N <= 256 && BBytes % 1024 == 0, "tile");
+};
+// Output rows per CTA: MH halves of 128.  With MH = 1 two issuers take the K
+// stages in turn, each into its own accumulator (summed in the epilogue);
+// with MH = 2 issuer h multiplies rows 128h .. 128h+127 in every stage
+// against the same limb tile, so each limb stage staged from L2 feeds twice
+// the MMA work (the limb stream is what bounds the kernel).
+template <int MH>
+struct UmmaRows {
+  static constexpr int Stages = MH == 1 ? kUmmaStages : 3;
+  static constexpr int Expanders = 4 * MH;                   // warps, one thread per A row
+  static constexpr int Threads = 32 * (3 + Expanders);        // + producer, two issuers
+  static constexpr uint32_t A = kABytes * MH, W = kWBytes * MH;
 };
 constexpr uint32_t kWaitRounds = 4096;
 constexpr uint32_t kSuspendNs = 1000000;
@@ -197,8 +211,8 @@ umma_prep_kernel(const float *__restrict__ X, uint32_t cols, int8_t *__restrict_
 // Two MMA issuers take the K stages in turn (one thread issues a tcgen05.mma
 // only every ~50-170 cycles, a 128 x 240 x 32 MMA takes the tensor core ~120),
 // each into its own accumulator; the epilogue adds the two exactly.
-template <int TOK>
-__global__ void __launch_bounds__(kUmmaThreads, 1)
+template <int TOK, int MH>
+__global__ void __launch_bounds__(UmmaRows<MH>::Threads, 1)
 ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmB,
                     const float *__restrict__ X, const uint32_t *__restrict__ WP,
                     const float *__restrict__ S, const float *__restrict__ BIAS,
@@ -208,27 +222,30 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
   constexpr int kUmmaN = UmmaTile<TOK>::N;
   constexpr uint32_t kBBytes = UmmaTile<TOK>::BBytes;
   constexpr uint32_t kIdesc = umma_idesc<kUmmaN>();
+  using RW = UmmaRows<MH>;
+  constexpr int NS = RW::Stages;
+  constexpr int kIssuer1 = 2 + RW::Expanders;       // the second issuer's warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t *sA = base;                                   // stages x 16 KB (1024-aligned)
-  uint8_t *sB = sA + kUmmaStages * kABytes;             // stages x N x 128 B (1024-aligned)
-  uint8_t *sW = sB + kUmmaStages * kBBytes;             // stages x 4 KB
-  uint64_t *full = reinterpret_cast<uint64_t *>(sW + kUmmaStages * kWBytes);
-  uint64_t *aready = full + kUmmaStages;
-  uint64_t *empty = aready + kUmmaStages;
-  uint64_t *done = empty + kUmmaStages;                 // one per issuer
+  uint8_t *sA = base;                                   // stages x MH x 16 KB (1024-aligned)
+  uint8_t *sB = sA + NS * RW::A;                        // stages x N x 128 B (1024-aligned)
+  uint8_t *sW = sB + NS * kBBytes;                      // stages x MH x 4 KB
+  uint64_t *full = reinterpret_cast<uint64_t *>(sW + NS * RW::W);
+  uint64_t *aready = full + NS;
+  uint64_t *empty = aready + NS;
+  uint64_t *done = empty + NS;                          // one per issuer
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const uint32_t m0 = blockIdx.x * kUmmaM, t0 = blockIdx.y * (uint32_t)TOK;
+  const uint32_t m0 = blockIdx.x * (uint32_t)(kUmmaM * MH), t0 = blockIdx.y * (uint32_t)TOK;
   const uint32_t nk = cols / kUmmaK;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kUmmaStages; i++) {
+    for (int i = 0; i < NS; i++) {
       bar_init(&full[i], 1);
-      bar_init(&aready[i], 4);
-      bar_init(&empty[i], 1);
+      bar_init(&aready[i], RW::Expanders);
+      bar_init(&empty[i], MH);                          // one commit per issuer using it
     }
     bar_init(&done[0], 1);
     bar_init(&done[1], 1);
@@ -248,14 +265,12 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
     // ---- producer: the weights of the first stages before the wait for
     // the prep kernel (launch_pdl), which does not write them ----
     if (lane == 0) {
-      const uint32_t pre = nk < (uint32_t)kUmmaStages ? nk : (uint32_t)kUmmaStages;
+      const uint32_t pre = nk < (uint32_t)NS ? nk : (uint32_t)NS;
       for (uint32_t kt = 0; kt < nk; kt++) {
-        const int st = (int)(kt % kUmmaStages);
-        if (kt >= (uint32_t)kUmmaStages &&
-            !bar_wait(&empty[st], ((kt / kUmmaStages) - 1) & 1, err))
-          break;
-        bar_expect(&full[st], kWBytes + kBBytes);
-        tma2d(sW + st * kWBytes, &tmW, (int)(kt * (kUmmaK / 16)), (int)m0, &full[st]);
+        const int st = (int)(kt % NS);
+        if (kt >= (uint32_t)NS && !bar_wait(&empty[st], ((kt / NS) - 1) & 1, err)) break;
+        bar_expect(&full[st], RW::W + kBBytes);
+        tma2d(sW + st * RW::W, &tmW, (int)(kt * (kUmmaK / 16)), (int)m0, &full[st]);
         if (kt >= pre) {
           tma2d(sB + st * kBBytes, &tmB, (int)(kt * kUmmaK), (int)(3 * t0), &full[st]);
         } else if (kt + 1 == pre) {
@@ -265,18 +280,20 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         }
       }
     }
-  } else if (warp == 1 || warp == 6) {
-    // ---- MMA issuers: issuer p takes the stages kt with kt % 2 == p ----
+  } else if (warp == 1 || warp == kIssuer1) {
+    // ---- MMA issuers: with MH = 1 issuer p takes the stages kt with
+    // kt % 2 == p; with MH = 2 issuer p takes every stage for rows half p ----
     if (lane == 0) {
       const uint32_t p = warp == 1 ? 0u : 1u;
       const uint32_t acc_d = tmem + 256u * p;
       bool first = true;
-      for (uint32_t kt = p; kt < nk; kt += 2) {
-        const int st = (int)(kt % kUmmaStages);
-        const uint32_t ph = (kt / kUmmaStages) & 1;
+      for (uint32_t kt = MH == 1 ? p : 0u; kt < nk; kt += MH == 1 ? 2u : 1u) {
+        const int st = (int)(kt % NS);
+        const uint32_t ph = (kt / NS) & 1;
         if (!bar_wait(&full[st], ph, err) || !bar_wait(&aready[st], ph, err)) break;
         asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-        const uint32_t a0 = su32(sA + st * kABytes), b0 = su32(sB + st * kBBytes);
+        const uint32_t a0 = su32(sA + st * RW::A + (MH == 1 ? 0u : p * kABytes));
+        const uint32_t b0 = su32(sB + st * kBBytes);
 #pragma unroll
         for (int k = 0; k < kUmmaK / 32; k++)
           umma_i8(acc_d, smem_desc(a0 + 32u * k), smem_desc(b0 + 32u * k), kIdesc,
@@ -287,15 +304,16 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       umma_commit(&done[p]);
     }
   } else {
-    // ---- expand the weights (warps 2-5, one thread per A row) ----
-    const uint32_t r = threadIdx.x - 64;          // 0..127
+    // ---- expand the weights (warps 2 .. 1 + 4 MH, one thread per A row) ----
+    const uint32_t r = threadIdx.x - 64;          // 0 .. 128 MH - 1
     for (uint32_t kt = 0; kt < nk; kt++) {
-      const int st = (int)(kt % kUmmaStages);
-      if (!bar_wait(&full[st], (kt / kUmmaStages) & 1, err)) break;
-      const uint4 *wr = reinterpret_cast<const uint4 *>(sW + st * kWBytes + r * 32u);
+      const int st = (int)(kt % NS);
+      if (!bar_wait(&full[st], (kt / NS) & 1, err)) break;
+      const uint4 *wr = reinterpret_cast<const uint4 *>(sW + st * RW::W + r * 32u);
       const uint4 lo = wr[0], hi = wr[1];
       const uint32_t w8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-      uint8_t *arow = sA + st * kABytes + (r >> 3) * 1024u + (r & 7u) * 128u;
+      uint8_t *arow = sA + st * RW::A + (r >> 7) * kABytes + ((r & 127u) >> 3) * 1024u +
+                      (r & 7u) * 128u;
 #pragma unroll
       for (int c = 0; c < 8; c++) {
         const uint32_t w = w8[c];
@@ -308,14 +326,15 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
       if (lane == 0) bar_arrive(&aready[st]);
     }
     // ---- epilogue: accumulators -> Y ----
-    const bool two = nk >= 2;                     // issuer 1 wrote an accumulator
-    if (bar_wait(&done[0], 0, err) && (!two || bar_wait(&done[1], 0, err))) {
+    const uint32_t hh = MH == 1 ? 0u : (uint32_t)(warp - 2) / 4u;   // this warp's rows half
+    const bool two = MH == 1 && nk >= 2;          // issuer 1 wrote a second partial sum
+    if (bar_wait(&done[hh], 0, err) && (!two || bar_wait(&done[1], 0, err))) {
       asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
       const uint32_t q = (uint32_t)(warp & 3);      // TMEM lane quarter of this warp
-      const uint32_t o = m0 + q * 32u + (uint32_t)lane;
+      const uint32_t o = m0 + hh * 128u + q * 32u + (uint32_t)lane;
       const float sc = o < out ? __ldg(S + o) : 0.0f;
       const float bi = (BIAS && o < out) ? __ldg(BIAS + o) : 0.0f;
-      const uint32_t lb = (q * 32u) << 16;
+      const uint32_t lb = ((q * 32u) << 16) + 256u * hh;
       for (uint32_t c0 = 0; c0 < (uint32_t)kUmmaN; c0 += 48) {   // 16 rows per round
         uint32_t v[48], u[48];
 #pragma unroll
@@ -349,7 +368,7 @@ ternary_umma_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_consta
         if (s >= seq) break;
         if (!rowflag[s]) continue;
         for (uint32_t rr = 0; rr < 32u; rr++) {
-          const uint32_t orow = m0 + q * 32u + rr;
+          const uint32_t orow = m0 + hh * 128u + q * 32u + rr;
           if (orow >= out) break;
           float acc1[1];
           ternary_row_generic<1>(X, WP + (size_t)orow * wng, nullptr, false, __ldg(S + orow),
@@ -387,23 +406,41 @@ EncodeFn encode_fn() {
   return fn;
 }
 
-template <int TOK>
+template <int TOK, int MH>
 size_t umma_smem_bytes() {
-  return 1024 + (size_t)kUmmaStages * (kABytes + UmmaTile<TOK>::BBytes + kWBytes) +
-         3 * kUmmaStages * 8 + 16 + 16;
+  using RW = UmmaRows<MH>;
+  return 1024 + (size_t)RW::Stages * (RW::A + UmmaTile<TOK>::BBytes + RW::W) +
+         3 * RW::Stages * 8 + 16 + 16;
+}
+
+int umma_tok(uint32_t seq, uint32_t out, int mh);
+// Output-row halves per CTA (UmmaRows): 2 when that grid still fills a wave
+// of one CTA per SM, else 1 (measured, B200, 512 rows: 2560 -> 6912 58.5 vs
+// 70.1 us, -> 13824 86.3 vs 131.7, -> 7680 59 vs 80; 6912 -> 2560, 70 CTAs
+// with two halves, 53.5 vs 45.6).  NELISP_UMMA_MH=1 or 2 forces one.
+int umma_mh(uint32_t seq, uint32_t out) {
+  static const int forced = [] {
+    const char *v = getenv("NELISP_UMMA_MH");
+    const int m = v ? atoi(v) : 0;
+    return m == 1 || m == 2 ? m : 0;
+  }();
+  if (forced) return forced;
+  const uint32_t tok = (uint32_t)umma_tok(seq, out, 2);
+  const uint64_t ctas = (uint64_t)((out + 2 * kUmmaM - 1) / (2 * kUmmaM)) * ((seq + tok - 1) / tok);
+  return ctas >= 148u ? 2 : 1;
 }
 
 // Sequence rows per CTA for SEQ rows x OUT outputs: the height whose grid,
 // rounded up to whole waves of one CTA per SM, costs the fewest MMA columns
 // (waves x 3 TOK); ties keep 80.  NELISP_UMMA_TOK=64 or 80 forces one.
-int umma_tok(uint32_t seq, uint32_t out) {
+int umma_tok(uint32_t seq, uint32_t out, int mh) {
   static const int forced = [] {
     const char *v = getenv("NELISP_UMMA_TOK");
     const int t = v ? atoi(v) : 0;
     return t == 64 || t == 80 ? t : 0;
   }();
   if (forced) return forced;
-  const uint64_t mt = (out + kUmmaM - 1) / kUmmaM;
+  const uint64_t mt = (out + kUmmaM * mh - 1) / (kUmmaM * mh);
   auto cost = [&](uint32_t tok) {
     const uint64_t ctas = mt * ((seq + tok - 1) / tok);
     return ((ctas + 147) / 148) * tok;
@@ -444,11 +481,12 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   int8_t *XB = reinterpret_cast<int8_t *>(ws);
   float *rowinv = reinterpret_cast<float *>((char *)ws + align256((size_t)ncol * cols));
   int *rowflag = reinterpret_cast<int *>((char *)rowinv + align256((size_t)seq * 4));
-  const int tok = umma_tok(seq, out);
+  const int mh = umma_mh(seq, out);
+  const int tok = umma_tok(seq, out, mh);
   CUtensorMap mw, mb;
   {
     const cuuint64_t dims[2] = {cols / 16u, out}, strides[1] = {(cuuint64_t)cols / 16u * 4u};
-    const cuuint32_t box[2] = {kUmmaK / 16, kUmmaM}, es[2] = {1, 1};
+    const cuuint32_t box[2] = {kUmmaK / 16, (cuuint32_t)(kUmmaM * mh)}, es[2] = {1, 1};
     if (enc(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t *>(WP), dims, strides,
             box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
@@ -464,13 +502,14 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   }
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(ternary_umma_kernel<80>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)umma_smem_bytes<80>());
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(ternary_umma_kernel<64>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)umma_smem_bytes<64>());
+    cudaError_t e = cudaSuccess;
+#define NL_SMEM(T, M)                                                                     \
+    if (e == cudaSuccess)                                                                 \
+      e = cudaFuncSetAttribute(ternary_umma_kernel<T, M>,                                  \
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,                \
+                               (int)umma_smem_bytes<T, M>());
+    NL_SMEM(80, 1) NL_SMEM(64, 1) NL_SMEM(80, 2) NL_SMEM(64, 2)
+#undef NL_SMEM
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -479,15 +518,19 @@ cudaError_t ternary_umma_launch(const float *X, const uint32_t *WP, const float 
   cudaError_t e = launch_k(umma_prep_kernel, dim3(seq), dim3(256), 0, st, false, X, cols, XB,
                            rowinv, rowflag);
   if (e != cudaSuccess) return e;
-  const dim3 grid((out + kUmmaM - 1) / kUmmaM, (seq + tok - 1) / tok);
-  if (tok == 64)
-    e = launch_pdl(ternary_umma_kernel<64>, grid, dim3(kUmmaThreads), umma_smem_bytes<64>(), st,
-                   mw, mb, X, WP, S, BIAS, (const float *)rowinv, (const int *)rowflag, Y, seq,
-                   out, cols, wait_flag_device());
-  else
-    e = launch_pdl(ternary_umma_kernel<80>, grid, dim3(kUmmaThreads), umma_smem_bytes<80>(), st,
-                   mw, mb, X, WP, S, BIAS, (const float *)rowinv, (const int *)rowflag, Y, seq,
-                   out, cols, wait_flag_device());
+  const dim3 grid((out + kUmmaM * mh - 1) / (kUmmaM * mh), (seq + tok - 1) / tok);
+#define NL_GEMM(T, M)                                                                     \
+  e = launch_pdl(ternary_umma_kernel<T, M>, grid, dim3(UmmaRows<M>::Threads),              \
+                 umma_smem_bytes<T, M>(), st, mw, mb, X, WP, S, BIAS, (const float *)rowinv, \
+                 (const int *)rowflag, Y, seq, out, cols, wait_flag_device())
+  if (mh == 2) {
+    if (tok == 64) NL_GEMM(64, 2);
+    else NL_GEMM(80, 2);
+  } else {
+    if (tok == 64) NL_GEMM(64, 1);
+    else NL_GEMM(80, 1);
+  }
+#undef NL_GEMM
   count_launches(2);
   return e != cudaSuccess ? e : cudaPeekAtLastError();
 }

@@ -60,7 +60,11 @@ __device__ float block_sum(float v, float *red) {
 // One CTA per row; VPT floats per thread held in registers (rows up to
 // VPT*256 columns).  The reference's max starts at A[base] and only a
 // strictly larger value replaces it; a NaN element therefore never becomes
-// the max there, as with fmaxf here.
+// the max there, as with fmaxf here.  The exponentials use the hardware
+// exp2 (__expf) and the normalisation one reciprocal per row: a few
+// instructions an element instead of a few dozen, so the kernel streams
+// HBM instead of issuing math; the error stays within 1e-5 relative for
+// exponents down to -60, below the reference's 1e-4 bar.
 template <int VPT>
 __global__ void __launch_bounds__(kRowThreads)
 softmax_reg_kernel(const float *__restrict__ A, float *__restrict__ C,
@@ -94,24 +98,26 @@ softmax_reg_kernel(const float *__restrict__ A, float *__restrict__ C,
   float s = 0.0f;
 #pragma unroll
   for (int k = 0; k < VPT; k++) {
-    v[k] = expf(v[k] - m);
+    v[k] = __expf(v[k] - m);
     s += v[k];
   }
   // Padding lanes held -inf and contribute exp(-inf) = 0.
   s = block_sum(s, red);
+  const float inv = 1.0f / s;
   if (vec) {
 #pragma unroll
     for (int k = 0; k < VPT / 4; k++) {
       uint32_t i = 4u * (threadIdx.x + (uint32_t)k * kRowThreads);
       if (i < N)
         __stcs(reinterpret_cast<float4 *>(c + i),
-               make_float4(v[4 * k] / s, v[4 * k + 1] / s, v[4 * k + 2] / s, v[4 * k + 3] / s));
+               make_float4(v[4 * k] * inv, v[4 * k + 1] * inv, v[4 * k + 2] * inv,
+                           v[4 * k + 3] * inv));
     }
   } else {
 #pragma unroll
     for (int k = 0; k < VPT; k++) {
       uint32_t i = threadIdx.x + (uint32_t)k * kRowThreads;
-      if (i < N) __stcs(c + i, v[k] / s);
+      if (i < N) __stcs(c + i, v[k] * inv);
     }
   }
 }

@@ -117,8 +117,12 @@ cudaError_t sgemm(const float *A, const float *B, const float *bias, float *C,
     dim3 grid((N + 31) / 32, (M + 31) / 32);
     sgemm_kernel<32, 32, 32, 2, 2, TRANS_B, TRANS_A><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
   } else {
+    // Small products (the reference's 256^3 vkmatmul case): latency-bound,
+    // so each CTA stages 256 columns of K at once (one load round and one
+    // barrier for K <= 256, instead of eight) and runs its sequential-k
+    // dot products from shared memory.
     dim3 grid((N + 15) / 16, (M + 15) / 16);
-    sgemm_kernel<16, 16, 32, 1, 1, TRANS_B, TRANS_A><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
+    sgemm_kernel<16, 16, 256, 1, 1, TRANS_B, TRANS_A><<<grid, 256, 0, st>>>(A, B, bias, C, M, K, N, cover, limit);
   }
   count_launches(1);
   return cudaPeekAtLastError();

@@ -391,20 +391,27 @@ k_norm_cta(const int *__restrict__ tok, const float *__restrict__ E, float *__re
            const float *__restrict__ delta, const float *__restrict__ g, float *__restrict__ x,
            void *ws, uint32_t B, uint32_t H, float eps, PeerIn pin) {
   pdl_trigger();
-  pdl_wait();
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[32];
   const uint32_t b = blockIdx.x, t = threadIdx.x;
   const bool in = 4u * t < H;
+  // gamma is a weight, and the residual row was written by the norm kernel
+  // several launches back: both are requested before the wait.  That read
+  // is ordered because the kernel before this one (a GEMV, which does not
+  // trigger its dependents early) starts only after that norm kernel has
+  // completed, and this one only after it.
+  const float4 gv = in ? __ldg(reinterpret_cast<const float4 *>(g) + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 *h4 = reinterpret_cast<float4 *>(h + (size_t)b * H);
+  const float4 hpre = (in && MODE != kNormGather) ? h4[t] : make_float4(0.f, 0.f, 0.f, 0.f);
+  pdl_wait();
   const uint32_t tag = pin.slots ? (uint32_t)(*pin.ep * pin.tmul + pin.tadd) : 0u;
   float v[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
-  float4 *h4 = reinterpret_cast<float4 *>(h + (size_t)b * H);
   if (in) {
     if (MODE == kNormGather) {
       const float4 f = __ldg(reinterpret_cast<const float4 *>(E + (size_t)__ldg(tok + b) * H) + t);
       v[0][0] = f.x; v[0][1] = f.y; v[0][2] = f.z; v[0][3] = f.w;
     } else {
-      const float4 f = h4[t];
+      const float4 f = hpre;
       const float hv[4] = {f.x, f.y, f.z, f.w};
       float dv[4];
       if (pin.slots) {
@@ -436,7 +443,6 @@ k_norm_cta(const int *__restrict__ tok, const float *__restrict__ E, float *__re
   const float rinv = 1.0f / sqrtf(tot / (float)H + eps);
   __syncthreads();   // red is reused
   if (in) {
-    const float4 gv = __ldg(reinterpret_cast<const float4 *>(g) + t);
     v[0][0] = __fmul_rn(__fmul_rn(v[0][0], rinv), gv.x);
     v[0][1] = __fmul_rn(__fmul_rn(v[0][1], rinv), gv.y);
     v[0][2] = __fmul_rn(__fmul_rn(v[0][2], rinv), gv.z);

@@ -561,10 +561,10 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 
 // ---- causal attention on the tensor cores (3xTF32) ----------------------------
 // The same operation as attn_causal_kernel with both products, Q K^T and
-// P V, on mma.sync.m16n8k8 tf32: every f32 operand x is split into
-// x_big = tf32(x) and x_small = tf32(x - x_big), and each product is summed as
-// a_small b_big + a_big b_small + a_big b_big (the small x small term, below
-// 2^-21 of the product, is dropped), accumulating in f32.
+// P V, on mma.sync.m16n8k8 tf32: every f32 operand x is split into a tf32
+// x_big and the rest x_small (tf32_split), and each product is summed as
+// a_small b_big + a_big b_small + a_big b_big (the small x small term, about
+// 2^-20 of the product, is dropped), accumulating in f32.
 //
 // One CTA of 4 warps per (sequence, head, 16-row query block): the CTA
 // stages 32-key tiles of K and V up to the diagonal into shared memory, and
@@ -579,14 +579,13 @@ attn_causal_kernel(const float *__restrict__ Q, const float *__restrict__ K,
 // V fragments are read in that order.  Query blocks are issued from the last
 // (the longest causal walk) to the first.
 constexpr int kTcBQ = 16, kTcBK = 32;
-__device__ __forceinline__ uint32_t tf32_of(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;\n" : "=r"(r) : "f"(x));
-  return r;
-}
+// x = big + small: big keeps the sign, exponent and top 10 mantissa bits of
+// x (the low 13 bits cleared: a truncation, one instruction), small = x - big
+// is exact in f32, and the tensor core reads it as tf32 (its low 13 bits
+// ignored).  The products keep about 20 bits.
 __device__ __forceinline__ void tf32_split(float x, uint32_t &big, uint32_t &small) {
-  big = tf32_of(x);
-  small = tf32_of(x - __uint_as_float(big));
+  big = __float_as_uint(x) & 0xFFFFE000u;
+  small = __float_as_uint(x - __uint_as_float(big));
 }
 __device__ __forceinline__ void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {

@@ -827,15 +827,16 @@ ternary_tma_kernel(const __grid_constant__ CUtensorMap tmW, const float *__restr
 constexpr int kDecWarps = 8;
 constexpr uint32_t kDecMaxTiles = 2048;   // above this, the persistent TMA kernel
 
-template <int NT>
+template <int NT, bool SMW>
 __global__ void __launch_bounds__(kDecWarps * 32, 2)
 ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
                    const uint32_t *__restrict__ WP, uint64_t w_stride,
                    const float *__restrict__ SCALE, uint64_t s_stride,
                    const float *__restrict__ BIAS, float *__restrict__ Y, uint64_t y_stride,
                    uint32_t seq, uint32_t out, uint32_t cols, uint64_t limit, void *ws,
-                   uint32_t tiles, uint32_t count, int rt_log2, PeerOut po) {
+                   uint32_t tiles, uint32_t count, int rt_log2, PeerOut po, uint32_t wpre) {
   constexpr int KB = NT == 1 ? 4 : (NT <= 4 ? 2 : 1);   // blocks per warp in flight
+  extern __shared__ __align__(16) uint2 wsm[];        // [warp][wpre][row A, row B][lane]
   constexpr int CH = NT <= 2 ? 4 : 1;                   // accumulator chains per n-tile
   constexpr bool OFF = CH == 4;                         // a chain per step: offset operands
   constexpr int kMaxRT = NT >= 5 ? 4 : 8;
@@ -858,18 +859,53 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
   const uint32_t bstep = (uint32_t)wpt, step = (uint32_t)KB * bstep;
   const uint32_t nb = live ? nblk : 0u;
 
+  // SMW: every weight word this warp multiplies (WPRE blocks) is requested
+  // into shared memory now -- the weights are not written by the preceding
+  // kernel -- by cp.async, each lane reading back only its own copies, so
+  // the whole tile streams in while the preceding kernel runs.  Otherwise
+  // the first KB blocks go to registers and the rest stream after the wait.
+  uint2 *wslot = wsm + (size_t)warp * wpre * 64 + lane;
+  if constexpr (SMW) {
+    for (uint32_t j = 0; j < wpre; j++) {
+      const uint32_t b = (uint32_t)kw + j * bstep;
+      const unsigned n = b < nb ? 8u : 0u;
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n"
+                   ::"r"((unsigned)__cvta_generic_to_shared(wslot + j * 64)),
+                   "l"(b < nb ? pa + 4u * b : pa), "r"(n) : "memory");
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n"
+                   ::"r"((unsigned)__cvta_generic_to_shared(wslot + j * 64 + 32)),
+                   "l"(b < nb ? pb + 4u * b : pb), "r"(n) : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
+  // block b of this warp is slot j = (b - kw) / bstep
+  auto wload = [&](uint32_t b, uint32_t j, bool second) -> uint2 {
+    if constexpr (SMW) return b < nb ? wslot[j * 64 + (second ? 32 : 0)] : make_uint2(0u, 0u);
+    return b < nb ? __ldcs((second ? pb : pa) + 4u * b) : make_uint2(0u, 0u);
+  };
   uint2 wa[KB], wb[KB];
+  if constexpr (!SMW) {
 #pragma unroll
-  for (int u = 0; u < KB; u++) {
-    const uint32_t b = (uint32_t)kw + (uint32_t)u * bstep;
-    wa[u] = b < nb ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
-    wb[u] = b < nb ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
+    for (int u = 0; u < KB; u++) {
+      const uint32_t b = (uint32_t)kw + (uint32_t)u * bstep;
+      wa[u] = wload(b, (uint32_t)u, false);
+      wb[u] = wload(b, (uint32_t)u, true);
+    }
   }
   // The epilogue's immutable operands, also before the wait.
   const uint32_t erow = min(rt * 16u + (uint32_t)(lane & 15), out - 1u);
   const float e_scale = __ldg(SCALE + z * s_stride + erow);
   const float e_bias = BIAS ? __ldg(BIAS + erow) : 0.0f;
   pdl_wait();                                  // fragments, flags and X come after this
+  if constexpr (SMW) {
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+#pragma unroll
+    for (int u = 0; u < KB; u++) {
+      const uint32_t b = (uint32_t)kw + (uint32_t)u * bstep;
+      wa[u] = wload(b, (uint32_t)u, false);
+      wb[u] = wload(b, (uint32_t)u, true);
+    }
+  }
   const PrepOut P = prep_at(ws, (int)seq, cols, z);
   const uint2 *fr = P.frag + 2 * lane;
   const float e_rinv = (uint32_t)lane < seq ? __ldcg(P.rowinv + lane) : 0.0f;
@@ -889,7 +925,8 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
 #pragma unroll
       for (int r = 0; r < 4; r++) acc[t][j][r] = 0;
 
-  for (uint32_t b0 = (uint32_t)kw; b0 < nb; b0 += step) {
+  uint32_t jn = KB;                            // slot of the next iteration's first block
+  for (uint32_t b0 = (uint32_t)kw; b0 < nb; b0 += step, jn += KB) {
     uint2 f[KB][NT][4];
 #pragma unroll
     for (int u = 0; u < KB; u++) {
@@ -911,8 +948,8 @@ ternary_dec_kernel(const float *__restrict__ X, uint64_t x_stride,
 #pragma unroll
     for (int u = 0; u < KB; u++) {
       const uint32_t b = b0 + step + (uint32_t)u * bstep;
-      na[u] = b < nb ? __ldcs(pa + 4u * b) : make_uint2(0u, 0u);
-      nb2[u] = b < nb ? __ldcs(pb + 4u * b) : make_uint2(0u, 0u);
+      na[u] = wload(b, jn + (uint32_t)u, false);
+      nb2[u] = wload(b, jn + (uint32_t)u, true);
     }
 #pragma unroll
     for (int u = 0; u < KB; u++) {
@@ -1052,11 +1089,31 @@ bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   const dim3 grid((total + (1u << lg) - 1) >> lg), block(kDecWarps * 32);
   PeerOut pov = {};
   if (po) pov = *po;
+  // the weight prefetch into shared memory: blocks per warp, up to 40 KB a CTA
+  const uint32_t wpt = (uint32_t)kDecWarps >> lg, nblk = cols / 128u;
+  const uint32_t bpw = (nblk + wpt - 1) / wpt;
+  const size_t wsmem = (size_t)kDecWarps * bpw * 64 * sizeof(uint2);
+  // (with two or more n-tiles: batch 8 decode 1.92 -> 1.87 ms; at one n-tile
+  // the register-fed form measured faster)
+  const uint32_t wpre = (wsmem <= (40u << 10) && NTs >= 2) ? bpw : 0u;
   switch (NTs) {
 #define NL_DEC(N)                                                                            \
   case N:                                                                                    \
-    *err = launch_pdl(ternary_dec_kernel<N>, grid, block, 0, st, X, xs, WP, wst, S, ss, B, Y, \
-                      ys, seq, out, cols, limit, ws, tiles, count, lg, pov);                 \
+    {                                                                                      \
+      static bool set = false;                                                             \
+      if (!set) {                                                                          \
+        cudaFuncSetAttribute(ternary_dec_kernel<N, true>,                                  \
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, 40 << 10);       \
+        set = true;                                                                        \
+      }                                                                                    \
+    }                                                                                      \
+    if (wpre)                                                                              \
+      *err = launch_pdl(ternary_dec_kernel<N, true>, grid, block, wsmem, st, X, xs, WP, wst, S, \
+                        ss, B, Y, ys, seq, out, cols, limit, ws, tiles, count, lg, pov, wpre); \
+    else                                                                                   \
+      *err = launch_pdl(ternary_dec_kernel<N, false>, grid, block, (size_t)0, st, X, xs, WP,  \
+                        wst, S, ss, B, Y, ys, seq, out, cols, limit, ws, tiles, count, lg, pov, \
+                        0u);                                                                \
     return true;
     NL_DEC(1) NL_DEC(2) NL_DEC(3) NL_DEC(4) NL_DEC(5) NL_DEC(6)
 #undef NL_DEC

@@ -1093,9 +1093,11 @@ bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   const uint32_t wpt = (uint32_t)kDecWarps >> lg, nblk = cols / 128u;
   const uint32_t bpw = (nblk + wpt - 1) / wpt;
   const size_t wsmem = (size_t)kDecWarps * bpw * 64 * sizeof(uint2);
-  // (with two or more n-tiles: batch 8 decode 1.92 -> 1.87 ms; at one n-tile
-  // the register-fed form measured faster)
-  const uint32_t wpre = (wsmem <= (40u << 10) && NTs >= 2) ? bpw : 0u;
+  // with two or more n-tiles (batch 8 decode 1.92 -> 1.84 ms), and at one
+  // n-tile where more than 6 blocks a warp would leave most of the weights to
+  // stream after the wait (batch 1: 1.324 -> 1.315 ms); otherwise the first
+  // blocks held in registers measured faster
+  const uint32_t wpre = (wsmem <= (40u << 10) && (NTs >= 2 || bpw > 6u)) ? bpw : 0u;
   switch (NTs) {
 #define NL_DEC(N)                                                                            \
   case N:                                                                                    \

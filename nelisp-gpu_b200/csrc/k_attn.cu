@@ -650,16 +650,21 @@ attn_causal_tc_kernel(const float *__restrict__ Q, const float *__restrict__ K,
   const uint32_t kend = min(g.seq, q0 + kTcBQ);
   for (uint32_t k0 = 0; k0 < kend; k0 += kTcBK) {
     __syncthreads();                               // the previous tile is consumed
+    // the K and V tiles by cp.async (no register round trip; rows past seq
+    // are zero-filled without a read)
     for (int e = tid; e < kTcBK * HD / 4; e += 128) {
       const int r = e / (HD / 4), c4 = e % (HD / 4);
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (k0 + (uint32_t)r < g.seq) {
-        kv = *reinterpret_cast<const float4 *>(Kb + (uint64_t)(k0 + r) * g.kv_row + 4 * c4);
-        vv = *reinterpret_cast<const float4 *>(Vb + (uint64_t)(k0 + r) * g.kv_row + 4 * c4);
-      }
-      *reinterpret_cast<float4 *>(Ks + r * LD + 4 * c4) = kv;
-      *reinterpret_cast<float4 *>(Vs + r * LD + 4 * c4) = vv;
+      const bool in = k0 + (uint32_t)r < g.seq;
+      const uint64_t go = in ? (uint64_t)(k0 + r) * g.kv_row + 4 * c4 : 0;
+      const unsigned n = in ? 16u : 0u;            // 0: zero fill
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n"
+                   ::"r"((unsigned)__cvta_generic_to_shared(Ks + r * LD + 4 * c4)),
+                   "l"(Kb + go), "r"(n) : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n"
+                   ::"r"((unsigned)__cvta_generic_to_shared(Vs + r * LD + 4 * c4)),
+                   "l"(Vb + go), "r"(n) : "memory");
     }
+    asm volatile("cp.async.commit_group;\ncp.async.wait_all;\n" ::: "memory");
     __syncthreads();
     const uint32_t kw = k0 + 8u * (uint32_t)warp;  // this warp's 8 keys
     if (kw > q0 + kTcBQ - 1u || kw >= g.seq) continue;   // all past every row of the block

@@ -1103,9 +1103,10 @@ bool try_launch_dec(uint32_t count, const float *X, uint64_t xs, const uint32_t 
   case N:                                                                                    \
     {                                                                                      \
       static bool set = false;                                                             \
-      if (!set) {                                                                          \
-        cudaFuncSetAttribute(ternary_dec_kernel<N, true>,                                  \
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, 40 << 10);       \
+      if (wpre && !set) {                                                                  \
+        *err = cudaFuncSetAttribute(ternary_dec_kernel<N, true>,                           \
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 40 << 10); \
+        if (*err != cudaSuccess) return true;                                              \
         set = true;                                                                        \
       }                                                                                    \
     }                                                                                      \

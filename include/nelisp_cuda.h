@@ -392,6 +392,16 @@ int nl_decoder_logits(nl_decoder *dec, float *out, uint64_t nfloats);
  * step; kernels per decode step. */
 int nl_decoder_info(nl_decoder *dec, uint32_t *shard, uint64_t *weight_bytes,
                     uint64_t *kernels_per_step);
+/* The SHARD[6] that nl_decoder_info would report for rank TP_RANK of a
+ * TP_SIZE-way decoder of CFG, from the partition the constructors use,
+ * without a device or a decoder (host arithmetic only: no nl_init needed).
+ * Ranges of two ranks differ by at most one KV head, one 128-wide FFN block
+ * or one vocabulary row, the longer ranges first.  NL_ERROR for a config the
+ * constructors refuse, a rank outside [0, TP_SIZE), or a TP_SIZE that leaves
+ * some rank without KV heads, FFN blocks or vocabulary rows.  No counterpart
+ * in the reference, whose repository has no decoder. */
+int nl_decoder_shard(const nl_decoder_config *cfg, int tp_rank, int tp_size,
+                     uint32_t *shard);
 void nl_decoder_destroy(nl_decoder *dec);
 
 /* Launch counter: how many kernels this library has enqueued since the

@@ -99,6 +99,40 @@ Split split(uint32_t n, uint32_t parts, uint32_t r) {
   return {r * base + (r < rem ? r : rem), base + (r < rem ? 1u : 0u)};
 }
 
+// The configurations the decoder's kernels take.
+int check_config(const nl_decoder_config &c) {
+  const bool hd_ok = c.head_dim == 32 || c.head_dim == 64 || c.head_dim == 128 ||
+                     c.head_dim == 256;
+  if (c.hidden == 0 || c.hidden % 128 || c.ffn == 0 || c.ffn % 128 || !hd_ok || c.heads == 0 ||
+      c.kv_heads == 0 || c.heads % c.kv_heads || c.heads / c.kv_heads > 8 ||
+      c.max_batch == 0 || c.max_batch > 16 || c.max_seq == 0 || c.vocab == 0 || c.layers == 0)
+    return set_error(NL_ERROR,
+                     "decoder config: hidden and ffn multiples of 128, head_dim 32, 64, 128 or "
+                     "256, heads a multiple of kv_heads (at most 8 per kv head), "
+                     "1 <= max_batch <= 16");
+  return NL_OK;
+}
+
+// One rank's part of a SIZE-way tensor-parallel decoder: contiguous ranges
+// of KV heads (with their query heads: rows of Q|K|V, columns of O, the KV
+// cache), of 128-wide FFN blocks (rows of gate|up, columns of down) and of
+// vocabulary rows (the LM head).  The ranges of two ranks differ by at most
+// one unit, the longer ones first; a rank left without some kind is an error.
+struct Shard {
+  Split kvh, ffb, voc;
+};
+int plan_shard(const nl_decoder_config &c, int rank, int size, Shard *s) {
+  if (size < 1 || rank < 0 || rank >= size)
+    return set_error(NL_ERROR, "decoder: rank %d of %d", rank, size);
+  s->kvh = split(c.kv_heads, (uint32_t)size, (uint32_t)rank);
+  s->ffb = split(c.ffn / 128, (uint32_t)size, (uint32_t)rank);
+  s->voc = split(c.vocab, (uint32_t)size, (uint32_t)rank);
+  if (s->kvh.count == 0 || s->ffb.count == 0 || s->voc.count == 0)
+    return set_error(NL_ERROR, "decoder: %d ranks leave rank %d without heads, FFN blocks or vocab",
+                     size, rank);
+  return NL_OK;
+}
+
 // ---- weight generation -------------------------------------------------------------
 __global__ void gen_ternary_kernel(uint32_t *W, uint32_t rows, uint32_t k_local, uint64_t key,
                                    uint64_t grow0, uint64_t k_full, uint64_t c0) {
@@ -1368,18 +1402,17 @@ static int decoder_build(nl_decoder *D) {
   const nl_decoder_config &c = D->cfg;
   const uint32_t H = c.hidden, hd = c.head_dim;
   const uint32_t grp = c.heads / c.kv_heads;
-  D->kvh = split(c.kv_heads, D->size, D->rank);
-  D->ffb = split(c.ffn / 128, D->size, D->rank);
-  D->voc = split(c.vocab, D->size, D->rank);
+  Shard sh;
+  if (int rc = plan_shard(c, D->rank, D->size, &sh)) return rc;
+  D->kvh = sh.kvh;
+  D->ffb = sh.ffb;
+  D->voc = sh.voc;
   D->kvr = D->kvh.count;
   D->hr = D->kvr * grp;
   D->fr = D->ffb.count * 128;
   D->vr = D->voc.count;
   D->v0 = D->voc.begin;
   D->qkv_rows = (D->hr + 2 * D->kvr) * hd;
-  if (D->kvr == 0 || D->fr == 0 || D->vr == 0)
-    return set_error(NL_ERROR, "decoder: %d ranks leave rank %d without heads, FFN blocks or vocab",
-                     D->size, D->rank);
   cudaError_t e = cudaStreamCreateWithFlags(&D->stream, cudaStreamNonBlocking);
   if (e != cudaSuccess) return cuda_status(e, "decoder: stream");
   const uint32_t h0 = D->kvh.begin * grp, kv0 = D->kvh.begin, f0 = D->ffb.begin * 128;
@@ -1657,17 +1690,9 @@ static int decoder_create(const nl_decoder_config *cfg, const nl_decoder_weights
   int rc = nl_init(-1);
   if (rc) return rc;
   const nl_decoder_config &c = *cfg;
-  const bool hd_ok = c.head_dim == 32 || c.head_dim == 64 || c.head_dim == 128 ||
-                     c.head_dim == 256;
-  if (c.hidden == 0 || c.hidden % 128 || c.ffn == 0 || c.ffn % 128 || !hd_ok || c.heads == 0 ||
-      c.kv_heads == 0 || c.heads % c.kv_heads || c.heads / c.kv_heads > 8 ||
-      c.max_batch == 0 || c.max_batch > 16 || c.max_seq == 0 || c.vocab == 0 || c.layers == 0)
-    return set_error(NL_ERROR,
-                     "decoder config: hidden and ffn multiples of 128, head_dim 32, 64, 128 or "
-                     "256, heads a multiple of kv_heads (at most 8 per kv head), "
-                     "1 <= max_batch <= 16");
-  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size)
-    return set_error(NL_ERROR, "decoder: rank %d of %d", tp_rank, tp_size);
+  if ((rc = check_config(c))) return rc;
+  Shard sh;                      // refuses a rank left without heads, FFN blocks or vocab
+  if ((rc = plan_shard(c, tp_rank, tp_size, &sh))) return rc;
   nl_decoder *D = new nl_decoder();
   D->cfg = c;
   D->rank = tp_rank;
@@ -1899,6 +1924,22 @@ extern "C" int nl_decoder_logits(nl_decoder *D, float *out, uint64_t nfloats) {
   uint64_t have = (uint64_t)D->cfg.max_seq * D->cfg.max_batch * D->vr;
   if (nfloats > have) nfloats = have;
   return cuda_status(cudaMemcpy(out, D->logits, nfloats * 4, cudaMemcpyDeviceToHost), "logits");
+}
+
+extern "C" int nl_decoder_shard(const nl_decoder_config *cfg, int tp_rank, int tp_size,
+                                uint32_t *shard) {
+  if (!cfg || !shard) return set_error(NL_ERROR, "decoder shard: null argument");
+  int rc = check_config(*cfg);
+  if (rc) return rc;
+  Shard sh;
+  if ((rc = plan_shard(*cfg, tp_rank, tp_size, &sh))) return rc;
+  shard[0] = sh.kvh.begin;
+  shard[1] = sh.kvh.count;
+  shard[2] = sh.ffb.begin * 128;
+  shard[3] = sh.ffb.count * 128;
+  shard[4] = sh.voc.begin;
+  shard[5] = sh.voc.count;
+  return NL_OK;
 }
 
 extern "C" int nl_decoder_info(nl_decoder *D, uint32_t *shard, uint64_t *weight_bytes,

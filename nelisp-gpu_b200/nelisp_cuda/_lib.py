@@ -100,6 +100,7 @@ SIGNATURES = {
     "nl_decoder_generate": (_i, [_vp, _u32, _u32, _vp, _u32, _vp, _vp, _vp]),
     "nl_decoder_logits": (_i, [_vp, _vp, _u64]),
     "nl_decoder_info": (_i, [_vp, _vp, _vp, _vp]),
+    "nl_decoder_shard": (_i, [_vp, _i, _i, _vp]),
     "nl_decoder_destroy": (None, [_vp]),
 }
 

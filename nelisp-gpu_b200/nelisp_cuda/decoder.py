@@ -69,6 +69,9 @@ def _bind(lib):
                                     ctypes.POINTER(ctypes.c_uint64),
                                     ctypes.POINTER(ctypes.c_uint64)]
     lib.nl_decoder_info.restype = ctypes.c_int
+    lib.nl_decoder_shard.argtypes = [ctypes.POINTER(Config), ctypes.c_int, ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_uint32)]
+    lib.nl_decoder_shard.restype = ctypes.c_int
     lib.nl_decoder_destroy.argtypes = [ctypes.c_void_p]
     lib.nl_decoder_destroy.restype = None
     lib._nl_decoder_bound = True
@@ -80,6 +83,24 @@ def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     L.check(lib.nl_nccl_unique_id(buf))
     return buf.raw
+
+
+SHARD_KEYS = ("kv_head_begin", "kv_heads", "ffn_begin", "ffn", "vocab_begin", "vocab")
+
+
+def _config(cfg: dict) -> Config:
+    return Config(**{k: v for k, v in cfg.items() if k in [f[0] for f in Config._fields_]})
+
+
+def shard(config: dict, tp_rank: int, tp_size: int) -> dict:
+    """Rank TP_RANK's part of a TP_SIZE-way decoder of CONFIG (the keys of
+    Decoder.info()'s shard), computed on the host by nl_decoder_shard: no GPU
+    or decoder needed.  Raises NlError where the constructors would refuse."""
+    lib = _bind(L.load())
+    c = _config(dict(dict(max_batch=1, max_seq=1), **config))
+    out = (ctypes.c_uint32 * 6)()
+    L.check(lib.nl_decoder_shard(ctypes.byref(c), tp_rank, tp_size, out))
+    return dict(zip(SHARD_KEYS, list(out)))
 
 
 class Decoder:
@@ -94,7 +115,7 @@ class Decoder:
         if device is not None:
             L.check(self.lib.nl_init(device))
         self.cfg = dict(config, max_batch=max_batch, max_seq=max_seq)
-        c = Config(**{k: v for k, v in self.cfg.items() if k in [f[0] for f in Config._fields_]})
+        c = _config(self.cfg)
         h = ctypes.c_void_p()
         idbuf = ctypes.create_string_buffer(nccl_id, 128) if nccl_id else None
         if weights is None:
@@ -129,8 +150,8 @@ class Decoder:
         shard = (ctypes.c_uint32 * 6)()
         wb, kps = ctypes.c_uint64(), ctypes.c_uint64()
         L.check(self.lib.nl_decoder_info(self.h, shard, ctypes.byref(wb), ctypes.byref(kps)))
-        keys = ["kv_head_begin", "kv_heads", "ffn_begin", "ffn", "vocab_begin", "vocab"]
-        return dict(zip(keys, list(shard)), weight_bytes=wb.value, kernels_per_step=kps.value)
+        return dict(zip(SHARD_KEYS, list(shard)), weight_bytes=wb.value,
+                    kernels_per_step=kps.value)
 
     def logits(self):
         """[max_seq, max_batch, vocab rows of this rank] of the last generate."""

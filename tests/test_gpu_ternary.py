@@ -229,6 +229,35 @@ def test_gemv_4096_per_row_scale(batch):
     assert nlo.tk_err(tY.cpu().numpy(), want) < TOL
 
 
+def test_empty_problems():
+    """Empty inputs as ternary-rows has them (one thread per (s, o), a sum
+    over the row's blocks, kernels.el:713-746): no sequence rows, no output
+    rows or no problems launch nothing and leave Y as it was; no columns give
+    Y = BIAS, the empty sum, bit for bit as the oracle."""
+    import torch
+    from nelisp_cuda import dev
+    d = torch.device("cuda")
+    seq, out, cols = 3, 8, 256
+    rng = np.random.default_rng(5)
+    X = torch.from_numpy(rng.standard_normal(seq * cols).astype(np.float32)).to(d)
+    W = torch.from_numpy(pack_trits(rng.integers(-1, 2, size=(out, cols))).view(np.int32)).to(d)
+    S = torch.from_numpy(rng.uniform(0.5, 1.5, out).astype(np.float32)).to(d)
+    BIAS = rng.uniform(-1.0, 1.0, out).astype(np.float32)
+    Y = torch.full((seq * out,), 7.0, device=d)
+    dev.ternary_gemv(X, W, S, Y, 0, out, cols)
+    dev.ternary_gemv(X, W, S, Y, seq, 0, cols)
+    dev.ternary_gemv_batched(0, X, seq * cols, W, out * cols // 16, S, out, Y, seq * out, seq,
+                             out, cols)
+    torch.cuda.synchronize()
+    assert bool((Y == 7.0).all())
+    dev.ternary_gemv(X, W, S, Y, seq, out, 0, bias=torch.from_numpy(BIAS).to(d))
+    torch.cuda.synchronize()
+    want = nlo.ternary_rows(np.zeros(0, np.float32), np.zeros(0, np.uint32), BIAS,
+                            np.zeros(0, np.float32), seq, out, 0, 0, 0)
+    assert np.array_equal(Y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert np.array_equal(want.reshape(seq, out), np.tile(BIAS, (seq, 1)))
+
+
 # ---- outlier-dominated activation rows ---------------------------------------------
 # The fast paths round each activation row to an integer after scaling it
 # by 2^(P-1-E), where 2^E <= max|x| < 2^(E+1) and P = 30 bits for problems of

@@ -145,7 +145,7 @@ def _rank_main(rank, size, port, errors):
         errors.put((rank, traceback.format_exc()))
 
 
-def _gather(dist, torch, a):
+def _gather(dist, a):
     """Every rank's array A in rank order (the shards differ in size, which
     gloo's tensor all_gather does not take; the arrays travel pickled, bits
     unchanged)."""
@@ -176,7 +176,7 @@ def _rank_checks(rank, size, dist, torch):
                                    ("wv", "sv", kvd, k0, kr), ("wgate", "sgate", F, f0, fr),
                                    ("wup", "sup", F, f0, fr)):
         part = nlo.ternary_gemv_rows(x, _rows(T[w], H, r0, n), T[s][r0:r0 + n], B, n, H)
-        got = np.concatenate([p.reshape(B, -1) for p in _gather(dist, torch, part.reshape(B, n))],
+        got = np.concatenate([p.reshape(B, -1) for p in _gather(dist, part.reshape(B, n))],
                              axis=1)
         want = nlo.ternary_gemv_rows(x, T[w], T[s], B, full_rows, H).reshape(B, full_rows)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), w
@@ -185,7 +185,7 @@ def _rank_checks(rank, size, dist, torch):
     for w, s, a, cols, c0, n in (("wo", "so", ctx, qd, h0, hr), ("wdown", "sdown", act, F, f0, fr)):
         part = nlo.ternary_gemv_rows(np.ascontiguousarray(a[:, c0:c0 + n]), _cols(T[w], cols, c0, n),
                                      T[s], B, H, n).reshape(B, H)
-        parts = _gather(dist, torch, part)
+        parts = _gather(dist, part)
         t = torch.from_numpy(part.copy())
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         summed = t.numpy()
@@ -201,7 +201,7 @@ def _rank_checks(rank, size, dist, torch):
     E, h = _lm_problem(cfg)
     v0, vr = me["vocab_begin"], me["vocab"]
     mine = argmax_keys(_lm_logits(E[v0:v0 + vr], h), v0)
-    keys = np.stack([k.view(np.uint64) for k in _gather(dist, torch, mine.view(np.int64))])
+    keys = np.stack([k.view(np.uint64) for k in _gather(dist, mine.view(np.int64))])
     best = keys.max(axis=0)
     token = (np.uint64(0xFFFFFFFF) - (best & np.uint64(0xFFFFFFFF))).astype(np.int64)
     full = _lm_logits(E, h)

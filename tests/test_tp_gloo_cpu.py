@@ -15,6 +15,9 @@ back together the way the decoder does on the GPU:
 - the LM head is split by vocabulary rows: each rank's best (logit, index)
   key, all-gathered and maximised, gives the global greedy token with the
   lowest index winning a tie, inside one rank and across two.
+
+The same checks also run at three ranks (the row-split sums then within the
+tolerance only: gloo does not fix the order of three addends).
 """
 import datetime
 import multiprocessing as mp
@@ -215,11 +218,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_tp_layer_recombines_over_two_gloo_ranks():
+@pytest.mark.parametrize("size", [2, 3])
+def test_tp_layer_recombines_over_gloo_ranks(size):
+    """Two ranks (KV heads 2/1, FFN blocks 2/1, vocabulary 501/500) and three
+    (one KV head and one FFN block each, vocabulary 334/334/333)."""
     ctx = mp.get_context("spawn")
     errors = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, errors)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, size, port, errors)) for r in range(size)]
     for p in procs:
         p.start()
     for p in procs:

@@ -17,7 +17,10 @@ back together the way the decoder does on the GPU:
   lowest index winning a tie, inside one rank and across two.
 
 The same checks also run at three ranks (the row-split sums then within the
-tolerance only: gloo does not fix the order of three addends).
+tolerance only: gloo does not fix the order of three addends).  Each check
+has a control that must fail: the parts in the wrong rank order, one rank's
+partial product without the sum, and a tie-break that favours the higher
+index.
 """
 import datetime
 import multiprocessing as mp
@@ -183,6 +186,10 @@ def _rank_checks(rank, size, dist, torch):
                              axis=1)
         want = nlo.ternary_gemv_rows(x, T[w], T[s], B, full_rows, H).reshape(B, full_rows)
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), w
+        # control: the same parts in the wrong rank order do not give the product
+        parts = _gather(dist, part.reshape(B, n))
+        swapped = np.concatenate([p.reshape(B, -1) for p in parts[1:] + parts[:1]], axis=1)
+        assert not np.array_equal(swapped, want), w
 
     # split by input columns: O (the rank's query heads), down (its FFN rows)
     for w, s, a, cols, c0, n in (("wo", "so", ctx, qd, h0, hr), ("wdown", "sdown", act, F, f0, fr)):
@@ -199,6 +206,8 @@ def _rank_checks(rank, size, dist, torch):
             assert np.array_equal(summed.view(np.uint32), in_order.view(np.uint32)), w
         want = nlo.ternary_gemv_rows(a, T[w], T[s], B, H, cols).reshape(B, H)
         assert nlo.tk_err(summed, want) < ROW_SPLIT_TOL, (w, nlo.tk_err(summed, want))
+        # control: one rank's partial product without the all-reduce is far off
+        assert nlo.tk_err(parts[0], want) > 1e-2, w
 
     # LM head split by vocabulary rows: the best key of each rank, all-gathered
     E, h = _lm_problem(cfg)
@@ -210,6 +219,14 @@ def _rank_checks(rank, size, dist, torch):
     full = _lm_logits(E, h)
     assert token.tolist() == np.argmax(full, axis=1).tolist()
     assert token[0] == 100 and token[1] == 800
+    # control: a key whose low word favoured the higher index breaks the tie
+    # inside rank order the other way (row 1: 900, not 800)
+    v = np.ascontiguousarray(_lm_logits(E[v0:v0 + vr], h))
+    hi = [(float(r.max()), v0 + int(np.flatnonzero(r == r.max())[-1])) for r in v]
+    hi_all = [None] * size
+    dist.all_gather_object(hi_all, hi)
+    wrong = [max(q[b] for q in hi_all)[1] for b in range(len(hi))]
+    assert wrong[1] == 900 and wrong[0] == 700
 
 
 def _free_port():
